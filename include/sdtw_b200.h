@@ -1,0 +1,132 @@
+/*
+ * sdtw_b200.h -- C ABI of libsdtw_b200.so, the B200 (sm_100a) Soft-DTW engine.
+ *
+ * Plain pointers and sizes only: every device pointer is a CUDA device
+ * address of float32 data, row-major and contiguous; `stream` is a
+ * cudaStream_t passed as void* (NULL = the legacy default stream).  Every entry
+ * point validates its arguments, enqueues its kernels on `stream` and returns
+ * without synchronising.  The library allocates no device memory: the caller
+ * passes the outputs and a workspace of the size the *_workspace_bytes
+ * functions report.  The only persistent allocation is one mapped pinned host
+ * word used as the error status of the device-side bounded waits.
+ *
+ * Each entry point replaces one function of the reference package
+ * (BGU-CS-VIL/sdtw-cuda-torch, softdtw_cuda/...), cited below as file:line.
+ *
+ * The "score" table takes the place of the reference's R table
+ * (B, N+2, M+2): it holds T = -R * log2(e) / gamma for every cell in the
+ * anti-diagonal ("wavefront") layout the kernels write with coalesced stores.
+ * sdtw_score_to_R_f32 / sdtw_R_to_score_f32 convert to and from the
+ * reference layout.
+ */
+#ifndef SDTW_B200_H
+#define SDTW_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define SDTW_OK 0
+#define SDTW_ERR_INVALID_ARGUMENT 1 /* bad size, pointer, gamma or workspace */
+#define SDTW_ERR_CUDA 2             /* a CUDA runtime call failed (see sdtw_last_error_message) */
+#define SDTW_ERR_TIMEOUT 3          /* a device-side wait ran out of time; results are invalid */
+
+/* Library version string. */
+const char *sdtw_version(void);
+
+/* Human-readable text for a return code, and detail of the last failure on
+ * the calling thread. */
+const char *sdtw_error_string(int code);
+const char *sdtw_last_error_message(void);
+
+/* Reads and clears the device status word written by the kernels' bounded
+ * waits (0 = no failure).  It does not synchronise: call it after the stream
+ * has been synchronised to observe the kernels enqueued before. */
+int sdtw_status(void);
+
+/* Wall-clock limit of one device-side wait, in nanoseconds (default 2e9). */
+void sdtw_set_wait_timeout_ns(unsigned long long ns);
+
+/* Failure-detection test hook: the producer of stripe `stripe` (32-row band
+ * of the DP table) withholds its output so that its consumer's wait runs out.
+ * -1 disables.  Never set outside tests. */
+void sdtw_debug_stall_stripe(int stripe);
+
+/* Number of float32 elements of the score table for a (B,N,M) problem. */
+size_t sdtw_score_elems(int B, int N, int M);
+
+/* Workspace bytes of sdtw_forward_f32 / sdtw_backward_f32 (D input). */
+size_t sdtw_workspace_bytes(int B, int N, int M);
+
+/* Workspace bytes of sdtw_forward_xy_f32 / sdtw_backward_xy_f32 (x, y input). */
+size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim);
+
+/* Cost matrix D (B,N,M) from x (B,N,dim), y (B,M,dim).
+ *   direct == 0: ||x_i||^2 + ||y_j||^2 - 2 x_i.y_j clamped at 0
+ *                -- replaces softdtw_cuda/distances.py:6-28 (sqeuclidean)
+ *   direct != 0: sum_k (x_ik - y_jk)^2
+ *                -- the fused cost of softdtw_cuda/cuda/kernels.py:27-31 */
+int sdtw_cost_sqeuclid_f32(const float *x, const float *y, float *D, int B, int N, int M, int dim,
+                           int direct, void *stream);
+
+/* Forward DP over a cost matrix: score (sdtw_score_elems) and out (B,) = R[N,M].
+ * bandwidth <= 0 disables the Sakoe-Chiba band.
+ * -- replaces softdtw_cuda/cuda/launcher.py:167-223 (softdtw_forward_cuda) */
+int sdtw_forward_f32(const float *D, float *score, float *out, int B, int N, int M, float gamma,
+                     float bandwidth, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Reverse DP: E (B,N,M) = grad_out[b] * d out[b] / d D[b,i,j] (grad_out NULL = ones).
+ * -- replaces softdtw_cuda/cuda/launcher.py:226-300 (softdtw_backward_cuda_log)
+ *    together with the scaling of softdtw_cuda/autograd.py:46-47 */
+int sdtw_backward_f32(const float *score, const float *grad_out, float *E, int B, int N, int M,
+                      float gamma, float bandwidth, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
+/* Fused forward on x (B,N,dim), y (B,M,dim) with the direct squared-Euclidean
+ * cost.  -- replaces softdtw_cuda/cuda/launcher.py:33-87
+ *          (softdtw_forward_cuda_fused_sqeuclid) */
+int sdtw_forward_xy_f32(const float *x, const float *y, float *score, float *out, int B, int N, int M,
+                        int dim, float gamma, float bandwidth, void *workspace, size_t workspace_bytes,
+                        void *stream);
+
+/* Fused backward: grad_x (B,N,dim), grad_y (B,M,dim) of sum_b grad_out[b]*out[b]
+ * (either gradient pointer may be NULL).
+ * -- replaces softdtw_cuda/cuda/launcher.py:90-162
+ *    (softdtw_backward_cuda_fused_sqeuclid) and the chain rule of
+ *    softdtw_cuda/autograd_xy.py:32-51 */
+int sdtw_backward_xy_f32(const float *x, const float *y, const float *score, const float *grad_out,
+                         float *grad_x, float *grad_y, int B, int N, int M, int dim, float gamma,
+                         float bandwidth, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Chain rule of the unfused cost: given G = dL/dD (B,N,M) and the clamped cost
+ * D used as the clamp mask (NULL = no mask), writes grad_x, grad_y.
+ * -- replaces torch autograd of softdtw_cuda/distances.py:20-28 */
+int sdtw_grad_sqeuclid_f32(const float *G, const float *D_mask, const float *x, const float *y,
+                           float *grad_x, float *grad_y, int B, int N, int M, int dim, void *stream);
+
+/* Score table <-> reference R layout (B,N+2,M+2): R[:,0,0] = 0, other borders
+ * +inf, interior R = -T*gamma*ln 2.
+ * -- the R tensor of softdtw_cuda/cuda/launcher.py:55-56, 177-178 */
+int sdtw_score_to_R_f32(const float *score, float *R, int B, int N, int M, float gamma, void *stream);
+int sdtw_R_to_score_f32(const float *R, float *score, int B, int N, int M, float gamma, void *stream);
+
+/* Host implementation for CPU tensors (double precision, OpenMP over the
+ * batch).  R is the reference layout (B,N+2,M+2); E is (B,N,M) scaled by
+ * grad_out (NULL = ones).
+ * -- replaces softdtw_cuda/cuda/launcher.py:307-324 and :356-361
+ *    (_softdtw_forward_cpu_np, softdtw_forward_cpu) */
+int sdtw_cpu_forward_f64(const double *D, double *R, double *out, int B, int N, int M, double gamma,
+                         double bandwidth);
+/* -- replaces softdtw_cuda/cuda/launcher.py:327-353 and :364-368
+ *    (_softdtw_backward_cpu_np, softdtw_backward_cpu) */
+int sdtw_cpu_backward_f64(const double *R, const double *grad_out, double *E, int B, int N, int M,
+                          double gamma, double bandwidth);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SDTW_B200_H */

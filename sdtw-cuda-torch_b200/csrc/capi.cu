@@ -1,0 +1,287 @@
+// capi.cu -- the extern "C" entry points of libsdtw_b200.so (include/sdtw_b200.h).
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/sdtw_b200.h"
+#include "sdtw_kernels.h"
+
+namespace {
+
+using namespace sdtw;
+
+thread_local std::string g_last_error;
+std::atomic<uint32_t> g_seq{1};
+std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+std::atomic<int> g_debug_stall{-1};
+std::mutex g_init_mu;
+int* g_status_host = nullptr;    // mapped pinned word
+int* g_status_dev = nullptr;     // its device address
+int g_num_sms[64] = {0};
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr double kLn2 = 0.6931471805599453;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(SDTW_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+int ensure_status() {
+    if (g_status_dev) return SDTW_OK;
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (g_status_dev) return SDTW_OK;
+    int* h = nullptr;
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&h), sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(status)");
+    *h = 0;
+    int* d = nullptr;
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer(status)");
+    g_status_host = h;
+    g_status_dev = d;
+    return SDTW_OK;
+}
+
+int num_sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev < 0 || dev >= 64) return 148;
+    if (g_num_sms[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_num_sms[dev] = n;
+    }
+    return g_num_sms[dev];
+}
+
+// A failure recorded by an earlier launch surfaces at the next call.
+int pending_status() {
+    if (g_status_host) {
+        int s = *reinterpret_cast<volatile int*>(g_status_host);
+        if (s != 0) {
+            *reinterpret_cast<volatile int*>(g_status_host) = 0;
+            return fail(SDTW_ERR_TIMEOUT, "a device-side wait of an earlier launch timed out");
+        }
+    }
+    return SDTW_OK;
+}
+
+int check_dims(int B, int N, int M) {
+    if (B <= 0 || N <= 0 || M <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "B, N and M must be > 0");
+    if ((long long)N + 64 >= (1ll << 30) || (long long)M + 64 >= (1ll << 30))
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "sequence length too large");
+    return SDTW_OK;
+}
+
+int check_gamma(float gamma) {
+    if (!(gamma > 0.f) || !std::isfinite(gamma)) return fail(SDTW_ERR_INVALID_ARGUMENT, "gamma must be finite and > 0");
+    return SDTW_OK;
+}
+
+WaitCtx wait_ctx() {
+    WaitCtx w;
+    w.status = g_status_dev;
+    w.timeout_ns = g_timeout_ns.load();
+    return w;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Workspace layout: [wrap ring][cost or E scratch (xy paths)]
+size_t wave_ws(int B, int N, int M) {
+    WavePlan p = make_plan(B, N, M, num_sms());
+    return align_up(wrap_bytes(p), 256);
+}
+
+int run_forward(const float* D, float* score, float* out, int B, int N, int M, float gamma, float bw,
+                uint64_t* wrap, cudaStream_t stream) {
+    FwdArgs a{};
+    a.P = make_plan(B, N, M, num_sms());
+    a.D = D;
+    a.score = score;
+    a.out = out;
+    a.wrap = wrap;
+    a.kk = kLog2e / gamma;
+    a.inv_k = static_cast<float>(1.0 / static_cast<double>(a.kk));
+    a.bw = bw > 0.f ? bw : -1.f;
+    a.seq = g_seq.fetch_add(1);
+    a.debug_stall = g_debug_stall.load();
+    a.wait = wait_ctx();
+    cudaError_t e = launch_forward(a, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "forward launch");
+    return SDTW_OK;
+}
+
+int run_backward(const float* score, const float* grad_out, float* E, int B, int N, int M, float bw,
+                 uint64_t* wrap, cudaStream_t stream) {
+    BwdArgs a{};
+    a.P = make_plan(B, N, M, num_sms());
+    a.score = score;
+    a.grad_out = grad_out;
+    a.E = E;
+    a.wrap = wrap;
+    a.bw = bw > 0.f ? bw : -1.f;
+    a.seq = g_seq.fetch_add(1);
+    a.debug_stall = g_debug_stall.load();
+    a.wait = wait_ctx();
+    cudaError_t e = launch_backward(a, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+    return SDTW_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sdtw_version(void) { return "sdtw-b200 0.1.0 (sm_100a)"; }
+
+const char* sdtw_error_string(int code) {
+    switch (code) {
+        case SDTW_OK: return "ok";
+        case SDTW_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case SDTW_ERR_CUDA: return "CUDA runtime error";
+        case SDTW_ERR_TIMEOUT: return "device-side wait timed out";
+        default: return "unknown error";
+    }
+}
+
+const char* sdtw_last_error_message(void) { return g_last_error.c_str(); }
+
+int sdtw_status(void) {
+    if (!g_status_host) return 0;
+    int s = *reinterpret_cast<volatile int*>(g_status_host);
+    *reinterpret_cast<volatile int*>(g_status_host) = 0;
+    return s;
+}
+
+void sdtw_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1ull); }
+
+void sdtw_debug_stall_stripe(int stripe) { g_debug_stall.store(stripe); }
+
+size_t sdtw_score_elems(int B, int N, int M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return score_elems(B, N, M);
+}
+
+size_t sdtw_workspace_bytes(int B, int N, int M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return wave_ws(B, N, M);
+}
+
+size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim) {
+    if (B <= 0 || N <= 0 || M <= 0 || dim <= 0) return 0;
+    return wave_ws(B, N, M) + align_up((size_t)B * N * M * sizeof(float), 256);
+}
+
+int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int N, int M, int dim, int direct,
+                           void* stream) {
+    int rc = check_dims(B, N, M);
+    if (rc) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y || !D) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e = launch_cost(x, y, D, B, N, M, dim, direct != 0, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cost launch");
+    return SDTW_OK;
+}
+
+int sdtw_forward_f32(const float* D, float* score, float* out, int B, int N, int M, float gamma, float bandwidth,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if (!D || !score || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (workspace_bytes < wave_ws(B, N, M) || (wave_ws(B, N, M) && !workspace))
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    return run_forward(D, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace),
+                       static_cast<cudaStream_t>(stream));
+}
+
+int sdtw_backward_f32(const float* score, const float* grad_out, float* E, int B, int N, int M, float gamma,
+                      float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if (!score || !E) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (workspace_bytes < wave_ws(B, N, M) || (wave_ws(B, N, M) && !workspace))
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    return run_backward(score, grad_out, E, B, N, M, bandwidth, static_cast<uint64_t*>(workspace),
+                        static_cast<cudaStream_t>(stream));
+}
+
+int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out, int B, int N, int M, int dim,
+                        float gamma, float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y || !score || !out || !workspace) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (workspace_bytes < sdtw_workspace_bytes_xy(B, N, M, dim)) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t wrap_sz = wave_ws(B, N, M);
+    float* Dtmp = reinterpret_cast<float*>(static_cast<char*>(workspace) + wrap_sz);
+    cudaError_t e = launch_cost(x, y, Dtmp, B, N, M, dim, true, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cost launch");
+    return run_forward(Dtmp, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
+}
+
+int sdtw_backward_xy_f32(const float* x, const float* y, const float* score, const float* grad_out, float* grad_x,
+                         float* grad_y, int B, int N, int M, int dim, float gamma, float bandwidth, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y || !score || !workspace) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (workspace_bytes < sdtw_workspace_bytes_xy(B, N, M, dim)) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t wrap_sz = wave_ws(B, N, M);
+    float* Etmp = reinterpret_cast<float*>(static_cast<char*>(workspace) + wrap_sz);
+    rc = run_backward(score, grad_out, Etmp, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st);
+    if (rc) return rc;
+    cudaError_t e = launch_grad_xy(Etmp, nullptr, x, y, grad_x, grad_y, B, N, M, dim, st);
+    if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+    return SDTW_OK;
+}
+
+int sdtw_grad_sqeuclid_f32(const float* G, const float* D_mask, const float* x, const float* y, float* grad_x,
+                           float* grad_y, int B, int N, int M, int dim, void* stream) {
+    int rc = check_dims(B, N, M);
+    if (rc) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!G || !x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e = launch_grad_xy(G, D_mask, x, y, grad_x, grad_y, B, N, M, dim, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+    return SDTW_OK;
+}
+
+int sdtw_score_to_R_f32(const float* score, float* R, int B, int N, int M, float gamma, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    WavePlan p = make_plan(B, N, M, num_sms());
+    const float kk = kLog2e / gamma;
+    cudaError_t e = launch_score_to_R(score, R, p, static_cast<float>(1.0 / (double)kk), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "score_to_R launch");
+    return SDTW_OK;
+}
+
+int sdtw_R_to_score_f32(const float* R, float* score, int B, int N, int M, float gamma, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    WavePlan p = make_plan(B, N, M, num_sms());
+    cudaError_t e = launch_R_to_score(R, score, p, kLog2e / gamma, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "R_to_score launch");
+    return SDTW_OK;
+}
+
+}  // extern "C"

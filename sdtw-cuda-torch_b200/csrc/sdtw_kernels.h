@@ -1,0 +1,51 @@
+// sdtw_kernels.h -- argument blocks and launchers of the device kernels
+// (internal to libsdtw_b200; the public C-ABI is include/sdtw_b200.h).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "sdtw_device.cuh"
+#include "sdtw_plan.h"
+
+namespace sdtw {
+
+struct FwdArgs {
+    WavePlan P;
+    const float* D;   // (B,N,M) cost, row-major
+    float* score;     // wavefront-layout score store (see sdtw_plan.h)
+    float* out;       // (B,) R[N,M]
+    uint64_t* wrap;   // (B*M) band-wrap ring, null when n_bands == 1
+    float kk;         // log2(e) / gamma
+    float inv_k;      // gamma * ln(2)
+    float bw;         // Sakoe-Chiba bandwidth, <= 0 disables
+    uint32_t seq;     // launch sequence number (tags of the global ring)
+    int debug_stall;  // stripe whose output is withheld (failure-detection tests); -1 = none
+    WaitCtx wait;
+};
+
+struct BwdArgs {
+    WavePlan P;
+    const float* score;
+    const float* grad_out;  // (B,) upstream gradient, null = ones
+    float* E;               // (B,N,M) output: grad_out[b] * dR[N,M]/dD[i,j]
+    uint64_t* wrap;
+    float bw;
+    uint32_t seq;
+    int debug_stall;
+    WaitCtx wait;
+};
+
+cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
+cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
+cudaError_t launch_score_to_R(const float* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
+cudaError_t launch_R_to_score(const float* R, float* S, const WavePlan& P, float kk, cudaStream_t stream);
+
+// dense.cu
+cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, int M, int dim, bool direct,
+                        cudaStream_t stream);
+cudaError_t launch_grad_xy(const float* G, const float* mask, const float* x, const float* y, float* gx,
+                           float* gy, int B, int N, int M, int dim, cudaStream_t stream);
+
+}  // namespace sdtw

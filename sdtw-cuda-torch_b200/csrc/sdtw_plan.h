@@ -1,0 +1,79 @@
+// sdtw_plan.h -- launch geometry and the score-store layout of the wavefront
+// kernels (host and device).
+//
+// A problem (one (x_b, y_b) pair, N rows by M columns) is cut into horizontal
+// stripes of 32*K rows.  One warp owns a stripe: lane l holds rows
+// l*K .. l*K+K-1 of it and the warp sweeps the stripe's anti-diagonals, so at
+// local step t lane l works on columns t - l*K - k.  Stripes form a chain:
+// stripe s needs the bottom row of stripe s-1 (forward) or sends messages to it
+// (backward).  G consecutive stripes ("a band") run concurrently on the G warps
+// of one thread-block cluster (wpc warps per CTA, csize CTAs); longer problems
+// loop over bands inside the same cluster, the last warp of band b handing its
+// bottom row to the first warp of band b+1 through a global ring.
+//
+// Score store ("wavefront layout"): for problem b, stripe s, local
+// anti-diagonal t in [0, n_diag) and in-stripe position p = k*32 + l,
+//     score[((b*n_stripes + s)*n_diag + t)*(32*K) + p]
+// holds T(row = s*32*K + l*K + k, col = t - l*K - k) = -R(row, col)*log2(e)/gamma.
+// One warp step writes 32 consecutive floats per k: a coalesced 128-byte store.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace sdtw {
+
+struct WavePlan {
+    int B, N, M;
+    int K;          // rows per lane (template parameter of the kernels)
+    int wpc;        // warps per CTA
+    int csize;      // CTAs per problem (cluster size)
+    int G;          // warps per band = wpc * csize
+    int n_stripes;  // ceil(N / (32*K))
+    int n_bands;    // ceil(n_stripes / G)
+    int n_diag;     // M + 32*K - 1
+};
+
+// Rows per lane as a function of the problem only (the score layout depends on
+// it, so forward and backward must agree).
+inline int rows_per_lane(int N) {
+    (void)N;
+    return 1;
+}
+
+inline size_t score_elems(int B, int N, int M) {
+    const int K = rows_per_lane(N);
+    const size_t sr = 32u * (size_t)K;
+    const size_t ns = ((size_t)N + sr - 1) / sr;
+    return (size_t)B * ns * ((size_t)M + sr - 1) * sr;
+}
+
+inline WavePlan make_plan(int B, int N, int M, int num_sms) {
+    WavePlan p{};
+    p.B = B;
+    p.N = N;
+    p.M = M;
+    p.K = rows_per_lane(N);
+    const int sr = 32 * p.K;
+    p.n_stripes = (N + sr - 1) / sr;
+    p.n_diag = M + sr - 1;
+    // Spread a problem over up to 8 CTAs (portable cluster size) while the
+    // batch alone would leave SMs idle.
+    int cs = 1;
+    while (cs < 8 && (long long)B * cs * 2 <= (long long)num_sms && cs * 2 <= p.n_stripes) cs *= 2;
+    int wpc = (p.n_stripes + cs - 1) / cs;
+    if (wpc > 16) wpc = 16;
+    if (wpc < 1) wpc = 1;
+    p.csize = cs;
+    p.wpc = wpc;
+    p.G = wpc * cs;
+    p.n_bands = (p.n_stripes + p.G - 1) / p.G;
+    return p;
+}
+
+// Global band-wrap ring: one tagged u64 per column per problem.
+inline size_t wrap_bytes(const WavePlan& p) {
+    return p.n_bands > 1 ? (size_t)p.B * (size_t)p.M * 8u : 0u;
+}
+
+}  // namespace sdtw

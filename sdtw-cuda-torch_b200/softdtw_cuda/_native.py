@@ -1,0 +1,305 @@
+"""ctypes binding of libsdtw_b200.so (the C ABI declared in include/sdtw_b200.h).
+
+Every CUDA tensor operation of the package goes through this module.  There is
+no fallback: if the library is missing or a call fails, a RuntimeError is
+raised.  PyTorch supplies device memory (outputs and workspaces) and the
+current CUDA stream; the kernels are the library's.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libsdtw_b200.so")
+
+_lib = None
+_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+_Dbl = ctypes.c_double
+_SZ = ctypes.c_size_t
+
+_SIGS = {
+    "sdtw_version": ([], ctypes.c_char_p),
+    "sdtw_error_string": ([_I], ctypes.c_char_p),
+    "sdtw_last_error_message": ([], ctypes.c_char_p),
+    "sdtw_status": ([], _I),
+    "sdtw_set_wait_timeout_ns": ([ctypes.c_ulonglong], None),
+    "sdtw_debug_stall_stripe": ([_I], None),
+    "sdtw_score_elems": ([_I, _I, _I], _SZ),
+    "sdtw_workspace_bytes": ([_I, _I, _I], _SZ),
+    "sdtw_workspace_bytes_xy": ([_I, _I, _I, _I], _SZ),
+    "sdtw_cost_sqeuclid_f32": ([_P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "sdtw_forward_f32": ([_P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_backward_f32": ([_P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_forward_xy_f32": ([_P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_backward_xy_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_grad_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "sdtw_score_to_R_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
+    "sdtw_R_to_score_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
+    "sdtw_cpu_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
+    "sdtw_cpu_backward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
+}
+
+# Every symbol the header declares (tests check the library exports them).
+EXPORTED = tuple(_SIGS)
+
+
+def lib():
+    """Load the library once (RuntimeError if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"softdtw_cuda: native library {LIB_PATH} is missing; build it with "
+                    "`python -m softdtw_cuda._build` (or __graft_entry__.build())")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (args, res) in _SIGS.items():
+                fn = getattr(L, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = L
+    return _lib
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+# Kernel-launch accounting: number of library kernels each entry point enqueues.
+KERNELS_PER_OP = {"cost": 1, "forward": 1, "backward": 1, "forward_xy": 2, "backward_xy": 3,
+                  "grad_sqeuclid": 2, "score_to_R": 1, "R_to_score": 1}
+launch_count = 0
+# When a list, every op appends (name, start_event, end_event) recorded on the
+# stream it launched on (used by bench.py for per-kernel timing).
+profile_events = None
+
+
+def _op_begin(device):
+    if profile_events is None:
+        return None
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record(torch.cuda.current_stream(device))
+    return ev
+
+
+def _op_end(name, device, ev0, n_kernels=None):
+    global launch_count
+    launch_count += KERNELS_PER_OP[name] if n_kernels is None else n_kernels
+    if ev0 is not None:
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev1.record(torch.cuda.current_stream(device))
+        profile_events.append((name, ev0, ev1))
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        L = lib()
+        msg = L.sdtw_last_error_message().decode(errors="replace")
+        kind = L.sdtw_error_string(rc).decode(errors="replace")
+        raise NativeError(f"softdtw_cuda: {what} failed: {kind}: {msg}")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def status() -> int:
+    """Read and clear the device wait status (0 = ok).  Synchronise first."""
+    return int(lib().sdtw_status())
+
+
+def check_status(device=None) -> None:
+    """Synchronise ``device`` and raise if a device-side wait timed out."""
+    if torch.cuda.is_available():
+        torch.cuda.synchronize(device)
+    s = status()
+    if s != 0:
+        raise NativeError(f"softdtw_cuda: device-side wait failed (status {s}: "
+                          f"{lib().sdtw_error_string(s).decode()})")
+
+
+def set_wait_timeout(seconds: float) -> None:
+    lib().sdtw_set_wait_timeout_ns(int(seconds * 1e9))
+
+
+def debug_stall_stripe(stripe: int) -> None:
+    lib().sdtw_debug_stall_stripe(int(stripe))
+
+
+def version() -> str:
+    return lib().sdtw_version().decode()
+
+
+# ----------------------------------------------------------------------------- sizes
+def score_elems(B: int, N: int, M: int) -> int:
+    return int(lib().sdtw_score_elems(B, N, M))
+
+
+def workspace(B: int, N: int, M: int, device, dim: int | None = None) -> torch.Tensor:
+    L = lib()
+    n = L.sdtw_workspace_bytes(B, N, M) if dim is None else L.sdtw_workspace_bytes_xy(B, N, M, dim)
+    return torch.empty(max(int(n), 1), dtype=torch.uint8, device=device)
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to(dtype=torch.float32).contiguous()
+
+
+# ----------------------------------------------------------------------------- CUDA ops
+def cost_sqeuclid(x: torch.Tensor, y: torch.Tensor, direct: bool = False) -> torch.Tensor:
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    D = torch.empty((B, N, M), dtype=torch.float32, device=x.device)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_cost_sqeuclid_f32(_ptr(x), _ptr(y), _ptr(D), B, N, M, dim, int(direct), _stream(x.device))
+    _check(rc, "cost")
+    _op_end("cost", x.device, ev)
+    return D
+
+
+def forward(D: torch.Tensor, gamma: float, bandwidth: float):
+    """(out (B,), score) for a CUDA cost tensor D (B,N,M)."""
+    D = _f32(D)
+    B, N, M = D.shape
+    score = torch.empty(score_elems(B, N, M), dtype=torch.float32, device=D.device)
+    out = torch.empty(B, dtype=torch.float32, device=D.device)
+    ws = workspace(B, N, M, D.device)
+    ev = _op_begin(D.device)
+    with torch.cuda.device(D.device):
+        rc = lib().sdtw_forward_f32(_ptr(D), _ptr(score), _ptr(out), B, N, M, float(gamma), float(bandwidth),
+                                    _ptr(ws), ws.numel(), _stream(D.device))
+    _check(rc, "forward")
+    _op_end("forward", D.device, ev)
+    return out, score
+
+
+def backward(score: torch.Tensor, grad_out: torch.Tensor | None, B: int, N: int, M: int, gamma: float,
+             bandwidth: float) -> torch.Tensor:
+    """E (B,N,M) = grad_out[b] * dR[N,M]/dD."""
+    dev = score.device
+    E = torch.empty((B, N, M), dtype=torch.float32, device=dev)
+    g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    ws = workspace(B, N, M, dev)
+    ev = _op_begin(dev)
+    with torch.cuda.device(dev):
+        rc = lib().sdtw_backward_f32(_ptr(score), _ptr(g), _ptr(E), B, N, M, float(gamma), float(bandwidth),
+                                     _ptr(ws), ws.numel(), _stream(dev))
+    _check(rc, "backward")
+    _op_end("backward", dev, ev)
+    return E
+
+
+def forward_xy(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float):
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    score = torch.empty(score_elems(B, N, M), dtype=torch.float32, device=x.device)
+    out = torch.empty(B, dtype=torch.float32, device=x.device)
+    ws = workspace(B, N, M, x.device, dim)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_forward_xy_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(out), B, N, M, dim, float(gamma),
+                                       float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
+    _check(rc, "fused forward")
+    _op_end("forward_xy", x.device, ev)
+    return out, score
+
+
+def backward_xy(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad_out: torch.Tensor | None,
+                gamma: float, bandwidth: float, need_x: bool = True, need_y: bool = True):
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    gx = torch.empty_like(x) if need_x else None
+    gy = torch.empty_like(y) if need_y else None
+    g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    ws = workspace(B, N, M, x.device, dim)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_backward_xy_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(g), _ptr(gx), _ptr(gy), B, N, M, dim,
+                                        float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
+    _check(rc, "fused backward")
+    _op_end("backward_xy", x.device, ev, 1 + int(need_x) + int(need_y))
+    return gx, gy
+
+
+def grad_sqeuclid(G: torch.Tensor, D_mask: torch.Tensor | None, x: torch.Tensor, y: torch.Tensor,
+                  need_x: bool = True, need_y: bool = True):
+    G = _f32(G)
+    x = _f32(x)
+    y = _f32(y)
+    Dm = None if D_mask is None else _f32(D_mask)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    gx = torch.empty_like(x) if need_x else None
+    gy = torch.empty_like(y) if need_y else None
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_grad_sqeuclid_f32(_ptr(G), _ptr(Dm), _ptr(x), _ptr(y), _ptr(gx), _ptr(gy), B, N, M, dim,
+                                          _stream(x.device))
+    _check(rc, "cost gradient")
+    _op_end("grad_sqeuclid", x.device, ev, int(need_x) + int(need_y))
+    return gx, gy
+
+
+def score_to_R(score: torch.Tensor, B: int, N: int, M: int, gamma: float) -> torch.Tensor:
+    R = torch.empty((B, N + 2, M + 2), dtype=torch.float32, device=score.device)
+    with torch.cuda.device(score.device):
+        rc = lib().sdtw_score_to_R_f32(_ptr(score), _ptr(R), B, N, M, float(gamma), _stream(score.device))
+    _check(rc, "score_to_R")
+    _op_end("score_to_R", score.device, None)
+    return R
+
+
+def R_to_score(R: torch.Tensor, gamma: float) -> torch.Tensor:
+    R = _f32(R)
+    B, N2, M2 = R.shape
+    N, M = N2 - 2, M2 - 2
+    score = torch.empty(score_elems(B, N, M), dtype=torch.float32, device=R.device)
+    with torch.cuda.device(R.device):
+        rc = lib().sdtw_R_to_score_f32(_ptr(R), _ptr(score), B, N, M, float(gamma), _stream(R.device))
+    _check(rc, "R_to_score")
+    _op_end("R_to_score", R.device, None)
+    return score
+
+
+# ----------------------------------------------------------------------------- CPU ops
+def cpu_forward(D: torch.Tensor, gamma: float, bandwidth: float):
+    """(out, R) in float64 for a CPU cost tensor; R uses the reference layout."""
+    Dd = D.detach().to(dtype=torch.float64).contiguous()
+    B, N, M = Dd.shape
+    R = torch.empty((B, N + 2, M + 2), dtype=torch.float64)
+    out = torch.empty(B, dtype=torch.float64)
+    rc = lib().sdtw_cpu_forward_f64(_ptr(Dd), _ptr(R), _ptr(out), B, N, M, float(gamma), float(bandwidth))
+    _check(rc, "cpu forward")
+    return out, R
+
+
+def cpu_backward(R: torch.Tensor, grad_out: torch.Tensor | None, gamma: float, bandwidth: float) -> torch.Tensor:
+    Rd = R.detach().to(dtype=torch.float64).contiguous()
+    B, N2, M2 = Rd.shape
+    N, M = N2 - 2, M2 - 2
+    E = torch.empty((B, N, M), dtype=torch.float64)
+    g = None if grad_out is None else grad_out.detach().reshape(-1).to(dtype=torch.float64).contiguous()
+    rc = lib().sdtw_cpu_backward_f64(_ptr(Rd), _ptr(g), _ptr(E), B, N, M, float(gamma), float(bandwidth))
+    _check(rc, "cpu backward")
+    return E

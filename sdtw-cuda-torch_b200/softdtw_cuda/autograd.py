@@ -1,0 +1,59 @@
+"""Soft-DTW on an arbitrary cost matrix D (softdtw_cuda/autograd.py:11-48).
+
+``SoftDTWAutograd.apply(D, gamma, bandwidth)`` returns R[N,M] per batch
+element; its backward returns grad_D = grad_out[b] * E[b] where E is the
+expected alignment matrix.  CUDA tensors use the libsdtw_b200 wavefront kernels
+(float32 arithmetic; float16/bfloat16 inputs are computed in float32), CPU
+tensors the library's double-precision host implementation.
+"""
+from __future__ import annotations
+
+import torch
+from torch.autograd import Function
+
+from . import _native
+from .utils.checks import check_D
+
+
+def _normalize_bandwidth(bandwidth) -> float:
+    # None or <= 0 disables the band (autograd.py:19-23).
+    if bandwidth is None:
+        return -1.0
+    bw = float(bandwidth)
+    return -1.0 if bw <= 0 else bw
+
+
+class SoftDTWAutograd(Function):
+    @staticmethod
+    def forward(ctx, D: torch.Tensor, gamma: float, bandwidth: float | None):
+        check_D(D)
+        gamma_f = float(gamma)
+        if gamma_f <= 0:
+            raise ValueError(f"gamma must be > 0, got {gamma_f}")
+        bw = _normalize_bandwidth(bandwidth)
+        B, N, M = D.shape
+        if D.is_cuda:
+            if D.dtype == torch.float64:
+                raise NotImplementedError(
+                    "softdtw_cuda: float64 cost matrices on CUDA are not supported by the B200 kernels yet; "
+                    "use float32 (or a CPU tensor for float64)")
+            out, table = _native.forward(D, gamma_f, bw)
+        else:
+            out, table = _native.cpu_forward(D, gamma_f, bw)
+        ctx.save_for_backward(table)
+        ctx.gamma = gamma_f
+        ctx.bandwidth = bw
+        ctx.dims = (B, N, M)
+        ctx.cuda = D.is_cuda
+        ctx.dtype = D.dtype
+        return out.to(D.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        (table,) = ctx.saved_tensors
+        B, N, M = ctx.dims
+        if ctx.cuda:
+            E = _native.backward(table, grad_output, B, N, M, ctx.gamma, ctx.bandwidth)
+        else:
+            E = _native.cpu_backward(table, grad_output, ctx.gamma, ctx.bandwidth)
+        return E.to(ctx.dtype), None, None

@@ -1,0 +1,43 @@
+"""Fused squared-Euclidean Soft-DTW on x, y (softdtw_cuda/autograd_xy.py:12-51).
+
+``SoftDTWXYAutograd.apply(X, Y, gamma, bandwidth)`` computes the cost
+sum_k (x_ik - y_jk)^2 inside the library (no cost tensor is returned to the
+caller) and its backward returns dL/dX and dL/dY directly:
+    grad_X = 2 (X * rowsum(G) - G Y),  grad_Y = 2 (Y * colsum(G) - G^T X),
+G = grad_out[b] * E[b].  CUDA only, as in the reference.
+"""
+from __future__ import annotations
+
+import torch
+from torch.autograd import Function
+
+from . import _native
+from .autograd import _normalize_bandwidth
+
+
+class SoftDTWXYAutograd(Function):
+    @staticmethod
+    def forward(ctx, X: torch.Tensor, Y: torch.Tensor, gamma: float, bandwidth: float | None):
+        if not (X.is_cuda and Y.is_cuda):
+            raise ValueError("Expected CUDA tensors X and Y")
+        if X.dim() != 3 or Y.dim() != 3:
+            raise ValueError(f"Expected X,Y as (B,N,D)/(B,M,D). Got {tuple(X.shape)} and {tuple(Y.shape)}")
+        if X.shape[0] != Y.shape[0] or X.shape[2] != Y.shape[2]:
+            raise ValueError(f"Batch/features mismatch: {tuple(X.shape)} vs {tuple(Y.shape)}")
+        if X.dtype == torch.float64 or Y.dtype == torch.float64:
+            raise NotImplementedError(
+                "softdtw_cuda: float64 inputs on CUDA are not supported by the B200 kernels yet; use float32")
+        gamma_f = float(gamma)
+        bw = _normalize_bandwidth(bandwidth)
+        out, score = _native.forward_xy(X, Y, gamma_f, bw)
+        ctx.save_for_backward(X, Y, score)
+        ctx.gamma = gamma_f
+        ctx.bandwidth = bw
+        return out.to(X.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        X, Y, score = ctx.saved_tensors
+        gx, gy = _native.backward_xy(X, Y, score, grad_output, ctx.gamma, ctx.bandwidth,
+                                     need_x=ctx.needs_input_grad[0], need_y=ctx.needs_input_grad[1])
+        return (None if gx is None else gx.to(X.dtype)), (None if gy is None else gy.to(Y.dtype)), None, None

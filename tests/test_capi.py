@@ -1,0 +1,61 @@
+"""The C-ABI library loads, exports every entry point include/sdtw_b200.h
+declares, and rejects bad arguments before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from softdtw_cuda import _native
+
+HEADER = os.path.join(ROOT, "include", "sdtw_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(sdtw_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "sdtw_forward_f32" in names and "sdtw_backward_xy_f32" in names
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(_native.LIB_PATH)
+    missing = [n for n in _declared() if not hasattr(L, n)]
+    assert not missing, f"not exported: {missing}"
+    assert set(_declared()) <= set(_native.EXPORTED), "binding lacks a signature for a declared symbol"
+
+
+def test_sizes_without_gpu():
+    L = _native.lib()
+    assert L.sdtw_score_elems(4, 64, 64) == 4 * 2 * (64 + 31) * 32
+    assert L.sdtw_score_elems(0, 4, 4) == 0
+    assert L.sdtw_workspace_bytes(4, 64, 64) == 0          # one band: no wrap ring
+    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) >= 4 * 64 * 64 * 4
+
+
+def test_invalid_arguments_rejected():
+    L = _native.lib()
+    rc = L.sdtw_forward_f32(None, None, None, 0, 4, 4, 1.0, -1.0, None, 0, None)
+    assert rc == 1
+    assert b"must be > 0" in L.sdtw_last_error_message()
+    rc = L.sdtw_forward_f32(None, None, None, 1, 4, 4, -1.0, -1.0, None, 0, None)
+    assert rc == 1 and b"gamma" in L.sdtw_last_error_message()
+    rc = L.sdtw_cost_sqeuclid_f32(None, None, None, 1, 4, 4, 0, 0, None)
+    assert rc == 1
+    assert L.sdtw_error_string(3) == b"device-side wait timed out"
+
+
+def test_version():
+    assert "sm_100a" in _native.version()
+
+
+def test_native_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="native library"):
+        _native.lib()
