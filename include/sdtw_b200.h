@@ -14,8 +14,10 @@
  * (BGU-CS-VIL/sdtw-cuda-torch, softdtw_cuda/...), cited below as file:line.
  *
  * The "score" table takes the place of the reference's R table
- * (B, N+2, M+2): it holds T = -R * log2(e) / gamma for every cell in the
- * anti-diagonal ("wavefront") layout the kernels write with coalesced stores.
+ * (B, N+2, M+2): it holds T = -R * log2(e) / gamma for every cell, as a pair
+ * of float32 (hi, lo) with T = hi + lo, in the anti-diagonal ("wavefront")
+ * layout the kernels write with coalesced stores.  It must be 8-byte aligned;
+ * workspaces 16-byte aligned.
  * sdtw_score_to_R_f32 / sdtw_R_to_score_f32 convert to and from the
  * reference layout.
  */
@@ -43,8 +45,9 @@ const char *sdtw_error_string(int code);
 const char *sdtw_last_error_message(void);
 
 /* Reads and clears the device status word written by the kernels' bounded
- * waits (0 = no failure).  It does not synchronise: call it after the stream
- * has been synchronised to observe the kernels enqueued before. */
+ * waits (0 = no failure; on failure sdtw_last_error_message says which wait
+ * gave up).  It does not synchronise: call it after the stream has been
+ * synchronised to observe the kernels enqueued before. */
 int sdtw_status(void);
 
 /* Wall-clock limit of one device-side wait, in nanoseconds (default 2e9). */
@@ -54,6 +57,12 @@ void sdtw_set_wait_timeout_ns(unsigned long long ns);
  * of the DP table) withholds its output so that its consumer's wait runs out.
  * -1 disables.  Never set outside tests. */
 void sdtw_debug_stall_stripe(int stripe);
+
+/* Tuning/test hook: force the warps per CTA (1..16), the thread-block cluster
+ * size (1..8) and the DP rows per lane (1, 2 or 4) of the wavefront launches;
+ * 0 restores the automatic choice.  The score layout depends on the rows per
+ * lane, so a forward and its backward must run under the same setting. */
+void sdtw_set_plan_override(int warps_per_cta, int cluster_size, int rows_per_lane);
 
 /* Number of float32 elements of the score table for a (B,N,M) problem. */
 size_t sdtw_score_elems(int B, int N, int M);

@@ -10,6 +10,9 @@
 #include "../../include/sdtw_b200.h"
 #include "sdtw_kernels.h"
 
+// Device-side "some wait failed" flag, one per device that loads the library.
+__device__ int g_abort_flag;
+
 namespace {
 
 using namespace sdtw;
@@ -18,13 +21,15 @@ thread_local std::string g_last_error;
 std::atomic<uint32_t> g_seq{1};
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 std::atomic<int> g_debug_stall{-1};
+std::atomic<int> g_wpc_override{0};
+std::atomic<int> g_cs_override{0};
+std::atomic<int> g_k_override{0};
 std::mutex g_init_mu;
-int* g_status_host = nullptr;    // mapped pinned word
-int* g_status_dev = nullptr;     // its device address
+int* g_status_host = nullptr;    // mapped pinned words: [0] status, [8..15] WaitDiag
+int* g_status_dev = nullptr;     // their device address
 int g_num_sms[64] = {0};
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr double kLn2 = 0.6931471805599453;
 
 int fail(int code, const std::string& msg) {
     g_last_error = msg;
@@ -40,9 +45,9 @@ int ensure_status() {
     std::lock_guard<std::mutex> lk(g_init_mu);
     if (g_status_dev) return SDTW_OK;
     int* h = nullptr;
-    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&h), sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&h), 16 * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
     if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(status)");
-    *h = 0;
+    std::memset(h, 0, 16 * sizeof(int));
     int* d = nullptr;
     e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0);
     if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer(status)");
@@ -63,13 +68,41 @@ int num_sms() {
     return g_num_sms[dev];
 }
 
+int* abort_flag_dev() {
+    int* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_abort_flag) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return p;
+}
+
+// Clears the status word and the current device's abort flag.
+void clear_status() {
+    *reinterpret_cast<volatile int*>(g_status_host) = 0;
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_abort_flag, &zero, sizeof(int));
+}
+
+std::string diag_text() {
+    const volatile int* d = g_status_host + 8;
+    char buf[256];
+    std::snprintf(buf, sizeof buf,
+                  "%s pass, %s wait, problem %d, warp %d, band %d: expected %d, last seen %d",
+                  d[0] == 1 ? "forward" : (d[0] == 2 ? "backward" : "?"),
+                  d[1] == 1 ? "shared-memory ring" : (d[1] == 2 ? "global ring" : (d[1] == 3 ? "flow-control" : "?")),
+                  d[2], d[3], d[4], d[5], d[6]);
+    return buf;
+}
+
 // A failure recorded by an earlier launch surfaces at the next call.
 int pending_status() {
     if (g_status_host) {
         int s = *reinterpret_cast<volatile int*>(g_status_host);
         if (s != 0) {
-            *reinterpret_cast<volatile int*>(g_status_host) = 0;
-            return fail(SDTW_ERR_TIMEOUT, "a device-side wait of an earlier launch timed out");
+            std::string why = diag_text();
+            clear_status();
+            return fail(SDTW_ERR_TIMEOUT, "a device-side wait of an earlier launch timed out (" + why + ")");
         }
     }
     return SDTW_OK;
@@ -88,31 +121,45 @@ int check_gamma(float gamma) {
 }
 
 WaitCtx wait_ctx() {
-    WaitCtx w;
+    WaitCtx w{};
     w.status = g_status_dev;
+    w.diag = g_status_dev ? reinterpret_cast<volatile WaitDiag*>(g_status_dev + 8) : nullptr;
+    w.abort_flag = abort_flag_dev();
     w.timeout_ns = g_timeout_ns.load();
     return w;
 }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// |i - j| > bw  <=>  |i - j| > floor(bw) for integer |i - j| (launcher.py:315, :345).
+int int_band(float bw) {
+    if (!(bw > 0.f)) return 1 << 29;
+    const double f = std::floor(static_cast<double>(bw));
+    return f >= static_cast<double>(1 << 29) ? (1 << 29) : static_cast<int>(f);
+}
+
+WavePlan plan(int B, int N, int M) {
+    return make_plan(B, N, M, num_sms(), g_wpc_override.load(), g_cs_override.load(), g_k_override.load());
+}
+
 // Workspace layout: [wrap ring][cost or E scratch (xy paths)]
 size_t wave_ws(int B, int N, int M) {
-    WavePlan p = make_plan(B, N, M, num_sms());
+    WavePlan p = plan(B, N, M);
     return align_up(wrap_bytes(p), 256);
 }
 
 int run_forward(const float* D, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream) {
     FwdArgs a{};
-    a.P = make_plan(B, N, M, num_sms());
+    a.P = plan(B, N, M);
     a.D = D;
-    a.score = score;
+    a.score = reinterpret_cast<float2*>(score);
     a.out = out;
     a.wrap = wrap;
     a.kk = kLog2e / gamma;
     a.inv_k = static_cast<float>(1.0 / static_cast<double>(a.kk));
     a.bw = bw > 0.f ? bw : -1.f;
+    a.ibw = int_band(bw);
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
     a.wait = wait_ctx();
@@ -124,12 +171,13 @@ int run_forward(const float* D, float* score, float* out, int B, int N, int M, f
 int run_backward(const float* score, const float* grad_out, float* E, int B, int N, int M, float bw,
                  uint64_t* wrap, cudaStream_t stream) {
     BwdArgs a{};
-    a.P = make_plan(B, N, M, num_sms());
-    a.score = score;
+    a.P = plan(B, N, M);
+    a.score = reinterpret_cast<const float2*>(score);
     a.grad_out = grad_out;
     a.E = E;
     a.wrap = wrap;
     a.bw = bw > 0.f ? bw : -1.f;
+    a.ibw = int_band(bw);
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
     a.wait = wait_ctx();
@@ -159,8 +207,17 @@ const char* sdtw_last_error_message(void) { return g_last_error.c_str(); }
 int sdtw_status(void) {
     if (!g_status_host) return 0;
     int s = *reinterpret_cast<volatile int*>(g_status_host);
-    *reinterpret_cast<volatile int*>(g_status_host) = 0;
+    if (s != 0) {
+        g_last_error = "device-side wait timed out: " + diag_text();
+        clear_status();
+    }
     return s;
+}
+
+void sdtw_set_plan_override(int warps_per_cta, int cluster_size, int rows_per_lane) {
+    g_wpc_override.store(warps_per_cta > 0 ? warps_per_cta : 0);
+    g_cs_override.store(cluster_size > 0 ? cluster_size : 0);
+    g_k_override.store(rows_per_lane == 1 || rows_per_lane == 2 || rows_per_lane == 4 ? rows_per_lane : 0);
 }
 
 void sdtw_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1ull); }
@@ -169,7 +226,7 @@ void sdtw_debug_stall_stripe(int stripe) { g_debug_stall.store(stripe); }
 
 size_t sdtw_score_elems(int B, int N, int M) {
     if (B <= 0 || N <= 0 || M <= 0) return 0;
-    return score_elems(B, N, M);
+    return score_elems(B, N, M, g_k_override.load());
 }
 
 size_t sdtw_workspace_bytes(int B, int N, int M) {
@@ -198,6 +255,7 @@ int sdtw_forward_f32(const float* D, float* score, float* out, int B, int N, int
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (!D || !score || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
     if (workspace_bytes < wave_ws(B, N, M) || (wave_ws(B, N, M) && !workspace))
         return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
     if ((rc = ensure_status()) || (rc = pending_status())) return rc;
@@ -210,6 +268,7 @@ int sdtw_backward_f32(const float* score, const float* grad_out, float* E, int B
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (!score || !E) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
     if (workspace_bytes < wave_ws(B, N, M) || (wave_ws(B, N, M) && !workspace))
         return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
     if ((rc = ensure_status()) || (rc = pending_status())) return rc;
@@ -223,6 +282,8 @@ int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !score || !out || !workspace) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(score) % 8u || reinterpret_cast<uintptr_t>(workspace) % 16u)
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte and workspace 16-byte aligned");
     if (workspace_bytes < sdtw_workspace_bytes_xy(B, N, M, dim)) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
     if ((rc = ensure_status()) || (rc = pending_status())) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -240,6 +301,8 @@ int sdtw_backward_xy_f32(const float* x, const float* y, const float* score, con
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !score || !workspace) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(score) % 8u || reinterpret_cast<uintptr_t>(workspace) % 16u)
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte and workspace 16-byte aligned");
     if (workspace_bytes < sdtw_workspace_bytes_xy(B, N, M, dim)) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
     if ((rc = ensure_status()) || (rc = pending_status())) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -267,9 +330,11 @@ int sdtw_score_to_R_f32(const float* score, float* R, int B, int N, int M, float
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    WavePlan p = make_plan(B, N, M, num_sms());
+    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
+    WavePlan p = plan(B, N, M);
     const float kk = kLog2e / gamma;
-    cudaError_t e = launch_score_to_R(score, R, p, static_cast<float>(1.0 / (double)kk), static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_score_to_R(reinterpret_cast<const float2*>(score), R, p, static_cast<float>(1.0 / (double)kk),
+                                      static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "score_to_R launch");
     return SDTW_OK;
 }
@@ -278,8 +343,8 @@ int sdtw_R_to_score_f32(const float* R, float* score, int B, int N, int M, float
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    WavePlan p = make_plan(B, N, M, num_sms());
-    cudaError_t e = launch_R_to_score(R, score, p, kLog2e / gamma, static_cast<cudaStream_t>(stream));
+    WavePlan p = plan(B, N, M);
+    cudaError_t e = launch_R_to_score(R, reinterpret_cast<float2*>(score), p, kLog2e / gamma, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "R_to_score launch");
     return SDTW_OK;
 }

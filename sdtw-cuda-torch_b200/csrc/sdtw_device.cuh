@@ -65,6 +65,27 @@ __device__ __forceinline__ uint64_t ld_cluster_u64(uint32_t own_saddr) {
     asm volatile("ld.relaxed.cluster.shared::cta.u64 %0, [%1];" : "=l"(v) : "r"(own_saddr) : "memory");
     return v;
 }
+// Predicated forms (no branch around the store).
+__device__ __forceinline__ void st_cluster_u64_if(bool p, uint32_t cluster_addr, uint64_t v) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.relaxed.cluster.shared::cluster.u64 [%1], %2;\n\t}" ::"r"(
+            static_cast<int>(p)),
+        "r"(cluster_addr), "l"(v)
+        : "memory");
+}
+__device__ __forceinline__ void st_release_cluster_u32_if(bool p, uint32_t cluster_addr, uint32_t v) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.release.cluster.shared::cluster.u32 [%1], %2;\n\t}" ::"r"(
+            static_cast<int>(p)),
+        "r"(cluster_addr), "r"(v)
+        : "memory");
+}
+__device__ __forceinline__ void st_gpu_u64_if(bool p, uint64_t* ptr, uint64_t v) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.relaxed.gpu.global.u64 [%1], %2;\n\t}" ::"r"(
+                     static_cast<int>(p)),
+                 "l"(ptr), "l"(v)
+                 : "memory");
+}
 __device__ __forceinline__ void st_release_cluster_u32(uint32_t cluster_addr, uint32_t v) {
     asm volatile("st.release.cluster.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
@@ -95,41 +116,82 @@ __device__ __forceinline__ float val_of(uint64_t e) { return __uint_as_float(sta
 // ---------------------------------------------------------------- bounded waits
 // Status word: 0 = ok; otherwise the first error code recorded by any kernel.
 // It lives in mapped pinned host memory so the host can read it without a
-// device synchronisation.
+// device synchronisation; kernels only write it (once, on failure).  Waiters
+// learn about another waiter's failure from `abort_flag` in device memory,
+// which they read at most every few thousand polls.
 enum : int {
     kStatusOk = 0,
     kStatusTimeout = 3,
 };
 
-struct WaitCtx {
-    volatile int* status;   // mapped pinned host word (may be null)
-    uint64_t timeout_ns;    // wall-clock limit for one wait
+// Where a wait gave up (written next to the status word, for diagnostics).
+struct WaitDiag {
+    int kernel;   // 1 forward, 2 backward
+    int kind;     // 1 smem tag, 2 global tag, 3 flow-control counter
+    int problem;  // batch index
+    int warp;     // warp index within the band chain
+    int band;
+    int expect;   // expected tag / counter value
+    int seen;     // last tag / counter value seen
+    int pad;
 };
 
-__device__ __forceinline__ void record_error(const WaitCtx& w, int code) {
-    if (w.status) *w.status = code;  // plain volatile store; racing writers store the same code
+struct WaitCtx {
+    volatile int* status;      // mapped pinned host word (may be null)
+    volatile WaitDiag* diag;   // mapped pinned host record (may be null)
+    volatile int* abort_flag;  // device word, nonzero once any wait failed (may be null)
+    uint64_t timeout_ns;       // wall-clock limit for one wait
+    int kernel, problem, warp, band;
+};
+
+__device__ __forceinline__ void record_error(const WaitCtx& w, int code, int kind, uint32_t expect, uint32_t seen) {
+    if (w.abort_flag) *w.abort_flag = 1;
+    if (w.diag) {
+        w.diag->kernel = w.kernel;
+        w.diag->kind = kind;
+        w.diag->problem = w.problem;
+        w.diag->warp = w.warp;
+        w.diag->band = w.band;
+        w.diag->expect = static_cast<int>(expect);
+        w.diag->seen = static_cast<int>(seen);
+    }
+    __threadfence_system();
+    if (w.status) *w.status = code;
 }
-__device__ __forceinline__ bool aborted(const WaitCtx& w) { return w.status && *w.status != 0; }
+
+// Shared back-off policy of the slow paths: poll tightly, look at the clock
+// every 256 polls, at the device abort flag every 4096 polls once the wait is
+// older than 20 us, and sleep between polls once it is older than 1 ms.
+// Returns 0 to keep polling, 1 when the limit ran out, 2 on abort.
+__device__ __forceinline__ int backoff(uint32_t it, uint64_t& t0, const WaitCtx& w) {
+    if ((it & 255u) != 0u) return 0;
+    const uint64_t now = globaltimer_ns();
+    if (t0 == 0) {
+        t0 = now;
+        return 0;
+    }
+    const uint64_t el = now - t0;
+    if (el > w.timeout_ns) return 1;
+    if (el > 20000u && (it & 4095u) == 0u && w.abort_flag && *w.abort_flag) return 2;
+    if (el > 1000000u) __nanosleep(256);
+    return 0;
+}
 
 // Wait until the u64 at own-CTA smem address `saddr` carries `tag`; return its
 // value in `out`.  Returns false (after recording kStatusTimeout) when the
-// limit runs out or another waiter has already recorded an error.
+// limit runs out, or when another waiter has already failed.
 static __device__ __noinline__ bool wait_smem_tag_slow(uint32_t saddr, uint32_t tag, float& out, const WaitCtx& w) {
-    const uint64_t t0 = globaltimer_ns();
+    uint64_t t0 = 0;
+    uint64_t e = 0;
     for (uint32_t it = 1;; ++it) {
-        uint64_t e = ld_cluster_u64(saddr);
+        e = ld_cluster_u64(saddr);
         if (tag_of(e) == tag) {
             out = val_of(e);
             return true;
         }
-        if ((it & 31u) == 0u) {
-            if (aborted(w)) return false;
-            if (globaltimer_ns() - t0 > w.timeout_ns) {
-                record_error(w, kStatusTimeout);
-                return false;
-            }
-            __nanosleep(64);
-        }
+        const int r = backoff(it, t0, w);
+        if (r == 1) record_error(w, kStatusTimeout, 1, tag, tag_of(e));
+        if (r) return false;
     }
 }
 __device__ __forceinline__ bool wait_smem_tag(uint32_t saddr, uint32_t tag, float& out, const WaitCtx& w) {
@@ -142,21 +204,17 @@ __device__ __forceinline__ bool wait_smem_tag(uint32_t saddr, uint32_t tag, floa
 }
 
 static __device__ __noinline__ bool wait_gmem_tag_slow(const uint64_t* p, uint32_t tag, float& out, const WaitCtx& w) {
-    const uint64_t t0 = globaltimer_ns();
+    uint64_t t0 = 0;
+    uint64_t e = 0;
     for (uint32_t it = 1;; ++it) {
-        uint64_t e = ld_gpu_u64(p);
+        e = ld_gpu_u64(p);
         if (tag_of(e) == tag) {
             out = val_of(e);
             return true;
         }
-        if ((it & 31u) == 0u) {
-            if (aborted(w)) return false;
-            if (globaltimer_ns() - t0 > w.timeout_ns) {
-                record_error(w, kStatusTimeout);
-                return false;
-            }
-            __nanosleep(64);
-        }
+        const int r = backoff(it, t0, w);
+        if (r == 1) record_error(w, kStatusTimeout, 2, tag, tag_of(e));
+        if (r) return false;
     }
 }
 __device__ __forceinline__ bool wait_gmem_tag(const uint64_t* p, uint32_t tag, float& out, const WaitCtx& w) {
@@ -170,18 +228,13 @@ __device__ __forceinline__ bool wait_gmem_tag(const uint64_t* p, uint32_t tag, f
 
 // Wait until the u32 counter at own-CTA smem address `saddr` is >= `need`.
 static __device__ __noinline__ bool wait_counter_ge(uint32_t saddr, uint32_t need, uint32_t& seen, const WaitCtx& w) {
-    const uint64_t t0 = globaltimer_ns();
+    uint64_t t0 = 0;
     for (uint32_t it = 1;; ++it) {
         seen = ld_acquire_cluster_u32(saddr);
         if (static_cast<int32_t>(seen - need) >= 0) return true;
-        if ((it & 31u) == 0u) {
-            if (aborted(w)) return false;
-            if (globaltimer_ns() - t0 > w.timeout_ns) {
-                record_error(w, kStatusTimeout);
-                return false;
-            }
-            __nanosleep(64);
-        }
+        const int r = backoff(it, t0, w);
+        if (r == 1) record_error(w, kStatusTimeout, 3, need, seen);
+        if (r) return false;
     }
 }
 

@@ -14,12 +14,13 @@ namespace sdtw {
 struct FwdArgs {
     WavePlan P;
     const float* D;   // (B,N,M) cost, row-major
-    float* score;     // wavefront-layout score store (see sdtw_plan.h)
+    float2* score;    // wavefront-layout score store, (hi, lo) pairs (see sdtw_plan.h)
     float* out;       // (B,) R[N,M]
     uint64_t* wrap;   // (B*M) band-wrap ring, null when n_bands == 1
     float kk;         // log2(e) / gamma
     float inv_k;      // gamma * ln(2)
     float bw;         // Sakoe-Chiba bandwidth, <= 0 disables
+    int ibw;          // integer band: cell (i, j) is kept when |i - j| <= ibw (floor(bw), or 2^29 when disabled)
     uint32_t seq;     // launch sequence number (tags of the global ring)
     int debug_stall;  // stripe whose output is withheld (failure-detection tests); -1 = none
     WaitCtx wait;
@@ -27,11 +28,12 @@ struct FwdArgs {
 
 struct BwdArgs {
     WavePlan P;
-    const float* score;
+    const float2* score;
     const float* grad_out;  // (B,) upstream gradient, null = ones
     float* E;               // (B,N,M) output: grad_out[b] * dR[N,M]/dD[i,j]
     uint64_t* wrap;
     float bw;
+    int ibw;
     uint32_t seq;
     int debug_stall;
     WaitCtx wait;
@@ -39,8 +41,8 @@ struct BwdArgs {
 
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
-cudaError_t launch_score_to_R(const float* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
-cudaError_t launch_R_to_score(const float* R, float* S, const WavePlan& P, float kk, cudaStream_t stream);
+cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
+cudaError_t launch_R_to_score(const float* R, float2* S, const WavePlan& P, float kk, cudaStream_t stream);
 
 // dense.cu
 cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, int M, int dim, bool direct,

@@ -13,9 +13,10 @@
 //
 // Score store ("wavefront layout"): for problem b, stripe s, local
 // anti-diagonal t in [0, n_diag) and in-stripe position p = k*32 + l,
-//     score[((b*n_stripes + s)*n_diag + t)*(32*K) + p]
-// holds T(row = s*32*K + l*K + k, col = t - l*K - k) = -R(row, col)*log2(e)/gamma.
-// One warp step writes 32 consecutive floats per k: a coalesced 128-byte store.
+//     score[((b*n_stripes + s)*n_diag + t)*(32*K) + p]      (a float2)
+// holds T(row = s*32*K + l*K + k, col = t - l*K - k) = -R(row, col)*log2(e)/gamma
+// as an unevaluated pair hi + lo.  One warp step writes 32 consecutive float2
+// per k: a coalesced 256-byte store.
 #pragma once
 
 #include <cstddef>
@@ -36,24 +37,30 @@ struct WavePlan {
 
 // Rows per lane as a function of the problem only (the score layout depends on
 // it, so forward and backward must agree).
-inline int rows_per_lane(int N) {
+inline int rows_per_lane(int N, int k_override = 0) {
+    if (k_override == 1 || k_override == 2 || k_override == 4) return k_override;
     (void)N;
     return 1;
 }
 
-inline size_t score_elems(int B, int N, int M) {
-    const int K = rows_per_lane(N);
+// float32 elements (2 per cell: hi, lo) of the score store.
+inline size_t score_elems(int B, int N, int M, int k_override = 0) {
+    const int K = rows_per_lane(N, k_override);
     const size_t sr = 32u * (size_t)K;
     const size_t ns = ((size_t)N + sr - 1) / sr;
-    return (size_t)B * ns * ((size_t)M + sr - 1) * sr;
+    return 2u * (size_t)B * ns * ((size_t)M + sr - 1) * sr;
 }
 
-inline WavePlan make_plan(int B, int N, int M, int num_sms) {
+// wpc_override / cs_override / k_override (> 0) force the warps per CTA, the
+// cluster size and the rows per lane (tests use them to exercise many bands
+// and clusters on small problems).
+inline WavePlan make_plan(int B, int N, int M, int num_sms, int wpc_override = 0, int cs_override = 0,
+                          int k_override = 0) {
     WavePlan p{};
     p.B = B;
     p.N = N;
     p.M = M;
-    p.K = rows_per_lane(N);
+    p.K = rows_per_lane(N, k_override);
     const int sr = 32 * p.K;
     p.n_stripes = (N + sr - 1) / sr;
     p.n_diag = M + sr - 1;
@@ -61,9 +68,11 @@ inline WavePlan make_plan(int B, int N, int M, int num_sms) {
     // batch alone would leave SMs idle.
     int cs = 1;
     while (cs < 8 && (long long)B * cs * 2 <= (long long)num_sms && cs * 2 <= p.n_stripes) cs *= 2;
+    if (cs_override > 0) cs = cs_override < 8 ? cs_override : 8;
     int wpc = (p.n_stripes + cs - 1) / cs;
     if (wpc > 16) wpc = 16;
     if (wpc < 1) wpc = 1;
+    if (wpc_override > 0) wpc = wpc_override < 16 ? wpc_override : 16;
     p.csize = cs;
     p.wpc = wpc;
     p.G = wpc * cs;
@@ -71,9 +80,10 @@ inline WavePlan make_plan(int B, int N, int M, int num_sms) {
     return p;
 }
 
-// Global band-wrap ring: one tagged u64 per column per problem.
+// Global band-wrap ring: two tagged u64 per column per problem (hi and lo of
+// the forward's bottom row; the reverse pass uses the first).
 inline size_t wrap_bytes(const WavePlan& p) {
-    return p.n_bands > 1 ? (size_t)p.B * (size_t)p.M * 8u : 0u;
+    return p.n_bands > 1 ? (size_t)p.B * (size_t)p.M * 16u : 0u;
 }
 
 }  // namespace sdtw

@@ -13,6 +13,14 @@
 //   * scores T = -R * log2(e) / gamma in base 2, so one softmin is
 //     T = m + (lg2(sum_k ex2(T_k - m)) - D * log2(e)/gamma) with m = max_k T_k:
 //     three MUFU ex2 and one MUFU lg2 per cell, no division.
+//   * T is carried and stored as an unevaluated float32 pair (hi, lo),
+//     T = hi + lo with |lo| <= ulp(hi)/2: the new cell is m_hi + delta with the
+//     rounding error of that sum kept in lo (TwoSum), and D * log2(e)/gamma is
+//     split exactly (TwoProduct).  |T| grows along the path while the backward
+//     weights depend on differences of neighbouring T, so a plain float32 T
+//     loses ~ulp(T)/gamma of accuracy per weight; the pair keeps the weights
+//     at float32 relative accuracy.  (The lo of the max cancels out of
+//     sum_k ex2(T_k - m), so no arg-max is needed.)
 //   * the backward weight exp((R[c] - D[c] - R[p]) / gamma) equals the softmax
 //     weight of predecessor p among c's three predecessors, so the reverse pass
 //     recomputes it from the stored scores of c's predecessors, normalised to
@@ -33,9 +41,28 @@ __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
     return (seq << 12) | (static_cast<uint32_t>(band) & 0xfffu);
 }
 
+// ============================================================== step groups
+// Steps run in groups of PF.  Per group (warp-uniform code): the consumer lane
+// reads and checks the PF ring slots it will need, the producer lane checks
+// flow control once, and every 32 columns a release store reports progress.
+// Per step: no branches -- shuffles, the cell math, predicated stores.  The
+// cost (forward) or score rows (backward) of step t are loaded PF steps ahead.
+template <int K>
+struct StepCfg {
+    static constexpr int PF = (K >= 4) ? 4 : 8;
+};
+
+__device__ __forceinline__ bool report_due(int done, int PF, int M) {
+    // `done` columns consumed, PF more than after the previous group: report
+    // when a multiple of 32 was crossed, and at the end of the row.
+    return (done & 31) < PF || done >= M;
+}
+
 // ============================================================== forward
 template <int K>
 __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
+    constexpr int PF = StepCfg<K>::PF;
+    constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
     const int wpc = P.wpc;
@@ -44,23 +71,28 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     const int crank = static_cast<int>(cluster_ctarank());
     const int b = blockIdx.x / P.csize;
     const int g = crank * wpc + warp;
-    constexpr int SR = 32 * K;
     const int N = P.N, M = P.M;
 
-    uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                // [wpc][kRing]
-    uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * kRing);  // [wpc]
-    for (int i = threadIdx.x; i < wpc * kRing; i += blockDim.x) ring[i] = ~0ull;
+    // Per warp: kRing (hi, tag) slots, then kRing (lo, tag) slots.
+    uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][2][kRing]
+    uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
+    for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
 
-    const uint32_t my_ring = smem_addr(ring + warp * kRing);
+    const uint32_t my_ring = smem_addr(ring + warp * 2 * kRing);
     const uint32_t my_consumed = smem_addr(consumed + warp);
     uint32_t next_ring = 0, prev_consumed = 0;
-    if (g + 1 < P.G) next_ring = mapa_shared(smem_addr(ring + ((g + 1) % wpc) * kRing), (g + 1) / wpc);
+    if (g + 1 < P.G) next_ring = mapa_shared(smem_addr(ring + ((g + 1) % wpc) * 2 * kRing), (g + 1) / wpc);
     if (g > 0) prev_consumed = mapa_shared(smem_addr(consumed + (g - 1) % wpc), (g - 1) / wpc);
 
     const float kk = a.kk;
     const float NEG = neg_inf();
+    const int ibw = a.ibw;
+    WaitCtx wc = a.wait;
+    wc.kernel = 1;
+    wc.problem = b;
+    wc.warp = g;
     bool ok = true;          // false once a wait of this lane failed
     bool quit = false;       // warp-uniform
     uint32_t cons_seen = 0;  // lane 31: consumer progress last observed
@@ -68,80 +100,173 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     for (int band = 0; band < P.n_bands && !quit; ++band) {
         const int s = band * P.G + g;
         if (s >= P.n_stripes) break;
+        wc.band = band;
         const int R0 = s * SR;
-        const bool has_next = (s + 1 < P.n_stripes);
-        const bool next_wrap = (g == P.G - 1);
-        const bool prev_wrap = (g == 0);
-        const bool withhold = (s == a.debug_stall);
+        const bool has_in = R0 > 0;
+        const bool in_wrap = (g == 0);
+        const bool has_out = (s + 1 < P.n_stripes) && (s != a.debug_stall);
+        const bool out_wrap = (g == P.G - 1);
         const uint32_t band_base = static_cast<uint32_t>(band) * static_cast<uint32_t>(M);
-        float* Ts = a.score + (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * SR;
-        const float* Db = a.D + static_cast<size_t>(b) * N * M;
+        float2* Ts = a.score + (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * SR;
+        const uint64_t* wrap_in = a.wrap + static_cast<size_t>(b) * 2 * M;
+        uint64_t* wrap_out = a.wrap + static_cast<size_t>(b) * 2 * M;
+        const uint32_t in_tag_wrap = wrap_tag(a.seq, band - 1);
+        const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
 
-        float cur[K], old[K];
+        // Everything before this band counts as consumed (see the reverse pass).
+        if (has_in && !in_wrap && lane == 0) st_release_cluster_u32(prev_consumed, band_base);
+
+        const float* drow[K];
+        bool rowok[K];
 #pragma unroll
-        for (int k = 0; k < K; ++k) cur[k] = old[k] = NEG;
-        float up_prev = (R0 == 0) ? 0.f : NEG;  // T(R0-1, -1)
+        for (int k = 0; k < K; ++k) {
+            const int row = R0 + lane * K + k;
+            rowok[k] = row < N;
+            drow[k] = a.D + (static_cast<size_t>(b) * N + (rowok[k] ? row : 0)) * M;
+        }
+        float dq[PF][K];  // cost of the step due in slot u
+#pragma unroll
+        for (int u = 0; u < PF; ++u)
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int col = u - (lane * K + k);
+                dq[u][k] = (rowok[k] && static_cast<unsigned>(col) < static_cast<unsigned>(M)) ? __ldg(drow[k] + col) : 0.f;
+            }
+
+        // Three live anti-diagonals: c* = step t-1, o* = step t-2, as (hi, lo).
+        float ch[K], cl[K], oh[K], ol[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            ch[k] = oh[k] = NEG;
+            cl[k] = ol[k] = 0.f;
+        }
+        float uph_prev = (R0 == 0) ? 0.f : NEG;  // T(R0-1, -1)
+        float upl_prev = 0.f;
         const int n_steps = M + SR - 1;
 
-        for (int t = 0; t < n_steps; ++t) {
-            float up = __shfl_up_sync(SDTW_FULL_MASK, cur[K - 1], 1);
-            if (lane == 0) {
-                up = NEG;
-                if (R0 > 0 && t < M) {
-                    float v = NEG;
-                    if (ok) {
-                        if (prev_wrap)
-                            ok = wait_gmem_tag(a.wrap + static_cast<size_t>(b) * M + t, wrap_tag(a.seq, band - 1), v, a.wait);
-                        else
-                            ok = wait_smem_tag(my_ring + ((band_base + t) % kRing) * 8u, band_base + t, v, a.wait);
-                    }
-                    up = v;
-                    if (!prev_wrap && (((t + 1) % (kRing / 4)) == 0 || t == M - 1))
-                        st_release_cluster_u32(prev_consumed, band_base + t + 1);
-                }
-            }
-            const float dg_top = up_prev;
-            up_prev = up;
-            float nw[K];
+        for (int t0 = 0; t0 < n_steps; t0 += PF) {
+            // ---- group prologue: the row above for columns t0 .. t0+PF-1 (lane 0).
+            float rin_h[PF], rin_l[PF];
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                const int q = lane * K + k;
-                const int col = t - q;
-                const int row = R0 + q;
-                const float left = cur[k];
-                const float u = (k == 0) ? up : cur[k > 0 ? k - 1 : 0];
-                const float d = (k == 0) ? dg_top : old[k > 0 ? k - 1 : 0];
-                const bool inr = (col >= 0) && (col < M) && (row < N);
-                const float c = inr ? __ldg(Db + static_cast<size_t>(row) * M + col) : 0.f;
-                const float m = max3f(d, u, left);
-                const float sm = ex2f(d - m) + ex2f(u - m) + ex2f(left - m);
-                float v = m + (lg2f(sm) - c * kk);
-                const bool pruned = (a.bw > 0.f) && (fabsf(static_cast<float>(row - col)) > a.bw);
-                v = (inr && !pruned && m != NEG) ? v : NEG;
-                nw[k] = v;
-                if (inr) Ts[static_cast<size_t>(t) * SR + k * 32 + lane] = v;
-                if (row == N - 1 && col == M - 1) a.out[b] = -v * a.inv_k;
+            for (int u = 0; u < PF; ++u) {
+                rin_h[u] = NEG;
+                rin_l[u] = 0.f;
             }
-            if (lane == 31 && has_next && !withhold) {
-                const int col = t - (SR - 1);
-                if (col >= 0 && col < M) {
-                    if (next_wrap) {
-                        st_gpu_u64(a.wrap + static_cast<size_t>(b) * M + col, pack_tagged(nw[K - 1], wrap_tag(a.seq, band)));
-                    } else {
-                        const uint32_t gc = band_base + static_cast<uint32_t>(col);
-                        if (gc >= static_cast<uint32_t>(kRing) && ok &&
-                            static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)
-                            ok = wait_counter_ge(my_consumed, gc - kRing + 1, cons_seen, a.wait);
-                        st_cluster_u64(next_ring + (gc % kRing) * 8u, pack_tagged(nw[K - 1], gc));
+            if (has_in && t0 < M) {  // warp-uniform
+                bool all = true;
+                uint32_t tg[PF];
+#pragma unroll
+                for (int u = 0; u < PF; ++u) {
+                    const int col = t0 + u;
+                    tg[u] = in_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(col);
+                    if (col < M) {
+                        uint64_t eh, el;
+                        if (in_wrap) {
+                            eh = ld_gpu_u64(wrap_in + col);
+                            el = ld_gpu_u64(wrap_in + M + col);
+                        } else {
+                            const uint32_t slot = (tg[u] % kRing) * 8u;
+                            eh = ld_cluster_u64(my_ring + slot);
+                            el = ld_cluster_u64(my_ring + kRing * 8u + slot);
+                        }
+                        all = all && tag_of(eh) == tg[u] && tag_of(el) == tg[u];
+                        rin_h[u] = val_of(eh);
+                        rin_l[u] = val_of(el);
                     }
                 }
-            }
+                if (lane == 0 && !all) {  // rare: the producer is behind
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                old[k] = cur[k];
-                cur[k] = nw[k];
+                    for (int u = 0; u < PF; ++u) {
+                        const int col = t0 + u;
+                        if (col < M && ok) {
+                            if (in_wrap)
+                                ok = wait_gmem_tag(wrap_in + col, tg[u], rin_h[u], wc) &&
+                                     wait_gmem_tag(wrap_in + M + col, tg[u], rin_l[u], wc);
+                            else
+                                ok = wait_smem_tag(my_ring + (tg[u] % kRing) * 8u, tg[u], rin_h[u], wc) &&
+                                     wait_smem_tag(my_ring + kRing * 8u + (tg[u] % kRing) * 8u, tg[u], rin_l[u], wc);
+                        }
+                    }
+                }
+                const int done = min(t0 + PF, M);
+                if (!in_wrap && report_due(done, PF, M) && lane == 0)
+                    st_release_cluster_u32(prev_consumed, band_base + static_cast<uint32_t>(done));
             }
-            if ((t & 63) == 63 && __any_sync(SDTW_FULL_MASK, !ok)) {
+            // ---- flow control for the columns this group publishes (lane 31).
+            if (has_out && !out_wrap) {  // warp-uniform
+                const int col_last = min(t0 + PF - 1 - (SR - 1), M - 1);
+                if (col_last >= 0) {
+                    const uint32_t gc = band_base + static_cast<uint32_t>(col_last);
+                    if (lane == 31 && ok && gc >= static_cast<uint32_t>(kRing) &&
+                        static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)
+                        ok = wait_counter_ge(my_consumed, gc - kRing + 1, cons_seen, wc);
+                }
+            }
+            // ---- PF branch-free steps.
+#pragma unroll
+            for (int u = 0; u < PF; ++u) {
+                const int t = t0 + u;
+                float c[K];
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    c[k] = dq[u][k];
+                    const int col = t + PF - (lane * K + k);
+                    dq[u][k] = (rowok[k] && static_cast<unsigned>(col) < static_cast<unsigned>(M)) ? __ldg(drow[k] + col) : 0.f;
+                }
+                float uph = __shfl_up_sync(SDTW_FULL_MASK, ch[K - 1], 1);
+                float upl = __shfl_up_sync(SDTW_FULL_MASK, cl[K - 1], 1);
+                uph = (lane == 0) ? rin_h[u] : uph;
+                upl = (lane == 0) ? rin_l[u] : upl;
+                const float dgh = uph_prev, dgl = upl_prev;
+                uph_prev = uph;
+                upl_prev = upl;
+                float nh[K], nl[K];
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    const int q = lane * K + k;
+                    const int col = t - q;
+                    const int row = R0 + q;
+                    const float lh = ch[k], ll = cl[k];
+                    const float uh = (k == 0) ? uph : ch[k > 0 ? k - 1 : 0];
+                    const float ul = (k == 0) ? upl : cl[k > 0 ? k - 1 : 0];
+                    const float dh = (k == 0) ? dgh : oh[k > 0 ? k - 1 : 0];
+                    const float dl = (k == 0) ? dgl : ol[k > 0 ? k - 1 : 0];
+                    // TwoProduct: c*kk = p + e exactly.
+                    const float p = c[k] * kk;
+                    const float e = fmaf(c[k], kk, -p);
+                    const float m = max3f(dh, uh, lh);
+                    const float sm = ex2f((dh - m) + dl) + ex2f((uh - m) + ul) + ex2f((lh - m) + ll);
+                    const float delta = (lg2f(sm) - p) - e;
+                    // TwoSum: m + delta = hi + lo exactly.
+                    const float hi = m + delta;
+                    const float bb = hi - m;
+                    const float lo = (m - (hi - bb)) + (delta - bb);
+                    const bool inr = rowok[k] && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                    const bool inband = static_cast<unsigned>(row - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    const bool live = inr && inband && m != NEG;
+                    nh[k] = live ? hi : NEG;
+                    nl[k] = live ? lo : 0.f;
+                    if (inr) Ts[static_cast<size_t>(t) * SR + k * 32 + lane] = make_float2(nh[k], nl[k]);
+                    if (inr && row == N - 1 && col == M - 1) a.out[b] = fmaf(-nh[k], a.inv_k, -nl[k] * a.inv_k);
+                }
+                // Bottom row of the stripe goes to the next stripe's warp.
+                const int colb = t - (SR - 1);
+                const bool pub = has_out && lane == 31 && static_cast<unsigned>(colb) < static_cast<unsigned>(M);
+                const uint32_t gcb = band_base + static_cast<uint32_t>(colb);
+                const uint32_t slot = (gcb % kRing) * 8u;
+                st_gpu_u64_if(pub && out_wrap, wrap_out + colb, pack_tagged(nh[K - 1], out_tag_wrap));
+                st_gpu_u64_if(pub && out_wrap, wrap_out + M + colb, pack_tagged(nl[K - 1], out_tag_wrap));
+                st_cluster_u64_if(pub && !out_wrap, next_ring + slot, pack_tagged(nh[K - 1], gcb));
+                st_cluster_u64_if(pub && !out_wrap, next_ring + kRing * 8u + slot, pack_tagged(nl[K - 1], gcb));
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    oh[k] = ch[k];
+                    ol[k] = cl[k];
+                    ch[k] = nh[k];
+                    cl[k] = nl[k];
+                }
+            }
+            if (((t0 / PF) & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
@@ -154,10 +279,10 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
 
 // ============================================================== backward
 template <int K>
-__device__ __forceinline__ float load_score(const float* __restrict__ S, const WavePlan& P, int b, int row, int col) {
+__device__ __forceinline__ float2 load_score(const float2* __restrict__ S, const WavePlan& P, int b, int row, int col) {
     constexpr int SR = 32 * K;
-    if (row < 0) return (col < 0) ? 0.f : neg_inf();
-    if (col < 0) return neg_inf();
+    if (row < 0) return make_float2((col < 0) ? 0.f : neg_inf(), 0.f);
+    if (col < 0) return make_float2(neg_inf(), 0.f);
     const int s = row / SR;
     const int q = row - s * SR;
     const int l = q / K;
@@ -166,8 +291,15 @@ __device__ __forceinline__ float load_score(const float* __restrict__ S, const W
     return __ldg(S + idx);
 }
 
+// Reverse wavefront.  At reverse step t the lane holding row q handles cell
+// (q, j = t - q) and needs the scores of its predecessors (q-1, j-1), (q-1, j)
+// and (q, j-1): the stripe's anti-diagonal rows t-2 and t-1 (coalesced float2
+// loads, PF steps ahead), the row above from the neighbour lane by shuffle,
+// and for lane 0 the last row of the previous stripe (one prefetched load).
 template <int K>
 __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
+    constexpr int PF = StepCfg<K>::PF;
+    constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
     const int wpc = P.wpc;
@@ -176,7 +308,6 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
     const int crank = static_cast<int>(cluster_ctarank());
     const int b = blockIdx.x / P.csize;
     const int g = crank * wpc + warp;
-    constexpr int SR = 32 * K;
     const int N = P.N, M = P.M;
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);
@@ -194,6 +325,12 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
     if (g + 1 < P.G) below_consumed = mapa_shared(smem_addr(consumed + (g + 1) % wpc), (g + 1) / wpc);
 
     const float gb = a.grad_out ? __ldg(a.grad_out + b) : 1.f;
+    const float NEG = neg_inf();
+    const int ibw = a.ibw;
+    WaitCtx wc = a.wait;
+    wc.kernel = 2;
+    wc.problem = b;
+    wc.warp = g;
     bool ok = true;
     bool quit = false;
     uint32_t cons_seen = 0;  // lane 0: progress of the consumer above
@@ -201,86 +338,179 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
     for (int band = P.n_bands - 1; band >= 0 && !quit; --band) {
         const int s = band * P.G + g;
         if (s >= P.n_stripes) continue;
+        wc.band = band;
         const int R0 = s * SR;
-        const bool has_up = (s > 0);
+        const bool has_up = (s > 0) && (s != a.debug_stall);
         const bool up_wrap = (g == 0);
         const bool has_below = (s + 1 < P.n_stripes);
         const bool below_wrap = (g == P.G - 1);
-        const bool withhold = (s == a.debug_stall);
         const uint32_t band_base = static_cast<uint32_t>(P.n_bands - 1 - band) * static_cast<uint32_t>(M);
         float* Eb = a.E + static_cast<size_t>(b) * N * M;
+        const float2* Ts = a.score + (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * SR;
+        // Last row of the previous stripe, by column: Tp[col * SR].
+        const float2* Tp = (s > 0)
+            ? a.score + ((static_cast<size_t>(b) * P.n_stripes + s - 1) * P.n_diag + (SR - 1)) * SR + (K - 1) * 32 + 31
+            : a.score;
+        uint64_t* wrap_io = a.wrap + static_cast<size_t>(b) * 2 * M;
+        const uint32_t in_tag_wrap = wrap_tag(a.seq, band + 1);
+        const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
+
+        // Everything before this band counts as consumed: a warp whose stripe had
+        // no producer below it in the previous (later-numbered) band never
+        // advanced the counter, and the producer's flow control starts at band_base.
+        if (has_below && !below_wrap && lane == 31) st_release_cluster_u32(below_consumed, band_base);
+
+        const int n_steps = M + SR - 1;
+        const int t_last = ((n_steps + PF - 1) / PF) * PF - 1;  // padded: extra steps touch no live cell
+        // Own anti-diagonal rows A(t') = Ts[t'*SR + k*32 + lane] and the previous
+        // stripe's last row PS(col) = Tp[col*SR] (lane 0), loaded PF steps ahead.
+        const bool ps_live = (lane == 0) && (R0 > 0);
+        auto loadA = [&](int tp, int k) -> float2 {
+            return (tp >= 0 && tp < n_steps) ? __ldg(Ts + static_cast<size_t>(tp) * SR + k * 32 + lane)
+                                             : make_float2(NEG, 0.f);
+        };
+        auto loadPS = [&](int col) -> float2 {
+            return (ps_live && col >= 0 && col < M) ? __ldg(Tp + static_cast<size_t>(col) * SR) : make_float2(NEG, 0.f);
+        };
+
+        float2 aq[PF][K];  // A(t-2) for the step due in slot u
+        float2 pq[PF];     // PS(t-1) for the step due in slot u
+#pragma unroll
+        for (int u = 0; u < PF; ++u) {
+            const int t = t_last - u;
+#pragma unroll
+            for (int k = 0; k < K; ++k) aq[u][k] = loadA(t - 2, k);
+            pq[u] = loadPS(t - 1);
+        }
+        float2 A1[K];  // A(t-1)
+#pragma unroll
+        for (int k = 0; k < K; ++k) A1[k] = loadA(t_last - 1, k);
+        float2 S1;  // row above at anti-diagonal t-1
+        {
+            const float2 ps = loadPS(t_last);
+            S1.x = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].x, 1);
+            S1.y = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].y, 1);
+            if (lane == 0) S1 = ps;
+        }
 
         float accl[K], msg[K], dprev[K];
 #pragma unroll
         for (int k = 0; k < K; ++k) accl[k] = msg[k] = dprev[k] = 0.f;
-        const int n_steps = M + SR - 1;
 
-        for (int t = n_steps - 1; t >= 0; --t) {
-            float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
-            if (lane == 31) {
-                below = 0.f;
-                const int col = t - (SR - 1);
-                if (has_below && col >= 0 && col < M) {
-                    const uint32_t gc = band_base + static_cast<uint32_t>(M - 1 - col);
-                    float v = 0.f;
-                    if (ok) {
-                        if (below_wrap)
-                            ok = wait_gmem_tag(a.wrap + static_cast<size_t>(b) * M + col, wrap_tag(a.seq, band + 1), v, a.wait);
-                        else
-                            ok = wait_smem_tag(my_ring + (gc % kRing) * 8u, gc, v, a.wait);
-                    }
-                    below = v;
-                    if (!below_wrap && (((gc + 1) % (kRing / 4)) == 0 || col == 0))
-                        st_release_cluster_u32(below_consumed, gc + 1);
-                }
-            }
-            float nmsg[K];
+        for (int t0 = t_last; t0 >= 0; t0 -= PF) {
+            // ---- group prologue: messages for this lane's last row (lane 31),
+            // columns colb(t) = t - (SR-1) for t = t0 .. t0-PF+1.
+            float rin[PF];
 #pragma unroll
-            for (int k = K - 1; k >= 0; --k) {
-                const int q = lane * K + k;
-                const int col = t - q;
-                const int row = R0 + q;
-                const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
-                const bool inr = (col >= 0) && (col < M) && (row < N);
-                const bool pruned = (a.bw > 0.f) && (fabsf(static_cast<float>(row - col)) > a.bw);
-                const bool live = inr && !pruned;
-                float e = accl[k] + in_below;
-                if (row == N - 1 && col == M - 1) e = gb;
-                e = live ? e : 0.f;
-                if (inr) Eb[static_cast<size_t>(row) * M + col] = e;
-                float wd = 0.f, wu = 0.f, wl = 0.f;
-                if (live) {
-                    const float td = load_score<K>(a.score, P, b, row - 1, col - 1);
-                    const float tu = load_score<K>(a.score, P, b, row - 1, col);
-                    const float tl = load_score<K>(a.score, P, b, row, col - 1);
-                    const float m = max3f(td, tu, tl);
-                    const float ed = ex2f(td - m), eu = ex2f(tu - m), el = ex2f(tl - m);
-                    const float inv = rcpf(ed + eu + el);
-                    wd = ed * inv;
-                    wu = eu * inv;
-                    wl = el * inv;
-                }
-                accl[k] = e * wl;
-                nmsg[k] = e * wu + dprev[k];
-                dprev[k] = e * wd;
-            }
-            if (lane == 0 && has_up && !withhold) {
-                const int col = t;  // q = 0
-                if (col >= 0 && col < M) {
-                    if (up_wrap) {
-                        st_gpu_u64(a.wrap + static_cast<size_t>(b) * M + col, pack_tagged(nmsg[0], wrap_tag(a.seq, band)));
-                    } else {
-                        const uint32_t gc = band_base + static_cast<uint32_t>(M - 1 - col);
-                        if (gc >= static_cast<uint32_t>(kRing) && ok &&
-                            static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)
-                            ok = wait_counter_ge(my_consumed, gc - kRing + 1, cons_seen, a.wait);
-                        st_cluster_u64(up_ring + (gc % kRing) * 8u, pack_tagged(nmsg[0], gc));
+            for (int u = 0; u < PF; ++u) rin[u] = 0.f;
+            const int colb0 = t0 - (SR - 1);
+            if (has_below && colb0 - (PF - 1) < M && colb0 >= 0) {  // warp-uniform
+                bool all = true;
+                uint32_t tg[PF];
+#pragma unroll
+                for (int u = 0; u < PF; ++u) {
+                    const int col = colb0 - u;
+                    tg[u] = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
+                    if (col >= 0 && col < M) {
+                        const uint64_t e = below_wrap ? ld_gpu_u64(wrap_io + col) : ld_cluster_u64(my_ring + (tg[u] % kRing) * 8u);
+                        all = all && tag_of(e) == tg[u];
+                        rin[u] = val_of(e);
                     }
                 }
-            }
+                if (lane == 31 && !all) {
 #pragma unroll
-            for (int k = 0; k < K; ++k) msg[k] = nmsg[k];
-            if ((t & 63) == 0 && __any_sync(SDTW_FULL_MASK, !ok)) {
+                    for (int u = 0; u < PF; ++u) {
+                        const int col = colb0 - u;
+                        if (col >= 0 && col < M && ok) {
+                            if (below_wrap) ok = wait_gmem_tag(wrap_io + col, tg[u], rin[u], wc);
+                            else ok = wait_smem_tag(my_ring + (tg[u] % kRing) * 8u, tg[u], rin[u], wc);
+                        }
+                    }
+                }
+                // Consumption counter: columns > colb0 - PF are now out of the ring.
+                const int done = M - max(colb0 - PF + 1, 0);  // reversed columns consumed
+                if (!below_wrap && lane == 31 && report_due(done, PF, M))
+                    st_release_cluster_u32(below_consumed, band_base + static_cast<uint32_t>(done));
+            }
+            // ---- flow control for the messages this group publishes upward (lane 0, columns t0 .. t0-PF+1).
+            if (has_up && !up_wrap) {  // warp-uniform
+                const int col_last = max(t0 - (PF - 1), 0);
+                if (col_last < M) {
+                    const uint32_t gc = band_base + static_cast<uint32_t>(M - 1 - col_last);
+                    if (lane == 0 && ok && gc >= static_cast<uint32_t>(kRing) &&
+                        static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)
+                        ok = wait_counter_ge(my_consumed, gc - kRing + 1, cons_seen, wc);
+                }
+            }
+            // ---- PF branch-free reverse steps.
+#pragma unroll
+            for (int u = 0; u < PF; ++u) {
+                const int t = t0 - u;
+                float2 A2[K];
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    A2[k] = aq[u][k];
+                    aq[u][k] = loadA(t - 2 - PF, k);
+                }
+                float2 S2;
+                {
+                    const float2 ps = pq[u];
+                    pq[u] = loadPS(t - 1 - PF);
+                    S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
+                    S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
+                    S2.x = (lane == 0) ? ps.x : S2.x;
+                    S2.y = (lane == 0) ? ps.y : S2.y;
+                }
+                float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
+                below = (lane == 31) ? rin[u] : below;
+                float nmsg[K];
+#pragma unroll
+                for (int k = K - 1; k >= 0; --k) {
+                    const int q = lane * K + k;
+                    const int col = t - q;
+                    const int row = R0 + q;
+                    const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
+                    const bool inr = row < N && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                    const bool inband = static_cast<unsigned>(row - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    const bool live = inr && inband;
+                    float e = accl[k] + in_below;
+                    e = (row == N - 1 && col == M - 1) ? gb : e;
+                    e = live ? e : 0.f;
+                    if (inr) Eb[static_cast<size_t>(row) * M + col] = e;
+                    // Predecessor scores; column -1 is the border (+inf R), except
+                    // the corner (-1, -1) of row 0 (R = 0).
+                    float2 tl = A1[k];
+                    float2 tu = (k == 0) ? S1 : A1[k > 0 ? k - 1 : 0];
+                    float2 td = (k == 0) ? S2 : A2[k > 0 ? k - 1 : 0];
+                    const bool c0 = (col == 0);
+                    tl.x = c0 ? NEG : tl.x;
+                    tl.y = c0 ? 0.f : tl.y;
+                    td.x = c0 ? ((row == 0) ? 0.f : NEG) : td.x;
+                    td.y = c0 ? 0.f : td.y;
+                    // Softmax of the predecessors' scores; the lo of the max cancels.
+                    const float m = max3f(td.x, tu.x, tl.x);
+                    const float ed = ex2f((td.x - m) + td.y);
+                    const float eu = ex2f((tu.x - m) + tu.y);
+                    const float el = ex2f((tl.x - m) + tl.y);
+                    const float inv = live ? rcpf(ed + eu + el) : 0.f;
+                    const float ei = e * inv;
+                    accl[k] = ei * el;
+                    nmsg[k] = fmaf(ei, eu, dprev[k]);
+                    dprev[k] = ei * ed;
+                }
+                // Message of row 0 to the stripe above, column t.
+                const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
+                const uint32_t gcu = band_base + static_cast<uint32_t>(M - 1 - t);
+                st_gpu_u64_if(pub && up_wrap, wrap_io + t, pack_tagged(nmsg[0], out_tag_wrap));
+                st_cluster_u64_if(pub && !up_wrap, up_ring + (gcu % kRing) * 8u, pack_tagged(nmsg[0], gcu));
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    msg[k] = nmsg[k];
+                    A1[k] = A2[k];
+                }
+                S1 = S2;
+            }
+            if ((((t_last - t0) / PF) & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
@@ -294,7 +524,7 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
 // R (B, N+2, M+2) in the reference launcher layout (launcher.py:55-56, 177-178):
 // R[:,0,0] = 0, other borders +inf, interior R = -T * gamma * ln 2.
 template <int K>
-__global__ void score_to_R_kernel(const float* __restrict__ S, float* __restrict__ R, WavePlan P, float inv_k) {
+__global__ void score_to_R_kernel(const float2* __restrict__ S, float* __restrict__ R, WavePlan P, float inv_k) {
     const size_t total = static_cast<size_t>(P.B) * (P.N + 2) * (P.M + 2);
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -302,15 +532,20 @@ __global__ void score_to_R_kernel(const float* __restrict__ S, float* __restrict
         const int i = static_cast<int>((idx / (P.M + 2)) % (P.N + 2));
         const int b = static_cast<int>(idx / (static_cast<size_t>(P.M + 2) * (P.N + 2)));
         float v;
-        if (i == 0 && j == 0) v = 0.f;
-        else if (i == 0 || j == 0 || i == P.N + 1 || j == P.M + 1) v = pos_inf();
-        else v = -load_score<K>(S, P, b, i - 1, j - 1) * inv_k;
+        if (i == 0 && j == 0) {
+            v = 0.f;
+        } else if (i == 0 || j == 0 || i == P.N + 1 || j == P.M + 1) {
+            v = pos_inf();
+        } else {
+            const float2 t = load_score<K>(S, P, b, i - 1, j - 1);
+            v = (t.x == neg_inf()) ? pos_inf() : fmaf(-t.x, inv_k, -t.y * inv_k);
+        }
         R[idx] = v;
     }
 }
 
 template <int K>
-__global__ void R_to_score_kernel(const float* __restrict__ R, float* __restrict__ S, WavePlan P, float kk) {
+__global__ void R_to_score_kernel(const float* __restrict__ R, float2* __restrict__ S, WavePlan P, float kk) {
     constexpr int SR = 32 * K;
     const size_t total = static_cast<size_t>(P.B) * P.N * P.M;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -323,7 +558,13 @@ __global__ void R_to_score_kernel(const float* __restrict__ R, float* __restrict
         const int q = row - s * SR;
         const int l = q / K;
         const int k = q - l * K;
-        S[((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + (q + col)) * SR + k * 32 + l] = -r * kk;
+        float hi = -r * kk;
+        float lo = fmaf(-r, kk, -hi);
+        if (!(hi > neg_inf())) {  // R = +inf (unreachable or outside the band)
+            hi = neg_inf();
+            lo = 0.f;
+        }
+        S[((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + (q + col)) * SR + k * 32 + l] = make_float2(hi, lo);
     }
 }
 
@@ -346,7 +587,7 @@ static cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t 
 }
 
 static size_t ring_smem_bytes(const WavePlan& P) {
-    return static_cast<size_t>(P.wpc) * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
+    return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
 
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
@@ -355,6 +596,8 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
     switch (P.K) {
         case 1: return launch_cluster((const void*)fwd_kernel<1>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+        case 2: return launch_cluster((const void*)fwd_kernel<2>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+        case 4: return launch_cluster((const void*)fwd_kernel<4>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -365,27 +608,33 @@ cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
     switch (P.K) {
         case 1: return launch_cluster((const void*)bwd_kernel<1>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+        case 2: return launch_cluster((const void*)bwd_kernel<2>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+        case 4: return launch_cluster((const void*)bwd_kernel<4>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
         default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_score_to_R(const float* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream) {
+cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream) {
     const size_t total = static_cast<size_t>(P.B) * (P.N + 2) * (P.M + 2);
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<size_t>((total + threads - 1) / threads, 148u * 16u));
     switch (P.K) {
         case 1: score_to_R_kernel<1><<<blocks, threads, 0, stream>>>(S, R, P, inv_k); break;
+        case 2: score_to_R_kernel<2><<<blocks, threads, 0, stream>>>(S, R, P, inv_k); break;
+        case 4: score_to_R_kernel<4><<<blocks, threads, 0, stream>>>(S, R, P, inv_k); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_R_to_score(const float* R, float* S, const WavePlan& P, float kk, cudaStream_t stream) {
+cudaError_t launch_R_to_score(const float* R, float2* S, const WavePlan& P, float kk, cudaStream_t stream) {
     const size_t total = static_cast<size_t>(P.B) * P.N * P.M;
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<size_t>((total + threads - 1) / threads, 148u * 16u));
     switch (P.K) {
         case 1: R_to_score_kernel<1><<<blocks, threads, 0, stream>>>(R, S, P, kk); break;
+        case 2: R_to_score_kernel<2><<<blocks, threads, 0, stream>>>(R, S, P, kk); break;
+        case 4: R_to_score_kernel<4><<<blocks, threads, 0, stream>>>(R, S, P, kk); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

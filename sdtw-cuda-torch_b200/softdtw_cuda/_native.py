@@ -32,6 +32,7 @@ _SIGS = {
     "sdtw_status": ([], _I),
     "sdtw_set_wait_timeout_ns": ([ctypes.c_ulonglong], None),
     "sdtw_debug_stall_stripe": ([_I], None),
+    "sdtw_set_plan_override": ([_I, _I, _I], None),
     "sdtw_score_elems": ([_I, _I, _I], _SZ),
     "sdtw_workspace_bytes": ([_I, _I, _I], _SZ),
     "sdtw_workspace_bytes_xy": ([_I, _I, _I, _I], _SZ),
@@ -128,8 +129,14 @@ def check_status(device=None) -> None:
         torch.cuda.synchronize(device)
     s = status()
     if s != 0:
-        raise NativeError(f"softdtw_cuda: device-side wait failed (status {s}: "
-                          f"{lib().sdtw_error_string(s).decode()})")
+        raise NativeError(f"softdtw_cuda: device-side wait failed (status {s}): "
+                          f"{lib().sdtw_last_error_message().decode(errors='replace')}")
+
+
+def set_plan_override(warps_per_cta: int = 0, cluster_size: int = 0, rows_per_lane: int = 0) -> None:
+    """Force the wavefront launch geometry (zeros restore the automatic plan).
+    A forward and its backward must run under the same rows_per_lane."""
+    lib().sdtw_set_plan_override(int(warps_per_cta), int(cluster_size), int(rows_per_lane))
 
 
 def set_wait_timeout(seconds: float) -> None:

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_sizes_without_gpu():
     L = _native.lib()
-    assert L.sdtw_score_elems(4, 64, 64) == 4 * 2 * (64 + 31) * 32
+    assert L.sdtw_score_elems(4, 64, 64) == 2 * 4 * 2 * (64 + 31) * 32   # (hi, lo) per cell
     assert L.sdtw_score_elems(0, 4, 4) == 0
     assert L.sdtw_workspace_bytes(4, 64, 64) == 0          # one band: no wrap ring
     assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) >= 4 * 64 * 64 * 4

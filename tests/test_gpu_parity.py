@@ -76,7 +76,8 @@ def test_launcher_level_tables(name):
     Rn = R.cpu().numpy()
     fin = np.isfinite(z["R"])
     assert np.array_equal(np.isfinite(Rn), fin)
-    np.testing.assert_allclose(Rn[fin], z["R"][fin], rtol=2e-6, atol=1e-6)
+    # R accumulates float32 rounding along the path: absolute error ~ |R|max * 1e-6.
+    np.testing.assert_allclose(Rn[fin], z["R"][fin], rtol=2e-6, atol=2e-6 * np.abs(z["R"][fin]).max())
     E = launcher.softdtw_backward_cuda_log(D, R, m["gamma"], bw).cpu().numpy()
     _, R64, _ = O.forward(z["D"].astype(np.float64), m["gamma"], m["bandwidth"])
     E64 = O.backward(z["D"].astype(np.float64), R64, m["gamma"], m["bandwidth"])
@@ -154,6 +155,24 @@ def test_long_multiband_vs_oracle():
     out, gx, gy = _gpu_run(x, y, gamma=1.0, fused=True)
     assert np.isfinite(out).all() and np.isfinite(gx).all() and np.abs(gx).mean() > 0
     _check_against_oracle(x, y, out, gx, gy, gamma=1.0, fused=True)
+
+
+@pytest.mark.parametrize("wpc,cs,k", [(1, 1, 1), (1, 2, 1), (2, 1, 1), (3, 2, 1), (1, 8, 1), (2, 4, 1),
+                                      (1, 1, 2), (2, 2, 2), (1, 1, 4), (1, 2, 4)])
+def test_forced_plans_many_bands(wpc, cs, k):
+    """Small problems on forced launch geometries: many bands (band-wrap ring),
+    every cluster size, stripes split across CTAs, 1/2/4 DP rows per lane;
+    fused and unfused."""
+    rng = np.random.default_rng(wpc * 10 + cs + 100 * k)
+    x = rng.standard_normal((3, 230, 3)).astype(np.float32)
+    y = rng.standard_normal((3, 170, 3)).astype(np.float32)
+    _native.set_plan_override(wpc, cs, k)
+    try:
+        for fused in (False, True):
+            out, gx, gy = _gpu_run(x, y, gamma=0.5, fused=fused)
+            _check_against_oracle(x, y, out, gx, gy, gamma=0.5, fused=fused)
+    finally:
+        _native.set_plan_override(0, 0)
 
 
 def test_reference_long_and_small_gamma_smoke():
