@@ -39,9 +39,13 @@ PUBLISHED = {  # reference, B=32 N=M=512 D=64 fwd+bwd (unstated GPU
 }
 MUFU_PER_CELL = 7          # algorithmic ex2/lg2 per DP cell, forward + backward (reference algorithm)
 MUFU_PER_SM_CLK = 16       # ex2/lg2 results per SM per clock
-# Algorithmic HBM bytes per DP cell of each kernel (float32).
-ALG_BYTES = {"cost": 4, "forward": 8, "backward": 8, "grad_sqeuclid": 8}
-ALG_MUFU = {"forward": 3, "backward": 4}
+# Algorithmic HBM bytes per DP cell of each library kernel: every table entry
+# read or written once (cost 4 B, score 8 B as a (hi, lo) pair, E 4 B).
+ALG_BYTES = {"cost_wl": 4, "wavefront_fwd": 12, "wavefront_bwd": 12, "wl_to_rm": 8, "grad_xy": 8,
+             "rm_to_wl": 8, "cost_rowmajor": 4}
+# Algorithmic MUFU ops per cell of the reference algorithm: forward softmin
+# (2 ex2 + 1 lg2), reverse log-sum-exp (2 ex2 + 1 lg2) and E = exp(log E) (1 ex2).
+ALG_MUFU = {"wavefront_fwd": 3, "wavefront_bwd": 4}
 
 
 def parse():
@@ -224,6 +228,7 @@ def main():
 
     modes = {}
     launches = 0
+    breakdown = {}
     with sampler:
         for name, fused in (("fused", None), ("unfused", False)):
             for _ in range(args.warmup):
@@ -232,9 +237,15 @@ def main():
             barrier()
             torch.cuda.synchronize(dev)
             l0 = _native.launch_count
+            if name == "fused":
+                _native.timing_enable(True)  # per-kernel CUDA events on the launching stream
             ms = timed(lambda: step(fused), args.steps)
             if name == "fused":
                 launches = _native.launch_count - l0
+                kt = _native.timing_read()
+                _native.timing_enable(False)
+                breakdown = {k: v[0] / max(v[1], 1) * (v[1] / args.steps) for k, v in kt.items()}
+                per_launch = {k: v[0] / max(v[1], 1) for k, v in kt.items()}
             torch.cuda.synchronize(dev)
             barrier()
             _native.check_status(dev)
@@ -243,31 +254,6 @@ def main():
                            "median_ms": statistics.median(ms)}
             pub = PUBLISHED.get(args.workload, {}).get(name)
             modes[name]["vs_published"] = (modes[name]["value"] / world / pub) if pub else None
-
-    # Per-kernel breakdown of the headline path: the kernels it runs, each timed
-    # with CUDA events on the launching stream (cost -> forward wavefront ->
-    # reverse wavefront -> cost chain rule).
-    breakdown = {}
-    xb, yb = x.detach(), y.detach()
-    gout = torch.full((B,), 1.0 / B, device=dev)
-    for _ in range(args.warmup):
-        D = _native.cost_sqeuclid(xb, yb, direct=True)
-        out, score = _native.forward(D, gamma, -1.0)
-        E = _native.backward(score, gout, B, N, M, gamma, -1.0)
-        _native.grad_sqeuclid(E, None, xb, yb)
-    torch.cuda.synchronize(dev)
-    _native.profile_events = []
-    for _ in range(args.steps):
-        flush.zero_()
-        D = _native.cost_sqeuclid(xb, yb, direct=True)
-        out, score = _native.forward(D, gamma, -1.0)
-        E = _native.backward(score, gout, B, N, M, gamma, -1.0)
-        _native.grad_sqeuclid(E, None, xb, yb)
-    torch.cuda.synchronize(dev)
-    for nm, a, b in _native.profile_events:
-        breakdown.setdefault(nm, []).append(a.elapsed_time(b))
-    _native.profile_events = None
-    breakdown = {k: statistics.mean(v) for k, v in breakdown.items()}
 
     # End to end through the public API with host buffers.
     gx_h = torch.empty_like(x_h).pin_memory()
@@ -294,9 +280,9 @@ def main():
     clocks = sampler.summary()
     head = modes["fused"]
 
-    # Roofline of the dominant kernel.
+    # Roofline of the dominant kernel (largest device time per step).
     dom = max(breakdown, key=breakdown.get)
-    dom_ms = breakdown[dom]
+    dom_ms = per_launch[dom]
     alg_bytes = ALG_BYTES[dom] * cells
     peaks = {}
     try:
@@ -320,11 +306,11 @@ def main():
     sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
     mufu_peak = n_sm * MUFU_PER_SM_CLK * sm_mhz * 1e6
     step_mufu = MUFU_PER_CELL * cells / (head["ms_per_step"] / 1e3)
-    wf = {k: ALG_MUFU[k] * cells / (breakdown[k] / 1e3) for k in ALG_MUFU if k in breakdown}
+    wf = {k: ALG_MUFU[k] * cells / (per_launch[k] / 1e3) for k in ALG_MUFU if k in per_launch}
     roofline_mufu = {"bound": "mufu", "unit": "Gop/s", "peak": mufu_peak / 1e9,
                      "peak_basis": f"{n_sm} SMs x {MUFU_PER_SM_CLK} ex2/lg2 per clk x {sm_mhz:.0f} MHz (median under load)",
                      "step_achieved": step_mufu / 1e9, "step_frac": step_mufu / mufu_peak,
-                     "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms": breakdown[k],
+                     "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms": per_launch[k],
                                      "alg_ops_per_cell": ALG_MUFU[k]} for k, v in wf.items()},
                      "alg_ops_per_cell": MUFU_PER_CELL}
 
@@ -360,7 +346,7 @@ def main():
                    "l2": "flushed before every timed step (256 MiB write, outside the events)",
                    "vs_baseline_basis": "per-GPU value / BASELINE.md published fused number (unstated GPU)"},
         "modes": modes,
-        "kernel_ms": breakdown,
+        "kernel_ms_per_step": breakdown,
         "roofline": roofline,
         "roofline_mufu": roofline_mufu,
         "cpu_baseline": cpu_baseline,

@@ -17,7 +17,8 @@
  * (B, N+2, M+2): it holds T = -R * log2(e) / gamma for every cell, as a pair
  * of float32 (hi, lo) with T = hi + lo, in the anti-diagonal ("wavefront")
  * layout the kernels write with coalesced stores.  It must be 8-byte aligned;
- * workspaces 16-byte aligned.
+ * workspaces 256-byte aligned.  The cost table of the unfused x/y entry points
+ * (sdtw_cost_elems floats) uses the same anti-diagonal layout.
  * sdtw_score_to_R_f32 / sdtw_R_to_score_f32 convert to and from the
  * reference layout.
  */
@@ -53,6 +54,14 @@ int sdtw_status(void);
 /* Wall-clock limit of one device-side wait, in nanoseconds (default 2e9). */
 void sdtw_set_wait_timeout_ns(unsigned long long ns);
 
+/* Per-kernel device timing.  While enabled, every kernel the library launches
+ * is bracketed by CUDA events on its stream.  sdtw_timing_read synchronises the
+ * recorded events, and returns per kernel name (comma-separated in `names`)
+ * the total milliseconds and launch count accumulated since enabling; the
+ * return value is the number of entries.  Enabling clears the totals. */
+void sdtw_timing_enable(int on);
+int sdtw_timing_read(char *names, size_t names_len, double *total_ms, long *counts, int max_entries);
+
 /* Failure-detection test hook: the producer of stripe `stripe` (32-row band
  * of the DP table) withholds its output so that its consumer's wait runs out.
  * -1 disables.  Never set outside tests. */
@@ -67,10 +76,15 @@ void sdtw_set_plan_override(int warps_per_cta, int cluster_size, int rows_per_la
 /* Number of float32 elements of the score table for a (B,N,M) problem. */
 size_t sdtw_score_elems(int B, int N, int M);
 
+/* Number of float32 elements of the cost table kept between
+ * sdtw_forward_sqeuclid_f32 and sdtw_backward_sqeuclid_f32. */
+size_t sdtw_cost_elems(int B, int N, int M);
+
 /* Workspace bytes of sdtw_forward_f32 / sdtw_backward_f32 (D input). */
 size_t sdtw_workspace_bytes(int B, int N, int M);
 
-/* Workspace bytes of sdtw_forward_xy_f32 / sdtw_backward_xy_f32 (x, y input). */
+/* Workspace bytes of the x, y entry points (sdtw_forward_xy_f32,
+ * sdtw_backward_xy_f32, sdtw_forward_sqeuclid_f32, sdtw_backward_sqeuclid_f32). */
 size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim);
 
 /* Cost matrix D (B,N,M) from x (B,N,dim), y (B,M,dim).
@@ -109,6 +123,24 @@ int sdtw_forward_xy_f32(const float *x, const float *y, float *score, float *out
 int sdtw_backward_xy_f32(const float *x, const float *y, const float *score, const float *grad_out,
                          float *grad_x, float *grad_y, int B, int N, int M, int dim, float gamma,
                          float bandwidth, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Unfused x/y path: the cost ||x||^2 + ||y||^2 - 2 x.y clamped at 0 (as
+ * softdtw_cuda/distances.py:6-28) is computed into `cost` (sdtw_cost_elems
+ * floats, kept by the caller for the backward), then the forward DP runs on it.
+ * -- replaces softdtw_cuda/module.py:116-118 (pairwise_distance followed by
+ *    SoftDTWAutograd.apply) for CUDA tensors */
+int sdtw_forward_sqeuclid_f32(const float *x, const float *y, float *score, float *cost, float *out, int B,
+                              int N, int M, int dim, float gamma, float bandwidth, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
+/* Backward of sdtw_forward_sqeuclid_f32: grad_x, grad_y through the reverse DP
+ * and the cost's chain rule, zero where the clamp at 0 was active.
+ * -- replaces softdtw_cuda/autograd.py:33-48 followed by torch autograd of
+ *    softdtw_cuda/distances.py:20-28 */
+int sdtw_backward_sqeuclid_f32(const float *x, const float *y, const float *score, const float *cost,
+                               const float *grad_out, float *grad_x, float *grad_y, int B, int N, int M, int dim,
+                               float gamma, float bandwidth, void *workspace, size_t workspace_bytes,
+                               void *stream);
 
 /* Chain rule of the unfused cost: given G = dL/dD (B,N,M) and the clamped cost
  * D used as the clamp mask (NULL = no mask), writes grad_x, grad_y.

@@ -4,8 +4,10 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/sdtw_b200.h"
 #include "sdtw_kernels.h"
@@ -28,6 +30,50 @@ std::mutex g_init_mu;
 int* g_status_host = nullptr;    // mapped pinned words: [0] status, [8..15] WaitDiag
 int* g_status_dev = nullptr;     // their device address
 int g_num_sms[64] = {0};
+
+// Optional per-kernel timing (sdtw_timing_enable): CUDA events recorded on the
+// launching stream around each kernel.
+std::atomic<int> g_timing{0};
+std::mutex g_timing_mu;
+struct PendingEv {
+    const char* name;
+    cudaEvent_t e0, e1;
+};
+std::vector<PendingEv> g_pending;
+std::vector<cudaEvent_t> g_ev_pool;
+std::map<std::string, std::pair<double, long>> g_totals;
+
+cudaEvent_t pool_event() {
+    if (!g_ev_pool.empty()) {
+        cudaEvent_t e = g_ev_pool.back();
+        g_ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+struct KernelTimer {
+    const char* name;
+    cudaStream_t st;
+    cudaEvent_t e0 = nullptr;
+    KernelTimer(const char* n, cudaStream_t s) : name(n), st(s) {
+        if (g_timing.load()) {
+            std::lock_guard<std::mutex> lk(g_timing_mu);
+            e0 = pool_event();
+            cudaEventRecord(e0, st);
+        }
+    }
+    ~KernelTimer() {
+        if (e0) {
+            std::lock_guard<std::mutex> lk(g_timing_mu);
+            cudaEvent_t e1 = pool_event();
+            cudaEventRecord(e1, st);
+            g_pending.push_back({name, e0, e1});
+        }
+    }
+};
 
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -142,17 +188,22 @@ WavePlan plan(int B, int N, int M) {
     return make_plan(B, N, M, num_sms(), g_wpc_override.load(), g_cs_override.load(), g_k_override.load());
 }
 
-// Workspace layout: [wrap ring][cost or E scratch (xy paths)]
+// Workspace layouts (each region 256-byte aligned):
+//   D-input forward/backward : [wrap ring][WL table]
+//   x/y forward              : [wrap ring][WL cost]
+//   x/y backward, sqeuclid bwd: [wrap ring][WL E][row-major G]
 size_t wave_ws(int B, int N, int M) {
     WavePlan p = plan(B, N, M);
     return align_up(wrap_bytes(p), 256);
 }
+size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
+size_t rm_bytes(int B, int N, int M) { return align_up((size_t)B * N * M * sizeof(float), 256); }
 
-int run_forward(const float* D, float* score, float* out, int B, int N, int M, float gamma, float bw,
+int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream) {
     FwdArgs a{};
     a.P = plan(B, N, M);
-    a.D = D;
+    a.Dw = Dw;
     a.score = reinterpret_cast<float2*>(score);
     a.out = out;
     a.wrap = wrap;
@@ -163,26 +214,54 @@ int run_forward(const float* D, float* score, float* out, int B, int N, int M, f
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
     a.wait = wait_ctx();
-    cudaError_t e = launch_forward(a, stream);
+    cudaError_t e;
+    {
+        KernelTimer kt("wavefront_fwd", stream);
+        e = launch_forward(a, stream);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "forward launch");
     return SDTW_OK;
 }
 
-int run_backward(const float* score, const float* grad_out, float* E, int B, int N, int M, float bw,
+int run_backward(const float* score, const float* grad_out, float* Ew, int B, int N, int M, float bw,
                  uint64_t* wrap, cudaStream_t stream) {
     BwdArgs a{};
     a.P = plan(B, N, M);
     a.score = reinterpret_cast<const float2*>(score);
     a.grad_out = grad_out;
-    a.E = E;
+    a.Ew = Ew;
     a.wrap = wrap;
     a.bw = bw > 0.f ? bw : -1.f;
     a.ibw = int_band(bw);
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
     a.wait = wait_ctx();
-    cudaError_t e = launch_backward(a, stream);
+    cudaError_t e;
+    {
+        KernelTimer kt("wavefront_bwd", stream);
+        e = launch_backward(a, stream);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+    return SDTW_OK;
+}
+
+int check_common(int B, int N, int M, float gamma) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    return SDTW_OK;
+}
+
+int check_ws(void* ws, size_t have, size_t need) {
+    if (have < need) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
+    if (need && !ws) return fail(SDTW_ERR_INVALID_ARGUMENT, "null workspace");
+    if (reinterpret_cast<uintptr_t>(ws) % 256u) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+    return SDTW_OK;
+}
+
+int check_score(const float* score) {
+    if (!score) return fail(SDTW_ERR_INVALID_ARGUMENT, "null score");
+    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
     return SDTW_OK;
 }
 
@@ -222,6 +301,43 @@ void sdtw_set_plan_override(int warps_per_cta, int cluster_size, int rows_per_la
 
 void sdtw_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1ull); }
 
+void sdtw_timing_enable(int on) {
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    g_timing.store(on ? 1 : 0);
+    g_totals.clear();
+}
+
+int sdtw_timing_read(char* names, size_t names_len, double* total_ms, long* counts, int max_entries) {
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    for (const PendingEv& p : g_pending) {
+        float ms = 0.f;
+        if (cudaEventSynchronize(p.e1) == cudaSuccess && cudaEventElapsedTime(&ms, p.e0, p.e1) == cudaSuccess) {
+            auto& t = g_totals[p.name];
+            t.first += ms;
+            t.second += 1;
+        }
+        cudaGetLastError();
+        g_ev_pool.push_back(p.e0);
+        g_ev_pool.push_back(p.e1);
+    }
+    g_pending.clear();
+    int n = 0;
+    std::string joined;
+    for (const auto& kv : g_totals) {
+        if (n >= max_entries) break;
+        if (total_ms) total_ms[n] = kv.second.first;
+        if (counts) counts[n] = kv.second.second;
+        if (n) joined += ",";
+        joined += kv.first;
+        ++n;
+    }
+    if (names && names_len) {
+        std::strncpy(names, joined.c_str(), names_len - 1);
+        names[names_len - 1] = '\0';
+    }
+    return n;
+}
+
 void sdtw_debug_stall_stripe(int stripe) { g_debug_stall.store(stripe); }
 
 size_t sdtw_score_elems(int B, int N, int M) {
@@ -229,14 +345,19 @@ size_t sdtw_score_elems(int B, int N, int M) {
     return score_elems(B, N, M, g_k_override.load());
 }
 
+size_t sdtw_cost_elems(int B, int N, int M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return wl_cells(B, N, M, g_k_override.load());
+}
+
 size_t sdtw_workspace_bytes(int B, int N, int M) {
     if (B <= 0 || N <= 0 || M <= 0) return 0;
-    return wave_ws(B, N, M);
+    return wave_ws(B, N, M) + wl_bytes(B, N, M);
 }
 
 size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim) {
     if (B <= 0 || N <= 0 || M <= 0 || dim <= 0) return 0;
-    return wave_ws(B, N, M) + align_up((size_t)B * N * M * sizeof(float), 256);
+    return wave_ws(B, N, M) + wl_bytes(B, N, M) + rm_bytes(B, N, M);
 }
 
 int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int N, int M, int dim, int direct,
@@ -245,7 +366,11 @@ int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int 
     if (rc) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !D) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    cudaError_t e = launch_cost(x, y, D, B, N, M, dim, direct != 0, static_cast<cudaStream_t>(stream));
+    cudaError_t e;
+    {
+        KernelTimer kt("cost_rowmajor", static_cast<cudaStream_t>(stream));
+        e = launch_cost(x, y, D, B, N, M, dim, direct != 0, static_cast<cudaStream_t>(stream));
+    }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
     return SDTW_OK;
 }
@@ -253,66 +378,125 @@ int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int 
 int sdtw_forward_f32(const float* D, float* score, float* out, int B, int N, int M, float gamma, float bandwidth,
                      void* workspace, size_t workspace_bytes, void* stream) {
     int rc;
-    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
-    if (!D || !score || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
-    if (workspace_bytes < wave_ws(B, N, M) || (wave_ws(B, N, M) && !workspace))
-        return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
-    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
-    return run_forward(D, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace),
-                       static_cast<cudaStream_t>(stream));
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
+    if (!D || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t w0 = wave_ws(B, N, M);
+    if ((rc = check_ws(workspace, workspace_bytes, w0 + wl_bytes(B, N, M)))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* Dw = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
+    const WavePlan p = plan(B, N, M);
+    cudaError_t e;
+    {
+        KernelTimer kt("rm_to_wl", st);
+        e = launch_rm_to_wl(D, Dw, p, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "layout launch");
+    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
 }
 
 int sdtw_backward_f32(const float* score, const float* grad_out, float* E, int B, int N, int M, float gamma,
                       float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
     int rc;
-    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
-    if (!score || !E) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
-    if (workspace_bytes < wave_ws(B, N, M) || (wave_ws(B, N, M) && !workspace))
-        return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
-    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
-    return run_backward(score, grad_out, E, B, N, M, bandwidth, static_cast<uint64_t*>(workspace),
-                        static_cast<cudaStream_t>(stream));
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
+    if (!E) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t w0 = wave_ws(B, N, M);
+    if ((rc = check_ws(workspace, workspace_bytes, w0 + wl_bytes(B, N, M)))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
+    rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st);
+    if (rc) return rc;
+    cudaError_t e;
+    {
+        KernelTimer kt("wl_to_rm", st);
+        e = launch_wl_to_rm(Ew, nullptr, E, plan(B, N, M), st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "layout launch");
+    return SDTW_OK;
 }
 
 int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out, int B, int N, int M, int dim,
                         float gamma, float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
     int rc;
-    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
-    if (!x || !y || !score || !out || !workspace) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    if (reinterpret_cast<uintptr_t>(score) % 8u || reinterpret_cast<uintptr_t>(workspace) % 16u)
-        return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte and workspace 16-byte aligned");
-    if (workspace_bytes < sdtw_workspace_bytes_xy(B, N, M, dim)) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
-    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    if (!x || !y || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t w0 = wave_ws(B, N, M);
+    if ((rc = check_ws(workspace, workspace_bytes, w0 + wl_bytes(B, N, M)))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const size_t wrap_sz = wave_ws(B, N, M);
-    float* Dtmp = reinterpret_cast<float*>(static_cast<char*>(workspace) + wrap_sz);
-    cudaError_t e = launch_cost(x, y, Dtmp, B, N, M, dim, true, st);
+    float* Dw = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
+    cudaError_t e;
+    {
+        KernelTimer kt("cost_wl", st);
+        e = launch_cost_wl(x, y, Dw, plan(B, N, M), dim, true, st);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
-    return run_forward(Dtmp, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
+    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
+}
+
+// Backward through the x/y chain rule; mask_w (WL cost) applies the clamp mask
+// of the unfused cost, or is null for the fused cost.
+int backward_xy_common(const float* x, const float* y, const float* score, const float* mask_w, const float* grad_out,
+                       float* grad_x, float* grad_y, int B, int N, int M, int dim, float bandwidth, void* workspace,
+                       cudaStream_t st) {
+    const size_t w0 = wave_ws(B, N, M);
+    float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
+    float* G = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0 + wl_bytes(B, N, M));
+    int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st);
+    if (rc) return rc;
+    cudaError_t e;
+    {
+        KernelTimer kt("wl_to_rm", st);
+        e = launch_wl_to_rm(Ew, mask_w, G, plan(B, N, M), st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "layout launch");
+    {
+        KernelTimer kt("grad_xy", st);
+        e = launch_grad_xy(G, nullptr, x, y, grad_x, grad_y, B, N, M, dim, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+    return SDTW_OK;
 }
 
 int sdtw_backward_xy_f32(const float* x, const float* y, const float* score, const float* grad_out, float* grad_x,
                          float* grad_y, int B, int N, int M, int dim, float gamma, float bandwidth, void* workspace,
                          size_t workspace_bytes, void* stream) {
     int rc;
-    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
-    if (!x || !y || !score || !workspace) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    if (reinterpret_cast<uintptr_t>(score) % 8u || reinterpret_cast<uintptr_t>(workspace) % 16u)
-        return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte and workspace 16-byte aligned");
-    if (workspace_bytes < sdtw_workspace_bytes_xy(B, N, M, dim)) return fail(SDTW_ERR_INVALID_ARGUMENT, "workspace too small");
-    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    if (!x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if ((rc = check_ws(workspace, workspace_bytes, sdtw_workspace_bytes_xy(B, N, M, dim)))) return rc;
+    return backward_xy_common(x, y, score, nullptr, grad_out, grad_x, grad_y, B, N, M, dim, bandwidth, workspace,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, float* cost, float* out, int B, int N,
+                              int M, int dim, float gamma, float bandwidth, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    int rc;
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y || !cost || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if ((rc = check_ws(workspace, workspace_bytes, wave_ws(B, N, M)))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const size_t wrap_sz = wave_ws(B, N, M);
-    float* Etmp = reinterpret_cast<float*>(static_cast<char*>(workspace) + wrap_sz);
-    rc = run_backward(score, grad_out, Etmp, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st);
-    if (rc) return rc;
-    cudaError_t e = launch_grad_xy(Etmp, nullptr, x, y, grad_x, grad_y, B, N, M, dim, st);
-    if (e != cudaSuccess) return cuda_fail(e, "grad launch");
-    return SDTW_OK;
+    cudaError_t e;
+    {
+        KernelTimer kt("cost_wl", st);
+        e = launch_cost_wl(x, y, cost, plan(B, N, M), dim, false, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cost launch");
+    return run_forward(cost, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
+}
+
+int sdtw_backward_sqeuclid_f32(const float* x, const float* y, const float* score, const float* cost,
+                               const float* grad_out, float* grad_x, float* grad_y, int B, int N, int M, int dim,
+                               float gamma, float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y || !cost) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if ((rc = check_ws(workspace, workspace_bytes, sdtw_workspace_bytes_xy(B, N, M, dim)))) return rc;
+    return backward_xy_common(x, y, score, cost, grad_out, grad_x, grad_y, B, N, M, dim, bandwidth, workspace,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int sdtw_grad_sqeuclid_f32(const float* G, const float* D_mask, const float* x, const float* y, float* grad_x,
@@ -321,7 +505,11 @@ int sdtw_grad_sqeuclid_f32(const float* G, const float* D_mask, const float* x, 
     if (rc) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!G || !x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    cudaError_t e = launch_grad_xy(G, D_mask, x, y, grad_x, grad_y, B, N, M, dim, static_cast<cudaStream_t>(stream));
+    cudaError_t e;
+    {
+        KernelTimer kt("grad_xy", static_cast<cudaStream_t>(stream));
+        e = launch_grad_xy(G, D_mask, x, y, grad_x, grad_y, B, N, M, dim, static_cast<cudaStream_t>(stream));
+    }
     if (e != cudaSuccess) return cuda_fail(e, "grad launch");
     return SDTW_OK;
 }

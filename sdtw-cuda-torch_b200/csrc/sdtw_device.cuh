@@ -102,6 +102,33 @@ __device__ __forceinline__ uint64_t ld_gpu_u64(const uint64_t* p) {
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+// Generic-address forms: one instruction serves a remote shared-memory slot
+// (through mapa) and a global ring slot alike.
+__device__ __forceinline__ uint64_t mapa_generic(const void* p, uint32_t rank) {
+    uint64_t r;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(p), "r"(rank));
+    return r;
+}
+// Two tagged u64 (each single-copy atomic; the pair need not be) in one store.
+__device__ __forceinline__ void st_pair_if(bool p, uint64_t generic_addr, uint64_t a, uint64_t b) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.relaxed.cluster.v2.u64 [%1], {%2, %3};\n\t}" ::"r"(
+            static_cast<int>(p)),
+        "l"(generic_addr), "l"(a), "l"(b));
+}
+__device__ __forceinline__ void st_one_if(bool p, uint64_t generic_addr, uint64_t a) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.relaxed.cluster.u64 [%1], %2;\n\t}" ::"r"(
+                     static_cast<int>(p)),
+                 "l"(generic_addr), "l"(a));
+}
+__device__ __forceinline__ void ld_pair(uint64_t generic_addr, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.cluster.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(generic_addr));
+}
+__device__ __forceinline__ uint64_t ld_one(uint64_t generic_addr) {
+    uint64_t a;
+    asm volatile("ld.relaxed.cluster.u64 %0, [%1];" : "=l"(a) : "l"(generic_addr));
+    return a;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -177,64 +204,35 @@ __device__ __forceinline__ int backoff(uint32_t it, uint64_t& t0, const WaitCtx&
     return 0;
 }
 
-// Wait until the u64 at own-CTA smem address `saddr` carries `tag`; return its
-// value in `out`.  Returns false (after recording kStatusTimeout) when the
-// limit runs out, or when another waiter has already failed.
-static __device__ __noinline__ bool wait_smem_tag_slow(uint32_t saddr, uint32_t tag, float& out, const WaitCtx& w) {
+// Slow paths of the ring protocol.  They return their result by value (never
+// through a reference), so the caller's values stay in registers: a reference
+// into a non-inlined call would move them to local memory on the hot path.
+
+// Polls the u64 at generic address `ga` until it carries `tag`; returns the
+// last entry read (success iff its tag equals `tag`).
+static __device__ __noinline__ uint64_t wait_tag_generic(uint64_t ga, uint32_t tag, const WaitCtx& w) {
     uint64_t t0 = 0;
     uint64_t e = 0;
     for (uint32_t it = 1;; ++it) {
-        e = ld_cluster_u64(saddr);
-        if (tag_of(e) == tag) {
-            out = val_of(e);
-            return true;
-        }
+        e = ld_one(ga);
+        if (tag_of(e) == tag) return e;
         const int r = backoff(it, t0, w);
         if (r == 1) record_error(w, kStatusTimeout, 1, tag, tag_of(e));
-        if (r) return false;
+        if (r) return e;
     }
-}
-__device__ __forceinline__ bool wait_smem_tag(uint32_t saddr, uint32_t tag, float& out, const WaitCtx& w) {
-    uint64_t e = ld_cluster_u64(saddr);
-    if (tag_of(e) == tag) {
-        out = val_of(e);
-        return true;
-    }
-    return wait_smem_tag_slow(saddr, tag, out, w);
 }
 
-static __device__ __noinline__ bool wait_gmem_tag_slow(const uint64_t* p, uint32_t tag, float& out, const WaitCtx& w) {
+// Polls the u32 counter at own-CTA smem address `saddr` until it is >= `need`;
+// returns the last value read (success iff >= need).
+static __device__ __noinline__ uint32_t wait_counter_ge(uint32_t saddr, uint32_t need, const WaitCtx& w) {
     uint64_t t0 = 0;
-    uint64_t e = 0;
-    for (uint32_t it = 1;; ++it) {
-        e = ld_gpu_u64(p);
-        if (tag_of(e) == tag) {
-            out = val_of(e);
-            return true;
-        }
-        const int r = backoff(it, t0, w);
-        if (r == 1) record_error(w, kStatusTimeout, 2, tag, tag_of(e));
-        if (r) return false;
-    }
-}
-__device__ __forceinline__ bool wait_gmem_tag(const uint64_t* p, uint32_t tag, float& out, const WaitCtx& w) {
-    uint64_t e = ld_gpu_u64(p);
-    if (tag_of(e) == tag) {
-        out = val_of(e);
-        return true;
-    }
-    return wait_gmem_tag_slow(p, tag, out, w);
-}
-
-// Wait until the u32 counter at own-CTA smem address `saddr` is >= `need`.
-static __device__ __noinline__ bool wait_counter_ge(uint32_t saddr, uint32_t need, uint32_t& seen, const WaitCtx& w) {
-    uint64_t t0 = 0;
+    uint32_t seen = 0;
     for (uint32_t it = 1;; ++it) {
         seen = ld_acquire_cluster_u32(saddr);
-        if (static_cast<int32_t>(seen - need) >= 0) return true;
+        if (static_cast<int32_t>(seen - need) >= 0) return seen;
         const int r = backoff(it, t0, w);
         if (r == 1) record_error(w, kStatusTimeout, 3, need, seen);
-        if (r) return false;
+        if (r) return seen;
     }
 }
 

@@ -13,7 +13,7 @@ namespace sdtw {
 
 struct FwdArgs {
     WavePlan P;
-    const float* D;   // (B,N,M) cost, row-major
+    const float* Dw;  // (B,N,M) cost in the wavefront layout (layout.cu)
     float2* score;    // wavefront-layout score store, (hi, lo) pairs (see sdtw_plan.h)
     float* out;       // (B,) R[N,M]
     uint64_t* wrap;   // (B*M) band-wrap ring, null when n_bands == 1
@@ -30,7 +30,7 @@ struct BwdArgs {
     WavePlan P;
     const float2* score;
     const float* grad_out;  // (B,) upstream gradient, null = ones
-    float* E;               // (B,N,M) output: grad_out[b] * dR[N,M]/dD[i,j]
+    float* Ew;              // (B,N,M) output in the wavefront layout: grad_out[b] * dR[N,M]/dD[i,j]
     uint64_t* wrap;
     float bw;
     int ibw;
@@ -43,6 +43,12 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
 cudaError_t launch_R_to_score(const float* R, float2* S, const WavePlan& P, float kk, cudaStream_t stream);
+
+// layout.cu
+cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+                           cudaStream_t stream);
+cudaError_t launch_rm_to_wl(const float* A, float* Aw, const WavePlan& P, cudaStream_t stream);
+cudaError_t launch_wl_to_rm(const float* Aw, const float* maskw, float* A, const WavePlan& P, cudaStream_t stream);
 
 // dense.cu
 cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, int M, int dim, bool direct,

@@ -43,12 +43,17 @@ inline int rows_per_lane(int N, int k_override = 0) {
     return 1;
 }
 
-// float32 elements (2 per cell: hi, lo) of the score store.
-inline size_t score_elems(int B, int N, int M, int k_override = 0) {
+// Cells (with the layout's padding) of a (B,N,M) table in the wavefront layout.
+inline size_t wl_cells(int B, int N, int M, int k_override = 0) {
     const int K = rows_per_lane(N, k_override);
     const size_t sr = 32u * (size_t)K;
     const size_t ns = ((size_t)N + sr - 1) / sr;
-    return 2u * (size_t)B * ns * ((size_t)M + sr - 1) * sr;
+    return (size_t)B * ns * ((size_t)M + sr - 1) * sr;
+}
+
+// float32 elements (2 per cell: hi, lo) of the score store.
+inline size_t score_elems(int B, int N, int M, int k_override = 0) {
+    return 2u * wl_cells(B, N, M, k_override);
 }
 
 // wpc_override / cs_override / k_override (> 0) force the warps per CTA, the

@@ -45,8 +45,9 @@ __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
 // Steps run in groups of PF.  Per group (warp-uniform code): the consumer lane
 // reads and checks the PF ring slots it will need, the producer lane checks
 // flow control once, and every 32 columns a release store reports progress.
-// Per step: no branches -- shuffles, the cell math, predicated stores.  The
-// cost (forward) or score rows (backward) of step t are loaded PF steps ahead.
+// Per step: shuffles, the cell math, coalesced loads/stores of one
+// anti-diagonal row, one predicated ring store -- no branches.  The cost
+// (forward) or score rows (backward) of step t are loaded PF steps ahead.
 template <int K>
 struct StepCfg {
     static constexpr int PF = (K >= 4) ? 4 : 8;
@@ -58,7 +59,12 @@ __device__ __forceinline__ bool report_due(int done, int PF, int M) {
     return (done & 31) < PF || done >= M;
 }
 
+__device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
+    return (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * (32 * P.K);
+}
+
 // ============================================================== forward
+// Ring slot pair layout (per consumer warp): kRing x {hi, lo} tagged u64.
 template <int K>
 __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     constexpr int PF = StepCfg<K>::PF;
@@ -73,17 +79,17 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     const int g = crank * wpc + warp;
     const int N = P.N, M = P.M;
 
-    // Per warp: kRing (hi, tag) slots, then kRing (lo, tag) slots.
-    uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][2][kRing]
+    uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][kRing][2]
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
     for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
 
-    const uint32_t my_ring = smem_addr(ring + warp * 2 * kRing);
     const uint32_t my_consumed = smem_addr(consumed + warp);
-    uint32_t next_ring = 0, prev_consumed = 0;
-    if (g + 1 < P.G) next_ring = mapa_shared(smem_addr(ring + ((g + 1) % wpc) * 2 * kRing), (g + 1) / wpc);
+    const uint64_t my_ring_g = reinterpret_cast<uint64_t>(ring + warp * 2 * kRing);
+    uint64_t next_ring_g = 0;
+    uint32_t prev_consumed = 0;
+    if (g + 1 < P.G) next_ring_g = mapa_generic(ring + ((g + 1) % wpc) * 2 * kRing, (g + 1) / wpc);
     if (g > 0) prev_consumed = mapa_shared(smem_addr(consumed + (g - 1) % wpc), (g - 1) / wpc);
 
     const float kk = a.kk;
@@ -96,6 +102,8 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     bool ok = true;          // false once a wait of this lane failed
     bool quit = false;       // warp-uniform
     uint32_t cons_seen = 0;  // lane 31: consumer progress last observed
+    float outh = 0.f, outl = 0.f;
+    bool has_outv = false;
 
     for (int band = 0; band < P.n_bands && !quit; ++band) {
         const int s = band * P.G + g;
@@ -107,31 +115,26 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
         const bool has_out = (s + 1 < P.n_stripes) && (s != a.debug_stall);
         const bool out_wrap = (g == P.G - 1);
         const uint32_t band_base = static_cast<uint32_t>(band) * static_cast<uint32_t>(M);
-        float2* Ts = a.score + (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * SR;
-        const uint64_t* wrap_in = a.wrap + static_cast<size_t>(b) * 2 * M;
-        uint64_t* wrap_out = a.wrap + static_cast<size_t>(b) * 2 * M;
+        const size_t sb = stripe_base(P, b, s);
+        float2* Ts = a.score + sb;
+        const float* Ds = a.Dw + sb;
+        // Input and output rings as generic addresses: slot c holds {hi, lo}.
+        const uint64_t in_g = in_wrap ? reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M) : my_ring_g;
+        const uint64_t out_g = out_wrap ? reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M) : next_ring_g;
         const uint32_t in_tag_wrap = wrap_tag(a.seq, band - 1);
         const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
 
         // Everything before this band counts as consumed (see the reverse pass).
-        if (has_in && !in_wrap && lane == 0) st_release_cluster_u32(prev_consumed, band_base);
+        st_release_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed, band_base);
 
-        const float* drow[K];
-        bool rowok[K];
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const int row = R0 + lane * K + k;
-            rowok[k] = row < N;
-            drow[k] = a.D + (static_cast<size_t>(b) * N + (rowok[k] ? row : 0)) * M;
-        }
+        // The lane's cell of step t is at anti-diagonal row t, position k*32+lane;
+        // its column is t - q.  Last cell (N-1, M-1) belongs to one lane and k.
+        const int n_steps = M + SR - 1;
         float dq[PF][K];  // cost of the step due in slot u
 #pragma unroll
         for (int u = 0; u < PF; ++u)
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                const int col = u - (lane * K + k);
-                dq[u][k] = (rowok[k] && static_cast<unsigned>(col) < static_cast<unsigned>(M)) ? __ldg(drow[k] + col) : 0.f;
-            }
+            for (int k = 0; k < K; ++k) dq[u][k] = __ldg(Ds + static_cast<size_t>(u) * SR + k * 32 + lane);
 
         // Three live anti-diagonals: c* = step t-1, o* = step t-2, as (hi, lo).
         float ch[K], cl[K], oh[K], ol[K];
@@ -142,7 +145,8 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
         }
         float uph_prev = (R0 == 0) ? 0.f : NEG;  // T(R0-1, -1)
         float upl_prev = 0.f;
-        const int n_steps = M + SR - 1;
+        int q0 = lane * K;                // row offset of k = 0 in the stripe
+        const int rows_left = N - R0;     // rows q < rows_left are real
 
         for (int t0 = 0; t0 < n_steps; t0 += PF) {
             // ---- group prologue: the row above for columns t0 .. t0+PF-1 (lane 0).
@@ -153,53 +157,56 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                 rin_l[u] = 0.f;
             }
             if (has_in && t0 < M) {  // warp-uniform
+                // All lanes read the same slots (one broadcast transaction each),
+                // so the tag check is warp-uniform and the re-poll loop below is a
+                // uniform branch taken only when the producer is behind.
+                uint32_t tg0 = in_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(t0);
                 bool all = true;
-                uint32_t tg[PF];
-#pragma unroll
-                for (int u = 0; u < PF; ++u) {
-                    const int col = t0 + u;
-                    tg[u] = in_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(col);
-                    if (col < M) {
-                        uint64_t eh, el;
-                        if (in_wrap) {
-                            eh = ld_gpu_u64(wrap_in + col);
-                            el = ld_gpu_u64(wrap_in + M + col);
-                        } else {
-                            const uint32_t slot = (tg[u] % kRing) * 8u;
-                            eh = ld_cluster_u64(my_ring + slot);
-                            el = ld_cluster_u64(my_ring + kRing * 8u + slot);
-                        }
-                        all = all && tag_of(eh) == tg[u] && tag_of(el) == tg[u];
-                        rin_h[u] = val_of(eh);
-                        rin_l[u] = val_of(el);
-                    }
-                }
-                if (lane == 0 && !all) {  // rare: the producer is behind
+                auto read_group = [&]() {
+                    all = true;
 #pragma unroll
                     for (int u = 0; u < PF; ++u) {
                         const int col = t0 + u;
-                        if (col < M && ok) {
-                            if (in_wrap)
-                                ok = wait_gmem_tag(wrap_in + col, tg[u], rin_h[u], wc) &&
-                                     wait_gmem_tag(wrap_in + M + col, tg[u], rin_l[u], wc);
-                            else
-                                ok = wait_smem_tag(my_ring + (tg[u] % kRing) * 8u, tg[u], rin_h[u], wc) &&
-                                     wait_smem_tag(my_ring + kRing * 8u + (tg[u] % kRing) * 8u, tg[u], rin_l[u], wc);
+                        const uint32_t tg = in_wrap ? tg0 : tg0 + static_cast<uint32_t>(u);
+                        const uint32_t slot = in_wrap ? static_cast<uint32_t>(col) : (tg % kRing);
+                        if (col < M) {
+                            uint64_t eh, el;
+                            ld_pair(in_g + slot * 16u, eh, el);
+                            all = all && tag_of(eh) == tg && tag_of(el) == tg;
+                            rin_h[u] = val_of(eh);
+                            rin_l[u] = val_of(el);
+                        }
+                    }
+                };
+                read_group();
+                if (__any_sync(SDTW_FULL_MASK, !all) && ok) {
+                    uint64_t w0 = 0;
+                    for (uint32_t it = 1;; ++it) {
+                        read_group();
+                        if (!__any_sync(SDTW_FULL_MASK, !all)) break;
+                        const int r = backoff(it, w0, wc);
+                        if (r) {
+                            if (r == 1 && lane == 0) record_error(wc, kStatusTimeout, 1, tg0, 0);
+                            ok = false;
+                            break;
                         }
                     }
                 }
                 const int done = min(t0 + PF, M);
-                if (!in_wrap && report_due(done, PF, M) && lane == 0)
-                    st_release_cluster_u32(prev_consumed, band_base + static_cast<uint32_t>(done));
+                st_release_cluster_u32_if(!in_wrap && report_due(done, PF, M) && lane == 0, prev_consumed,
+                                          band_base + static_cast<uint32_t>(done));
             }
             // ---- flow control for the columns this group publishes (lane 31).
             if (has_out && !out_wrap) {  // warp-uniform
                 const int col_last = min(t0 + PF - 1 - (SR - 1), M - 1);
                 if (col_last >= 0) {
                     const uint32_t gc = band_base + static_cast<uint32_t>(col_last);
-                    if (lane == 31 && ok && gc >= static_cast<uint32_t>(kRing) &&
-                        static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)
-                        ok = wait_counter_ge(my_consumed, gc - kRing + 1, cons_seen, wc);
+                    // Every lane tracks cons_seen identically (uniform branch).
+                    if (__any_sync(SDTW_FULL_MASK, ok && gc >= static_cast<uint32_t>(kRing) &&
+                                                       static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)) {
+                        cons_seen = wait_counter_ge(my_consumed, gc - kRing + 1, wc);
+                        ok = ok && static_cast<int32_t>(cons_seen - (gc - kRing + 1)) >= 0;
+                    }
                 }
             }
             // ---- PF branch-free steps.
@@ -207,11 +214,14 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 + u;
                 float c[K];
+                // Prefetch from a clamped (always valid) row: a select on the loaded
+                // value would wait for the load here and defeat the prefetch.  Values
+                // of rows past the end only reach cells that are not live.
+                const size_t tpf = static_cast<size_t>(min(t + PF, n_steps - 1));
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
                     c[k] = dq[u][k];
-                    const int col = t + PF - (lane * K + k);
-                    dq[u][k] = (rowok[k] && static_cast<unsigned>(col) < static_cast<unsigned>(M)) ? __ldg(drow[k] + col) : 0.f;
+                    dq[u][k] = __ldg(Ds + tpf * SR + k * 32 + lane);
                 }
                 float uph = __shfl_up_sync(SDTW_FULL_MASK, ch[K - 1], 1);
                 float upl = __shfl_up_sync(SDTW_FULL_MASK, cl[K - 1], 1);
@@ -223,9 +233,8 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                 float nh[K], nl[K];
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
-                    const int q = lane * K + k;
+                    const int q = q0 + k;
                     const int col = t - q;
-                    const int row = R0 + q;
                     const float lh = ch[k], ll = cl[k];
                     const float uh = (k == 0) ? uph : ch[k > 0 ? k - 1 : 0];
                     const float ul = (k == 0) ? upl : cl[k > 0 ? k - 1 : 0];
@@ -241,23 +250,23 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                     const float hi = m + delta;
                     const float bb = hi - m;
                     const float lo = (m - (hi - bb)) + (delta - bb);
-                    const bool inr = rowok[k] && static_cast<unsigned>(col) < static_cast<unsigned>(M);
-                    const bool inband = static_cast<unsigned>(row - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    const bool inr = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                    const bool inband = static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
                     const bool live = inr && inband && m != NEG;
                     nh[k] = live ? hi : NEG;
                     nl[k] = live ? lo : 0.f;
-                    if (inr) Ts[static_cast<size_t>(t) * SR + k * 32 + lane] = make_float2(nh[k], nl[k]);
-                    if (inr && row == N - 1 && col == M - 1) a.out[b] = fmaf(-nh[k], a.inv_k, -nl[k] * a.inv_k);
+                    if (t < n_steps) Ts[static_cast<size_t>(t) * SR + k * 32 + lane] = make_float2(nh[k], nl[k]);
+                    const bool last = (q == rows_left - 1) && (col == M - 1);
+                    outh = last ? nh[k] : outh;
+                    outl = last ? nl[k] : outl;
+                    has_outv = has_outv || last;
                 }
                 // Bottom row of the stripe goes to the next stripe's warp.
                 const int colb = t - (SR - 1);
                 const bool pub = has_out && lane == 31 && static_cast<unsigned>(colb) < static_cast<unsigned>(M);
-                const uint32_t gcb = band_base + static_cast<uint32_t>(colb);
-                const uint32_t slot = (gcb % kRing) * 8u;
-                st_gpu_u64_if(pub && out_wrap, wrap_out + colb, pack_tagged(nh[K - 1], out_tag_wrap));
-                st_gpu_u64_if(pub && out_wrap, wrap_out + M + colb, pack_tagged(nl[K - 1], out_tag_wrap));
-                st_cluster_u64_if(pub && !out_wrap, next_ring + slot, pack_tagged(nh[K - 1], gcb));
-                st_cluster_u64_if(pub && !out_wrap, next_ring + kRing * 8u + slot, pack_tagged(nl[K - 1], gcb));
+                const uint32_t tgo = out_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(colb);
+                const uint32_t slot = out_wrap ? static_cast<uint32_t>(colb) : (tgo % kRing);
+                st_pair_if(pub, out_g + slot * 16u, pack_tagged(nh[K - 1], tgo), pack_tagged(nl[K - 1], tgo));
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
                     oh[k] = ch[k];
@@ -273,6 +282,7 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
     }
+    if (has_outv) a.out[b] = fmaf(-outh, a.inv_k, -outl * a.inv_k);
     // No CTA may leave while a peer can still write into its shared memory.
     cluster_sync_all();
 }
@@ -296,6 +306,7 @@ __device__ __forceinline__ float2 load_score(const float2* __restrict__ S, const
 // and (q, j-1): the stripe's anti-diagonal rows t-2 and t-1 (coalesced float2
 // loads, PF steps ahead), the row above from the neighbour lane by shuffle,
 // and for lane 0 the last row of the previous stripe (one prefetched load).
+// E is written in the wavefront layout.
 template <int K>
 __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
     constexpr int PF = StepCfg<K>::PF;
@@ -318,10 +329,11 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
 
     // Messages flow upward: the producer of this warp's input is warp g+1 (the
     // stripe below); this warp's output goes to warp g-1.
-    const uint32_t my_ring = smem_addr(ring + warp * kRing);
     const uint32_t my_consumed = smem_addr(consumed + warp);
-    uint32_t up_ring = 0, below_consumed = 0;
-    if (g > 0) up_ring = mapa_shared(smem_addr(ring + ((g - 1) % wpc) * kRing), (g - 1) / wpc);
+    const uint64_t my_ring_g = reinterpret_cast<uint64_t>(ring + warp * kRing);
+    uint64_t up_ring_g = 0;
+    uint32_t below_consumed = 0;
+    if (g > 0) up_ring_g = mapa_generic(ring + ((g - 1) % wpc) * kRing, (g - 1) / wpc);
     if (g + 1 < P.G) below_consumed = mapa_shared(smem_addr(consumed + (g + 1) % wpc), (g + 1) / wpc);
 
     const float gb = a.grad_out ? __ldg(a.grad_out + b) : 1.f;
@@ -345,32 +357,38 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
         const bool has_below = (s + 1 < P.n_stripes);
         const bool below_wrap = (g == P.G - 1);
         const uint32_t band_base = static_cast<uint32_t>(P.n_bands - 1 - band) * static_cast<uint32_t>(M);
-        float* Eb = a.E + static_cast<size_t>(b) * N * M;
-        const float2* Ts = a.score + (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * SR;
+        const size_t sb = stripe_base(P, b, s);
+        float* Es = a.Ew + sb;
+        const float2* Ts = a.score + sb;
         // Last row of the previous stripe, by column: Tp[col * SR].
-        const float2* Tp = (s > 0)
-            ? a.score + ((static_cast<size_t>(b) * P.n_stripes + s - 1) * P.n_diag + (SR - 1)) * SR + (K - 1) * 32 + 31
-            : a.score;
-        uint64_t* wrap_io = a.wrap + static_cast<size_t>(b) * 2 * M;
+        const float2* Tp = (s > 0) ? a.score + stripe_base(P, b, s - 1) + static_cast<size_t>(SR - 1) * SR + (K - 1) * 32 + 31
+                                   : a.score;
+        const uint64_t wrap_g = reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M);
+        const uint64_t in_g = below_wrap ? wrap_g : my_ring_g;
+        const uint64_t out_g = up_wrap ? wrap_g : up_ring_g;
         const uint32_t in_tag_wrap = wrap_tag(a.seq, band + 1);
         const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
 
         // Everything before this band counts as consumed: a warp whose stripe had
         // no producer below it in the previous (later-numbered) band never
         // advanced the counter, and the producer's flow control starts at band_base.
-        if (has_below && !below_wrap && lane == 31) st_release_cluster_u32(below_consumed, band_base);
+        st_release_cluster_u32_if(has_below && !below_wrap && lane == 31, below_consumed, band_base);
 
         const int n_steps = M + SR - 1;
         const int t_last = ((n_steps + PF - 1) / PF) * PF - 1;  // padded: extra steps touch no live cell
-        // Own anti-diagonal rows A(t') = Ts[t'*SR + k*32 + lane] and the previous
-        // stripe's last row PS(col) = Tp[col*SR] (lane 0), loaded PF steps ahead.
-        const bool ps_live = (lane == 0) && (R0 > 0);
+        // Queued loads read clamped (always valid) addresses and are used raw:
+        // a select on a loaded value would stall on the load at issue.  Rows or
+        // columns past either end only reach cells that are not live, or are
+        // masked where they are consumed (the column -1 border below, and the
+        // row above stripe 0, which is -inf).
+        const bool ps_live = R0 > 0;
         auto loadA = [&](int tp, int k) -> float2 {
-            return (tp >= 0 && tp < n_steps) ? __ldg(Ts + static_cast<size_t>(tp) * SR + k * 32 + lane)
-                                             : make_float2(NEG, 0.f);
+            const int tc = min(max(tp, 0), n_steps - 1);
+            return __ldg(Ts + static_cast<size_t>(tc) * SR + k * 32 + lane);
         };
         auto loadPS = [&](int col) -> float2 {
-            return (ps_live && col >= 0 && col < M) ? __ldg(Tp + static_cast<size_t>(col) * SR) : make_float2(NEG, 0.f);
+            const int cc = min(max(col, 0), M - 1);
+            return __ldg(Tp + static_cast<size_t>(cc) * SR);
         };
 
         float2 aq[PF][K];  // A(t-2) for the step due in slot u
@@ -390,12 +408,14 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
             const float2 ps = loadPS(t_last);
             S1.x = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].x, 1);
             S1.y = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].y, 1);
-            if (lane == 0) S1 = ps;
+            if (lane == 0) S1 = ps_live ? ps : make_float2(NEG, 0.f);
         }
 
         float accl[K], msg[K], dprev[K];
 #pragma unroll
         for (int k = 0; k < K; ++k) accl[k] = msg[k] = dprev[k] = 0.f;
+        const int q0 = lane * K;
+        const int rows_left = N - R0;
 
         for (int t0 = t_last; t0 >= 0; t0 -= PF) {
             // ---- group prologue: messages for this lane's last row (lane 31),
@@ -406,40 +426,49 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
             const int colb0 = t0 - (SR - 1);
             if (has_below && colb0 - (PF - 1) < M && colb0 >= 0) {  // warp-uniform
                 bool all = true;
-                uint32_t tg[PF];
-#pragma unroll
-                for (int u = 0; u < PF; ++u) {
-                    const int col = colb0 - u;
-                    tg[u] = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
-                    if (col >= 0 && col < M) {
-                        const uint64_t e = below_wrap ? ld_gpu_u64(wrap_io + col) : ld_cluster_u64(my_ring + (tg[u] % kRing) * 8u);
-                        all = all && tag_of(e) == tg[u];
-                        rin[u] = val_of(e);
-                    }
-                }
-                if (lane == 31 && !all) {
+                auto read_group = [&]() {
+                    all = true;
 #pragma unroll
                     for (int u = 0; u < PF; ++u) {
                         const int col = colb0 - u;
-                        if (col >= 0 && col < M && ok) {
-                            if (below_wrap) ok = wait_gmem_tag(wrap_io + col, tg[u], rin[u], wc);
-                            else ok = wait_smem_tag(my_ring + (tg[u] % kRing) * 8u, tg[u], rin[u], wc);
+                        const uint32_t tg = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
+                        const uint32_t slot = below_wrap ? static_cast<uint32_t>(col) * 2u : (tg % kRing);
+                        if (col >= 0 && col < M) {
+                            const uint64_t e = ld_one(in_g + slot * 8u);
+                            all = all && tag_of(e) == tg;
+                            rin[u] = val_of(e);
+                        }
+                    }
+                };
+                read_group();
+                if (__any_sync(SDTW_FULL_MASK, !all) && ok) {  // uniform: all lanes read the same slots
+                    uint64_t w0 = 0;
+                    for (uint32_t it = 1;; ++it) {
+                        read_group();
+                        if (!__any_sync(SDTW_FULL_MASK, !all)) break;
+                        const int r = backoff(it, w0, wc);
+                        if (r) {
+                            if (r == 1 && lane == 0) record_error(wc, kStatusTimeout, 1, static_cast<uint32_t>(colb0), 0);
+                            ok = false;
+                            break;
                         }
                     }
                 }
                 // Consumption counter: columns > colb0 - PF are now out of the ring.
                 const int done = M - max(colb0 - PF + 1, 0);  // reversed columns consumed
-                if (!below_wrap && lane == 31 && report_due(done, PF, M))
-                    st_release_cluster_u32(below_consumed, band_base + static_cast<uint32_t>(done));
+                st_release_cluster_u32_if(!below_wrap && lane == 31 && report_due(done, PF, M), below_consumed,
+                                          band_base + static_cast<uint32_t>(done));
             }
             // ---- flow control for the messages this group publishes upward (lane 0, columns t0 .. t0-PF+1).
             if (has_up && !up_wrap) {  // warp-uniform
                 const int col_last = max(t0 - (PF - 1), 0);
                 if (col_last < M) {
                     const uint32_t gc = band_base + static_cast<uint32_t>(M - 1 - col_last);
-                    if (lane == 0 && ok && gc >= static_cast<uint32_t>(kRing) &&
-                        static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)
-                        ok = wait_counter_ge(my_consumed, gc - kRing + 1, cons_seen, wc);
+                    if (__any_sync(SDTW_FULL_MASK, ok && gc >= static_cast<uint32_t>(kRing) &&
+                                                       static_cast<int32_t>(cons_seen - (gc - kRing + 1)) < 0)) {
+                        cons_seen = wait_counter_ge(my_consumed, gc - kRing + 1, wc);
+                        ok = ok && static_cast<int32_t>(cons_seen - (gc - kRing + 1)) >= 0;
+                    }
                 }
             }
             // ---- PF branch-free reverse steps.
@@ -458,25 +487,24 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
                     pq[u] = loadPS(t - 1 - PF);
                     S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
                     S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
-                    S2.x = (lane == 0) ? ps.x : S2.x;
-                    S2.y = (lane == 0) ? ps.y : S2.y;
+                    S2.x = (lane == 0) ? (ps_live ? ps.x : NEG) : S2.x;
+                    S2.y = (lane == 0) ? (ps_live ? ps.y : 0.f) : S2.y;
                 }
                 float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
                 below = (lane == 31) ? rin[u] : below;
                 float nmsg[K];
 #pragma unroll
                 for (int k = K - 1; k >= 0; --k) {
-                    const int q = lane * K + k;
+                    const int q = q0 + k;
                     const int col = t - q;
-                    const int row = R0 + q;
                     const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
-                    const bool inr = row < N && static_cast<unsigned>(col) < static_cast<unsigned>(M);
-                    const bool inband = static_cast<unsigned>(row - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    const bool inr = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                    const bool inband = static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
                     const bool live = inr && inband;
                     float e = accl[k] + in_below;
-                    e = (row == N - 1 && col == M - 1) ? gb : e;
+                    e = (q == rows_left - 1 && col == M - 1) ? gb : e;
                     e = live ? e : 0.f;
-                    if (inr) Eb[static_cast<size_t>(row) * M + col] = e;
+                    if (t >= 0 && t < n_steps) Es[static_cast<size_t>(t) * SR + k * 32 + lane] = e;
                     // Predecessor scores; column -1 is the border (+inf R), except
                     // the corner (-1, -1) of row 0 (R = 0).
                     float2 tl = A1[k];
@@ -485,7 +513,7 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
                     const bool c0 = (col == 0);
                     tl.x = c0 ? NEG : tl.x;
                     tl.y = c0 ? 0.f : tl.y;
-                    td.x = c0 ? ((row == 0) ? 0.f : NEG) : td.x;
+                    td.x = c0 ? ((R0 + q == 0) ? 0.f : NEG) : td.x;
                     td.y = c0 ? 0.f : td.y;
                     // Softmax of the predecessors' scores; the lo of the max cancels.
                     const float m = max3f(td.x, tu.x, tl.x);
@@ -500,9 +528,9 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
                 }
                 // Message of row 0 to the stripe above, column t.
                 const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
-                const uint32_t gcu = band_base + static_cast<uint32_t>(M - 1 - t);
-                st_gpu_u64_if(pub && up_wrap, wrap_io + t, pack_tagged(nmsg[0], out_tag_wrap));
-                st_cluster_u64_if(pub && !up_wrap, up_ring + (gcu % kRing) * 8u, pack_tagged(nmsg[0], gcu));
+                const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
+                const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
+                st_one_if(pub, out_g + slot * 8u, pack_tagged(nmsg[0], tgo));
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
                     msg[k] = nmsg[k];

@@ -32,8 +32,11 @@ _SIGS = {
     "sdtw_status": ([], _I),
     "sdtw_set_wait_timeout_ns": ([ctypes.c_ulonglong], None),
     "sdtw_debug_stall_stripe": ([_I], None),
+    "sdtw_timing_enable": ([_I], None),
+    "sdtw_timing_read": ([ctypes.c_char_p, _SZ, _P, _P, _I], _I),
     "sdtw_set_plan_override": ([_I, _I, _I], None),
     "sdtw_score_elems": ([_I, _I, _I], _SZ),
+    "sdtw_cost_elems": ([_I, _I, _I], _SZ),
     "sdtw_workspace_bytes": ([_I, _I, _I], _SZ),
     "sdtw_workspace_bytes_xy": ([_I, _I, _I, _I], _SZ),
     "sdtw_cost_sqeuclid_f32": ([_P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
@@ -41,6 +44,8 @@ _SIGS = {
     "sdtw_backward_f32": ([_P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_forward_xy_f32": ([_P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_backward_xy_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_forward_sqeuclid_f32": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_backward_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_grad_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
     "sdtw_score_to_R_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
     "sdtw_R_to_score_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
@@ -77,8 +82,9 @@ class NativeError(RuntimeError):
 
 
 # Kernel-launch accounting: number of library kernels each entry point enqueues.
-KERNELS_PER_OP = {"cost": 1, "forward": 1, "backward": 1, "forward_xy": 2, "backward_xy": 3,
-                  "grad_sqeuclid": 2, "score_to_R": 1, "R_to_score": 1}
+KERNELS_PER_OP = {"cost": 1, "forward": 2, "backward": 2, "forward_xy": 2, "backward_xy": 4,
+                  "forward_sqeuclid": 2, "backward_sqeuclid": 4, "grad_sqeuclid": 2, "score_to_R": 1,
+                  "R_to_score": 1}
 launch_count = 0
 # When a list, every op appends (name, start_event, end_event) recorded on the
 # stream it launched on (used by bench.py for per-kernel timing).
@@ -147,6 +153,22 @@ def debug_stall_stripe(stripe: int) -> None:
     lib().sdtw_debug_stall_stripe(int(stripe))
 
 
+def timing_enable(on: bool = True) -> None:
+    """Bracket every library kernel with CUDA events on its stream (clears totals)."""
+    lib().sdtw_timing_enable(1 if on else 0)
+
+
+def timing_read() -> dict:
+    """{kernel name: (total ms, launches)} since timing_enable (synchronises the events)."""
+    import numpy as np
+    buf = ctypes.create_string_buffer(4096)
+    ms = np.zeros(64, dtype=np.float64)
+    cnt = np.zeros(64, dtype=np.int64)
+    n = lib().sdtw_timing_read(buf, 4096, ms.ctypes.data_as(ctypes.c_void_p), cnt.ctypes.data_as(ctypes.c_void_p), 64)
+    names = buf.value.decode().split(",") if n else []
+    return {names[i]: (float(ms[i]), int(cnt[i])) for i in range(n)}
+
+
 def version() -> str:
     return lib().sdtw_version().decode()
 
@@ -156,10 +178,16 @@ def score_elems(B: int, N: int, M: int) -> int:
     return int(lib().sdtw_score_elems(B, N, M))
 
 
+def cost_elems(B: int, N: int, M: int) -> int:
+    return int(lib().sdtw_cost_elems(B, N, M))
+
+
 def workspace(B: int, N: int, M: int, device, dim: int | None = None) -> torch.Tensor:
+    """Caller-owned scratch of the size the library asks for (torch allocations
+    are 256-byte aligned, as the library requires)."""
     L = lib()
     n = L.sdtw_workspace_bytes(B, N, M) if dim is None else L.sdtw_workspace_bytes_xy(B, N, M, dim)
-    return torch.empty(max(int(n), 1), dtype=torch.uint8, device=device)
+    return torch.empty(max(int(n), 256), dtype=torch.uint8, device=device)
 
 
 def _f32(t: torch.Tensor) -> torch.Tensor:
@@ -245,7 +273,47 @@ def backward_xy(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad_out:
         rc = lib().sdtw_backward_xy_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(g), _ptr(gx), _ptr(gy), B, N, M, dim,
                                         float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
     _check(rc, "fused backward")
-    _op_end("backward_xy", x.device, ev, 1 + int(need_x) + int(need_y))
+    _op_end("backward_xy", x.device, ev, 2 + int(need_x) + int(need_y))
+    return gx, gy
+
+
+def forward_sqeuclid(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float):
+    """Unfused path: (out, score, cost) with the clamped expanded cost kept for the backward."""
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    score = torch.empty(score_elems(B, N, M), dtype=torch.float32, device=x.device)
+    cost = torch.empty(cost_elems(B, N, M), dtype=torch.float32, device=x.device)
+    out = torch.empty(B, dtype=torch.float32, device=x.device)
+    ws = workspace(B, N, M, x.device)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_forward_sqeuclid_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(out), B, N, M, dim,
+                                             float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
+    _check(rc, "unfused forward")
+    _op_end("forward_sqeuclid", x.device, ev)
+    return out, score, cost
+
+
+def backward_sqeuclid(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, cost: torch.Tensor,
+                      grad_out: torch.Tensor | None, gamma: float, bandwidth: float, need_x: bool = True,
+                      need_y: bool = True):
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    gx = torch.empty_like(x) if need_x else None
+    gy = torch.empty_like(y) if need_y else None
+    g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    ws = workspace(B, N, M, x.device, dim)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_backward_sqeuclid_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(g), _ptr(gx), _ptr(gy),
+                                              B, N, M, dim, float(gamma), float(bandwidth), _ptr(ws), ws.numel(),
+                                              _stream(x.device))
+    _check(rc, "unfused backward")
+    _op_end("backward_sqeuclid", x.device, ev, 2 + int(need_x) + int(need_y))
     return gx, gy
 
 

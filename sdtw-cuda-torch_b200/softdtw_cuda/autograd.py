@@ -57,3 +57,34 @@ class SoftDTWAutograd(Function):
         else:
             E = _native.cpu_backward(table, grad_output, ctx.gamma, ctx.bandwidth)
         return E.to(ctx.dtype), None, None
+
+
+class SoftDTWSqEuclidAutograd(Function):
+    """Unfused squared-Euclidean Soft-DTW on CUDA float tensors.
+
+    Computes the same quantity as ``SoftDTWAutograd.apply(sqeuclidean(X, Y), ...)``
+    (softdtw_cuda/module.py:116-118): the cost matrix is built explicitly as
+    ||x||^2 + ||y||^2 - 2 x.y clamped at 0 and kept (in the library's
+    anti-diagonal layout) for the backward, whose chain rule to X and Y zeroes
+    the cells where the clamp was active, as torch autograd of
+    distances.py:20-28 does.
+    """
+
+    @staticmethod
+    def forward(ctx, X: torch.Tensor, Y: torch.Tensor, gamma: float, bandwidth: float | None):
+        gamma_f = float(gamma)
+        if gamma_f <= 0:
+            raise ValueError(f"gamma must be > 0, got {gamma_f}")
+        bw = _normalize_bandwidth(bandwidth)
+        out, score, cost = _native.forward_sqeuclid(X, Y, gamma_f, bw)
+        ctx.save_for_backward(X, Y, score, cost)
+        ctx.gamma = gamma_f
+        ctx.bandwidth = bw
+        return out.to(X.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        X, Y, score, cost = ctx.saved_tensors
+        gx, gy = _native.backward_sqeuclid(X, Y, score, cost, grad_output, ctx.gamma, ctx.bandwidth,
+                                           need_x=ctx.needs_input_grad[0], need_y=ctx.needs_input_grad[1])
+        return (None if gx is None else gx.to(X.dtype)), (None if gy is None else gy.to(Y.dtype)), None, None

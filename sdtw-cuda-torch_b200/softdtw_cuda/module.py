@@ -16,9 +16,9 @@ import math
 import torch
 from torch import nn
 
-from .autograd import SoftDTWAutograd
+from .autograd import SoftDTWAutograd, SoftDTWSqEuclidAutograd
 from .autograd_xy import SoftDTWXYAutograd
-from .distances import _SQEUCLID_NAMES, pairwise_distance
+from .distances import _KERNEL_DTYPES, _SQEUCLID_NAMES, pairwise_distance
 
 
 class SoftDTW(nn.Module):
@@ -98,5 +98,9 @@ class SoftDTW(nn.Module):
     def _pairs(self, x: torch.Tensor, y: torch.Tensor, use_fused: bool) -> torch.Tensor:
         if use_fused:
             return SoftDTWXYAutograd.apply(x, y, self.gamma, self.bandwidth)
+        if (self.dist.lower() in _SQEUCLID_NAMES and x.is_cuda and y.is_cuda and x.device == y.device
+                and x.dtype in _KERNEL_DTYPES and y.dtype == x.dtype):
+            # Unfused: explicit cost matrix (kept by the library for the backward).
+            return SoftDTWSqEuclidAutograd.apply(x, y, self.gamma, self.bandwidth)
         D = pairwise_distance(x, y, dist=self.dist)
         return SoftDTWAutograd.apply(D, self.gamma, self.bandwidth)

@@ -34,8 +34,11 @@ def test_sizes_without_gpu():
     L = _native.lib()
     assert L.sdtw_score_elems(4, 64, 64) == 2 * 4 * 2 * (64 + 31) * 32   # (hi, lo) per cell
     assert L.sdtw_score_elems(0, 4, 4) == 0
-    assert L.sdtw_workspace_bytes(4, 64, 64) == 0          # one band: no wrap ring
-    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) >= 4 * 64 * 64 * 4
+    cells = 4 * 2 * (64 + 31) * 32
+    assert L.sdtw_cost_elems(4, 64, 64) == cells
+    # One band: no wrap ring; the wavefront-layout table of the cost / E.
+    assert L.sdtw_workspace_bytes(4, 64, 64) == -(-cells * 4 // 256) * 256
+    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) >= cells * 4 + 4 * 64 * 64 * 4
 
 
 def test_invalid_arguments_rejected():
@@ -48,6 +51,12 @@ def test_invalid_arguments_rejected():
     rc = L.sdtw_cost_sqeuclid_f32(None, None, None, 1, 4, 4, 0, 0, None)
     assert rc == 1
     assert L.sdtw_error_string(3) == b"device-side wait timed out"
+
+
+def test_timing_registry_without_gpu():
+    _native.timing_enable(True)
+    assert _native.timing_read() == {}
+    _native.timing_enable(False)
 
 
 def test_version():
