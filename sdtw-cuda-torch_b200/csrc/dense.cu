@@ -102,9 +102,10 @@ cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, 
 }
 
 constexpr int GT = 32;   // rows (or columns) per CTA
-constexpr int GF = 64;   // feature chunk
 
-// gx[b, i0:i0+32, :] from G rows i0..i0+31 and all of y[b].
+// gx[b, i0:i0+32, :] from G rows i0..i0+31 and all of y[b].  GF = feature
+// chunk (8, 16, 32 or 64, chosen from the feature count).
+template <int GF>
 __global__ void __launch_bounds__(256) grad_x_kernel(const float* __restrict__ G, const float* __restrict__ mask,
                                                      const float* __restrict__ x, const float* __restrict__ y,
                                                      float* __restrict__ gx, int N, int M, int dim) {
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(256) grad_x_kernel(const float* __restrict__ G
                 Gs[ii][jj] = gv;
             }
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
+            for (int r = 0; r < GF / 8; ++r) {
                 const int e = threadIdx.x + r * 256;
                 const int jj = e / GF, ff = e % GF;
                 Ys[jj][ff] = (j0 + jj < M && fc + ff < dim) ? __ldg(yb + static_cast<size_t>(j0 + jj) * dim + fc + ff) : 0.f;
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(256) grad_x_kernel(const float* __restrict__ G
 }
 
 // gy[b, j0:j0+32, :] from G columns j0..j0+31 and all of x[b].
+template <int GF>
 __global__ void __launch_bounds__(256) grad_y_kernel(const float* __restrict__ G, const float* __restrict__ mask,
                                                      const float* __restrict__ x, const float* __restrict__ y,
                                                      float* __restrict__ gy, int N, int M, int dim) {
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(256) grad_y_kernel(const float* __restrict__ G
                 Gs[ii][jj] = gv;
             }
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
+            for (int r = 0; r < GF / 8; ++r) {
                 const int e = threadIdx.x + r * 256;
                 const int ii = e / GF, ff = e % GF;
                 Xs[ii][ff] = (i0 + ii < N && fc + ff < dim) ? __ldg(xb + static_cast<size_t>(i0 + ii) * dim + fc + ff) : 0.f;
@@ -226,10 +228,19 @@ __global__ void __launch_bounds__(256) grad_y_kernel(const float* __restrict__ G
     }
 }
 
+template <int GF>
+static void grad_launch(const float* G, const float* mask, const float* x, const float* y, float* gx, float* gy, int B,
+                        int N, int M, int dim, cudaStream_t stream) {
+    if (gx) grad_x_kernel<GF><<<dim3((N + GT - 1) / GT, B), 256, 0, stream>>>(G, mask, x, y, gx, N, M, dim);
+    if (gy) grad_y_kernel<GF><<<dim3((M + GT - 1) / GT, B), 256, 0, stream>>>(G, mask, x, y, gy, N, M, dim);
+}
+
 cudaError_t launch_grad_xy(const float* G, const float* mask, const float* x, const float* y, float* gx,
                            float* gy, int B, int N, int M, int dim, cudaStream_t stream) {
-    if (gx) grad_x_kernel<<<dim3((N + GT - 1) / GT, B), 256, 0, stream>>>(G, mask, x, y, gx, N, M, dim);
-    if (gy) grad_y_kernel<<<dim3((M + GT - 1) / GT, B), 256, 0, stream>>>(G, mask, x, y, gy, N, M, dim);
+    if (dim <= 8) grad_launch<8>(G, mask, x, y, gx, gy, B, N, M, dim, stream);
+    else if (dim <= 16) grad_launch<16>(G, mask, x, y, gx, gy, B, N, M, dim, stream);
+    else if (dim <= 32) grad_launch<32>(G, mask, x, y, gx, gy, B, N, M, dim, stream);
+    else grad_launch<64>(G, mask, x, y, gx, gy, B, N, M, dim, stream);
     return cudaGetLastError();
 }
 

@@ -22,7 +22,6 @@
 namespace sdtw {
 
 constexpr int kTB = 32;   // anti-diagonals per tile
-constexpr int kFC = 32;   // feature chunk of the cost tiles
 
 __device__ __forceinline__ size_t wl_row_base(const WavePlan& P, int b, int s, int t) {
     return ((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * (32 * P.K);
@@ -32,7 +31,7 @@ __device__ __forceinline__ size_t wl_row_base(const WavePlan& P, int b, int s, i
 // the parallelogram of cells (q, t - q), q in [0, 32K), t in [t0, t0 + kTB):
 // x rows R0 .. R0+32K-1 and y rows t0-32K+1 .. t0+kTB-1, staged in shared
 // memory feature chunk by feature chunk.
-template <int K, bool DIRECT>
+template <int K, bool DIRECT, int kFC>
 __global__ void __launch_bounds__(256) cost_wl_kernel(const float* __restrict__ x, const float* __restrict__ y,
                                                       float* __restrict__ Dw, WavePlan P, int dim) {
     constexpr int SR = 32 * K;
@@ -183,19 +182,31 @@ static dim3 wl_grid(const WavePlan& P) {
     return dim3((P.n_diag + kTB - 1) / kTB, P.n_stripes, P.B);
 }
 
-cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+template <int K, int FC>
+static void cost_wl_launch(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
                            cudaStream_t stream) {
     const dim3 g = wl_grid(P);
-#define SDTW_COST(KK)                                                                                 \
-    (direct ? cost_wl_kernel<KK, true><<<g, 256, 0, stream>>>(x, y, Dw, P, dim)                       \
-            : cost_wl_kernel<KK, false><<<g, 256, 0, stream>>>(x, y, Dw, P, dim))
+    if (direct) cost_wl_kernel<K, true, FC><<<g, 256, 0, stream>>>(x, y, Dw, P, dim);
+    else cost_wl_kernel<K, false, FC><<<g, 256, 0, stream>>>(x, y, Dw, P, dim);
+}
+
+template <int K>
+static void cost_wl_by_dim(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+                           cudaStream_t stream) {
+    // Feature chunk sized to the feature count: no padded work for small dims.
+    if (dim <= 8) cost_wl_launch<K, 8>(x, y, Dw, P, dim, direct, stream);
+    else if (dim <= 16) cost_wl_launch<K, 16>(x, y, Dw, P, dim, direct, stream);
+    else cost_wl_launch<K, 32>(x, y, Dw, P, dim, direct, stream);
+}
+
+cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+                           cudaStream_t stream) {
     switch (P.K) {
-        case 1: SDTW_COST(1); break;
-        case 2: SDTW_COST(2); break;
-        case 4: SDTW_COST(4); break;
+        case 1: cost_wl_by_dim<1>(x, y, Dw, P, dim, direct, stream); break;
+        case 2: cost_wl_by_dim<2>(x, y, Dw, P, dim, direct, stream); break;
+        case 4: cost_wl_by_dim<4>(x, y, Dw, P, dim, direct, stream); break;
         default: return cudaErrorInvalidValue;
     }
-#undef SDTW_COST
     return cudaGetLastError();
 }
 
