@@ -166,6 +166,26 @@ int sdtw_cpu_forward_f64(const double *D, double *R, double *out, int B, int N, 
 int sdtw_cpu_backward_f64(const double *R, const double *grad_out, double *E, int B, int N, int M,
                           double gamma, double bandwidth);
 
+/* Allocation-free variant of sdtw_forward_f32 (no counterpart in the
+ * reference).  For callers that cannot allocate device memory at call time --
+ * a host runtime whose allocator owns all of device memory, a plugin boundary
+ * that passes only inputs and outputs, a loop where cudaMalloc's possible
+ * device synchronisation is not allowed -- it takes no workspace: its scratch
+ * (band-wrap ring and the anti-diagonal copy of D) is a fixed 8 MiB device
+ * array inside the library, present on every GPU that loads the library until
+ * the process exits.  Problems whose scratch would exceed it are rejected with
+ * SDTW_ERR_INVALID_ARGUMENT (roughly B*N*M up to 2 million cells; see
+ * sdtw_workspace_bytes for the exact need).  It calls no cudaMalloc, cudaFree
+ * or other allocating routine.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current; make
+ * that first call before any stream capture.  All calls on a device share that
+ * device's array, which keeps the previous call's contents (each call resets
+ * what must start fresh): calls on one device that overlap on the GPU -- issued
+ * on different streams without ordering -- race on it, so the caller must
+ * order them, e.g. by issuing them on one stream. */
+int sdtw_forward_noalloc_f32(const float *D, float *score, float *out, int B, int N, int M, float gamma,
+                             float bandwidth, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -537,4 +537,74 @@ int sdtw_R_to_score_f32(const float* R, float* score, int B, int N, int M, float
     return SDTW_OK;
 }
 
+
+// ----------------------------------------------------------------------------
+// Allocation-free forward.
+//
+// Some callers cannot allocate device memory when they call us: a host runtime
+// whose allocator owns all of device memory and lends out no scratch, a plugin
+// boundary that hands over only input and output buffers, or a latency-critical
+// loop in which cudaMalloc (which can synchronise the device) is not allowed.
+// For them the D-input forward has a variant whose scratch (band-wrap ring and
+// the anti-diagonal copy of D) lives in a fixed device array compiled into the
+// library.  Every GPU that loads the library holds this array until the process
+// exits.  The caller still passes D, score and out.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static void* g_noalloc_base[64];  // device address of g_noalloc_scratch, per device
+static std::mutex g_noalloc_mu;
+
+// Host code cannot use the array's name as a device address; look the address
+// up once per device, with that device current.
+static int noalloc_base(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(SDTW_ERR_INVALID_ARGUMENT, "device index out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+        g_noalloc_base[dev] = p;
+    }
+    *out = g_noalloc_base[dev];
+    return SDTW_OK;
+}
+
+int sdtw_forward_noalloc_f32(const float* D, float* score, float* out, int B, int N, int M, float gamma,
+                             float bandwidth, void* stream) {
+    int rc;
+    if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma)) || (rc = check_score(score))) return rc;
+    if (!D || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t w0 = wave_ws(B, N, M);
+    const size_t need = w0 + wl_bytes(B, N, M);
+    if (need > kNoAllocScratchBytes)
+        return fail(SDTW_ERR_INVALID_ARGUMENT,
+                    "problem too large for the allocation-free forward: needs " + std::to_string(need) +
+                        " bytes of scratch, the fixed array holds " + std::to_string(kNoAllocScratchBytes) +
+                        " (use sdtw_forward_f32 with a workspace)");
+    // A failure recorded by an earlier launch still surfaces here; the status
+    // word is only read if another entry point already created it.
+    if ((rc = pending_status())) return rc;
+    void* base = nullptr;
+    if ((rc = noalloc_base(&base))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The array keeps the previous call's contents.  The anti-diagonal copy of D
+    // is fully rewritten below; the band-wrap ring's slots are reset so that no
+    // stale entry can carry a matching tag.
+    if (w0) {
+        cudaError_t e = cudaMemsetAsync(base, 0xff, w0, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc ring)");
+    }
+    float* Dw = reinterpret_cast<float*>(static_cast<char*>(base) + w0);
+    cudaError_t e;
+    {
+        KernelTimer kt("rm_to_wl", st);
+        e = launch_rm_to_wl(D, Dw, plan(B, N, M), st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "layout launch");
+    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(base), st);
+}
+
 }  // extern "C"

@@ -44,6 +44,7 @@ _SIGS = {
     "sdtw_backward_f32": ([_P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_forward_xy_f32": ([_P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_backward_xy_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_forward_noalloc_f32": ([_P, _P, _P, _I, _I, _I, _F, _F, _P], _I),
     "sdtw_forward_sqeuclid_f32": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_backward_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_grad_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
