@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # Profiling runs: only the fused timed steps (no unfused mode, no end-to-end leg).
+    ap.add_argument("--fused-only", action="store_true")
     return ap.parse_args()
 
 
@@ -230,7 +232,7 @@ def main():
     launches = 0
     breakdown = {}
     with sampler:
-        for name, fused in (("fused", None), ("unfused", False)):
+        for name, fused in (("fused", None), ("unfused", False))[:1 if args.fused_only else 2]:
             for _ in range(args.warmup):
                 step(fused)
             torch.cuda.synchronize(dev)
@@ -269,11 +271,13 @@ def main():
         gx_h.copy_(xd.grad, non_blocking=True)
         gy_h.copy_(yd.grad, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = max_over_ranks(statistics.mean(timed(e2e_step, args.steps)))
+    e2e_ms = float("nan")
+    if not args.fused_only:
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = max_over_ranks(statistics.mean(timed(e2e_step, args.steps)))
     h2d = x_h.numel() * 4 + y_h.numel() * 4
     d2h = 4 + gx_h.numel() * 4 + gy_h.numel() * 4
 
@@ -350,9 +354,10 @@ def main():
         "roofline": roofline,
         "roofline_mufu": roofline_mufu,
         "cpu_baseline": cpu_baseline,
-        "e2e": {"value": world * cells / (e2e_ms / 1e3), "unit": "cells/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "softdtw_cuda.SoftDTW (pinned host x,y in; loss, dL/dx, dL/dy out)"},
+        "e2e": None if args.fused_only else {
+            "value": world * cells / (e2e_ms / 1e3), "unit": "cells/s", "ms_per_step": e2e_ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "softdtw_cuda.SoftDTW (pinned host x,y in; loss, dL/dx, dL/dy out)"},
         "gpu_launches": launches,
         "clocks": clocks,
     }
