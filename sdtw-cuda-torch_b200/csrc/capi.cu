@@ -2,6 +2,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -135,8 +136,10 @@ std::string diag_text() {
     char buf[256];
     std::snprintf(buf, sizeof buf,
                   "%s pass, %s wait, problem %d, warp %d, band %d: expected %d, last seen %d",
-                  d[0] == 1 ? "forward" : (d[0] == 2 ? "backward" : "?"),
-                  d[1] == 1 ? "shared-memory ring" : (d[1] == 2 ? "global ring" : (d[1] == 3 ? "flow-control" : "?")),
+                  d[0] == 1 ? "forward" : (d[0] == 2 ? "backward" : (d[0] == 5 ? "tensor-core gradient" : "?")),
+                  d[1] == 1 ? "shared-memory ring"
+                            : (d[1] == 2 ? "global ring"
+                                         : (d[1] == 3 ? "flow-control" : (d[1] == 4 ? "MMA completion" : "?"))),
                   d[2], d[3], d[4], d[5], d[6]);
     return buf;
 }
@@ -191,13 +194,12 @@ WavePlan plan(int B, int N, int M) {
 // Workspace layouts (each region 256-byte aligned):
 //   D-input forward/backward : [wrap ring][WL table]
 //   x/y forward              : [wrap ring][WL cost]
-//   x/y backward, sqeuclid bwd: [wrap ring][WL E][row-major G]
+//   x/y backward, sqeuclid bwd: [wrap ring][WL E]
 size_t wave_ws(int B, int N, int M) {
     WavePlan p = plan(B, N, M);
     return align_up(wrap_bytes(p), 256);
 }
 size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
-size_t rm_bytes(int B, int N, int M) { return align_up((size_t)B * N * M * sizeof(float), 256); }
 
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream) {
@@ -357,7 +359,7 @@ size_t sdtw_workspace_bytes(int B, int N, int M) {
 
 size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim) {
     if (B <= 0 || N <= 0 || M <= 0 || dim <= 0) return 0;
-    return wave_ws(B, N, M) + wl_bytes(B, N, M) + rm_bytes(B, N, M);
+    return wave_ws(B, N, M) + wl_bytes(B, N, M);
 }
 
 int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int N, int M, int dim, int direct,
@@ -440,18 +442,34 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
                        cudaStream_t st) {
     const size_t w0 = wave_ws(B, N, M);
     float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
-    float* G = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0 + wl_bytes(B, N, M));
     int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st);
     if (rc) return rc;
+    if (!grad_x && !grad_y) return SDTW_OK;
+    GradTcArgs g{};
+    g.P = plan(B, N, M);
+    g.Ew = Ew;
+    g.Mw = mask_w;
+    g.x = x;
+    g.y = y;
+    g.gx = grad_x;
+    g.gy = grad_y;
+    g.dim = dim;
+    grad_tc_geometry(dim, mask_w != nullptr, &g.fb, &g.nt, &g.n_fblk, &g.tmem_cols, &g.stages);
+    {
+        // Tuning knob: SDTW_GRAD_STAGES=2 trades pipeline depth for two CTAs per SM.
+        static const int env_stages = [] {
+            const char* v = std::getenv("SDTW_GRAD_STAGES");
+            return v ? std::atoi(v) : 0;
+        }();
+        if (env_stages == 2 || (env_stages == 3 && g.stages == 3)) g.stages = env_stages;
+    }
+    g.tiles_x = grad_x ? (N + 127) / 128 : 0;
+    g.tiles_y = grad_y ? (M + 127) / 128 : 0;
+    g.wait = wait_ctx();
     cudaError_t e;
     {
-        KernelTimer kt("wl_to_rm", st);
-        e = launch_wl_to_rm(Ew, mask_w, G, plan(B, N, M), st);
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "layout launch");
-    {
         KernelTimer kt("grad_xy", st);
-        e = launch_grad_xy(G, nullptr, x, y, grad_x, grad_y, B, N, M, dim, st);
+        e = launch_grad_tc(g, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "grad launch");
     return SDTW_OK;

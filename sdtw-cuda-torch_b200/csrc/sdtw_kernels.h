@@ -56,4 +56,26 @@ cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, 
 cudaError_t launch_grad_xy(const float* G, const float* mask, const float* x, const float* y, float* gx,
                            float* gy, int B, int N, int M, int dim, cudaStream_t stream);
 
+// tcgemm.cu: grad_x / grad_y from E in the wavefront layout on the tensor cores.
+struct GradTcArgs {
+    WavePlan P;
+    const float* Ew;  // E in the wavefront layout
+    const float* Mw;  // unfused cost in the wavefront layout (clamp mask: G = E * (D > 0)), or null
+    const float* x;   // (B,N,dim)
+    const float* y;   // (B,M,dim)
+    float* gx;        // (B,N,dim) or null
+    float* gy;        // (B,M,dim) or null
+    int dim;
+    int fb;           // features per block
+    int nt;           // MMA N: fb + 1 (ones column) rounded up to 16
+    int n_fblk;       // feature blocks
+    int tiles_x;      // 128-row tiles of grad_x per problem (0 when gx is null)
+    int tiles_y;      // 128-row tiles of grad_y per problem (0 when gy is null)
+    int tmem_cols;    // tensor-memory columns allocated per CTA (power of two >= nt)
+    int stages;       // shared-memory pipeline depth (2 or 3)
+    WaitCtx wait;
+};
+void grad_tc_geometry(int dim, bool masked, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages);
+cudaError_t launch_grad_tc(const GradTcArgs& args, cudaStream_t stream);
+
 }  // namespace sdtw

@@ -103,6 +103,18 @@ def test_shapes_vs_oracle(shape, fused):
     _check_against_oracle(x, y, out, gx, gy, gamma=1.0, fused=fused)
 
 
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("dim", [1, 33, 128, 241, 300, 513])
+def test_feature_dims(dim, fused):
+    """Gradients on the tensor cores (3xTF32): feature blocks of up to 240
+    columns plus the row-sum column, partial 128-row tiles and K chunks."""
+    rng = np.random.default_rng(dim)
+    x = (rng.standard_normal((2, 70, dim)) / np.sqrt(dim)).astype(np.float32)
+    y = (rng.standard_normal((2, 90, dim)) / np.sqrt(dim)).astype(np.float32)
+    out, gx, gy = _gpu_run(x, y, gamma=1.0, fused=fused)
+    _check_against_oracle(x, y, out, gx, gy, gamma=1.0, fused=fused)
+
+
 @pytest.mark.parametrize("gamma", [0.01, 0.1, 1.0, 10.0])
 @pytest.mark.parametrize("fused", [False, True])
 def test_gamma_sweep_mid(gamma, fused):
