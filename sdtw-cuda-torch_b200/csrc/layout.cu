@@ -9,13 +9,14 @@
 // The wavefront kernels touch one such anti-diagonal row per step, so every
 // per-step load or store of D, E or the scores is one coalesced transaction.
 //
-//   cost_wl_kernel    D in WL layout straight from x, y:
+//   cost_wl_kernel    D in WL layout straight from x, y (register-tiled FP32):
 //                     <false> clamp(||x||^2 + ||y||^2 - 2 x.y, 0)   (distances.py:6-28)
 //                     <true>  sum_k (x_k - y_k)^2                     (kernels.py:27-31)
 //   rm_to_wl_kernel   row-major (B,N,M) -> WL (caller-supplied cost matrices)
 //   wl_to_rm_kernel   WL -> row-major, optionally multiplied by (D_wl > 0),
 //                     the clamp mask of the unfused cost's chain rule
 #include <algorithm>
+#include <cstdint>
 
 #include "sdtw_kernels.h"
 
@@ -27,96 +28,140 @@ __device__ __forceinline__ size_t wl_row_base(const WavePlan& P, int b, int s, i
     return ((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * (32 * P.K);
 }
 
-// One CTA per (anti-diagonal block of kTB, stripe, problem).  The block covers
-// the parallelogram of cells (q, t - q), q in [0, 32K), t in [t0, t0 + kTB):
-// x rows R0 .. R0+32K-1 and y rows t0-32K+1 .. t0+kTB-1, staged in shared
-// memory feature chunk by feature chunk.
-template <int K, bool DIRECT, int kFC>
-__global__ void __launch_bounds__(256) cost_wl_kernel(const float* __restrict__ x, const float* __restrict__ y,
-                                                      float* __restrict__ Dw, WavePlan P, int dim) {
+// Cost tiles.  One CTA (256 threads) per (block of CJ = 4096 / (32K) columns,
+// stripe, problem): the rectangle of cells q in [0, 32K) x j in [j0, j0+CJ),
+// with x rows R0 .. R0+32K-1 and y rows j0 .. j0+CJ-1 staged in shared
+// memory FC features at a time.  Each thread owns 16 cells: 4 consecutive rows
+// q = 4a+i times the 4 columns j = j0 + jb + (CJ/4) c.  Per group of 4
+// features it reads 4 x rows (the same for the whole warp: broadcasts) and 4
+// y rows (consecutive across lanes) as float4, 8 shared loads for 64
+// cell-features, so the kernel is bound by the FP32 pipe rather than by
+// shared-memory bandwidth.  Rows are padded to a multiple of 4 floats whose
+// quotient by 4 is odd, so the 8 lanes of a 128-bit load phase hit distinct
+// banks.  The cells go through a shared-memory tile indexed by anti-diagonal
+// to stores of anti-diagonal rows; cells of the table's padding are not
+// written.
+template <int FC>
+struct CostPitch {
+    static constexpr int v = ((FC + 4) / 4) % 2 ? FC + 4 : FC + 8;
+};
+
+template <int K, bool DIRECT, int FC, bool VEC>
+__global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                                         float* __restrict__ Dw, WavePlan P, int dim) {
     constexpr int SR = 32 * K;
-    constexpr int YR = SR + kTB - 1;  // y rows touched by the block
-    constexpr int CELLS = SR * kTB / 256;
-    __shared__ float xs[SR][kFC + 1];     // indexed by stripe position p
-    __shared__ float ys[YR][kFC + 1];
-    __shared__ float xn[SR], yn[YR];
-    const int t0 = blockIdx.x * kTB;
+    constexpr int CJ = 4096 / SR;        // columns per tile
+    constexpr int CG = CJ / 4;           // column stride of a thread's cells
+    constexpr int PITCH = CostPitch<FC>::v;
+    constexpr int NOFF = (SR + CJ + 3) / 4 * 4;  // norms region, rounded to 16 bytes
+    extern __shared__ __align__(16) float cs[];
+    float* xn = cs;                      // [SR]
+    float* yn = xn + SR;                 // [CJ]
+    float* xs = cs + NOFF;               // [SR][PITCH]
+    float* ys = xs + SR * PITCH;         // [CJ][PITCH]
+    const int j0 = blockIdx.x * CJ;
     const int s = blockIdx.y;
     const int b = blockIdx.z;
     const int R0 = s * SR;
-    const int j0 = t0 - SR + 1;  // first y row of the block
     const float* xb = x + static_cast<size_t>(b) * P.N * dim;
     const float* yb = y + static_cast<size_t>(b) * P.M * dim;
+    const int jb = threadIdx.x % CG;  // columns j0 + jb + CG c
+    const int ag = threadIdx.x / CG;  // rows 4ag .. 4ag+3
 
-    float acc[CELLS];
+    float acc[4][4];
 #pragma unroll
-    for (int c = 0; c < CELLS; ++c) acc[c] = 0.f;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[i][c] = 0.f;
     if (!DIRECT) {
-        for (int i = threadIdx.x; i < SR; i += 256) xn[i] = 0.f;
-        for (int i = threadIdx.x; i < YR; i += 256) yn[i] = 0.f;
+        for (int i = threadIdx.x; i < SR + CJ; i += 256) xn[i] = 0.f;  // xn and yn are adjacent
     }
-    for (int f0 = 0; f0 < dim; f0 += kFC) {
+    for (int f0 = 0; f0 < dim; f0 += FC) {
         __syncthreads();
-        for (int e = threadIdx.x; e < SR * kFC; e += 256) {
-            const int p = e / kFC, f = e % kFC;
-            const int q = (p % 32) * K + p / 32;
-            const int row = R0 + q;
-            xs[p][f] = (row < P.N && f0 + f < dim) ? __ldg(xb + static_cast<size_t>(row) * dim + f0 + f) : 0.f;
-        }
-        for (int e = threadIdx.x; e < YR * kFC; e += 256) {
-            const int r = e / kFC, f = e % kFC;
-            const int j = j0 + r;
-            ys[r][f] = (j >= 0 && j < P.M && f0 + f < dim) ? __ldg(yb + static_cast<size_t>(j) * dim + f0 + f) : 0.f;
+        if (VEC) {  // dim % 4 == 0 and 16-byte aligned rows: float4 loads
+            for (int e = threadIdx.x; e < (SR + CJ) * (FC / 4); e += 256) {
+                const int r = e / (FC / 4), f = (e % (FC / 4)) * 4;
+                const bool isx = r < SR;
+                const int row = isx ? R0 + r : j0 + r - SR;
+                const bool in = (isx ? row < P.N : row < P.M) && f0 + f < dim;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (in) v = __ldg(reinterpret_cast<const float4*>((isx ? xb : yb) + static_cast<size_t>(row) * dim + f0 + f));
+                *reinterpret_cast<float4*>(xs + r * PITCH + f) = v;  // ys follows xs: row r of [xs; ys]
+            }
+        } else {
+            for (int e = threadIdx.x; e < (SR + CJ) * FC; e += 256) {
+                const int r = e / FC, f = e % FC;
+                const bool isx = r < SR;
+                const int row = isx ? R0 + r : j0 + r - SR;
+                const bool in = (isx ? row < P.N : row < P.M) && f0 + f < dim;
+                xs[r * PITCH + f] = in ? __ldg((isx ? xb : yb) + static_cast<size_t>(row) * dim + f0 + f) : 0.f;
+            }
         }
         __syncthreads();
         if (!DIRECT) {
-            for (int i = threadIdx.x; i < SR; i += 256) {
-                float a = xn[i];
-#pragma unroll 8
-                for (int f = 0; f < kFC; ++f) a = fmaf(xs[i][f], xs[i][f], a);
-                xn[i] = a;
-            }
-            for (int i = threadIdx.x; i < YR; i += 256) {
-                float a = yn[i];
-#pragma unroll 8
-                for (int f = 0; f < kFC; ++f) a = fmaf(ys[i][f], ys[i][f], a);
-                yn[i] = a;
+            for (int i = threadIdx.x; i < SR + CJ; i += 256) {
+                const float* row = xs + i * PITCH;
+                float a = 0.f;
+#pragma unroll
+                for (int f = 0; f < FC; ++f) a = fmaf(row[f], row[f], a);
+                xn[i] += a;  // xn[SR + r] is yn[r]
             }
         }
+        const float* xrow = xs + (4 * ag) * PITCH;
+        const float* yrow = ys + jb * PITCH;
 #pragma unroll
-        for (int c = 0; c < CELLS; ++c) {
-            const int idx = threadIdx.x + c * 256;
-            const int p = idx % SR;
-            const int tt = idx / SR;
-            const int q = (p % 32) * K + p / 32;
-            const int r = tt + (SR - 1) - q;  // y row of cell (q, t0 + tt - q), relative to j0
-            float a = acc[c];
-#pragma unroll 8
-            for (int f = 0; f < kFC; ++f) {
-                if (DIRECT) {
-                    const float df = xs[p][f] - ys[r][f];
-                    a = fmaf(df, df, a);
-                } else {
-                    a = fmaf(xs[p][f], ys[r][f], a);
+        for (int f = 0; f < FC; f += 4) {
+            float4 xv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xrow + i * PITCH + f);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 yv = *reinterpret_cast<const float4*>(yrow + c * CG * PITCH + f);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 a = xv[i];
+                    float r = acc[i][c];
+                    if (DIRECT) {
+                        const float d0 = a.x - yv.x, d1 = a.y - yv.y, d2 = a.z - yv.z, d3 = a.w - yv.w;
+                        r = fmaf(d0, d0, r);
+                        r = fmaf(d1, d1, r);
+                        r = fmaf(d2, d2, r);
+                        r = fmaf(d3, d3, r);
+                    } else {
+                        r = fmaf(a.x, yv.x, r);
+                        r = fmaf(a.y, yv.y, r);
+                        r = fmaf(a.z, yv.z, r);
+                        r = fmaf(a.w, yv.w, r);
+                    }
+                    acc[i][c] = r;
                 }
             }
-            acc[c] = a;
         }
     }
     __syncthreads();
+    // Stage by local anti-diagonal tl = q + (j - j0) in [0, SR + CJ - 1), row
+    // pitch SR + 1 (aliases xs/ys, not the norms), then store.
+    float* stg = xs;
 #pragma unroll
-    for (int c = 0; c < CELLS; ++c) {
-        const int idx = threadIdx.x + c * 256;
-        const int p = idx % SR;
-        const int tt = idx / SR;
-        const int t = t0 + tt;
-        if (t >= P.n_diag) continue;
+    for (int i = 0; i < 4; ++i) {
+        const int q = 4 * ag + i;
+        const int p = (q % K) * 32 + q / K;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int jl = jb + CG * c;
+            float v = acc[i][c];
+            if (!DIRECT) v = fmaxf((xn[q] + yn[jl]) - 2.f * v, 0.f);
+            stg[(q + jl) * (SR + 1) + p] = v;
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < (SR + CJ - 1) * SR; e += 256) {
+        const int tl = e / SR, p = e % SR;
         const int q = (p % 32) * K + p / 32;
-        const int col = t - q;
-        if (R0 + q >= P.N || col < 0 || col >= P.M) continue;
-        float v = acc[c];
-        if (!DIRECT) v = fmaxf((xn[p] + yn[tt + (SR - 1) - q]) - 2.f * v, 0.f);
-        Dw[wl_row_base(P, b, s, t) + p] = v;
+        const int jl = tl - q;
+        const int j = j0 + jl;
+        if (jl >= 0 && jl < CJ && j < P.M && R0 + q < P.N)
+            Dw[wl_row_base(P, b, s, j0 + tl) + p] = stg[tl * (SR + 1) + p];
     }
 }
 
@@ -183,31 +228,47 @@ static dim3 wl_grid(const WavePlan& P) {
 }
 
 template <int K, int FC>
-static void cost_wl_launch(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
-                           cudaStream_t stream) {
-    const dim3 g = wl_grid(P);
-    if (direct) cost_wl_kernel<K, true, FC><<<g, 256, 0, stream>>>(x, y, Dw, P, dim);
-    else cost_wl_kernel<K, false, FC><<<g, 256, 0, stream>>>(x, y, Dw, P, dim);
+static size_t cost_wl_smem() {
+    constexpr int SR = 32 * K, CJ = 4096 / SR;
+    constexpr int NOFF = (SR + CJ + 3) / 4 * 4;
+    const size_t in = static_cast<size_t>(SR + CJ) * CostPitch<FC>::v;
+    const size_t stage = static_cast<size_t>(SR + CJ - 1) * (SR + 1);
+    return (NOFF + (in > stage ? in : stage)) * sizeof(float);
+}
+
+template <int K, int FC>
+static cudaError_t cost_wl_launch(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+                                  cudaStream_t stream) {
+    constexpr int CJ = 4096 / (32 * K);
+    const dim3 g((P.M + CJ - 1) / CJ, P.n_stripes, P.B);
+    const size_t smem = cost_wl_smem<K, FC>();
+    const bool vec = (dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+    auto fn = direct ? (vec ? cost_wl_kernel<K, true, FC, true> : cost_wl_kernel<K, true, FC, false>)
+                     : (vec ? cost_wl_kernel<K, false, FC, true> : cost_wl_kernel<K, false, FC, false>);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    fn<<<g, 256, smem, stream>>>(x, y, Dw, P, dim);
+    return cudaGetLastError();
 }
 
 template <int K>
-static void cost_wl_by_dim(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
-                           cudaStream_t stream) {
+static cudaError_t cost_wl_by_dim(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+                                  cudaStream_t stream) {
     // Feature chunk sized to the feature count: no padded work for small dims.
-    if (dim <= 8) cost_wl_launch<K, 8>(x, y, Dw, P, dim, direct, stream);
-    else if (dim <= 16) cost_wl_launch<K, 16>(x, y, Dw, P, dim, direct, stream);
-    else cost_wl_launch<K, 32>(x, y, Dw, P, dim, direct, stream);
+    if (dim <= 4) return cost_wl_launch<K, 4>(x, y, Dw, P, dim, direct, stream);
+    if (dim <= 8) return cost_wl_launch<K, 8>(x, y, Dw, P, dim, direct, stream);
+    if (dim <= 16) return cost_wl_launch<K, 16>(x, y, Dw, P, dim, direct, stream);
+    return cost_wl_launch<K, 32>(x, y, Dw, P, dim, direct, stream);
 }
 
 cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
                            cudaStream_t stream) {
     switch (P.K) {
-        case 1: cost_wl_by_dim<1>(x, y, Dw, P, dim, direct, stream); break;
-        case 2: cost_wl_by_dim<2>(x, y, Dw, P, dim, direct, stream); break;
-        case 4: cost_wl_by_dim<4>(x, y, Dw, P, dim, direct, stream); break;
+        case 1: return cost_wl_by_dim<1>(x, y, Dw, P, dim, direct, stream);
+        case 2: return cost_wl_by_dim<2>(x, y, Dw, P, dim, direct, stream);
+        case 4: return cost_wl_by_dim<4>(x, y, Dw, P, dim, direct, stream);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_rm_to_wl(const float* A, float* Aw, const WavePlan& P, cudaStream_t stream) {
