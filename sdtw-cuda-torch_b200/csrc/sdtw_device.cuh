@@ -73,6 +73,21 @@ __device__ __forceinline__ void st_cluster_u64_if(bool p, uint32_t cluster_addr,
         "r"(cluster_addr), "l"(v)
         : "memory");
 }
+// Progress reports of the ring flow control.  A release store would wait for
+// every earlier store of the thread (the score rows written to global memory)
+// to be performed: measured on B200 that cost the consumer warps about 150
+// cycles per step.  The report only needs to follow the reads of the ring
+// slots it releases; those values were consumed (their tags voted on with
+// __any_sync) before the report is issued, so the loads have completed.  A
+// slot overwritten early could only show a newer tag, which the consumer
+// rejects (it would time out, never read a wrong value).
+__device__ __forceinline__ void st_relaxed_cluster_u32_if(bool p, uint32_t cluster_addr, uint32_t v) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.relaxed.cluster.shared::cluster.u32 [%1], %2;\n\t}" ::"r"(
+            static_cast<int>(p)),
+        "r"(cluster_addr), "r"(v)
+        : "memory");
+}
 __device__ __forceinline__ void st_release_cluster_u32_if(bool p, uint32_t cluster_addr, uint32_t v) {
     asm volatile(
         "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %0, 0;\n\t@q st.release.cluster.shared::cluster.u32 [%1], %2;\n\t}" ::"r"(
@@ -127,6 +142,18 @@ __device__ __forceinline__ void ld_pair(uint64_t generic_addr, uint64_t& a, uint
 __device__ __forceinline__ uint64_t ld_one(uint64_t generic_addr) {
     uint64_t a;
     asm volatile("ld.relaxed.cluster.u64 %0, [%1];" : "=l"(a) : "l"(generic_addr));
+    return a;
+}
+// The same reads for a ring in this CTA's shared memory, by shared-window
+// address.  Measured on B200, the generic-address forms above cost a consumer
+// warp about 1000 cycles per group of 8 slots even when the data was ready;
+// these cost about as much as ordinary shared loads.
+__device__ __forceinline__ void ld_pair_shared(uint32_t saddr, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.cluster.shared::cta.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(saddr));
+}
+__device__ __forceinline__ uint64_t ld_one_shared(uint32_t saddr) {
+    uint64_t a;
+    asm volatile("ld.relaxed.cluster.shared::cta.u64 %0, [%1];" : "=l"(a) : "r"(saddr));
     return a;
 }
 __device__ __forceinline__ uint64_t globaltimer_ns() {

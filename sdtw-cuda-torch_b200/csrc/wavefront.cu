@@ -44,7 +44,7 @@ __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
 // ============================================================== step groups
 // Steps run in groups of PF.  Per group (warp-uniform code): the consumer lane
 // reads and checks the PF ring slots it will need, the producer lane checks
-// flow control once, and every 32 columns a release store reports progress.
+// flow control once, and every 32 columns a relaxed store reports progress.
 // Per step: shuffles, the cell math, coalesced loads/stores of one
 // anti-diagonal row, one predicated ring store -- no branches.  The cost
 // (forward) or score rows (backward) of step t are loaded PF steps ahead.
@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
 
     const uint32_t my_consumed = smem_addr(consumed + warp);
     const uint64_t my_ring_g = reinterpret_cast<uint64_t>(ring + warp * 2 * kRing);
+    const uint32_t my_ring_s = smem_addr(ring + warp * 2 * kRing);
     uint64_t next_ring_g = 0;
     uint32_t prev_consumed = 0;
     if (g + 1 < P.G) next_ring_g = mapa_generic(ring + ((g + 1) % wpc) * 2 * kRing, (g + 1) / wpc);
@@ -157,25 +158,33 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                 rin_l[u] = 0.f;
             }
             if (has_in && t0 < M) {  // warp-uniform
-                // All lanes read the same slots (one broadcast transaction each),
-                // so the tag check is warp-uniform and the re-poll loop below is a
-                // uniform branch taken only when the producer is behind.
+                // Lane u (mod PF) reads slot u: one load instruction for the whole
+                // group (measured on B200: eight loads issued by one lane cost about
+                // 850 cycles per group, one warp-wide load about 200 with the
+                // vote and the shuffles).  The tag vote makes the re-poll loop
+                // below a uniform branch, taken only when the producer is behind.
                 uint32_t tg0 = in_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(t0);
                 bool all = true;
                 auto read_group = [&]() {
-                    all = true;
+                    const int u = lane & (PF - 1);
+                    const int col = t0 + u;
+                    const uint32_t tg = in_wrap ? tg0 : tg0 + static_cast<uint32_t>(u);
+                    const uint32_t slot = in_wrap ? static_cast<uint32_t>(col) : (tg % kRing);
+                    bool mine = true;
+                    float vh = NEG, vl = 0.f;
+                    if (col < M) {
+                        uint64_t eh, el;
+                        if (in_wrap) ld_pair(in_g + slot * 16u, eh, el);
+                        else ld_pair_shared(my_ring_s + slot * 16u, eh, el);
+                        mine = tag_of(eh) == tg && tag_of(el) == tg;
+                        vh = val_of(eh);
+                        vl = val_of(el);
+                    }
+                    all = __all_sync(SDTW_FULL_MASK, mine);
 #pragma unroll
-                    for (int u = 0; u < PF; ++u) {
-                        const int col = t0 + u;
-                        const uint32_t tg = in_wrap ? tg0 : tg0 + static_cast<uint32_t>(u);
-                        const uint32_t slot = in_wrap ? static_cast<uint32_t>(col) : (tg % kRing);
-                        if (col < M) {
-                            uint64_t eh, el;
-                            ld_pair(in_g + slot * 16u, eh, el);
-                            all = all && tag_of(eh) == tg && tag_of(el) == tg;
-                            rin_h[u] = val_of(eh);
-                            rin_l[u] = val_of(el);
-                        }
+                    for (int w = 0; w < PF; ++w) {
+                        rin_h[w] = __shfl_sync(SDTW_FULL_MASK, vh, w);
+                        rin_l[w] = __shfl_sync(SDTW_FULL_MASK, vl, w);
                     }
                 };
                 read_group();
@@ -193,7 +202,7 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                     }
                 }
                 const int done = min(t0 + PF, M);
-                st_release_cluster_u32_if(!in_wrap && report_due(done, PF, M) && lane == 0, prev_consumed,
+                st_relaxed_cluster_u32_if(!in_wrap && report_due(done, PF, M) && lane == 0, prev_consumed,
                                           band_base + static_cast<uint32_t>(done));
             }
             // ---- flow control for the columns this group publishes (lane 31).
@@ -331,6 +340,7 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
     // stripe below); this warp's output goes to warp g-1.
     const uint32_t my_consumed = smem_addr(consumed + warp);
     const uint64_t my_ring_g = reinterpret_cast<uint64_t>(ring + warp * kRing);
+    const uint32_t my_ring_s = smem_addr(ring + warp * kRing);
     uint64_t up_ring_g = 0;
     uint32_t below_consumed = 0;
     if (g > 0) up_ring_g = mapa_generic(ring + ((g - 1) % wpc) * kRing, (g - 1) / wpc);
@@ -427,21 +437,25 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
             if (has_below && colb0 - (PF - 1) < M && colb0 >= 0) {  // warp-uniform
                 bool all = true;
                 auto read_group = [&]() {
-                    all = true;
-#pragma unroll
-                    for (int u = 0; u < PF; ++u) {
-                        const int col = colb0 - u;
-                        const uint32_t tg = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
-                        const uint32_t slot = below_wrap ? static_cast<uint32_t>(col) * 2u : (tg % kRing);
-                        if (col >= 0 && col < M) {
-                            const uint64_t e = ld_one(in_g + slot * 8u);
-                            all = all && tag_of(e) == tg;
-                            rin[u] = val_of(e);
-                        }
+                    // Lane u (mod PF) reads slot u (one load instruction per group,
+                    // as in the forward), then the values are broadcast by shuffles.
+                    const int u = lane & (PF - 1);
+                    const int col = colb0 - u;
+                    const uint32_t tg = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
+                    const uint32_t slot = below_wrap ? static_cast<uint32_t>(col) * 2u : (tg % kRing);
+                    bool mine = true;
+                    float v = 0.f;
+                    if (col >= 0 && col < M) {
+                        const uint64_t e = below_wrap ? ld_one(in_g + slot * 8u) : ld_one_shared(my_ring_s + slot * 8u);
+                        mine = tag_of(e) == tg;
+                        v = val_of(e);
                     }
+                    all = __all_sync(SDTW_FULL_MASK, mine);
+#pragma unroll
+                    for (int w = 0; w < PF; ++w) rin[w] = __shfl_sync(SDTW_FULL_MASK, v, w);
                 };
                 read_group();
-                if (__any_sync(SDTW_FULL_MASK, !all) && ok) {  // uniform: all lanes read the same slots
+                if (__any_sync(SDTW_FULL_MASK, !all) && ok) {  // uniform: the tag vote is warp-wide
                     uint64_t w0 = 0;
                     for (uint32_t it = 1;; ++it) {
                         read_group();
@@ -456,7 +470,7 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
                 }
                 // Consumption counter: columns > colb0 - PF are now out of the ring.
                 const int done = M - max(colb0 - PF + 1, 0);  // reversed columns consumed
-                st_release_cluster_u32_if(!below_wrap && lane == 31 && report_due(done, PF, M), below_consumed,
+                st_relaxed_cluster_u32_if(!below_wrap && lane == 31 && report_due(done, PF, M), below_consumed,
                                           band_base + static_cast<uint32_t>(done));
             }
             // ---- flow control for the messages this group publishes upward (lane 0, columns t0 .. t0-PF+1).
