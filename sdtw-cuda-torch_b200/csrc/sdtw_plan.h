@@ -32,8 +32,15 @@ struct WavePlan {
     int G;          // warps per band = wpc * csize
     int n_stripes;  // ceil(N / (32*K))
     int n_bands;    // ceil(n_stripes / G)
-    int n_diag;     // M + 32*K - 1
+    int n_diag;     // anti-diagonal rows per stripe: wl_diag(M, 32K) (M + 32K - 1, padded)
 };
+
+// Anti-diagonal rows stored per stripe.  A stripe has M + 32K - 1 of them;
+// the table is padded to a multiple of 16 plus 16 rows, so that the wavefront
+// kernels may run whole step groups and prefetch up to 16 rows ahead without
+// clamping addresses (the padding holds cells outside the table, which no
+// real cell reads).
+inline int wl_diag(int M, int sr) { return (M + sr - 1 + 15) / 16 * 16 + 16; }
 
 // Rows per lane as a function of the problem only (the score layout depends on
 // it, so forward and backward must agree).
@@ -51,13 +58,17 @@ inline size_t wl_cells(int B, int N, int M, int k_override = 0) {
     const int K = rows_per_lane(N, k_override);
     const size_t sr = 32u * (size_t)K;
     const size_t ns = ((size_t)N + sr - 1) / sr;
-    return (size_t)B * ns * ((size_t)M + sr - 1) * sr;
+    return (size_t)B * ns * (size_t)wl_diag(M, (int)sr) * sr;
 }
 
 // float32 elements (2 per cell: hi, lo) of the score store.
 inline size_t score_elems(int B, int N, int M, int k_override = 0) {
     return 2u * wl_cells(B, N, M, k_override);
 }
+
+// Warps per CTA the wavefront kernels are compiled for: 16 with one DP row per
+// lane, 8 with more (their registers then need 255 per thread).
+inline int wpc_max(int K) { return K == 1 ? 16 : 8; }
 
 // wpc_override / cs_override / k_override (> 0) force the warps per CTA, the
 // cluster size and the rows per lane (tests use them to exercise many bands
@@ -71,16 +82,20 @@ inline WavePlan make_plan(int B, int N, int M, int num_sms, int wpc_override = 0
     p.K = rows_per_lane(N, k_override);
     const int sr = 32 * p.K;
     p.n_stripes = (N + sr - 1) / sr;
-    p.n_diag = M + sr - 1;
+    p.n_diag = wl_diag(M, sr);
     // Spread a problem over up to 8 CTAs (portable cluster size) while the
-    // batch alone would leave SMs idle.
+    // batch alone would leave SMs idle, and further while a problem's stripes
+    // would need more warps per CTA than the kernels allow (one band) and the
+    // clusters still fit on the GPU at one CTA per SM.
+    const int wmax = wpc_max(p.K);
     int cs = 1;
     while (cs < 8 && (long long)B * cs * 2 <= (long long)num_sms && cs * 2 <= p.n_stripes) cs *= 2;
+    while (cs < 8 && (p.n_stripes + cs - 1) / cs > wmax && (long long)B * cs * 2 <= 2LL * num_sms) cs *= 2;
     if (cs_override > 0) cs = cs_override < 8 ? cs_override : 8;
     int wpc = (p.n_stripes + cs - 1) / cs;
-    if (wpc > 16) wpc = 16;
+    if (wpc > wmax) wpc = wmax;
     if (wpc < 1) wpc = 1;
-    if (wpc_override > 0) wpc = wpc_override < 16 ? wpc_override : 16;
+    if (wpc_override > 0) wpc = wpc_override < wmax ? wpc_override : wmax;
     p.csize = cs;
     p.wpc = wpc;
     p.G = wpc * cs;

@@ -29,6 +29,8 @@
 //     neighbour rows exchanged with one warp shuffle per step, stripe-to-stripe
 //     rows handed over through tagged u64 ring slots in the consumer's shared
 //     memory (DSMEM stores across the CTAs of a cluster), bounded waits only.
+#include <type_traits>
+
 #include "sdtw_device.cuh"
 #include "sdtw_kernels.h"
 #include "sdtw_plan.h"
@@ -64,10 +66,23 @@ __device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
 }
 
 // ============================================================== forward
-// Ring slot pair layout (per consumer warp): kRing x {hi, lo} tagged u64.
-template <int K>
-__global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
+// Ring slot pair layout (per consumer warp): kRing x {hi, lo} tagged u64;
+// column c of band b's row above is tagged g = b * M + c and sits in slot
+// g % kRing, so that the slots, like the flow-control counter, advance
+// sequentially across band boundaries.
+//
+// Step code.  The anti-diagonal rows are padded (wl_diag), so every group runs
+// PF whole steps and the cost rows are prefetched PD = 2*PF steps ahead (two
+// register phases, each a compile-time half of dq) without clamping
+// addresses.  Groups that contain cells outside the table (left of column 0,
+// right of column M-1, rows past N) and every group of a banded table run the
+// masked variant, which stores -inf for cells outside the table or the band;
+// the other groups (most of a long stripe) store the computed cells as they
+// are.  The last cell's score is read back from the store after the stripe.
+template <int K, bool BANDED>
+__global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a) {
     constexpr int PF = StepCfg<K>::PF;
+    constexpr int PD = 2 * PF;  // prefetch distance (steps)
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
@@ -86,7 +101,6 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     cluster_sync_all();
 
     const uint32_t my_consumed = smem_addr(consumed + warp);
-    const uint64_t my_ring_g = reinterpret_cast<uint64_t>(ring + warp * 2 * kRing);
     const uint32_t my_ring_s = smem_addr(ring + warp * 2 * kRing);
     uint64_t next_ring_g = 0;
     uint32_t prev_consumed = 0;
@@ -102,9 +116,7 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
     wc.warp = g;
     bool ok = true;          // false once a wait of this lane failed
     bool quit = false;       // warp-uniform
-    uint32_t cons_seen = 0;  // lane 31: consumer progress last observed
-    float outh = 0.f, outl = 0.f;
-    bool has_outv = false;
+    uint32_t cons_seen = 0;  // consumer progress last observed
 
     for (int band = 0; band < P.n_bands && !quit; ++band) {
         const int s = band * P.G + g;
@@ -117,25 +129,25 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
         const bool out_wrap = (g == P.G - 1);
         const uint32_t band_base = static_cast<uint32_t>(band) * static_cast<uint32_t>(M);
         const size_t sb = stripe_base(P, b, s);
-        float2* Ts = a.score + sb;
-        const float* Ds = a.Dw + sb;
-        // Input and output rings as generic addresses: slot c holds {hi, lo}.
-        const uint64_t in_g = in_wrap ? reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M) : my_ring_g;
-        const uint64_t out_g = out_wrap ? reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M) : next_ring_g;
+        float2* Tl = a.score + sb + lane;  // this lane's position of anti-diagonal row 0 (k = 0)
+        const float* Dl = a.Dw + sb + lane;
+        // Global band-wrap ring: slot c = column c (two u64: hi, lo).
+        const uint64_t wrap_g = reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M);
+        const uint64_t out_g = out_wrap ? wrap_g : next_ring_g;
         const uint32_t in_tag_wrap = wrap_tag(a.seq, band - 1);
         const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
+        const bool pub31 = has_out && lane == 31;
 
         // Everything before this band counts as consumed (see the reverse pass).
         st_release_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed, band_base);
 
-        // The lane's cell of step t is at anti-diagonal row t, position k*32+lane;
-        // its column is t - q.  Last cell (N-1, M-1) belongs to one lane and k.
         const int n_steps = M + SR - 1;
-        float dq[PF][K];  // cost of the step due in slot u
+        const int n_groups = (n_steps + PF - 1) / PF;
+        float dq[PD][K];  // cost rows: slot (t mod PD) holds row t
 #pragma unroll
-        for (int u = 0; u < PF; ++u)
+        for (int u = 0; u < PD; ++u)
 #pragma unroll
-            for (int k = 0; k < K; ++k) dq[u][k] = __ldg(Ds + static_cast<size_t>(u) * SR + k * 32 + lane);
+            for (int k = 0; k < K; ++k) dq[u][k] = __ldg(Dl + u * SR + k * 32);
 
         // Three live anti-diagonals: c* = step t-1, o* = step t-2, as (hi, lo).
         float ch[K], cl[K], oh[K], ol[K];
@@ -146,11 +158,14 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
         }
         float uph_prev = (R0 == 0) ? 0.f : NEG;  // T(R0-1, -1)
         float upl_prev = 0.f;
-        int q0 = lane * K;                // row offset of k = 0 in the stripe
-        const int rows_left = N - R0;     // rows q < rows_left are real
+        const int q0 = lane * K;  // row offset of k = 0 in the stripe
+        const int rows_left = N - R0;
+        const bool partial = rows_left < SR;  // last stripe with rows past N
 
-        for (int t0 = 0; t0 < n_steps; t0 += PF) {
-            // ---- group prologue: the row above for columns t0 .. t0+PF-1 (lane 0).
+        auto group = [&](auto phase_c, auto masked_c, int t0) {
+            constexpr int PH = decltype(phase_c)::value;
+            constexpr bool MASKED = decltype(masked_c)::value;
+            // ---- prologue: the row above for columns t0 .. t0+PF-1 (lane 0).
             float rin_h[PF], rin_l[PF];
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
@@ -163,36 +178,30 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                 // 850 cycles per group, one warp-wide load about 200 with the
                 // vote and the shuffles).  The tag vote makes the re-poll loop
                 // below a uniform branch, taken only when the producer is behind.
-                uint32_t tg0 = in_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(t0);
+                const uint32_t tg0 = in_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(t0);
                 bool all = true;
-                auto read_group = [&]() {
+                float vh = NEG, vl = 0.f;
+                auto probe = [&]() {  // load + tag vote; re-polls repeat only this
                     const int u = lane & (PF - 1);
                     const int col = t0 + u;
                     const uint32_t tg = in_wrap ? tg0 : tg0 + static_cast<uint32_t>(u);
-                    const uint32_t slot = in_wrap ? static_cast<uint32_t>(col) : (tg % kRing);
                     bool mine = true;
-                    float vh = NEG, vl = 0.f;
                     if (col < M) {
                         uint64_t eh, el;
-                        if (in_wrap) ld_pair(in_g + slot * 16u, eh, el);
-                        else ld_pair_shared(my_ring_s + slot * 16u, eh, el);
+                        if (in_wrap) ld_pair(wrap_g + static_cast<uint32_t>(col) * 16u, eh, el);
+                        else ld_pair_shared(my_ring_s + (tg % kRing) * 16u, eh, el);
                         mine = tag_of(eh) == tg && tag_of(el) == tg;
                         vh = val_of(eh);
                         vl = val_of(el);
                     }
                     all = __all_sync(SDTW_FULL_MASK, mine);
-#pragma unroll
-                    for (int w = 0; w < PF; ++w) {
-                        rin_h[w] = __shfl_sync(SDTW_FULL_MASK, vh, w);
-                        rin_l[w] = __shfl_sync(SDTW_FULL_MASK, vl, w);
-                    }
                 };
-                read_group();
-                if (__any_sync(SDTW_FULL_MASK, !all) && ok) {
+                probe();
+                if (!all && ok) {  // uniform (vote)
                     uint64_t w0 = 0;
                     for (uint32_t it = 1;; ++it) {
-                        read_group();
-                        if (!__any_sync(SDTW_FULL_MASK, !all)) break;
+                        probe();
+                        if (all) break;
                         const int r = backoff(it, w0, wc);
                         if (r) {
                             if (r == 1 && lane == 0) record_error(wc, kStatusTimeout, 1, tg0, 0);
@@ -200,6 +209,11 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                             break;
                         }
                     }
+                }
+#pragma unroll
+                for (int w = 0; w < PF; ++w) {
+                    rin_h[w] = __shfl_sync(SDTW_FULL_MASK, vh, w);
+                    rin_l[w] = __shfl_sync(SDTW_FULL_MASK, vl, w);
                 }
                 const int done = min(t0 + PF, M);
                 st_relaxed_cluster_u32_if(!in_wrap && report_due(done, PF, M) && lane == 0, prev_consumed,
@@ -218,19 +232,19 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                     }
                 }
             }
-            // ---- PF branch-free steps.
+            // ---- PF steps.
+            float2* Tg = Tl + static_cast<size_t>(t0) * SR;
+            const float* Dg = Dl + static_cast<size_t>(t0 + PD) * SR;
+            const int colb0 = t0 - (SR - 1);  // bottom-row column of step t0
+            const uint32_t tgo0 = out_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(colb0);
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 + u;
                 float c[K];
-                // Prefetch from a clamped (always valid) row: a select on the loaded
-                // value would wait for the load here and defeat the prefetch.  Values
-                // of rows past the end only reach cells that are not live.
-                const size_t tpf = static_cast<size_t>(min(t + PF, n_steps - 1));
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
-                    c[k] = dq[u][k];
-                    dq[u][k] = __ldg(Ds + tpf * SR + k * 32 + lane);
+                    c[k] = dq[PH * PF + u][k];
+                    dq[PH * PF + u][k] = __ldg(Dg + u * SR + k * 32);  // row t + PD
                 }
                 float uph = __shfl_up_sync(SDTW_FULL_MASK, ch[K - 1], 1);
                 float upl = __shfl_up_sync(SDTW_FULL_MASK, cl[K - 1], 1);
@@ -242,8 +256,6 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                 float nh[K], nl[K];
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
-                    const int q = q0 + k;
-                    const int col = t - q;
                     const float lh = ch[k], ll = cl[k];
                     const float uh = (k == 0) ? uph : ch[k > 0 ? k - 1 : 0];
                     const float ul = (k == 0) ? upl : cl[k > 0 ? k - 1 : 0];
@@ -259,21 +271,23 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                     const float hi = m + delta;
                     const float bb = hi - m;
                     const float lo = (m - (hi - bb)) + (delta - bb);
-                    const bool inr = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
-                    const bool inband = static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                    const bool live = inr && inband && m != NEG;
-                    nh[k] = live ? hi : NEG;
-                    nl[k] = live ? lo : 0.f;
-                    if (t < n_steps) Ts[static_cast<size_t>(t) * SR + k * 32 + lane] = make_float2(nh[k], nl[k]);
-                    const bool last = (q == rows_left - 1) && (col == M - 1);
-                    outh = last ? nh[k] : outh;
-                    outl = last ? nl[k] : outl;
-                    has_outv = has_outv || last;
+                    if constexpr (MASKED) {
+                        const int col = t - (q0 + k);
+                        bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && q0 + k < rows_left;
+                        if constexpr (BANDED)
+                            live = live && static_cast<unsigned>(R0 + q0 + k - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                        nh[k] = live ? hi : NEG;
+                        nl[k] = live ? lo : 0.f;
+                    } else {
+                        nh[k] = hi;
+                        nl[k] = lo;
+                    }
+                    Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
                 }
                 // Bottom row of the stripe goes to the next stripe's warp.
-                const int colb = t - (SR - 1);
-                const bool pub = has_out && lane == 31 && static_cast<unsigned>(colb) < static_cast<unsigned>(M);
-                const uint32_t tgo = out_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(colb);
+                const int colb = colb0 + u;
+                const bool pub = pub31 && static_cast<unsigned>(colb) < static_cast<unsigned>(M);
+                const uint32_t tgo = out_wrap ? tgo0 : tgo0 + static_cast<uint32_t>(u);
                 const uint32_t slot = out_wrap ? static_cast<uint32_t>(colb) : (tgo % kRing);
                 st_pair_if(pub, out_g + slot * 16u, pack_tagged(nh[K - 1], tgo), pack_tagged(nl[K - 1], tgo));
 #pragma unroll
@@ -284,14 +298,43 @@ __global__ void __launch_bounds__(512) fwd_kernel(const FwdArgs a) {
                     cl[k] = nl[k];
                 }
             }
-            if (((t0 / PF) & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
+        };
+        using P0 = std::integral_constant<int, 0>;
+        using P1 = std::integral_constant<int, 1>;
+        using Masked = std::integral_constant<bool, true>;
+        using Plain = std::integral_constant<bool, BANDED>;  // banded tables mask every group
+        // A group has cells outside the table (stored as -inf) when its first
+        // step is left of column 0 for some lane (t0 < SR - 1), its last step
+        // right of column M-1 (t0 + PF - 1 >= M), or the stripe has rows past N.
+        auto edge = [&](int t0) { return partial || t0 < SR - 1 || t0 + PF - 1 >= M; };
+        for (int gi = 0; gi < n_groups; gi += 2) {
+            const int t0 = gi * PF;
+            if (edge(t0)) group(P0{}, Masked{}, t0);
+            else group(P0{}, Plain{}, t0);
+            if (gi + 1 < n_groups) {
+                if (edge(t0 + PF)) group(P1{}, Masked{}, t0 + PF);
+                else group(P1{}, Plain{}, t0 + PF);
+            }
+            if ((gi & 15) == 14 && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
+        // Rows past the last group are padding: -inf, like every cell outside the table.
+        for (int t = n_groups * PF; t < P.n_diag; ++t)
+#pragma unroll
+            for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = make_float2(NEG, 0.f);
+        if (!quit && s == P.n_stripes - 1) {
+            // Last cell (N-1, M-1): row q of this stripe, step q + M - 1; the
+            // owning lane reads back its own store.
+            const int q = N - 1 - R0;
+            if (lane == q / K) {
+                const float2 v = Tl[static_cast<size_t>(q + M - 1) * SR + (q % K) * 32];
+                a.out[b] = fmaf(-v.x, a.inv_k, -v.y * a.inv_k);
+            }
+        }
     }
-    if (has_outv) a.out[b] = fmaf(-outh, a.inv_k, -outl * a.inv_k);
     // No CTA may leave while a peer can still write into its shared memory.
     cluster_sync_all();
 }
@@ -317,7 +360,7 @@ __device__ __forceinline__ float2 load_score(const float2* __restrict__ S, const
 // and for lane 0 the last row of the previous stripe (one prefetched load).
 // E is written in the wavefront layout.
 template <int K>
-__global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
+__global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a) {
     constexpr int PF = StepCfg<K>::PF;
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -436,30 +479,29 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
             const int colb0 = t0 - (SR - 1);
             if (has_below && colb0 - (PF - 1) < M && colb0 >= 0) {  // warp-uniform
                 bool all = true;
-                auto read_group = [&]() {
+                float v = 0.f;
+                auto probe = [&]() {
                     // Lane u (mod PF) reads slot u (one load instruction per group,
-                    // as in the forward), then the values are broadcast by shuffles.
+                    // as in the forward); the values are broadcast by shuffles once
+                    // the tag vote has passed.
                     const int u = lane & (PF - 1);
                     const int col = colb0 - u;
                     const uint32_t tg = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
                     const uint32_t slot = below_wrap ? static_cast<uint32_t>(col) * 2u : (tg % kRing);
                     bool mine = true;
-                    float v = 0.f;
                     if (col >= 0 && col < M) {
                         const uint64_t e = below_wrap ? ld_one(in_g + slot * 8u) : ld_one_shared(my_ring_s + slot * 8u);
                         mine = tag_of(e) == tg;
                         v = val_of(e);
                     }
                     all = __all_sync(SDTW_FULL_MASK, mine);
-#pragma unroll
-                    for (int w = 0; w < PF; ++w) rin[w] = __shfl_sync(SDTW_FULL_MASK, v, w);
                 };
-                read_group();
-                if (__any_sync(SDTW_FULL_MASK, !all) && ok) {  // uniform: the tag vote is warp-wide
+                probe();
+                if (!all && ok) {  // uniform: the tag vote is warp-wide
                     uint64_t w0 = 0;
                     for (uint32_t it = 1;; ++it) {
-                        read_group();
-                        if (!__any_sync(SDTW_FULL_MASK, !all)) break;
+                        probe();
+                        if (all) break;
                         const int r = backoff(it, w0, wc);
                         if (r) {
                             if (r == 1 && lane == 0) record_error(wc, kStatusTimeout, 1, static_cast<uint32_t>(colb0), 0);
@@ -468,6 +510,8 @@ __global__ void __launch_bounds__(512) bwd_kernel(const BwdArgs a) {
                         }
                     }
                 }
+#pragma unroll
+                for (int w = 0; w < PF; ++w) rin[w] = __shfl_sync(SDTW_FULL_MASK, v, w);
                 // Consumption counter: columns > colb0 - PF are now out of the ring.
                 const int done = M - max(colb0 - PF + 1, 0);  // reversed columns consumed
                 st_relaxed_cluster_u32_if(!below_wrap && lane == 31 && report_due(done, PF, M), below_consumed,
@@ -634,12 +678,17 @@ static size_t ring_smem_bytes(const WavePlan& P) {
 
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
+    // The band check runs only when a band can exclude a cell of the table.
+    const bool banded = args.ibw < P.N + P.M;
     dim3 grid(P.B * P.csize), block(P.wpc * 32);
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
     switch (P.K) {
-        case 1: return launch_cluster((const void*)fwd_kernel<1>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
-        case 2: return launch_cluster((const void*)fwd_kernel<2>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
-        case 4: return launch_cluster((const void*)fwd_kernel<4>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+        case 1: return launch_cluster(banded ? (const void*)fwd_kernel<1, true> : (const void*)fwd_kernel<1, false>, grid, block,
+                                      ring_smem_bytes(P), P.csize, stream, kargs);
+        case 2: return launch_cluster(banded ? (const void*)fwd_kernel<2, true> : (const void*)fwd_kernel<2, false>, grid, block,
+                                      ring_smem_bytes(P), P.csize, stream, kargs);
+        case 4: return launch_cluster(banded ? (const void*)fwd_kernel<4, true> : (const void*)fwd_kernel<4, false>, grid, block,
+                                      ring_smem_bytes(P), P.csize, stream, kargs);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -32,9 +32,10 @@ def test_library_exports_every_declared_symbol():
 
 def test_sizes_without_gpu():
     L = _native.lib()
-    assert L.sdtw_score_elems(4, 64, 64) == 2 * 4 * 2 * (64 + 31) * 32   # (hi, lo) per cell
+    n_diag = (64 + 31 + 15) // 16 * 16 + 16  # anti-diagonal rows per stripe, padded
+    assert L.sdtw_score_elems(4, 64, 64) == 2 * 4 * 2 * n_diag * 32   # (hi, lo) per cell
     assert L.sdtw_score_elems(0, 4, 4) == 0
-    cells = 4 * 2 * (64 + 31) * 32
+    cells = 4 * 2 * n_diag * 32
     assert L.sdtw_cost_elems(4, 64, 64) == cells
     # One band: no wrap ring; the wavefront-layout table of the cost / E.
     assert L.sdtw_workspace_bytes(4, 64, 64) == -(-cells * 4 // 256) * 256
