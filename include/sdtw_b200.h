@@ -74,6 +74,12 @@ void sdtw_debug_stall_stripe(int stripe);
  * lane, so a forward and its backward must run under the same setting. */
 void sdtw_set_plan_override(int warps_per_cta, int cluster_size, int rows_per_lane);
 
+/* Diagnostic: the launch geometry chosen for a (B,N,M) problem on the
+ * current device.  info[0..5] = DP rows per lane, warps per CTA, cluster size,
+ * bands, stripes, clusters of that geometry that fit on the device at once
+ * (-1 if unknown).  No counterpart in the reference. */
+int sdtw_plan_info(int B, int N, int M, int *info);
+
 /* Number of float32 elements of the score table for a (B,N,M) problem. */
 size_t sdtw_score_elems(int B, int N, int M);
 

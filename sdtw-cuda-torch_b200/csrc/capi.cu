@@ -8,6 +8,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/sdtw_b200.h"
@@ -187,8 +188,47 @@ int int_band(float bw) {
     return f >= static_cast<double>(1 << 29) ? (1 << 29) : static_cast<int>(f);
 }
 
+// Resident clusters per geometry, cached per device (the occupancy query is a
+// host call; the plan is computed at every launch).
+int cached_cluster_fit(const WavePlan& p) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, int>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    const auto key = std::make_tuple(dev, p.K, p.wpc, p.csize);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    const int n = max_active_clusters(p);
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = n;
+    return n;
+}
+
+// Launch geometry.  make_plan's choice unless its clusters do not all fit on
+// the GPU at once (a second wave would double the time): then the candidate
+// with fewer waves, then fewer bands, then larger clusters.
 WavePlan plan(int B, int N, int M) {
-    return make_plan(B, N, M, num_sms(), g_wpc_override.load(), g_cs_override.load(), g_k_override.load());
+    const int wo = g_wpc_override.load(), co = g_cs_override.load(), ko = g_k_override.load();
+    WavePlan p = make_plan(B, N, M, num_sms(), wo, co, ko);
+    if (wo > 0 || co > 0) return p;
+    const int fit = cached_cluster_fit(p);
+    if (fit <= 0 || B <= fit) return p;
+    auto waves = [&](int f) { return f > 0 ? (B + f - 1) / f : 1 << 30; };
+    WavePlan best = p;
+    int best_w = waves(fit);
+    for (int cs = 8; cs >= 1; cs /= 2) {
+        if (cs == p.csize) continue;
+        const WavePlan q = make_plan(B, N, M, num_sms(), 0, cs, ko);
+        const int w = waves(cached_cluster_fit(q));
+        if (w < best_w || (w == best_w && q.n_bands < best.n_bands)) {
+            best = q;
+            best_w = w;
+        }
+    }
+    return best;
 }
 
 // Workspace layouts (each region 256-byte aligned):
@@ -341,6 +381,20 @@ int sdtw_timing_read(char* names, size_t names_len, double* total_ms, long* coun
 }
 
 void sdtw_debug_stall_stripe(int stripe) { g_debug_stall.store(stripe); }
+
+int sdtw_plan_info(int B, int N, int M, int* info) {
+    if (!info) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    int rc = check_dims(B, N, M);
+    if (rc) return rc;
+    const WavePlan p = plan(B, N, M);
+    info[0] = p.K;
+    info[1] = p.wpc;
+    info[2] = p.csize;
+    info[3] = p.n_bands;
+    info[4] = p.n_stripes;
+    info[5] = cached_cluster_fit(p);
+    return SDTW_OK;
+}
 
 size_t sdtw_score_elems(int B, int N, int M) {
     if (B <= 0 || N <= 0 || M <= 0) return 0;

@@ -40,6 +40,7 @@ struct BwdArgs {
 };
 
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
+int max_active_clusters(const WavePlan& P);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
 cudaError_t launch_R_to_score(const float* R, float2* S, const WavePlan& P, float kk, cudaStream_t stream);

@@ -46,11 +46,12 @@ inline int wl_diag(int M, int sr) { return (M + sr - 1 + 15) / 16 * 16 + 16; }
 // it, so forward and backward must agree).
 inline int rows_per_lane(int N, int k_override = 0) {
     if (k_override == 1 || k_override == 2 || k_override == 4) return k_override;
-    // One row per lane keeps the dependent chain of a step shortest (latency-bound
-    // problems); two rows per lane give every step two independent cells, which
-    // pays off once stripes are long enough to keep all SMs busy (measured on
-    // B200: N=M=512 best at 1, N=M=4096 best at 2).
-    return N > 1024 ? 2 : 1;
+    // One row per lane keeps the dependent chain of a step shortest.  Measured
+    // on B200 with the occupancy-aware plan, one row per lane is also the
+    // faster choice for long sequences (N = M = 4096: 2.5 ms forward at 1, 2.6
+    // ms at 2); 2 and 4 stay available through the plan override.
+    (void)N;
+    return 1;
 }
 
 // Cells (with the layout's padding) of a (B,N,M) table in the wavefront layout.

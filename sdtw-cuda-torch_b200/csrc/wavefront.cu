@@ -38,6 +38,11 @@
 namespace sdtw {
 
 constexpr int kRing = 128;  // ring slots per warp (power of two)
+// Prefetch distance of the forward in groups.  Two register phases (the
+// step body compiled twice) measured faster than one on B200; a third body
+// for interior groups without the edge masks measured slower (the bodies no
+// longer fit the instruction cache), so every group runs the masked body.
+constexpr int kFwdPhases = 2;
 
 __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
     return (seq << 12) | (static_cast<uint32_t>(band) & 0xfffu);
@@ -74,15 +79,14 @@ __device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
 // Step code.  The anti-diagonal rows are padded (wl_diag), so every group runs
 // PF whole steps and the cost rows are prefetched PD = 2*PF steps ahead (two
 // register phases, each a compile-time half of dq) without clamping
-// addresses.  Groups that contain cells outside the table (left of column 0,
-// right of column M-1, rows past N) and every group of a banded table run the
-// masked variant, which stores -inf for cells outside the table or the band;
-// the other groups (most of a long stripe) store the computed cells as they
-// are.  The last cell's score is read back from the store after the stripe.
+// addresses.  Cells outside the table (left of column 0, right of column M-1,
+// rows past N) or the band are stored as -inf.  The last cell's score is read
+// back from the store after the stripe.
 template <int K, bool BANDED>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a) {
     constexpr int PF = StepCfg<K>::PF;
-    constexpr int PD = 2 * PF;  // prefetch distance (steps)
+    constexpr int NPH = kFwdPhases;  // prefetch distance in groups
+    constexpr int PD = NPH * PF;     // prefetch distance (steps)
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
@@ -160,11 +164,9 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         float upl_prev = 0.f;
         const int q0 = lane * K;  // row offset of k = 0 in the stripe
         const int rows_left = N - R0;
-        const bool partial = rows_left < SR;  // last stripe with rows past N
 
-        auto group = [&](auto phase_c, auto masked_c, int t0) {
+        auto group = [&](auto phase_c, int t0) {
             constexpr int PH = decltype(phase_c)::value;
-            constexpr bool MASKED = decltype(masked_c)::value;
             // ---- prologue: the row above for columns t0 .. t0+PF-1 (lane 0).
             float rin_h[PF], rin_l[PF];
 #pragma unroll
@@ -271,17 +273,13 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     const float hi = m + delta;
                     const float bb = hi - m;
                     const float lo = (m - (hi - bb)) + (delta - bb);
-                    if constexpr (MASKED) {
-                        const int col = t - (q0 + k);
-                        bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && q0 + k < rows_left;
-                        if constexpr (BANDED)
-                            live = live && static_cast<unsigned>(R0 + q0 + k - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                        nh[k] = live ? hi : NEG;
-                        nl[k] = live ? lo : 0.f;
-                    } else {
-                        nh[k] = hi;
-                        nl[k] = lo;
-                    }
+                    // Cells outside the table (or the band) read as -inf.
+                    const int col = t - (q0 + k);
+                    bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && q0 + k < rows_left;
+                    if constexpr (BANDED)
+                        live = live && static_cast<unsigned>(R0 + q0 + k - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    nh[k] = live ? hi : NEG;
+                    nl[k] = live ? lo : 0.f;
                     Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
                 }
                 // Bottom row of the stripe goes to the next stripe's warp.
@@ -301,21 +299,13 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         };
         using P0 = std::integral_constant<int, 0>;
         using P1 = std::integral_constant<int, 1>;
-        using Masked = std::integral_constant<bool, true>;
-        using Plain = std::integral_constant<bool, BANDED>;  // banded tables mask every group
-        // A group has cells outside the table (stored as -inf) when its first
-        // step is left of column 0 for some lane (t0 < SR - 1), its last step
-        // right of column M-1 (t0 + PF - 1 >= M), or the stripe has rows past N.
-        auto edge = [&](int t0) { return partial || t0 < SR - 1 || t0 + PF - 1 >= M; };
-        for (int gi = 0; gi < n_groups; gi += 2) {
+        for (int gi = 0; gi < n_groups; gi += NPH) {
             const int t0 = gi * PF;
-            if (edge(t0)) group(P0{}, Masked{}, t0);
-            else group(P0{}, Plain{}, t0);
-            if (gi + 1 < n_groups) {
-                if (edge(t0 + PF)) group(P1{}, Masked{}, t0 + PF);
-                else group(P1{}, Plain{}, t0 + PF);
+            group(P0{}, t0);
+            if constexpr (NPH == 2) {
+                if (gi + 1 < n_groups) group(P1{}, t0 + PF);
             }
-            if ((gi & 15) == 14 && __any_sync(SDTW_FULL_MASK, !ok)) {
+            if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
@@ -359,9 +349,13 @@ __device__ __forceinline__ float2 load_score(const float2* __restrict__ S, const
 // loads, PF steps ahead), the row above from the neighbour lane by shuffle,
 // and for lane 0 the last row of the previous stripe (one prefetched load).
 // E is written in the wavefront layout.
-template <int K>
+template <int K, bool BANDED>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a) {
     constexpr int PF = StepCfg<K>::PF;
+    // Prefetch distance: one group (K = 1, whose 512-thread launches leave 128
+    // registers per thread) or two groups (K > 1).
+    constexpr int NPH = K == 1 ? 1 : 2;
+    constexpr int PD = NPH * PF;
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
@@ -428,30 +422,34 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         st_release_cluster_u32_if(has_below && !below_wrap && lane == 31, below_consumed, band_base);
 
         const int n_steps = M + SR - 1;
-        const int t_last = ((n_steps + PF - 1) / PF) * PF - 1;  // padded: extra steps touch no live cell
-        // Queued loads read clamped (always valid) addresses and are used raw:
-        // a select on a loaded value would stall on the load at issue.  Rows or
+        const int n_groups = (n_steps + PF - 1) / PF;
+        const int t_last = n_groups * PF - 1;  // steps past n_steps - 1 touch cells outside the table
+        // Queued loads: the step due in register slot j reads A(t-2) and
+        // PS(t-1), refilled PD steps ahead from clamped (always valid)
+        // addresses and used raw: a select on a loaded value would stall on the
+        // load at issue.  Rows or
         // columns past either end only reach cells that are not live, or are
         // masked where they are consumed (the column -1 border below, and the
         // row above stripe 0, which is -inf).
         const bool ps_live = R0 > 0;
+        const float2* Tl = Ts + lane;
         auto loadA = [&](int tp, int k) -> float2 {
             const int tc = min(max(tp, 0), n_steps - 1);
-            return __ldg(Ts + static_cast<size_t>(tc) * SR + k * 32 + lane);
+            return __ldg(Tl + static_cast<size_t>(tc) * SR + k * 32);
         };
         auto loadPS = [&](int col) -> float2 {
             const int cc = min(max(col, 0), M - 1);
             return __ldg(Tp + static_cast<size_t>(cc) * SR);
         };
 
-        float2 aq[PF][K];  // A(t-2) for the step due in slot u
-        float2 pq[PF];     // PS(t-1) for the step due in slot u
+        float2 aq[PD][K];  // A(t-2) for the step due in slot j
+        float2 pq[PD];     // PS(t-1) for the step due in slot j
 #pragma unroll
-        for (int u = 0; u < PF; ++u) {
-            const int t = t_last - u;
+        for (int j = 0; j < PD; ++j) {
+            const int t = t_last - j;
 #pragma unroll
-            for (int k = 0; k < K; ++k) aq[u][k] = loadA(t - 2, k);
-            pq[u] = loadPS(t - 1);
+            for (int k = 0; k < K; ++k) aq[j][k] = loadA(t - 2, k);
+            pq[j] = loadPS(t - 1);
         }
         float2 A1[K];  // A(t-1)
 #pragma unroll
@@ -469,8 +467,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         for (int k = 0; k < K; ++k) accl[k] = msg[k] = dprev[k] = 0.f;
         const int q0 = lane * K;
         const int rows_left = N - R0;
+        float* El = Es + lane;
 
-        for (int t0 = t_last; t0 >= 0; t0 -= PF) {
+        auto group = [&](auto phase_c, int t0) {
+            constexpr int PH = decltype(phase_c)::value;
             // ---- group prologue: messages for this lane's last row (lane 31),
             // columns colb(t) = t - (SR-1) for t = t0 .. t0-PF+1.
             float rin[PF];
@@ -529,20 +529,22 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                     }
                 }
             }
-            // ---- PF branch-free reverse steps.
+            // ---- PF reverse steps.
+            float* Eg = El + static_cast<size_t>(t0) * SR;
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 - u;
+                constexpr int J0 = PH * PF;
                 float2 A2[K];
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
-                    A2[k] = aq[u][k];
-                    aq[u][k] = loadA(t - 2 - PF, k);
+                    A2[k] = aq[J0 + u][k];
+                    aq[J0 + u][k] = loadA(t - 2 - PD, k);
                 }
                 float2 S2;
                 {
-                    const float2 ps = pq[u];
-                    pq[u] = loadPS(t - 1 - PF);
+                    const float2 ps = pq[J0 + u];
+                    pq[J0 + u] = loadPS(t - 1 - PD);
                     S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
                     S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
                     S2.x = (lane == 0) ? (ps_live ? ps.x : NEG) : S2.x;
@@ -556,23 +558,23 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                     const int q = q0 + k;
                     const int col = t - q;
                     const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
-                    const bool inr = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
-                    const bool inband = static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                    const bool live = inr && inband;
                     float e = accl[k] + in_below;
-                    e = (q == rows_left - 1 && col == M - 1) ? gb : e;
-                    e = live ? e : 0.f;
-                    if (t >= 0 && t < n_steps) Es[static_cast<size_t>(t) * SR + k * 32 + lane] = e;
-                    // Predecessor scores; column -1 is the border (+inf R), except
-                    // the corner (-1, -1) of row 0 (R = 0).
                     float2 tl = A1[k];
                     float2 tu = (k == 0) ? S1 : A1[k > 0 ? k - 1 : 0];
                     float2 td = (k == 0) ? S2 : A2[k > 0 ? k - 1 : 0];
+                    bool live = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                    if constexpr (BANDED)
+                        live = live && static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    e = (q == rows_left - 1 && col == M - 1) ? gb : e;
+                    e = live ? e : 0.f;
+                    // Predecessor scores; column -1 is the border (+inf R),
+                    // except the corner (-1, -1) of row 0 (R = 0).
                     const bool c0 = (col == 0);
                     tl.x = c0 ? NEG : tl.x;
                     tl.y = c0 ? 0.f : tl.y;
                     td.x = c0 ? ((R0 + q == 0) ? 0.f : NEG) : td.x;
                     td.y = c0 ? 0.f : td.y;
+                    Eg[-static_cast<ptrdiff_t>(u) * SR + k * 32] = e;
                     // Softmax of the predecessors' scores; the lo of the max cancels.
                     const float m = max3f(td.x, tu.x, tl.x);
                     const float ed = ex2f((td.x - m) + td.y);
@@ -596,11 +598,24 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                 }
                 S1 = S2;
             }
-            if ((((t_last - t0) / PF) & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
+        };
+        using P0 = std::integral_constant<int, 0>;
+        using P1 = std::integral_constant<int, 1>;
+        for (int gi = 0; gi < n_groups; gi += NPH) {
+            const int t0 = t_last - gi * PF;
+            group(P0{}, t0);
+            if constexpr (NPH == 2) {
+                if (gi + 1 < n_groups) group(P1{}, t0 - PF);
+            }
+            if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
         }
+        // Rows past the last group are padding: zero, like every cell outside the table.
+        for (int t = n_groups * PF; t < P.n_diag; ++t)
+#pragma unroll
+            for (int k = 0; k < K; ++k) El[static_cast<size_t>(t) * SR + k * 32] = 0.f;
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
     }
     cluster_sync_all();
@@ -676,6 +691,41 @@ static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
 
+// Clusters of this geometry that can be resident at once on the current
+// device (the smaller of the forward's and the backward's figure), or -1 if
+// the runtime cannot tell.  Clusters are placed within one GPC, so on B200 the
+// figure can be below (SMs / cluster size).
+int max_active_clusters(const WavePlan& P) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(P.csize);
+    cfg.blockDim = dim3(P.wpc * 32);
+    cfg.dynamicSmemBytes = ring_smem_bytes(P);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = P.csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const void* fns[2] = {nullptr, nullptr};
+    switch (P.K) {
+        case 1: fns[0] = (const void*)fwd_kernel<1, false>; fns[1] = (const void*)bwd_kernel<1, false>; break;
+        case 2: fns[0] = (const void*)fwd_kernel<2, false>; fns[1] = (const void*)bwd_kernel<2, false>; break;
+        case 4: fns[0] = (const void*)fwd_kernel<4, false>; fns[1] = (const void*)bwd_kernel<4, false>; break;
+        default: return -1;
+    }
+    int best = -1;
+    for (const void* fn : fns) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return -1;
+        }
+        best = (best < 0 || n < best) ? n : best;
+    }
+    return best;
+}
+
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
     // The band check runs only when a band can exclude a cell of the table.
@@ -695,12 +745,16 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
 
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
+    const bool banded = args.ibw < P.N + P.M;
     dim3 grid(P.B * P.csize), block(P.wpc * 32);
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
     switch (P.K) {
-        case 1: return launch_cluster((const void*)bwd_kernel<1>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
-        case 2: return launch_cluster((const void*)bwd_kernel<2>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
-        case 4: return launch_cluster((const void*)bwd_kernel<4>, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+        case 1: return launch_cluster(banded ? (const void*)bwd_kernel<1, true> : (const void*)bwd_kernel<1, false>, grid, block,
+                                      ring_smem_bytes(P), P.csize, stream, kargs);
+        case 2: return launch_cluster(banded ? (const void*)bwd_kernel<2, true> : (const void*)bwd_kernel<2, false>, grid, block,
+                                      ring_smem_bytes(P), P.csize, stream, kargs);
+        case 4: return launch_cluster(banded ? (const void*)bwd_kernel<4, true> : (const void*)bwd_kernel<4, false>, grid, block,
+                                      ring_smem_bytes(P), P.csize, stream, kargs);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -35,6 +35,7 @@ _SIGS = {
     "sdtw_timing_enable": ([_I], None),
     "sdtw_timing_read": ([ctypes.c_char_p, _SZ, _P, _P, _I], _I),
     "sdtw_set_plan_override": ([_I, _I, _I], None),
+    "sdtw_plan_info": ([_I, _I, _I, _P], _I),
     "sdtw_score_elems": ([_I, _I, _I], _SZ),
     "sdtw_cost_elems": ([_I, _I, _I], _SZ),
     "sdtw_workspace_bytes": ([_I, _I, _I], _SZ),
@@ -144,6 +145,15 @@ def set_plan_override(warps_per_cta: int = 0, cluster_size: int = 0, rows_per_la
     """Force the wavefront launch geometry (zeros restore the automatic plan).
     A forward and its backward must run under the same rows_per_lane."""
     lib().sdtw_set_plan_override(int(warps_per_cta), int(cluster_size), int(rows_per_lane))
+
+
+def plan_info(B: int, N: int, M: int) -> dict:
+    """Launch geometry the library chooses for a (B, N, M) problem on the
+    current device (diagnostic)."""
+    info = (ctypes.c_int * 6)()
+    _check(lib().sdtw_plan_info(int(B), int(N), int(M), info), "plan_info")
+    keys = ("rows_per_lane", "warps_per_cta", "cluster_size", "bands", "stripes", "clusters_fit")
+    return dict(zip(keys, list(info)))
 
 
 def set_wait_timeout(seconds: float) -> None:
