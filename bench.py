@@ -1,18 +1,28 @@
 #!/usr/bin/env python
 """Soft-DTW forward+backward DP-cell throughput on B200.
 
-Workload: per GPU B=32, N=M=512, D=64 float32 x, y ~ N(0,1)
-(seeded, synthetic), gamma=1, squared-Euclidean cost;
-one step = SoftDTW(fused=...)(x, y).mean().backward() producing dL/dx and dL/dy.
-Metric: DP cells per second, cells = B*N*M per step, summed over all GPUs
-(weak scaling: every rank runs its own B=32 batch; no collective on the path).
-The headline `value` is the default CUDA path (fused=None -> fused); the
-unfused path is reported under "modes".
-
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c3|c4a|c4b|c5]
 
-`--impl reference` times the reference's CPU algorithm (the oracle port in
-oracle/, all host threads) on the same workload.
+Workloads (synthetic, seeded data with the configs' shapes and
+value distributions):
+  c2   B=32/GPU, N=M=512, D=64, x,y ~ N(0,1), gamma=1 (default; headline).  One
+       step = SoftDTW(fused=...)(x, y).mean().backward() -> dL/dx, dL/dy.  The
+       headline `value` is the default CUDA path (fused=None -> fused); the
+       unfused path is reported under "modes".
+  c3   B=16/GPU, N=M=4096, D=8, gamma=0.1, fused: x = phase-shifted sines + noise,
+       y = x time-warped by a random monotone cubic map + noise.
+  c4a  B=64/GPU, N=1024, M=768, D=128, N(0,1), gamma=1, unfused (headline), fused
+       under "modes".
+  c4b  B=64/GPU, N=M=1024, D=128, normalize=True (3B problems, cells = 3*B*N*M).
+  c5   barycenter of 4096 sequences (length 100, D=3, random-phase sines with
+       random shifts + noise), gamma=1, Adam lr 0.1; one step = one Adam
+       iteration over the whole set, cells = 4096*100*100.  The set is sharded
+       over the ranks (strong scaling, one NCCL all-reduce per step); the other
+       workloads run B problems per rank (weak scaling, no collective).
+Metric: DP cells per second summed over all GPUs.  `--impl reference` times the
+reference's CPU algorithm (the oracle restatement in oracle/, all host
+threads) on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -28,11 +38,19 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "sdtw-cuda-torch_b200"))
 
+# name: (B, N, M, D, gamma, normalize, headline mode, other modes, description)
 WORKLOADS = {
-    # name: (B, N, M, D, gamma, description)
-    "c2": (32, 512, 512, 64, 1.0, "BASELINE config 2: B=32/GPU, N=M=512, D=64, gamma=1, fwd+bwd, mean reduction"),
-    "c3": (16, 4096, 4096, 8, 0.1, "BASELINE config 3 shape: B=16/GPU, N=M=4096, D=8, gamma=0.1, fwd+bwd"),
-    "c4a": (64, 1024, 768, 128, 1.0, "BASELINE config 4a: B=64/GPU, N=1024, M=768, D=128, gamma=1"),
+    "c2": (32, 512, 512, 64, 1.0, False, "fused", ("unfused",),
+           "BASELINE config 2: B=32/GPU, N=M=512, D=64, gamma=1, fwd+bwd, mean reduction"),
+    "c3": (16, 4096, 4096, 8, 0.1, False, "fused", (),
+           "BASELINE config 3: B=16/GPU, N=M=4096, D=8, gamma=0.1, sines + time warp, fused fwd+bwd"),
+    "c4a": (64, 1024, 768, 128, 1.0, False, "unfused", ("fused",),
+            "BASELINE config 4a: B=64/GPU, N=1024, M=768, D=128, gamma=1, unfused fwd+bwd"),
+    "c4b": (64, 1024, 1024, 128, 1.0, True, "fused", ("unfused",),
+            "BASELINE config 4b: B=64/GPU, N=M=1024, D=128, normalize=True (3B problems), fwd+bwd"),
+    "c5": (4096, 100, 100, 3, 1.0, False, "barycenter", (),
+           "BASELINE config 5: barycenter of 4096 sequences x 100 x 3, gamma=1, Adam lr=0.1, "
+           "one step = one iteration over the whole set, sharded over the ranks"),
 }
 PUBLISHED = {  # reference, B=32 N=M=512 D=64 fwd+bwd (unstated GPU)
     "c2": {"fused": 32 * 512 * 512 / 0.14136, "unfused": 32 * 512 * 512 / 0.02010},
@@ -41,24 +59,67 @@ MUFU_PER_CELL = 7          # algorithmic ex2/lg2 per DP cell, forward + backward
 MUFU_PER_SM_CLK = 16       # ex2/lg2 results per SM per clock
 # Algorithmic HBM bytes per DP cell of each library kernel: every table entry
 # read or written once (cost 4 B, score 8 B as a (hi, lo) pair, E 4 B).
-ALG_BYTES = {"cost_wl": 4, "wavefront_fwd": 12, "wavefront_bwd": 12, "wl_to_rm": 8, "grad_xy": 8,
+ALG_BYTES = {"cost_wl": 4, "cost_tc": 4, "wavefront_fwd": 12, "wavefront_bwd": 12, "wl_to_rm": 8, "grad_xy": 8,
              "rm_to_wl": 8, "cost_rowmajor": 4}
 # Algorithmic MUFU ops per cell of the reference algorithm: forward softmin
 # (2 ex2 + 1 lg2), reverse log-sum-exp (2 ex2 + 1 lg2) and E = exp(log E) (1 ex2).
 ALG_MUFU = {"wavefront_fwd": 3, "wavefront_bwd": 4}
+# DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum,
+# one launch each, cold L2) for the C2 workload; see profiles/c2_kernels_full.md.
+TRAFFIC_C2 = {"wavefront_fwd": 53.88e6, "wavefront_bwd": 81.90e6, "cost_wl": 8.42e6}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    # Profiling runs: only the fused timed steps (no unfused mode, no end-to-end leg).
+    # Profiling runs: only the headline timed steps (no other modes, no end-to-end leg).
     ap.add_argument("--fused-only", action="store_true")
     return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- data
+def make_data(name, B, N, M, D, seed):
+    """Seeded synthetic inputs with the shapes and value distributions of the
+    BASELINE config (numpy float32)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    if name == "c3":
+        t = np.arange(N, dtype=np.float64)
+        f = rng.uniform(1, 8, size=(B, 1, D))
+        ph = rng.uniform(0, 2 * np.pi, size=(B, 1, D))
+        clean = np.sin(2 * np.pi * f * t[None, :, None] / N + ph)
+        x = clean + 0.1 * rng.standard_normal((B, N, D))
+        # y: x warped by w(u) = u + a u (1 - u)(1 - 2u), |a| < 0.8 (w' > 0, w(0) = 0, w(1) = 1).
+        u = np.linspace(0.0, 1.0, M)
+        a = rng.uniform(-0.8, 0.8, size=(B, 1))
+        w = (u[None, :] + a * u[None, :] * (1 - u[None, :]) * (1 - 2 * u[None, :])) * (N - 1)
+        y = np.empty((B, M, D))
+        for bi in range(B):
+            for c in range(D):
+                y[bi, :, c] = np.interp(w[bi], t, clean[bi, :, c])
+        y += 0.1 * rng.standard_normal((B, M, D))
+        return x.astype(np.float32), y.astype(np.float32)
+    if name == "c5":
+        t = np.arange(N, dtype=np.float64)
+        ph = rng.uniform(0, 2 * np.pi, size=(B, 1, D))
+        k = np.arange(1, D + 1, dtype=np.float64)[None, None, :]
+        shift = rng.integers(-10, 11, size=(B, 1, 1))
+        ts = np.clip(t[None, :, None] - shift, 0, N - 1)  # edge-padded shift
+        X = np.sin(2 * np.pi * ts / N * k + ph) + 0.2 * rng.standard_normal((B, N, D))
+        return X.astype(np.float32), None
+    x = rng.standard_normal((B, N, D)).astype(np.float32)
+    y = rng.standard_normal((B, M, D)).astype(np.float32)
+    return x, y
+
+
+def cells_of(name):
+    B, N, M, D, gamma, normalize, *_ = WORKLOADS[name]
+    return (3 if normalize else 1) * B * N * M
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -125,39 +186,61 @@ class ClockSampler:
                 "reasons": sorted(active), "samples": len(self.samples)}
 
 
-# ----------------------------------------------------------------------------- reference arm
-def run_reference(args):
+# ----------------------------------------------------------------------------- CPU (oracle) timing
+def time_oracle(name, budget_s):
+    """Reference CPU algorithm (oracle/, all host threads) on a bounded sample
+    of the workload: returns (cells/s, threads, sample description)."""
     import numpy as np
-    import torch
-
     from oracle import oracle as O
 
-    B, N, M, Dm, gamma, desc = WORKLOADS[args.workload]
-    torch.manual_seed(1234)
-    x = torch.randn(B, N, Dm).numpy()
-    y = torch.randn(B, M, Dm).numpy()
-    g = np.full(B, 1.0 / B)
-    cores = O.num_threads()
-    for _ in range(args.warmup):
-        O.loss_and_grads(x, y, gamma=gamma, grad_out=g)
-    times = []
+    B, N, M, D, gamma, normalize, mode, _, _ = WORKLOADS[name]
+    if name == "c5":
+        X, _ = make_data(name, B, N, M, D, seed=1234)
+        sub = 256  # sequences per sampled iteration
+        bary = X[:sub].mean(axis=0)
+        x = np.broadcast_to(bary, (sub, N, D)).copy()
+        y = X[:sub]
+        kw = dict(gamma=gamma, grad_out=np.full(sub, 1.0 / B))
+        unit_cells = sub * N * N
+        desc = f"{sub} of 4096 sequences per iteration (loss and barycenter gradient)"
+    else:
+        per = N * M * (3 if normalize else 1)
+        b_s = max(1, min(B, int(2e7 // per)))  # about one second of CPU work per call
+        x, y = make_data(name, b_s, N, M, D, seed=1234)
+        kw = dict(gamma=gamma, normalize=normalize, grad_out=np.full(b_s, 1.0 / B))
+        unit_cells = (3 if normalize else 1) * b_s * N * M
+        desc = (f"{b_s} of {B} problems ({N}x{M}, D={D}{', normalize' if normalize else ''}) per call, "
+                "unfused reference algorithm")
+    O.loss_and_grads(x, y, **kw)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while reps == 0 or (time.perf_counter() - t0 < budget_s and reps < 1000):
+        O.loss_and_grads(x, y, **kw)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return reps * unit_cells / dt, O.num_threads(), f"{reps} x {desc}, {dt:.1f} s"
+
+
+def run_reference(args):
+    name = args.workload
+    B, N, M, D, gamma, normalize, mode, _, desc = WORKLOADS[name]
+    cells = cells_of(name) if name != "c5" else B * N * N
+    # Every step is a bounded sample (about two seconds) of the workload.
+    for _ in range(max(args.warmup, 0)):
+        time_oracle(name, 0.0)
+    per_step, cores, sample = [], None, ""
     for _ in range(args.steps):
-        t0 = time.perf_counter()
-        O.loss_and_grads(x, y, gamma=gamma, grad_out=g)
-        times.append(time.perf_counter() - t0)
-    cells = B * N * M
-    ms = 1e3 * statistics.mean(times)
-    value = cells / (ms / 1e3)
+        v, cores, sample = time_oracle(name, 2.0)
+        per_step.append(v)
+    value = statistics.mean(per_step)
     line = {
         "impl": "reference", "metric": "fwd+bwd DP cells/s", "value": value, "unit": "cells/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 DP)",
-        "data": "synthetic N(0,1), seeded",
-        "config": {"workload": desc + " (CPU: unfused, the reference has no CPU fused mode)",
-                   "global_batch": B, "seq_len": N, "dim": Dm, "parallelism": "host threads"},
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * cells / value,
+        "higher_is_better": True, "scaling": "strong" if name == "c5" else "weak", "vs_baseline": None,
+        "dtype": "f32 (f64 DP)", "data": "synthetic, seeded (BASELINE config shapes and distributions)",
+        "config": {"workload": f"{name}: {desc} (CPU: unfused; the reference has no CPU fused mode)",
+                   "global_batch": B, "seq_len": N, "dim": D, "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "cells/s", "cores": cores, "kind": "port",
-                         "sample": f"full batch ({B}x{N}x{M}, D={Dm}) per step; oracle/ restatement of "
-                                   "launcher.py:305-368 + numpy cost and chain rule"},
+                         "sample": sample + "; oracle/ restatement of launcher.py:305-368 + numpy cost and chain rule"},
         "e2e": {"value": value, "unit": "cells/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -179,6 +262,7 @@ def main():
     from datetime import timedelta
 
     from softdtw_cuda import SoftDTW, _native
+    from softdtw_cuda.distributed import shard_bounds, sharded_barycenter
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -196,27 +280,37 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    B, N, M, Dm, gamma, desc = WORKLOADS[args.workload]
-    cells = B * N * M
-    gen = torch.Generator().manual_seed(1234 + rank)
-    x_h = torch.randn(B, N, Dm, generator=gen).pin_memory()
-    y_h = torch.randn(B, M, Dm, generator=gen).pin_memory()
-    x = x_h.to(dev)
-    y = y_h.to(dev)
+    name = args.workload
+    B, N, M, Dm, gamma, normalize, head_mode, other_modes, desc = WORKLOADS[name]
+    is_bary = name == "c5"
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    stream = torch.cuda.current_stream(dev)
 
-    def step(fused):
+    if is_bary:
+        Xn, _ = make_data(name, B, N, M, Dm, seed=1234)
+        lo, hi = shard_bounds(B, rank, world)
+        X_h = torch.from_numpy(Xn[lo:hi]).pin_memory()
+        X_d = X_h.to(dev)
+        cells = B * N * N  # whole job per iteration
+        my_cells = (hi - lo) * N * N
+    else:
+        xn, yn = make_data(name, B, N, M, Dm, seed=1234 + rank)
+        x_h = torch.from_numpy(xn).pin_memory()
+        y_h = torch.from_numpy(yn).pin_memory()
+        x = x_h.to(dev)
+        y = y_h.to(dev)
+        cells = world * cells_of(name)
+        my_cells = cells_of(name)
+
+    def step(mode):
         xr = x.detach().requires_grad_(True)
         yr = y.detach().requires_grad_(True)
-        out = SoftDTW(gamma=gamma, fused=fused)(xr, yr)
+        out = SoftDTW(gamma=gamma, normalize=normalize, fused=(None if mode == "fused" else False))(xr, yr)
         out.mean().backward()
         return xr.grad, yr.grad
 
-    sampler = ClockSampler(local)
-
     def timed(fn, k):
         times = []
-        stream = torch.cuda.current_stream(dev)
         for _ in range(k):
             flush.zero_()
             e0 = torch.cuda.Event(enable_timing=True)
@@ -228,66 +322,123 @@ def main():
         torch.cuda.synchronize(dev)
         return [a.elapsed_time(b) for a, b in times]
 
+    sampler = ClockSampler(local)
     modes = {}
     launches = 0
     breakdown = {}
+    per_launch = {}
+    all_modes = (head_mode,) + (() if args.fused_only else tuple(other_modes))
     with sampler:
-        for name, fused in (("fused", None), ("unfused", False))[:1 if args.fused_only else 2]:
-            for _ in range(args.warmup):
-                step(fused)
-            torch.cuda.synchronize(dev)
-            barrier()
-            torch.cuda.synchronize(dev)
-            l0 = _native.launch_count
-            if name == "fused":
-                _native.timing_enable(True)  # per-kernel CUDA events on the launching stream
-            ms = timed(lambda: step(fused), args.steps)
-            if name == "fused":
-                launches = _native.launch_count - l0
+        for mode in all_modes:
+            allreduce_ms = None
+            if is_bary:
+                # One call of K iterations (the optimiser state carries over),
+                # timed as a whole; the per-step figure is the average.
+                sharded_barycenter(X_d, gamma=gamma, max_iter=args.warmup, lr=0.1, early_stopping=False)
+                torch.cuda.synchronize(dev)
+                barrier()
+                torch.cuda.synchronize(dev)
+                l0 = _native.launches()
+                _native.timing_enable(True)
+                stats = {}
+                flush.zero_()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                sharded_barycenter(X_d, gamma=gamma, max_iter=args.steps, lr=0.1, early_stopping=False, stats=stats)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                ms = [e0.elapsed_time(e1) / args.steps] * args.steps
+                n_launch = _native.launches() - l0
                 kt = _native.timing_read()
                 _native.timing_enable(False)
-                breakdown = {k: v[0] / max(v[1], 1) * (v[1] / args.steps) for k, v in kt.items()}
-                per_launch = {k: v[0] / max(v[1], 1) for k, v in kt.items()}
+                allreduce_ms = 1e3 * stats.get("allreduce_s", 0.0) / max(args.steps, 1)
+            else:
+                for _ in range(args.warmup):
+                    step(mode)
+                torch.cuda.synchronize(dev)
+                barrier()
+                torch.cuda.synchronize(dev)
+                l0 = _native.launches()
+                _native.timing_enable(True)  # per-kernel CUDA events on the launching stream
+                ms = timed(lambda: step(mode), args.steps)
+                n_launch = _native.launches() - l0
+                kt = _native.timing_read()
+                _native.timing_enable(False)
+            bd = {k: v[0] / args.steps for k, v in kt.items()}
+            pl = {k: v[0] / max(v[1], 1) for k, v in kt.items()}
+            if mode == head_mode:
+                breakdown, per_launch, launches = bd, pl, n_launch
             torch.cuda.synchronize(dev)
             barrier()
             _native.check_status(dev)
             mean_ms = max_over_ranks(statistics.mean(ms))
-            modes[name] = {"value": world * cells / (mean_ms / 1e3), "ms_per_step": mean_ms,
-                           "median_ms": statistics.median(ms)}
-            pub = PUBLISHED.get(args.workload, {}).get(name)
-            modes[name]["vs_published"] = (modes[name]["value"] / world / pub) if pub else None
+            modes[mode] = {"value": cells / (mean_ms / 1e3), "ms_per_step": mean_ms,
+                           "median_ms": statistics.median(ms), "kernel_ms_per_step": bd, "gpu_launches": n_launch}
+            if allreduce_ms is not None:
+                modes[mode]["allreduce_ms_per_step"] = max_over_ranks(allreduce_ms)
+            pub = PUBLISHED.get(name, {}).get(mode)
+            modes[mode]["vs_published"] = (modes[mode]["value"] / world / pub) if pub else None
 
     # End to end through the public API with host buffers.
-    gx_h = torch.empty_like(x_h).pin_memory()
-    gy_h = torch.empty_like(y_h).pin_memory()
-    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
-
-    def e2e_step():
-        xd = x_h.to(dev, non_blocking=True).requires_grad_(True)
-        yd = y_h.to(dev, non_blocking=True).requires_grad_(True)
-        loss = SoftDTW(gamma=gamma)(xd, yd).mean()
-        loss.backward()
-        loss_h.copy_(loss.detach(), non_blocking=True)
-        gx_h.copy_(xd.grad, non_blocking=True)
-        gy_h.copy_(yd.grad, non_blocking=True)
-
-    e2e_ms = float("nan")
+    e2e = None
     if not args.fused_only:
-        for _ in range(args.warmup):
-            e2e_step()
-        torch.cuda.synchronize(dev)
-        barrier()
-        e2e_ms = max_over_ranks(statistics.mean(timed(e2e_step, args.steps)))
-    h2d = x_h.numel() * 4 + y_h.numel() * 4
-    d2h = 4 + gx_h.numel() * 4 + gy_h.numel() * 4
+        if is_bary:
+            out_h = torch.empty(N, Dm).pin_memory()
+
+            def e2e_run(k):
+                Xd = X_h.to(dev, non_blocking=True)
+                bary = sharded_barycenter(Xd, gamma=gamma, max_iter=k, lr=0.1, early_stopping=False)
+                out_h.copy_(bary, non_blocking=True)
+
+            e2e_run(args.warmup)
+            torch.cuda.synchronize(dev)
+            barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            e2e_run(args.steps)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+            h2d = X_h.numel() * 4 / args.steps
+            d2h = out_h.numel() * 4 / args.steps
+            api = ("softdtw_cuda.distributed.sharded_barycenter (pinned host sequences in, barycenter out; "
+                   "per-step bytes = one call's copies / steps)")
+        else:
+            gx_h = torch.empty_like(x_h).pin_memory()
+            gy_h = torch.empty_like(y_h).pin_memory()
+            loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+            fused = None if head_mode == "fused" else False
+
+            def e2e_step():
+                xd = x_h.to(dev, non_blocking=True).requires_grad_(True)
+                yd = y_h.to(dev, non_blocking=True).requires_grad_(True)
+                loss = SoftDTW(gamma=gamma, normalize=normalize, fused=fused)(xd, yd).mean()
+                loss.backward()
+                loss_h.copy_(loss.detach(), non_blocking=True)
+                gx_h.copy_(xd.grad, non_blocking=True)
+                gy_h.copy_(yd.grad, non_blocking=True)
+
+            for _ in range(args.warmup):
+                e2e_step()
+            torch.cuda.synchronize(dev)
+            barrier()
+            e2e_ms = max_over_ranks(statistics.mean(timed(e2e_step, args.steps)))
+            h2d = x_h.numel() * 4 + y_h.numel() * 4
+            d2h = 4 + gx_h.numel() * 4 + gy_h.numel() * 4
+            api = f"softdtw_cuda.SoftDTW ({head_mode}; pinned host x,y in; loss, dL/dx, dL/dy out)"
+        e2e = {"value": cells / (e2e_ms / 1e3), "unit": "cells/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
 
     clocks = sampler.summary()
-    head = modes["fused"]
+    head = modes[head_mode]
 
     # Roofline of the dominant kernel (largest device time per step).
     dom = max(breakdown, key=breakdown.get)
     dom_ms = per_launch[dom]
-    alg_bytes = ALG_BYTES[dom] * cells
+    launches_per_step = breakdown[dom] / dom_ms
+    alg_bytes = ALG_BYTES.get(dom, 0) * my_cells / launches_per_step  # per launch
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -295,69 +446,53 @@ def main():
     except OSError:
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic_c2.json")) as f:
-            traffic = json.load(f).get(dom)
-    except (OSError, ValueError):
-        pass
     achieved = alg_bytes / (dom_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "traffic": traffic,
+                "frac": achieved / hbm_peak,
+                "traffic": TRAFFIC_C2.get(dom) if name == "c2" else None,
                 "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                "alg_bytes_per_cell": ALG_BYTES[dom]}
+                "alg_bytes_per_cell": ALG_BYTES.get(dom, 0)}
     n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
     sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
     mufu_peak = n_sm * MUFU_PER_SM_CLK * sm_mhz * 1e6
-    step_mufu = MUFU_PER_CELL * cells / (head["ms_per_step"] / 1e3)
-    wf = {k: ALG_MUFU[k] * cells / (per_launch[k] / 1e3) for k in ALG_MUFU if k in per_launch}
+    step_mufu = MUFU_PER_CELL * my_cells / (head["ms_per_step"] / 1e3)
+    wf = {k: ALG_MUFU[k] * my_cells / (breakdown[k] / 1e3) for k in ALG_MUFU if k in breakdown}
     roofline_mufu = {"bound": "mufu", "unit": "Gop/s", "peak": mufu_peak / 1e9,
                      "peak_basis": f"{n_sm} SMs x {MUFU_PER_SM_CLK} ex2/lg2 per clk x {sm_mhz:.0f} MHz (median under load)",
                      "step_achieved": step_mufu / 1e9, "step_frac": step_mufu / mufu_peak,
-                     "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms": per_launch[k],
+                     "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms_per_step": breakdown[k],
                                      "alg_ops_per_cell": ALG_MUFU[k]} for k, v in wf.items()},
                      "alg_ops_per_cell": MUFU_PER_CELL}
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import numpy as np
-        from oracle import oracle as O
-        xn, yn = x_h.numpy(), y_h.numpy()
-        g = np.full(B, 1.0 / B)
-        O.loss_and_grads(xn, yn, gamma=gamma, grad_out=g)  # warm
-        reps, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < 10.0 and reps < 200:
-            O.loss_and_grads(xn, yn, gamma=gamma, grad_out=g)
-            reps += 1
-        dt = time.perf_counter() - t0
-        cpu_baseline = {"value": reps * cells / dt, "unit": "cells/s", "cores": O.num_threads(), "kind": "port",
-                        "sample": f"{reps} x full batch ({B}x{N}x{M}, D={Dm}) fwd+bwd, unfused reference "
-                                  f"algorithm (oracle/), {dt:.1f} s"}
+        v, cores, sample = time_oracle(name, 10.0)
+        cpu_baseline = {"value": v, "unit": "cells/s", "cores": cores, "kind": "port", "sample": sample}
 
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
-    pub = PUBLISHED.get(args.workload, {}).get("fused")
+    pub = PUBLISHED.get(name, {}).get(head_mode)
     line = {
         "metric": "fwd+bwd DP cells/s", "value": head["value"], "unit": "cells/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
-        "higher_is_better": True, "scaling": "weak",
+        "higher_is_better": True, "scaling": "strong" if is_bary else "weak",
         "vs_baseline": (head["value"] / world / pub) if pub else None,
-        "dtype": "f32", "data": "synthetic N(0,1), seeded",
-        "config": {"workload": desc + "; headline = default CUDA path (fused=None -> fused)",
-                   "global_batch": B * world, "seq_len": N, "dim": Dm, "parallelism": f"dp{world} (batch-sharded)",
-                   "l2": "flushed before every timed step (256 MiB write, outside the events)",
-                   "vs_baseline_basis": "per-GPU value / BASELINE.md published fused number (unstated GPU)"},
+        "dtype": "f32", "data": "synthetic, seeded (BASELINE config shapes and distributions)",
+        "config": {"workload": f"{name}: {desc}; headline mode = {head_mode}",
+                   "global_batch": B if is_bary else B * world, "seq_len": N, "dim": Dm,
+                   "parallelism": (f"dp{world} (sequence-sharded barycenter, NCCL all-reduce per step)" if is_bary
+                                   else f"dp{world} (batch-sharded, no collective)"),
+                   "l2": ("per-iteration working set (about 1 GB of tables) larger than the 126 MB L2" if is_bary else
+                          "flushed before every timed step (256 MiB write, outside the events)"),
+                   "vs_baseline_basis": "per-GPU value / BASELINE.md published number (unstated GPU)"},
         "modes": modes,
         "kernel_ms_per_step": breakdown,
         "roofline": roofline,
         "roofline_mufu": roofline_mufu,
         "cpu_baseline": cpu_baseline,
-        "e2e": None if args.fused_only else {
-            "value": world * cells / (e2e_ms / 1e3), "unit": "cells/s", "ms_per_step": e2e_ms,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "softdtw_cuda.SoftDTW (pinned host x,y in; loss, dL/dx, dL/dy out)"},
+        "e2e": e2e,
         "gpu_launches": launches,
         "clocks": clocks,
     }

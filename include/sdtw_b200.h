@@ -74,6 +74,11 @@ void sdtw_debug_stall_stripe(int stripe);
  * lane, so a forward and its backward must run under the same setting. */
 void sdtw_set_plan_override(int warps_per_cta, int cluster_size, int rows_per_lane);
 
+/* Diagnostic: number of kernels the library has launched since it was loaded
+ * (every entry point counts the kernels it enqueues).  No counterpart in the
+ * reference. */
+unsigned long long sdtw_launch_count(void);
+
 /* Diagnostic: the launch geometry chosen for a (B,N,M) problem on the
  * current device.  info[0..5] = DP rows per lane, warps per CTA, cluster size,
  * bands, stripes, clusters of that geometry that fit on the device at once

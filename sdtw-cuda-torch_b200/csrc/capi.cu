@@ -56,11 +56,16 @@ cudaEvent_t pool_event() {
     return e;
 }
 
+// Kernels launched by the library since load (every launch site counts its
+// kernels here).
+std::atomic<unsigned long long> g_launches{0};
+
 struct KernelTimer {
     const char* name;
     cudaStream_t st;
     cudaEvent_t e0 = nullptr;
-    KernelTimer(const char* n, cudaStream_t s) : name(n), st(s) {
+    KernelTimer(const char* n, cudaStream_t s, int kernels = 1) : name(n), st(s) {
+        g_launches.fetch_add(static_cast<unsigned long long>(kernels));
         if (g_timing.load()) {
             std::lock_guard<std::mutex> lk(g_timing_mu);
             e0 = pool_event();
@@ -137,7 +142,9 @@ std::string diag_text() {
     char buf[256];
     std::snprintf(buf, sizeof buf,
                   "%s pass, %s wait, problem %d, warp %d, band %d: expected %d, last seen %d",
-                  d[0] == 1 ? "forward" : (d[0] == 2 ? "backward" : (d[0] == 5 ? "tensor-core gradient" : "?")),
+                  d[0] == 1 ? "forward"
+                            : (d[0] == 2 ? "backward"
+                                         : (d[0] == 5 ? "tensor-core gradient" : (d[0] == 6 ? "tensor-core cost" : "?"))),
                   d[1] == 1 ? "shared-memory ring"
                             : (d[1] == 2 ? "global ring"
                                          : (d[1] == 3 ? "flow-control" : (d[1] == 4 ? "MMA completion" : "?"))),
@@ -382,6 +389,8 @@ int sdtw_timing_read(char* names, size_t names_len, double* total_ms, long* coun
 
 void sdtw_debug_stall_stripe(int stripe) { g_debug_stall.store(stripe); }
 
+unsigned long long sdtw_launch_count(void) { return g_launches.load(); }
+
 int sdtw_plan_info(int B, int N, int M, int* info) {
     if (!info) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     int rc = check_dims(B, N, M);
@@ -551,7 +560,10 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
     if ((rc = check_ws(workspace, workspace_bytes, wave_ws(B, N, M)))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    {
+    if (cost_tc_supported(x, y, dim)) {
+        KernelTimer kt("cost_tc", st);
+        e = launch_cost_tc(x, y, cost, plan(B, N, M), dim, wait_ctx(), st);
+    } else {
         KernelTimer kt("cost_wl", st);
         e = launch_cost_wl(x, y, cost, plan(B, N, M), dim, false, st);
     }
@@ -579,7 +591,7 @@ int sdtw_grad_sqeuclid_f32(const float* G, const float* D_mask, const float* x, 
     if (!G || !x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     cudaError_t e;
     {
-        KernelTimer kt("grad_xy", static_cast<cudaStream_t>(stream));
+        KernelTimer kt("grad_xy", static_cast<cudaStream_t>(stream), (grad_x ? 1 : 0) + (grad_y ? 1 : 0));
         e = launch_grad_xy(G, D_mask, x, y, grad_x, grad_y, B, N, M, dim, static_cast<cudaStream_t>(stream));
     }
     if (e != cudaSuccess) return cuda_fail(e, "grad launch");

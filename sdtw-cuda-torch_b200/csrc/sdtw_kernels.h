@@ -78,5 +78,11 @@ struct GradTcArgs {
 };
 void grad_tc_geometry(int dim, bool masked, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages);
 cudaError_t launch_grad_tc(const GradTcArgs& args, cudaStream_t stream);
+// tcgemm.cu: the unfused (expanded, clamped) cost on the tensor cores, written
+// in the wavefront layout.  Requires dim >= 16, dim % 4 == 0 and 16-byte
+// aligned x, y (cost_tc_supported).
+bool cost_tc_supported(const float* x, const float* y, int dim);
+cudaError_t launch_cost_tc(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
+                           cudaStream_t stream);
 
 }  // namespace sdtw

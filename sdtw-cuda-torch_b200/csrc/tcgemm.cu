@@ -555,4 +555,250 @@ cudaError_t launch_grad_tc(const GradTcArgs& args, cudaStream_t stream) {
     }
 }
 
+// ============================================================== unfused cost
+// D = clamp(||x_q||^2 + ||y_j||^2 - 2 x_q . y_j, 0) in the wavefront layout,
+// the expanded squared-Euclidean cost of softdtw_cuda/distances.py:6-28 with
+// the dot products on the tensor cores (3xTF32, float32 accumulators in
+// tensor memory).  One CTA (8 warps) per 128 x 128 tile (rows q, columns j) of
+// one problem; K = features in chunks of 32, two stages fed by 16-byte
+// cp.async (rows are 16-byte aligned: dim % 4 == 0), split in place into high
+// parts and remainders.  Consecutive threads take consecutive rows of the same
+// 16-byte column (conflict-free shared stores); each thread also sums the
+// squares of the elements it splits, and the two threads of a row add their
+// sums in a fixed order.  The
+// epilogue writes the tile's cells into shared memory by anti-diagonal and
+// stores anti-diagonal rows of the layout (cells of neighbouring tiles in the
+// same rows are left alone).
+constexpr int kCostStages = 2;
+
+template <int K>
+__global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                                              float* __restrict__ Dw, const WavePlan P, int dim,
+                                                              const WaitCtx wait) {
+    constexpr int SR = 32 * K;
+    constexpr int NSL = kTileM / SR;       // stripes in the 128-row tile
+    constexpr int TL = SR + kTileM - 1;    // anti-diagonal rows of one stripe slice
+    constexpr int UPT = kTileM * kKT / 4 / kThreads;  // 16-byte units per thread per operand (4)
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const int N = P.N, M = P.M;
+    const int j0 = blockIdx.x * kTileM;
+    const int q0 = blockIdx.y * kTileM;
+    const int b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t op_bytes = kTileM / 8 * kSBO;     // one 128 x 32 operand buffer
+    const uint32_t stage_bytes = 4 * op_bytes;       // A_hi, A_lo, B_hi, B_lo
+    unsigned char* ctrl = smem_raw + kCostStages * stage_bytes;
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(ctrl);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 64);
+    float* xn = reinterpret_cast<float*>(ctrl + 128);  // [2][128] partial, then [128]
+    float* yn = xn + 2 * kTileM;                      // [2][128] partial, then [128]
+    const uint32_t smem_base = smem_addr(smem_raw);
+    const float* xb = x + static_cast<size_t>(b) * N * dim;
+    const float* yb = y + static_cast<size_t>(b) * M * dim;
+    const int n_chunks = (dim + kKT - 1) / kKT;
+
+    WaitCtx wc = wait;
+    wc.kernel = 6;
+    wc.problem = b;
+    wc.warp = blockIdx.x;
+    wc.band = blockIdx.y;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kCostStages; ++s) mbar_init(smem_addr(mbar + s), 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_addr(tmem_slot), 128u);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t idesc = idesc_tf32(kTileM, kTileM);
+
+    // Unit u = threadIdx.x + 256 i: row u % 128, features 4 (u / 128) .. +3 of
+    // the chunk; a thread keeps one row (threadIdx.x % 128).
+    const int urow = threadIdx.x & (kTileM - 1);
+    float xs2 = 0.f, ys2 = 0.f;  // partial squared norms of the thread's row
+    auto issue = [&](int c) {
+        const int st = c % kCostStages;
+        const uint32_t dA = smem_base + st * stage_bytes;
+        const uint32_t dB = dA + 2 * op_bytes;
+        const int f0 = c * kKT;
+#pragma unroll
+        for (int i = 0; i < UPT; ++i) {
+            const int u = threadIdx.x + kThreads * i;
+            const int row = u & (kTileM - 1), kc = u >> 7;
+            const int f = f0 + 4 * kc;
+            const bool fx = q0 + row < N && f < dim;
+            const bool fy = j0 + row < M && f < dim;
+            const uint32_t off = op_off(row, 4 * kc);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dA + off),
+                         "l"(fx ? xb + static_cast<size_t>(q0 + row) * dim + f : xb), "r"(fx ? 16u : 0u)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dB + off),
+                         "l"(fy ? yb + static_cast<size_t>(j0 + row) * dim + f : yb), "r"(fy ? 16u : 0u)
+                         : "memory");
+        }
+    };
+    auto split = [&](int c) {
+        const int st = c % kCostStages;
+        unsigned char* A = smem_raw + st * stage_bytes;
+        unsigned char* Bm = A + 2 * op_bytes;
+#pragma unroll
+        for (int i = 0; i < UPT; ++i) {
+            const int u = threadIdx.x + kThreads * i;
+            const uint32_t off = op_off(u & (kTileM - 1), 4 * (u >> 7));
+#pragma unroll
+            for (int o = 0; o < 2; ++o) {
+                unsigned char* hi = o == 0 ? A : Bm;
+                float4 v = *reinterpret_cast<const float4*>(hi + off);
+                float4 h, l;
+                h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+                h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+                h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+                h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+                l.x = v.x - h.x;
+                l.y = v.y - h.y;
+                l.z = v.z - h.z;
+                l.w = v.w - h.w;
+                *reinterpret_cast<float4*>(hi + off) = h;
+                *reinterpret_cast<float4*>(hi + op_bytes + off) = l;
+                float& acc = o == 0 ? xs2 : ys2;
+                acc = fmaf(v.x, v.x, acc);
+                acc = fmaf(v.y, v.y, acc);
+                acc = fmaf(v.z, v.z, acc);
+                acc = fmaf(v.w, v.w, acc);
+            }
+        }
+    };
+
+    bool ok = true;
+    issue(0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int c = 0; c < n_chunks; ++c) {
+        const int st = c % kCostStages;
+        // Refill the other stage with chunk c+1 once the MMAs of chunk c-1 are done.
+        if (c + 1 < n_chunks) {
+            if (c >= 1 && ok) ok = mbar_wait(smem_addr(mbar + (c - 1) % kCostStages), static_cast<uint32_t>(((c - 1) / kCostStages) & 1), wc);
+            issue(c + 1);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        split(c);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (threadIdx.x == 0 && ok) {
+            const uint32_t aH = smem_base + st * stage_bytes;
+            const uint32_t aL = aH + op_bytes;
+            const uint32_t bH = aL + op_bytes;
+            const uint32_t bL = bH + op_bytes;
+#pragma unroll
+            for (int ks = 0; ks < kKT / 8; ++ks) {
+                const uint32_t o = static_cast<uint32_t>(ks) * 2 * kLBO;
+                const uint32_t acc0 = (c > 0 || ks > 0) ? 1u : 0u;
+                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bH + o), idesc, acc0);
+                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bL + o), idesc, 1u);
+                mma_tf32(tmem, smem_desc(aL + o), smem_desc(bH + o), idesc, 1u);
+            }
+            mma_commit(smem_addr(mbar + st));
+        }
+    }
+    // Squared norms: threads r and r + 128 hold the two halves of row r.
+    xn[(threadIdx.x >> 7) * kTileM + urow] = xs2;
+    yn[(threadIdx.x >> 7) * kTileM + urow] = ys2;
+    if (n_chunks > 0 && ok) {
+        const int cl = n_chunks - 1;
+        ok = mbar_wait(smem_addr(mbar + cl % kCostStages), static_cast<uint32_t>((cl / kCostStages) & 1), wc);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    tc_fence_after();
+    const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+    if (threadIdx.x < kTileM) {
+        xn[threadIdx.x] = xn[threadIdx.x] + xn[kTileM + threadIdx.x];
+        yn[threadIdx.x] = yn[threadIdx.x] + yn[kTileM + threadIdx.x];
+    }
+    __syncthreads();
+
+    if (all_ok) {
+        // ---- epilogue: warp w holds tile rows 32 (w % 4) + lane, columns of
+        // half w / 4; cells go to shared memory by (stripe slice, anti-diagonal).
+        float* stg = reinterpret_cast<float*>(smem_raw);  // [NSL][TL][SR]
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = quarter * 32 + lane;
+        const int sl = r / SR, ql = r % SR;
+        const int p = (ql % K) * 32 + ql / K;
+        const float xr = xn[r];
+        const uint32_t tw = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        float v[16];
+        for (int c16 = half * 4; c16 < half * 4 + 4; ++c16) {
+            tmem_ld16(tw + static_cast<uint32_t>(c16 * 16), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int c = c16 * 16 + i;
+                const float d = fmaxf((xr + yn[c]) - 2.f * v[i], 0.f);
+                stg[(sl * TL + ql + c) * SR + p] = d;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 128u);
+    if (all_ok) {
+        const float* stg = reinterpret_cast<const float*>(smem_raw);
+        for (int e = threadIdx.x; e < NSL * TL * SR; e += kThreads) {
+            const int pp = e % SR;
+            const int tl = (e / SR) % TL;
+            const int sl = e / (SR * TL);
+            const int ql = (pp % 32) * K + pp / 32;
+            const int jl = tl - ql;   // column within the tile
+            const int q = q0 + sl * SR + ql;
+            const int j = j0 + jl;
+            if (jl >= 0 && jl < kTileM && j < M && q < N) {
+                const int s = q / SR;
+                const int t = ql + j;
+                Dw[((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * SR + pp] = stg[e];
+            }
+        }
+    }
+}
+
+static size_t cost_tc_smem_bytes(int K) {
+    const size_t ops = static_cast<size_t>(kCostStages) * 4 * (kTileM / 8) * kSBO;
+    const size_t stage = static_cast<size_t>(kTileM / (32 * K)) * (32 * K + kTileM - 1) * (32 * K) * sizeof(float);
+    return (ops > stage ? ops : stage) + 128 + 4 * kTileM * sizeof(float);
+}
+
+bool cost_tc_supported(const float* x, const float* y, int dim) {
+    return dim >= 16 && dim % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+}
+
+cudaError_t launch_cost_tc(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
+                           cudaStream_t stream) {
+    const dim3 grid((P.M + kTileM - 1) / kTileM, (P.N + kTileM - 1) / kTileM, P.B);
+    const size_t smem = cost_tc_smem_bytes(P.K);
+    cudaError_t e = cudaSuccess;
+    switch (P.K) {
+        case 1:
+            e = cudaFuncSetAttribute(cost_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e == cudaSuccess) cost_tc_kernel<1><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
+            break;
+        case 2:
+            e = cudaFuncSetAttribute(cost_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e == cudaSuccess) cost_tc_kernel<2><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
+            break;
+        case 4:
+            e = cudaFuncSetAttribute(cost_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e == cudaSuccess) cost_tc_kernel<4><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
+            break;
+        default:
+            return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 }  // namespace sdtw

@@ -36,6 +36,7 @@ _SIGS = {
     "sdtw_timing_read": ([ctypes.c_char_p, _SZ, _P, _P, _I], _I),
     "sdtw_set_plan_override": ([_I, _I, _I], None),
     "sdtw_plan_info": ([_I, _I, _I, _P], _I),
+    "sdtw_launch_count": ([], ctypes.c_ulonglong),
     "sdtw_score_elems": ([_I, _I, _I], _SZ),
     "sdtw_cost_elems": ([_I, _I, _I], _SZ),
     "sdtw_workspace_bytes": ([_I, _I, _I], _SZ),
@@ -83,11 +84,11 @@ class NativeError(RuntimeError):
     pass
 
 
-# Kernel-launch accounting: number of library kernels each entry point enqueues.
-KERNELS_PER_OP = {"cost": 1, "forward": 2, "backward": 2, "forward_xy": 2, "backward_xy": 4,
-                  "forward_sqeuclid": 2, "backward_sqeuclid": 4, "grad_sqeuclid": 2, "score_to_R": 1,
-                  "R_to_score": 1}
-launch_count = 0
+def launches() -> int:
+    """Kernels the library has launched since it was loaded (its own counter)."""
+    return int(lib().sdtw_launch_count())
+
+
 # When a list, every op appends (name, start_event, end_event) recorded on the
 # stream it launched on (used by bench.py for per-kernel timing).
 profile_events = None
@@ -102,8 +103,6 @@ def _op_begin(device):
 
 
 def _op_end(name, device, ev0, n_kernels=None):
-    global launch_count
-    launch_count += KERNELS_PER_OP[name] if n_kernels is None else n_kernels
     if ev0 is not None:
         ev1 = torch.cuda.Event(enable_timing=True)
         ev1.record(torch.cuda.current_stream(device))
