@@ -241,12 +241,37 @@ WavePlan plan(int B, int N, int M) {
 // Workspace layouts (each region 256-byte aligned):
 //   D-input forward/backward : [wrap ring][WL table]
 //   x/y forward              : [wrap ring][WL cost]
-//   x/y backward, sqeuclid bwd: [wrap ring][WL E]
+//   x/y backward, sqeuclid bwd: [wrap ring][WL E][gradient operands]
+//     one row per lane: x, y in the chunked transposed layout (B, ceil(N/32),
+//     dim, 36) and (B, ceil(M/32), dim, 36);
+//     more rows per lane: G, G^T, x^T, y^T row-major, rows padded to a
+//     multiple of 32 floats
 size_t wave_ws(int B, int N, int M) {
     WavePlan p = plan(B, N, M);
     return align_up(wrap_bytes(p), 256);
 }
 size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
+size_t pad32(int n) { return (static_cast<size_t>(n) + 31) & ~static_cast<size_t>(31); }
+struct GradOperands {
+    size_t g, gt, xt, yt, total;  // byte offsets from the start of the region
+};
+GradOperands grad_operands(int B, int N, int M, int dim) {
+    GradOperands o;
+    const size_t b = static_cast<size_t>(B);
+    if (rows_per_lane(N, g_k_override.load()) == 1) {  // xTc, yTc: rows of 36 floats per 32 positions
+        o.g = o.gt = 0;
+        o.xt = 0;
+        o.yt = align_up(b * (pad32(N) / 32) * dim * 36 * sizeof(float), 256);
+        o.total = o.yt + align_up(b * (pad32(M) / 32) * dim * 36 * sizeof(float), 256);
+        return o;
+    }
+    o.g = 0;
+    o.gt = o.g + align_up(b * N * pad32(M) * sizeof(float), 256);
+    o.xt = o.gt + align_up(b * M * pad32(N) * sizeof(float), 256);
+    o.yt = o.xt + align_up(b * dim * pad32(N) * sizeof(float), 256);
+    o.total = o.yt + align_up(b * dim * pad32(M) * sizeof(float), 256);
+    return o;
+}
 
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream) {
@@ -422,7 +447,7 @@ size_t sdtw_workspace_bytes(int B, int N, int M) {
 
 size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim) {
     if (B <= 0 || N <= 0 || M <= 0 || dim <= 0) return 0;
-    return wave_ws(B, N, M) + wl_bytes(B, N, M);
+    return wave_ws(B, N, M) + wl_bytes(B, N, M) + grad_operands(B, N, M, dim).total;
 }
 
 int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int N, int M, int dim, int direct,
@@ -517,22 +542,55 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     g.gx = grad_x;
     g.gy = grad_y;
     g.dim = dim;
-    grad_tc_geometry(dim, mask_w != nullptr, &g.fb, &g.nt, &g.n_fblk, &g.tmem_cols, &g.stages);
-    {
-        // Tuning knob: SDTW_GRAD_STAGES=2 trades pipeline depth for two CTAs per SM.
-        static const int env_stages = [] {
-            const char* v = std::getenv("SDTW_GRAD_STAGES");
-            return v ? std::atoi(v) : 0;
-        }();
-        if (env_stages == 2 || (env_stages == 3 && g.stages == 3)) g.stages = env_stages;
-    }
     g.tiles_x = grad_x ? (N + 127) / 128 : 0;
     g.tiles_y = grad_y ? (M + 127) / 128 : 0;
     g.wait = wait_ctx();
     cudaError_t e;
+    char* region = static_cast<char*>(workspace) + w0 + wl_bytes(B, N, M);
+    const GradOperands o = grad_operands(B, N, M, dim);
+    if (grad_wl_supported(g.P) && (reinterpret_cast<uintptr_t>(mask_w) & 15u) == 0) {
+        // G straight from the wavefront layout; x, y in the chunked transposed layout.
+        float* xTc = reinterpret_cast<float*>(region + o.xt);
+        float* yTc = reinterpret_cast<float*>(region + o.yt);
+        {
+            KernelTimer kt("grad_operands", st, (grad_x ? 1 : 0) + (grad_y ? 1 : 0));
+            e = cudaSuccess;
+            if (grad_x) e = launch_transpose_chunked(y, yTc, B, M, dim, st);
+            if (e == cudaSuccess && grad_y) e = launch_transpose_chunked(x, xTc, B, N, dim, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "layout launch");
+        g.xTc = xTc;
+        g.yTc = yTc;
+        grad_wl_geometry(dim, mask_w != nullptr, &g);
+        {
+            KernelTimer kt("grad_xy", st);
+            e = launch_grad_wl(g, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+        return SDTW_OK;
+    }
+    // More rows per lane: operands in row-major layouts (mask applied to G),
+    // then the tensor-core contractions with 16-byte operand copies.
+    float* G = reinterpret_cast<float*>(region + o.g);
+    float* GT = reinterpret_cast<float*>(region + o.gt);
+    float* xT = reinterpret_cast<float*>(region + o.xt);
+    float* yT = reinterpret_cast<float*>(region + o.yt);
+    const int Np = static_cast<int>(pad32(N)), Mp = static_cast<int>(pad32(M));
+    {
+        KernelTimer kt("grad_operands", st, 1 + (grad_x ? 1 : 0) + (grad_y ? 1 : 0));
+        e = launch_wl_to_rm_cm(Ew, mask_w, grad_x ? G : nullptr, Mp, grad_y ? GT : nullptr, Np, g.P, st);
+        if (e == cudaSuccess && grad_x) e = launch_transpose_brc(y, yT, B, M, dim, Mp, st);
+        if (e == cudaSuccess && grad_y) e = launch_transpose_brc(x, xT, B, N, dim, Np, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "layout launch");
+    g.G = G;
+    g.GT = GT;
+    g.xT = xT;
+    g.yT = yT;
+    grad_rm_geometry(dim, &g.fb, &g.nt, &g.n_fblk, &g.tmem_cols, &g.stages);
     {
         KernelTimer kt("grad_xy", st);
-        e = launch_grad_tc(g, st);
+        e = launch_grad_rm(g, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "grad launch");
     return SDTW_OK;

@@ -15,6 +15,8 @@
 //   rm_to_wl_kernel   row-major (B,N,M) -> WL (caller-supplied cost matrices)
 //   wl_to_rm_kernel   WL -> row-major, optionally multiplied by (D_wl > 0),
 //                     the clamp mask of the unfused cost's chain rule
+//   wl_to_rm_cm_kernel  the same, writing the table and its transpose
+//   transpose_kernel  (B,R,C) -> (B,C,R) (feature-major copies of x and y)
 #include <algorithm>
 #include <cstdint>
 
@@ -223,6 +225,113 @@ __global__ void __launch_bounds__(256) wl_to_rm_kernel(const float* __restrict__
     }
 }
 
+// Both row-major A (B,N,lda) and AT (B,M,ldt) from the WL table, by rectangles
+// of 32K rows x CB = 4096 / (32K) columns: the WL rows t in [j0, j0 + CB +
+// 32K - 1) of the stripe hold the rectangle, each row read once by one warp
+// (the neighbouring rectangles read the overlap, mostly from L2).  Both stores
+// are then aligned runs: 128-byte runs of A's rows and 32K-float runs of AT's
+// rows.  The padding columns (M .. lda of A, N .. ldt of AT) are written as
+// zeros.  The tile pitch CB + 2 keeps the skewed writes (cell (q, t - q)) on
+// distinct banks for K = 1.
+template <int K>
+__global__ void __launch_bounds__(256) wl_to_rm_cm_kernel(const float* __restrict__ Aw, const float* __restrict__ maskw,
+                                                          float* __restrict__ A, int lda, float* __restrict__ AT,
+                                                          int ldt, WavePlan P) {
+    constexpr int SR = 32 * K, CB = 4096 / SR, PITCH = CB + 2;
+    __shared__ float tile[SR * PITCH];
+    const int j0 = blockIdx.x * CB;
+    const int s = blockIdx.y;
+    const int b = blockIdx.z;
+    const int R0 = s * SR;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t_end = min(j0 + CB, P.M) + SR - 1;
+#pragma unroll 4
+    for (int t = j0 + warp; t < t_end; t += 8) {
+        const size_t base = wl_row_base(P, b, s, t);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            float v = __ldg(Aw + base + k * 32 + lane);
+            if (maskw && !(__ldg(maskw + base + k * 32 + lane) > 0.f)) v = 0.f;
+            const int q = lane * K + k;
+            const int c = t - q - j0;
+            if (c >= 0 && c < CB) tile[q * PITCH + c] = v;
+        }
+    }
+    __syncthreads();
+    if (A) {
+        for (int q = warp; q < SR; q += 8) {
+            const int row = R0 + q;
+            if (row >= P.N) break;
+            float* dst = A + (static_cast<size_t>(b) * P.N + row) * lda;
+#pragma unroll
+            for (int c = lane; c < CB; c += 32) {
+                const int col = j0 + c;
+                if (col < P.M) dst[col] = tile[q * PITCH + c];
+                else if (col < lda) dst[col] = 0.f;
+            }
+        }
+    }
+    if (AT) {
+        for (int c = warp; c < CB; c += 8) {
+            const int col = j0 + c;
+            if (col >= P.M) break;
+            float* dst = AT + (static_cast<size_t>(b) * P.M + col) * ldt;
+#pragma unroll
+            for (int q = lane; q < SR; q += 32) {
+                const int row = R0 + q;
+                if (row < P.N) dst[row] = tile[q * PITCH + c];
+                else if (row < ldt) dst[row] = 0.f;
+            }
+        }
+    }
+}
+
+// 32 x 32 tiles through shared memory; grid (ceil(C/32), ceil(ldo/32), B).
+// Output columns R .. ldo are written as zeros.
+__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int R,
+                                                        int C, int ldo) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    const size_t in_off = static_cast<size_t>(blockIdx.z) * R * C;
+    const size_t out_off = static_cast<size_t>(blockIdx.z) * C * ldo;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = warp; i < 32; i += 8) {
+        const int r = r0 + i, c = c0 + lane;
+        if (r < R && c < C) tile[i][lane] = __ldg(in + in_off + static_cast<size_t>(r) * C + c);
+    }
+    __syncthreads();
+    for (int i = warp; i < 32; i += 8) {
+        const int c = c0 + i, r = r0 + lane;
+        if (r < ldo && c < C) out[out_off + static_cast<size_t>(c) * ldo + r] = r < R ? tile[lane][i] : 0.f;
+    }
+}
+
+// 32 x 32 blocks (32 sequence positions x 32 features) through shared memory;
+// grid (ceil(R/32), ceil(C/32), B).  Output rows are 36 floats: 32 positions
+// and 4 zeros.
+__global__ void __launch_bounds__(256) transpose_chunked_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                                                int R, int C) {
+    __shared__ float tile[32][33];
+    const int c = blockIdx.x, f0 = blockIdx.y * 32;
+    const int n_chunks = (R + 31) / 32;
+    const size_t in_off = static_cast<size_t>(blockIdx.z) * R * C;
+    const size_t out_off = (static_cast<size_t>(blockIdx.z) * n_chunks + c) * C * 36;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = warp; i < 32; i += 8) {
+        const int r = 32 * c + i, f = f0 + lane;
+        tile[i][lane] = (r < R && f < C) ? __ldg(in + in_off + static_cast<size_t>(r) * C + f) : 0.f;
+    }
+    __syncthreads();
+    for (int i = warp; i < 32; i += 8) {
+        const int f = f0 + i;
+        if (f < C) {
+            float* row = out + out_off + static_cast<size_t>(f) * 36;
+            row[lane] = tile[lane][i];
+            if (lane < 4) row[32 + lane] = 0.f;
+        }
+    }
+}
+
 static dim3 wl_grid(const WavePlan& P) {
     return dim3((P.n_diag + kTB - 1) / kTB, P.n_stripes, P.B);
 }
@@ -290,6 +399,34 @@ cudaError_t launch_wl_to_rm(const float* Aw, const float* maskw, float* A, const
         case 4: wl_to_rm_kernel<4><<<g, 256, 0, stream>>>(Aw, maskw, A, P); break;
         default: return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_wl_to_rm_cm(const float* Aw, const float* maskw, float* A, int lda, float* AT, int ldt,
+                               const WavePlan& P, cudaStream_t stream) {
+    if (lda < P.M || ldt < P.N) return cudaErrorInvalidValue;
+    const int cb = 4096 / (32 * P.K);
+    const dim3 g((P.M + cb - 1) / cb, P.n_stripes, P.B);
+    switch (P.K) {
+        case 1: wl_to_rm_cm_kernel<1><<<g, 256, 0, stream>>>(Aw, maskw, A, lda, AT, ldt, P); break;
+        case 2: wl_to_rm_cm_kernel<2><<<g, 256, 0, stream>>>(Aw, maskw, A, lda, AT, ldt, P); break;
+        case 4: wl_to_rm_cm_kernel<4><<<g, 256, 0, stream>>>(Aw, maskw, A, lda, AT, ldt, P); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_chunked(const float* in, float* out, int B, int R, int C, cudaStream_t stream) {
+    if (B <= 0 || R <= 0 || C <= 0) return cudaSuccess;
+    const dim3 g((R + 31) / 32, (C + 31) / 32, B);
+    transpose_chunked_kernel<<<g, 256, 0, stream>>>(in, out, R, C);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_brc(const float* in, float* out, int B, int R, int C, int ldo, cudaStream_t stream) {
+    if (B <= 0 || R <= 0 || C <= 0) return cudaSuccess;
+    const dim3 g((C + 31) / 32, (ldo + 31) / 32, B);
+    transpose_kernel<<<g, 256, 0, stream>>>(in, out, R, C, ldo);
     return cudaGetLastError();
 }
 

@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "sdtw_device.cuh"
@@ -50,6 +51,15 @@ cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const Wave
                            cudaStream_t stream);
 cudaError_t launch_rm_to_wl(const float* A, float* Aw, const WavePlan& P, cudaStream_t stream);
 cudaError_t launch_wl_to_rm(const float* Aw, const float* maskw, float* A, const WavePlan& P, cudaStream_t stream);
+// WL -> row-major A (B,N,lda) and its transpose AT (B,M,ldt), with the optional
+// mask; lda >= M, ldt >= N are the row pitches (padding written as zeros).
+cudaError_t launch_wl_to_rm_cm(const float* Aw, const float* maskw, float* A, int lda, float* AT, int ldt,
+                               const WavePlan& P, cudaStream_t stream);
+// (B,R,C) -> (B,C,ldo), ldo >= R, columns R .. ldo zero.
+// (B,R,C) -> chunked (B, ceil(R/32), C, 36): out[b][c][f][kk] = in[b][32c+kk][f]
+// for kk < 32, zero for 32c+kk >= R and for kk >= 32.
+cudaError_t launch_transpose_chunked(const float* in, float* out, int B, int R, int C, cudaStream_t stream);
+cudaError_t launch_transpose_brc(const float* in, float* out, int B, int R, int C, int ldo, cudaStream_t stream);
 
 // dense.cu
 cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, int M, int dim, bool direct,
@@ -59,8 +69,21 @@ cudaError_t launch_grad_xy(const float* G, const float* mask, const float* x, co
 
 // tcgemm.cu: grad_x / grad_y from E in the wavefront layout on the tensor cores.
 struct GradTcArgs {
+    // grad_wl: 2-D views (rows of 32 floats) of E and of the mask for the
+    // grad_y tiles' tensor copies; filled in by launch_grad_wl.
+    alignas(64) CUtensorMap tm_e;
+    alignas(64) CUtensorMap tm_m;
     WavePlan P;
-    const float* Ew;  // E in the wavefront layout
+    const float* Ew;  // E in the wavefront layout (grad_wl)
+    // grad_wl: x and y in the chunked transposed layout [b][c][f][kk] = x[b][32c+kk][f],
+    // rows of 36 floats (the last 4 zero)
+    const float* xTc;
+    const float* yTc;
+    // grad_rm operands, rows zero-padded to Np = N rounded up to 32, Mp likewise:
+    const float* G;   // G = E (clamp mask applied) (B,N,Mp)
+    const float* GT;  // G transposed (B,M,Np)
+    const float* xT;  // x transposed (B,dim,Np)
+    const float* yT;  // y transposed (B,dim,Mp)
     const float* Mw;  // unfused cost in the wavefront layout (clamp mask: G = E * (D > 0)), or null
     const float* x;   // (B,N,dim)
     const float* y;   // (B,M,dim)
@@ -68,16 +91,23 @@ struct GradTcArgs {
     float* gy;        // (B,M,dim) or null
     int dim;
     int fb;           // features per block
-    int nt;           // MMA N: fb + 1 (ones column) rounded up to 16
+    int nt;           // fb rounded up to 16
     int n_fblk;       // feature blocks
     int tiles_x;      // 128-row tiles of grad_x per problem (0 when gx is null)
     int tiles_y;      // 128-row tiles of grad_y per problem (0 when gy is null)
     int tmem_cols;    // tensor-memory columns allocated per CTA (power of two >= nt)
-    int stages;       // shared-memory pipeline depth (2 or 3)
+    int stages;       // shared-memory pipeline depth (grad_rm)
+    int stages_x;     // ring slots of the grad_x tiles (grad_wl)
+    int stages_y;     // ring slots of the grad_y tiles (grad_wl)
     WaitCtx wait;
 };
-void grad_tc_geometry(int dim, bool masked, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages);
-cudaError_t launch_grad_tc(const GradTcArgs& args, cudaStream_t stream);
+// From E in the wavefront layout with bulk copies (one row per lane only).
+bool grad_wl_supported(const WavePlan& P);
+void grad_wl_geometry(int dim, bool masked, GradTcArgs* g);
+cudaError_t launch_grad_wl(const GradTcArgs& args, cudaStream_t stream);
+// The same from row-major G, G^T, x^T and y^T (16-byte operand copies).
+void grad_rm_geometry(int dim, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages);
+cudaError_t launch_grad_rm(const GradTcArgs& args, cudaStream_t stream);
 // tcgemm.cu: the unfused (expanded, clamped) cost on the tensor cores, written
 // in the wavefront layout.  Requires dim >= 16, dim % 4 == 0 and 16-byte
 // aligned x, y (cost_tc_supported).

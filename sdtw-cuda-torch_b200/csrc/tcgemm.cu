@@ -6,22 +6,24 @@
 //   grad_y[b,j,:] = 2 (y_j * sum_q G(q,j) - sum_q G(q,j) x_q)
 //
 // G = E, the reverse pass's output (fused cost), or E * (D > 0), the clamp mask
-// of the unfused cost; both are read straight from the wavefront layout.  This
-// replaces the two bmm of softdtw_cuda/autograd_xy.py:41-49 (fused) and torch's
-// autograd of softdtw_cuda/distances.py:20-28 (unfused).
+// of the unfused cost.  This replaces the two bmm of
+// softdtw_cuda/autograd_xy.py:41-49 (fused) and torch's autograd of
+// softdtw_cuda/distances.py:20-28 (unfused).
 //
 // One CTA (8 warps) computes a 128-row output tile (rows q for grad_x, rows j
 // for grad_y) for one block of features.  Per K chunk of 32 it stages the G tile
 // and the x or y tile in shared memory, each split into a tf32-exact high part
 // (low 13 mantissa bits cleared) and the float32 remainder; one thread issues
-// hi*hi + hi*lo + lo*hi as tcgen05.mma kind::tf32 (M=128, N = features + 1,
-// K = 8 per instruction) into one float32 accumulator in tensor memory.  The
-// extra column of ones in the B operand makes the accumulator's last column the
-// row (or column) sum of G.  Two or three stages fed by cp.async: the copies
-// of the next chunks overlap the split and MMAs of the current one, and the
-// MMAs signal completion through an mbarrier (tcgen05.commit).  The epilogue reads the accumulator with tcgen05.ld
-// (warp w may read tensor-memory lanes 32(w%4)..32(w%4)+31, i.e. those tile
-// rows; the two warp groups take alternate 16-column chunks).
+// the tcgen05.mma kind::tf32 instructions (M = 128, K = 8 per instruction) into
+// float32 accumulators in tensor memory, and the MMAs signal completion through
+// an mbarrier (tcgen05.commit).  The epilogue reads the accumulator with
+// tcgen05.ld (warp w may read tensor-memory lanes 32(w%4)..32(w%4)+31, i.e.
+// those tile rows; the two warp groups take alternate 16-column chunks).
+#include <algorithm>
+#include <type_traits>
+
+#include <cudaTypedefs.h>
+
 #include "sdtw_device.cuh"
 #include "sdtw_kernels.h"
 
@@ -144,42 +146,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     v[15] = __uint_as_float(r15);
 }
 
-// 4-byte asynchronous global -> shared copy; src_bytes = 0 writes zero and
-// reads nothing (the address is still a valid one).
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// Splits the float32 at hi_base + off in place into its tf32-exact high part
-// (low 13 mantissa bits cleared) and writes the float32 remainder to lo_base +
-// off; with a mask value, elements whose mask is not > 0 become zero.
-__device__ __forceinline__ void split_in_place(unsigned char* hi_base, unsigned char* lo_base, uint32_t off) {
-    const float v = *reinterpret_cast<const float*>(hi_base + off);
-    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-    *reinterpret_cast<float*>(hi_base + off) = h;
-    *reinterpret_cast<float*>(lo_base + off) = v - h;
-}
-__device__ __forceinline__ void split_in_place_masked(unsigned char* hi_base, unsigned char* lo_base,
-                                                      const unsigned char* mask_base, uint32_t off) {
-    float v = *reinterpret_cast<const float*>(hi_base + off);
-    if (!(*reinterpret_cast<const float*>(mask_base + off) > 0.f)) v = 0.f;
-    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-    *reinterpret_cast<float*>(hi_base + off) = h;
-    *reinterpret_cast<float*>(lo_base + off) = v - h;
-}
-
-// Stores v as a tf32-exact high part and the float32 remainder.
-__device__ __forceinline__ void st_split(unsigned char* hi_base, unsigned char* lo_base, uint32_t off, float v) {
-    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-    *reinterpret_cast<float*>(hi_base + off) = h;
-    *reinterpret_cast<float*>(lo_base + off) = v - h;
-}
-
 // Bounded wait for an mbarrier phase; false (and an error record) on timeout.
 __device__ __noinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, const WaitCtx& w) {
     uint64_t t0 = 0;
@@ -197,294 +163,221 @@ __device__ __noinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, const Wai
 
 using namespace tc;
 
-// Grid: x = (tiles_x + tiles_y) * n_fblk, y = problem.  blockIdx.x below
-// tiles_x * n_fblk computes a grad_x tile, the rest grad_y tiles.
+// ============================================================== gradients from row-major G
+// The same contractions from operands in plain row-major layouts, so that
+// every operand load is a coalesced 16-byte load: grad_x's A = G (rows q,
+// K = j) and B = y^T (rows = features, K = j); grad_y's A = G^T (rows j,
+// K = q) and B = x^T (rows = features, K = q).  G and G^T (clamp mask applied)
+// come from the wavefront layout through wl_to_rm_cm_kernel, x^T and y^T from
+// transpose_kernel; each has its rows padded with zeros to a multiple of 32
+// floats, so a K chunk never needs a bound check.
 //
-// Loading the G tile.  A 128 x 32 tile of G is skewed in the wavefront layout
-// (cell (q, j) of stripe s sits in anti-diagonal row t = q_local + j), so each
-// warp walks one "diagonal" d of the tile per iteration: lane l takes the slot
-// of its row whose column makes t = const (or const + 32 m), which puts the 32
-// lanes on at most K+1 anti-diagonal rows at consecutive positions (coalesced)
-// and makes every loaded element a slot of this tile (no waste).  With
-//   grad_x: rows q (tile), K = j (chunk): lane l, sub-row k: qloc = l*K + k,
-//           kk = (d - qloc) mod 32, t = k0 + qloc + kk
-//   grad_y: rows j (tile), K = q (chunk): lane pi: qloc = qb + pi,
-//           jr = (d - pi) mod 128, t = r0 + qloc + jr
-// 128 warp-iterations cover the 4096 slots of the tile: 16 per thread.  A
-// slot's wavefront-layout offset relative to a per-chunk base, its
-// shared-memory offset and its validity do not change from chunk to chunk, so
-// they are computed once; only the last chunk (partial in K) checks the
-// column or row against the sequence length.  The B tile is the block of 32
-// rows of x or y; its ones column and zero padding never change and are
-// written once.
-//
-// Pipeline: every thread copies its slots with 4-byte cp.async straight into
-// the high-part buffer of a stage (zero-filled where out of range), up to
-// `stages - 1` chunks ahead; when a chunk has landed, each thread splits its
-// own slots in place (high part, remainder into the low-part buffer, the
-// clamp mask applied from a third buffer), then one thread issues the MMAs.
-// A stage is refilled once the mbarrier of its previous MMAs has completed.
-template <int K, int NB, bool is_x>
-__device__ __forceinline__ void grad_tile(const GradTcArgs& a, unsigned char* smem_raw) {
-    constexpr int SR = 32 * K;
-    constexpr int APER = kTileM * kKT / kThreads;  // A slots per thread (16)
+// Each thread loads its 16-byte units of a chunk into registers two chunks
+// ahead, splits them there into the tf32 high part and the remainder, and
+// stores both into one of two shared-memory buffers.  B is stored as
+// B' = [B_lo ; B_hi ; ones(16)], so that 3xTF32 and the row sums take two MMAs
+// per K step (A is read twice, not three times, from shared memory):
+//     D[:, 0 .. 2nt+16)   += A_hi * B'          (N = 2nt + 16)
+//     D[:, nt .. 2nt+16)  += A_lo * [B_hi ; 1]  (N = nt + 16)
+// giving A*B = D[:, 0..nt) + D[:, nt..2nt) and sum_k A = D[:, 2nt].  nt <= 112
+// keeps N <= 256 and (at nt <= 64) two CTAs per SM.
+constexpr int kRmMaxNt = 112;
+
+// Thread t's i-th 16-byte unit of a 32-wide K chunk (i < 4): row
+// 8 * (c >> 1) + (lane & 7), column 4 * (4 * (c & 1) + (lane >> 3)) with
+// c = warp + 8 i; 8 consecutive lanes cover 8 rows of one 16-byte column, 128
+// contiguous bytes of the shared-memory layout (no bank conflicts), and each
+// row is read as two full 32-byte sectors.
+__device__ __forceinline__ int rm_row(int warp, int lane, int i) { return 8 * ((warp + 8 * i) >> 1) + (lane & 7); }
+__device__ __forceinline__ int rm_col(int warp, int lane, int i) {
+    return 4 * (4 * ((warp + 8 * i) & 1) + (lane >> 3));
+}
+
+__device__ __forceinline__ void st_split4(unsigned char* hi, unsigned char* lo, uint32_t off_hi, uint32_t off_lo,
+                                          float4 v) {
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    l.x = v.x - h.x;
+    l.y = v.y - h.y;
+    l.z = v.z - h.z;
+    l.w = v.w - h.w;
+    *reinterpret_cast<float4*>(hi + off_hi) = h;
+    *reinterpret_cast<float4*>(lo + off_lo) = l;
+}
+
+template <int S>
+using Slot = std::integral_constant<int, S>;
+
+template <bool GX>
+__device__ __forceinline__ void grad_rm_tile(const GradTcArgs& a, unsigned char* smem_raw) {
     const WavePlan& P = a.P;
     const int N = P.N, M = P.M, dim = a.dim;
     const int b = blockIdx.y;
-    const int nt = a.nt;
+    const int nt = a.nt;  // B rows: the feature block rounded up to 16
     const int fb = a.fb;
-    const int S = a.stages;
-    const bool masked = a.Mw != nullptr;
-    const int local = is_x ? blockIdx.x : blockIdx.x - a.tiles_x * a.n_fblk;
+    const int local = GX ? blockIdx.x : blockIdx.x - a.tiles_x * a.n_fblk;
     const int tile = local / a.n_fblk;
-    const int f0 = (local % a.n_fblk) * fb;  // first feature of this block
-    const int r0 = tile * kTileM;            // first output row (q for grad_x, j for grad_y)
-    const int k_total = is_x ? M : N;        // contraction length
-    const int rows_other = is_x ? M : N;
-    const int n_chunks = (k_total + kKT - 1) / kKT;
-    const float* __restrict__ Ew = a.Ew;
-    const float* __restrict__ Mw = a.Mw;
-    const float* __restrict__ ob = (is_x ? a.y : a.x) + static_cast<size_t>(b) * rows_other * dim + f0;
-    const size_t prob = static_cast<size_t>(b) * P.n_stripes;
+    const int f0 = (local % a.n_fblk) * fb;
+    const int r0 = tile * kTileM;
+    const int rows_out = GX ? N : M;  // rows of A (output rows)
+    const int kt = GX ? M : N;        // contraction length
+    const int ld = (kt + 31) & ~31;   // row pitch of A and of B
+    const int n_chunks = ld / kKT;
+    const float* __restrict__ Ag = (GX ? a.G : a.GT) + static_cast<size_t>(b) * rows_out * ld;
+    const float* __restrict__ Bg = (GX ? a.yT : a.xT) + static_cast<size_t>(b) * dim * ld;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b_units = nt / 4;  // (row group, column half) pairs of B
 
-    // Shared memory per stage: A_hi, A_lo (128 x 32), [mask raw (128 x 32)],
-    // B_hi, B_lo (nt x 32); then the mbarriers and the tensor-memory address.
     const uint32_t a_bytes = kTileM / 8 * kSBO;
-    const uint32_t b_bytes = static_cast<uint32_t>(nt) / 8 * kSBO;
-    const uint32_t m_bytes = masked ? a_bytes : 0u;
-    const uint32_t stage_bytes = 2 * a_bytes + m_bytes + 2 * b_bytes;
-    unsigned char* ctrl = smem_raw + S * stage_bytes;
+    const uint32_t b_bytes = static_cast<uint32_t>(2 * nt + 16) / 8 * kSBO;
+    const uint32_t buf_bytes = 2 * a_bytes + b_bytes;
+    unsigned char* ctrl = smem_raw + 2 * buf_bytes;
     uint64_t* mbar = reinterpret_cast<uint64_t*>(ctrl);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 64);
     const uint32_t smem_base = smem_addr(smem_raw);
-    auto sA_hi = [&](int st) { return smem_raw + st * stage_bytes; };
-    auto sMk = [&](int st) { return smem_raw + st * stage_bytes + 2 * a_bytes; };
-    auto sB_hi = [&](int st) { return smem_raw + st * stage_bytes + 2 * a_bytes + m_bytes; };
 
     WaitCtx wc = a.wait;
     wc.kernel = 5;
     wc.problem = b;
     wc.warp = blockIdx.x;
-    wc.band = 0;
+    wc.band = 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) mbar_init(smem_addr(mbar + s), 1);
+        mbar_init(smem_addr(mbar + 0), 1);
+        mbar_init(smem_addr(mbar + 1), 1);
         fence_mbar_init();
     }
     if (warp == 0) {
         tmem_alloc(smem_addr(tmem_slot), static_cast<uint32_t>(a.tmem_cols));
         tmem_relinquish();
     }
-    // Constant B columns of every stage: ones at fb (row/column sums), zeros
-    // above it.
-    for (int e = threadIdx.x; e < (nt - fb) * kKT; e += kThreads) {
-        const int f = fb + e % (nt - fb);
-        const int kk = e / (nt - fb);
-        for (int s = 0; s < S; ++s) {
-            unsigned char* bh = sB_hi(s);
-            const float v = f == fb ? 1.f : 0.f;
-            *reinterpret_cast<float*>(bh + op_off(f, kk)) = v;
-            *reinterpret_cast<float*>(bh + b_bytes + op_off(f, kk)) = 0.f;
-        }
+    for (int e = threadIdx.x; e < 2 * 16 * kKT; e += kThreads) {  // the ones rows of both buffers
+        const int bi = e / (16 * kKT), r = (e / kKT) % 16, k = e % kKT;
+        *reinterpret_cast<float*>(smem_raw + bi * buf_bytes + 2 * a_bytes + op_off(2 * nt + r, k)) = 1.f;
     }
 
-    // ---- per-thread slots (chunk-invariant).
-    // A: wavefront-layout offset relative to the chunk base; meta = shared
-    // offset | kk << 16 (grad_x: column in the chunk) | valid << 24.
-    uint32_t a_goff[APER], a_meta[APER];
+    float4 ra[2][4], rb[2][4];
+    auto load = [&](auto slot, int c) {
+        constexpr int S = decltype(slot)::value;
+        const int k0 = c * kKT;
 #pragma unroll
-    for (int i = 0; i < APER; ++i) {
-        const int it = warp + (kThreads / 32) * i;
-        uint32_t goff, soff, kk = 0, valid;
-        if constexpr (is_x) {
-            const int d = it & 31;
-            const int rest = it >> 5;  // (stripe of the tile, sub-row)
-            const int k = rest % K;
-            const int sl = rest / K;
-            const int qloc = lane * K + k;
-            const int c = (d - qloc) & 31;
-            goff = static_cast<uint32_t>((sl * P.n_diag + qloc + c) * SR + k * 32 + lane);
-            soff = op_off(sl * SR + qloc, c);
-            kk = static_cast<uint32_t>(c);
-            valid = (r0 + sl * SR + qloc) < N;
-        } else {
-            const int jr = (it - lane) & (kTileM - 1);
-            goff = static_cast<uint32_t>((jr + lane) * SR + (lane % K) * 32 + lane / K);
-            soff = op_off(jr, lane);
-            valid = (r0 + jr) < M;
+        for (int i = 0; i < 4; ++i) {
+            const int row = r0 + rm_row(warp, lane, i);
+            ra[S][i] = row < rows_out
+                           ? __ldg(reinterpret_cast<const float4*>(Ag + static_cast<size_t>(row) * ld + k0 +
+                                                                   rm_col(warp, lane, i)))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        a_goff[i] = goff;
-        a_meta[i] = soff | (kk << 16) | (valid << 24);
-    }
-    // B: the rows k0 .. k0+31 of x or y, features f0 .. f0+fb-1: element e of
-    // the block (row e / fb, feature e % fb).  meta = shared offset | row << 16 |
-    // slot exists << 24 | feature in range << 25.
-    const int nb_elems = kKT * fb;
-    uint32_t b_goff[NB], b_meta[NB];
 #pragma unroll
-    for (int u = 0; u < NB; ++u) {
-        const int e = threadIdx.x + kThreads * u;
-        const int kk = e / fb, f = e - (e / fb) * fb;  // kk < 32 whenever e < nb_elems
-        const bool exists = e < nb_elems;
-        const bool fin = exists && f0 + f < dim;
-        b_goff[u] = fin ? static_cast<uint32_t>(kk * dim + f) : 0u;
-        b_meta[u] = exists ? (op_off(f, kk) | (static_cast<uint32_t>(kk) << 16) | (1u << 24) |
-                              (static_cast<uint32_t>(fin) << 25))
-                           : 0u;
-    }
+        for (int i = 0; i < 4; ++i) {
+            const int fr = rm_row(warp, lane, i);
+            const bool ok = warp + 8 * i < b_units && fr < fb && f0 + fr < dim;
+            rb[S][i] = ok ? __ldg(reinterpret_cast<const float4*>(Bg + static_cast<size_t>(f0 + fr) * ld + k0 +
+                                                                  rm_col(warp, lane, i)))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store = [&](auto slot, int c) {
+        constexpr int S = decltype(slot)::value;
+        unsigned char* Ah = smem_raw + (c & 1) * buf_bytes;
+        unsigned char* Al = Ah + a_bytes;
+        unsigned char* Bp = Al + a_bytes;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t off = op_off(rm_row(warp, lane, i), rm_col(warp, lane, i));
+            st_split4(Ah, Al, off, off, ra[S][i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (warp + 8 * i < b_units) {
+                const int fr = rm_row(warp, lane, i), k = rm_col(warp, lane, i);
+                st_split4(Bp, Bp, op_off(nt + fr, k), op_off(fr, k), rb[S][i]);
+            }
+        }
+    };
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t idesc = idesc_tf32(kTileM, nt);
-
-    auto issue_chunk = [&](int c) {
-        const int st = c % S;
-        const int k0 = c * kKT;
-        const bool last = (c == n_chunks - 1);
-        size_t base;
-        if constexpr (is_x) {
-            base = ((prob + r0 / SR) * P.n_diag + k0) * SR;
-        } else {
-            const int s = k0 / SR;
-            const int qb = k0 - s * SR;
-            base = ((prob + s) * P.n_diag + r0 + qb) * SR + qb / K;
-        }
-        const float* Eb = Ew + base;
-        const float* Mb = masked ? Mw + base : nullptr;
-        const bool q_ok = is_x || (k0 + lane < N);  // grad_y: this lane's column q
-        const uint32_t dA = smem_addr(sA_hi(st));
-        const uint32_t dM = smem_addr(sMk(st));
-#pragma unroll
-        for (int i = 0; i < APER; ++i) {
-            bool ok = (a_meta[i] >> 24) & 1u;
-            if constexpr (is_x) ok = ok && (!last || k0 + static_cast<int>((a_meta[i] >> 16) & 0xFFu) < M);
-            else ok = ok && q_ok;
-            const uint32_t off = a_meta[i] & 0xFFFFu;
-            const uint32_t g = ok ? a_goff[i] : 0u;  // in range either way: nothing is read when !ok
-            cp_async4(dA + off, Eb + g, ok ? 4u : 0u);
-            if (masked) cp_async4(dM + off, Mb + g, ok ? 4u : 0u);
-        }
-        const float* Bb = ob + static_cast<size_t>(k0) * dim;
-        const uint32_t dB = smem_addr(sB_hi(st));
-#pragma unroll
-        for (int u = 0; u < NB; ++u) {
-            if ((b_meta[u] >> 24) & 1u) {
-                const bool ok = ((b_meta[u] >> 25) & 1u) &&
-                                (!last || k0 + static_cast<int>((b_meta[u] >> 16) & 0xFFu) < rows_other);
-                cp_async4(dB + (b_meta[u] & 0xFFFFu), ok ? Bb + b_goff[u] : ob, ok ? 4u : 0u);
-            }
-        }
-    };
-    auto split_chunk = [&](int st) {
-        unsigned char* ah = sA_hi(st);
-        unsigned char* bh = sB_hi(st);
-        if (masked) {
-            const unsigned char* mk = sMk(st);
-#pragma unroll
-            for (int i = 0; i < APER; ++i) split_in_place_masked(ah, ah + a_bytes, mk, a_meta[i] & 0xFFFFu);
-        } else {
-#pragma unroll
-            for (int i = 0; i < APER; ++i) split_in_place(ah, ah + a_bytes, a_meta[i] & 0xFFFFu);
-        }
-#pragma unroll
-        for (int u = 0; u < NB; ++u)
-            if ((b_meta[u] >> 24) & 1u) split_in_place(bh, bh + b_bytes, b_meta[u] & 0xFFFFu);
-    };
+    const uint32_t idesc1 = idesc_tf32(kTileM, 2 * nt + 16);
+    const uint32_t idesc2 = idesc_tf32(kTileM, nt + 16);
 
     bool ok = true;
-    // Prologue: chunks 0 .. S-2 in flight (one commit group per chunk slot, empty or not).
-    for (int c = 0; c < S - 1; ++c) {
-        if (c < n_chunks) issue_chunk(c);
-        cp_async_commit();
-    }
-    for (int c = 0; c < n_chunks; ++c) {
-        const int st = c % S;
-        // Groups committed so far: chunks 0 .. c+S-2; chunk c's is complete when
-        // at most S-2 newer ones are pending.
-        if (S == 3) cp_async_wait<1>();
-        else cp_async_wait<0>();
-        split_chunk(st);
+    auto step = [&](auto slot, int c) {
+        if (c >= 2 && ok) ok = mbar_wait(smem_addr(mbar + (c & 1)), static_cast<uint32_t>(((c - 2) >> 1) & 1), wc);
+        store(slot, c);
+        if (c + 2 < n_chunks) load(slot, c + 2);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
         if (threadIdx.x == 0 && ok) {
-            const uint32_t aH = smem_base + static_cast<uint32_t>(sA_hi(st) - smem_raw);
+            const uint32_t aH = smem_base + (c & 1) * buf_bytes;
             const uint32_t aL = aH + a_bytes;
-            const uint32_t bH = smem_base + static_cast<uint32_t>(sB_hi(st) - smem_raw);
-            const uint32_t bL = bH + b_bytes;
+            const uint32_t bP = aL + a_bytes;
+            const uint32_t bH = bP + static_cast<uint32_t>(nt / 8) * kSBO;
 #pragma unroll
             for (int ks = 0; ks < kKT / 8; ++ks) {
                 const uint32_t o = static_cast<uint32_t>(ks) * 2 * kLBO;
-                const uint32_t acc0 = (c > 0 || ks > 0) ? 1u : 0u;
-                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bH + o), idesc, acc0);
-                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bL + o), idesc, 1u);
-                mma_tf32(tmem, smem_desc(aL + o), smem_desc(bH + o), idesc, 1u);
+                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bP + o), idesc1, (c > 0 || ks > 0) ? 1u : 0u);
+                mma_tf32(tmem + static_cast<uint32_t>(nt), smem_desc(aL + o), smem_desc(bH + o), idesc2, 1u);
             }
-            mma_commit(smem_addr(mbar + st));
+            mma_commit(smem_addr(mbar + (c & 1)));
         }
-        // Refill the stage of chunk c-1 with chunk c+S-1 once its MMAs are done.
-        const int nc = c + S - 1;
-        if (nc < n_chunks) {
-            if (c >= 1 && ok) {
-                const int pc = c - 1;
-                ok = mbar_wait(smem_addr(mbar + pc % S), static_cast<uint32_t>((pc / S) & 1), wc);
-            }
-            issue_chunk(nc);
-        }
-        cp_async_commit();
+    };
+
+    load(Slot<0>{}, 0);
+    if (n_chunks > 1) load(Slot<1>{}, 1);
+    for (int c = 0; c < n_chunks; c += 2) {
+        step(Slot<0>{}, c);
+        if (c + 1 < n_chunks) step(Slot<1>{}, c + 1);
     }
-    // All MMAs done: the last commit covers every earlier one.
-    if (n_chunks > 0 && ok) {
+    if (ok) {
         const int cl = n_chunks - 1;
-        ok = mbar_wait(smem_addr(mbar + cl % S), static_cast<uint32_t>((cl / S) & 1), wc);
+        ok = mbar_wait(smem_addr(mbar + (cl & 1)), static_cast<uint32_t>((cl >> 1) & 1), wc);
     }
-    cp_async_wait<0>();
     tc_fence_after();
     const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
 
     if (all_ok) {
-        // ---- epilogue: warp w reads tensor-memory lanes 32*(w%4) (tile rows),
-        // column chunks of 16 alternating between the two warp groups.
         const int quarter = warp & 3;
         const int half = warp >> 2;
         const int r = r0 + quarter * 32 + lane;
-        const int rows_out = is_x ? N : M;
-        const float* own = is_x ? a.x : a.y;
-        float* g = is_x ? a.gx : a.gy;
+        const float* own = GX ? a.x : a.y;
+        float* g = GX ? a.gx : a.gy;
         const uint32_t tw = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-        float v[16];
-        tmem_ld16(tw + static_cast<uint32_t>((fb / 16) * 16), v);
-        float sum = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-            if (i == fb % 16) sum = v[i];
+        float v[16], w[16];
+        tmem_ld16(tw + static_cast<uint32_t>(2 * nt), v);
+        const float sum = v[0];
         const size_t row_off = (static_cast<size_t>(b) * rows_out + r) * dim + f0;
         const bool vec = ((dim & 3) == 0) && ((f0 & 3) == 0) &&
                          ((reinterpret_cast<uintptr_t>(own) | reinterpret_cast<uintptr_t>(g)) & 15u) == 0;
         for (int c16 = half; c16 * 16 < fb; c16 += 2) {  // warp-uniform
             tmem_ld16(tw + static_cast<uint32_t>(c16 * 16), v);
+            tmem_ld16(tw + static_cast<uint32_t>(nt + c16 * 16), w);
             if (r < rows_out) {
-                const int fl = c16 * 16;  // first feature of the chunk, within the block
+                const int fl = c16 * 16;
                 if (vec && fl + 16 <= fb && f0 + fl + 16 <= dim) {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const float4 o = __ldg(reinterpret_cast<const float4*>(own + row_off + fl) + u);
-                        float4 w;
-                        w.x = 2.f * (o.x * sum - v[4 * u + 0]);
-                        w.y = 2.f * (o.y * sum - v[4 * u + 1]);
-                        w.z = 2.f * (o.z * sum - v[4 * u + 2]);
-                        w.w = 2.f * (o.w * sum - v[4 * u + 3]);
-                        reinterpret_cast<float4*>(g + row_off + fl)[u] = w;
+                        float4 y4;
+                        y4.x = 2.f * (o.x * sum - (v[4 * u + 0] + w[4 * u + 0]));
+                        y4.y = 2.f * (o.y * sum - (v[4 * u + 1] + w[4 * u + 1]));
+                        y4.z = 2.f * (o.z * sum - (v[4 * u + 2] + w[4 * u + 2]));
+                        y4.w = 2.f * (o.w * sum - (v[4 * u + 3] + w[4 * u + 3]));
+                        reinterpret_cast<float4*>(g + row_off + fl)[u] = y4;
                     }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int f = fl + i;
-                        if (f < fb && f0 + f < dim) g[row_off + f] = 2.f * (__ldg(own + row_off + f) * sum - v[i]);
+                        if (f < fb && f0 + f < dim)
+                            g[row_off + f] = 2.f * (__ldg(own + row_off + f) * sum - (v[i] + w[i]));
                     }
                 }
             }
@@ -495,64 +388,481 @@ __device__ __forceinline__ void grad_tile(const GradTcArgs& a, unsigned char* sm
     if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(a.tmem_cols));
 }
 
-template <int K, int NB>
-__global__ void __launch_bounds__(kThreads, 1) grad_tc_kernel(const GradTcArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) grad_rm_kernel(const GradTcArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    if (static_cast<int>(blockIdx.x) < a.tiles_x * a.n_fblk) grad_tile<K, NB, true>(a, smem_raw);
-    else grad_tile<K, NB, false>(a, smem_raw);
+    if (static_cast<int>(blockIdx.x) < a.tiles_x * a.n_fblk) grad_rm_tile<true>(a, smem_raw);
+    else grad_rm_tile<false>(a, smem_raw);
 }
 
-// Feature blocking: N of the MMA = features of the block + the ones column,
-// rounded up to 16 (M = 128 needs N % 16 == 0, N <= 256).  With the clamp
-// mask a stage holds one more 128 x 32 buffer, so blocks are narrower.
-void grad_tc_geometry(int dim, bool masked, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages) {
-    const int fmax = masked ? 176 : 240;
-    const int f = dim <= fmax ? dim : fmax;
-    *fb = f;
-    *nt = ((f + 1) + 15) / 16 * 16;
-    *n_fblk = (dim + f - 1) / f;
+// Feature blocks of at most kRmMaxNt features, of equal size.
+void grad_rm_geometry(int dim, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages) {
+    const int nb = (dim + kRmMaxNt - 1) / kRmMaxNt;
+    *n_fblk = nb;
+    *fb = (dim + nb - 1) / nb;
+    *nt = (*fb + 15) / 16 * 16;
     int tc = 32;
-    while (tc < *nt) tc *= 2;
+    while (tc < 2 * *nt + 16) tc *= 2;
     *tmem_cols = tc;
-    const size_t stage = (masked ? 3u : 2u) * (kTileM / 8) * kSBO + 2u * static_cast<size_t>(*nt) / 8 * kSBO;
-    *stages = (3 * stage + 128 <= 227u * 1024u) ? 3 : 2;
+    *stages = 2;
 }
 
-static size_t grad_tc_smem_bytes(const GradTcArgs& a) {
-    const size_t stage = (a.Mw ? 3u : 2u) * (kTileM / 8) * kSBO + 2u * static_cast<size_t>(a.nt) / 8 * kSBO;
-    return static_cast<size_t>(a.stages) * stage + 128u;
+static size_t grad_rm_smem(int nt) {
+    return 2u * (2u * (kTileM / 8) * kSBO + static_cast<size_t>(2 * nt + 16) / 8 * kSBO) + 128;
 }
 
-template <int K, int NB>
-static cudaError_t grad_tc_go(const GradTcArgs& args, dim3 grid, size_t smem, cudaStream_t stream) {
-    cudaError_t e = cudaFuncSetAttribute(grad_tc_kernel<K, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+cudaError_t launch_grad_rm(const GradTcArgs& args, cudaStream_t stream) {
+    const WavePlan& P = args.P;
+    if (args.nt < 16 || args.nt > kRmMaxNt || args.nt % 16) return cudaErrorInvalidValue;
+    const size_t smem = grad_rm_smem(args.nt);
+    dim3 grid((args.tiles_x + args.tiles_y) * args.n_fblk, P.B);
+    cudaError_t e = cudaFuncSetAttribute(grad_rm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    grad_tc_kernel<K, NB><<<grid, kThreads, smem, stream>>>(args);
+    grad_rm_kernel<<<grid, kThreads, smem, stream>>>(args);
     return cudaGetLastError();
 }
 
-template <int K>
-static cudaError_t grad_tc_by_nb(const GradTcArgs& args, dim3 grid, size_t smem, cudaStream_t stream) {
-    // B elements per thread: 32 rows x fb features over 256 threads.
-    const int nb = (kKT * args.fb + kThreads - 1) / kThreads;
-    if (nb <= 4) return grad_tc_go<K, 4>(args, grid, smem, stream);
-    if (nb <= 8) return grad_tc_go<K, 8>(args, grid, smem, stream);
-    if (nb <= 16) return grad_tc_go<K, 16>(args, grid, smem, stream);
-    return grad_tc_go<K, 30>(args, grid, smem, stream);
+// ============================================================== gradients from the wavefront layout
+// One row per lane (32-row stripes).  G is read straight from the wavefront
+// layout by the bulk-copy engine into a ring of shared-memory slots (completion
+// counted in bytes on an mbarrier) and de-skewed from there while it is split
+// into the MMA operands.  B comes from x or y in a chunked transposed layout
+// (xTc[b][c][f][kk] = x[b][32c + kk][f], rows of 36 floats), one copy of
+// nf * 144 contiguous bytes per chunk.  Copies are few and large: the engine's
+// cost is per copy, and 128-byte copies run far below bandwidth.
+//
+//   grad_x tile (rows q in [r0, r0 + 128) = 4 stripes, K = j): chunk c covers
+//     j in [32c, 32c + 32), whose cells sit in anti-diagonal rows
+//     t in [32c, 32c + 63) of each stripe.  Load unit k is the 32-row block
+//     t in [32k, 32k + 32) of the 4 stripes (4 KB each, one copy per stripe)
+//     and B chunk k - 1; chunk c reads units c and c + 1.  Lanes take 32
+//     consecutive rows q (cell (q, t - q) at slot word t*32 + q: one bank per
+//     lane) and each thread 4 consecutive j, stored as one 16-byte vector.
+//   grad_y tile (rows j in [r0, r0 + 128), K = q): chunk c is stripe c, whose
+//     cells sit in rows t in [r0, r0 + 159); load unit c is one 2-D tensor copy
+//     of those rows with the 128-byte swizzle (16-byte column group g of row r
+//     lands at group g ^ (r % 8)), plus B chunk c.  Lanes take 8 rows j x 4
+//     consecutive q, which the swizzle puts on 32 different banks; the stores
+//     are 4-byte, 128 contiguous bytes per warp.
+//
+// Per chunk: the warp 0 lanes issue the copies S - 1 units ahead; every thread
+// waits for its chunk's units, loads and splits its A and B elements into
+// registers, waits for the previous chunk's MMAs (one operand buffer), stores
+// them, and thread 0 issues the MMAs.  Cells outside the table (q >= N,
+// j >= M) and the clamp mask (unfused cost, D <= 0) become zeros in the split.
+constexpr int kWlMaxNt = 128;
+constexpr uint32_t kBPitch = 144;  // bytes per row of the chunked transposed x, y
+constexpr int kYRows = 159;        // anti-diagonal rows of one grad_y chunk
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(mbar)
+                 : "memory");
+}
+__device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+// Bounded wait with an inline fast path (the slow path is a call).
+__device__ __forceinline__ bool mbar_wait_fast(uint32_t mbar, uint32_t parity, const WaitCtx& w) {
+    if (mbar_try_wait(mbar, parity)) return true;
+    return mbar_wait(mbar, parity, w);
+}
+__device__ __forceinline__ float split_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
+// Offset (floats) of anti-diagonal row t of stripe s of problem b, one row per lane.
+__device__ __forceinline__ size_t wl_row(const WavePlan& P, int b, int s, int t) {
+    return ((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * 32;
 }
 
-cudaError_t launch_grad_tc(const GradTcArgs& args, cudaStream_t stream) {
-    const WavePlan& P = args.P;
-    if (args.stages < 2 || args.stages > 3) return cudaErrorInvalidValue;
-    const size_t smem = grad_tc_smem_bytes(args);
-    dim3 grid((args.tiles_x + args.tiles_y) * args.n_fblk, P.B);
-    switch (P.K) {
-        case 1: return grad_tc_by_nb<1>(args, grid, smem, stream);
-        case 2: return grad_tc_by_nb<2>(args, grid, smem, stream);
-        case 4: return grad_tc_by_nb<4>(args, grid, smem, stream);
-        default: return cudaErrorInvalidValue;
+__host__ __device__ constexpr uint32_t round1k(uint32_t v) { return (v + 1023u) & ~1023u; }
+__host__ __device__ constexpr uint32_t wl_ops_bytes(int nt) {
+    return round1k(2u * (kTileM / 8) * kSBO + static_cast<uint32_t>(2 * nt + 16) / 8 * kSBO);
+}
+__host__ __device__ constexpr uint32_t wl_a_ring(bool gx) {
+    return gx ? 4u * 32u * 128u : round1k(static_cast<uint32_t>(kYRows) * 128u);
+}
+__host__ __device__ constexpr uint32_t wl_slot_bytes(int nt, bool gx, bool masked) {
+    return round1k((masked ? 2u : 1u) * wl_a_ring(gx) + static_cast<uint32_t>(nt) * kBPitch);
+}
+
+template <bool GX>
+__device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char* smem_dyn) {
+    // The 128-byte swizzle of the tensor copies is a function of address bits
+    // 4-9, so the slots start on 1024-byte boundaries (1 KB spare is allocated).
+    unsigned char* smem_raw = smem_dyn + ((1024u - (smem_addr(smem_dyn) & 1023u)) & 1023u);
+    const WavePlan& P = a.P;
+    const int N = P.N, M = P.M, dim = a.dim;
+    const int b = blockIdx.y;
+    const int nt = a.nt, fb = a.fb;
+    const int S = GX ? a.stages_x : a.stages_y;
+    const int local = GX ? blockIdx.x : blockIdx.x - a.tiles_x * a.n_fblk;
+    const int tile = local / a.n_fblk;
+    const int f0 = (local % a.n_fblk) * fb;
+    const int nf = min(fb, dim - f0);  // feature rows of B actually present
+    const int r0 = tile * kTileM;
+    const int rows_out = GX ? N : M;
+    const int kt = GX ? M : N;
+    const int n_chunks = (kt + kKT - 1) / kKT;
+    const int n_units = GX ? n_chunks + 1 : n_chunks;
+    const bool masked = a.Mw != nullptr;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* __restrict__ Bsrc = (GX ? a.yTc : a.xTc) + static_cast<size_t>(b) * n_chunks * dim * (kBPitch / 4);
+
+    // Shared memory: [operands: A_hi | A_lo | B' = B_lo ; B_hi ; ones] [S ring
+    // slots: A | mask A | B] [ctrl], operands and slots 1024-byte aligned.
+    const uint32_t a_op = kTileM / 8 * kSBO;
+    const uint32_t ops_bytes = wl_ops_bytes(nt);
+    const uint32_t a_ring = wl_a_ring(GX);
+    const uint32_t a_ring_all = masked ? 2 * a_ring : a_ring;
+    const uint32_t slot_bytes = wl_slot_bytes(nt, GX, masked);
+    unsigned char* ring = smem_raw + ops_bytes;
+    unsigned char* ctrl = ring + S * slot_bytes;
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(ctrl);  // [0, S): ring slots, S: MMAs
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 64);
+    const uint32_t smem_base = smem_addr(smem_raw);
+    const uint32_t ring_base = smem_base + ops_bytes;
+
+    WaitCtx wc = a.wait;
+    wc.kernel = 5;
+    wc.problem = b;
+    wc.warp = blockIdx.x;
+    wc.band = GX ? 1 : 2;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i <= S; ++i) mbar_init(smem_addr(mbar + i), 1);
+        fence_mbar_init();
     }
+    if (warp == 0) {
+        tmem_alloc(smem_addr(tmem_slot), static_cast<uint32_t>(a.tmem_cols));
+        tmem_relinquish();
+    }
+    for (int e = threadIdx.x; e < 16 * kKT; e += kThreads)  // the ones rows of B'
+        *reinterpret_cast<float*>(smem_raw + 2 * a_op + op_off(2 * nt + e / kKT, e % kKT)) = 1.f;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // ---- copies of load unit k (warp 0)
+    auto issue = [&](int k) {
+        fence_async_smem();  // the slot's last generic reads before the async writes
+        const int sl = k % S;
+        const uint32_t dst = ring_base + sl * slot_bytes;
+        const uint32_t bar = smem_addr(mbar + sl);
+        const int bchunk = GX ? k - 1 : k;
+        const int t0 = 32 * k;
+        const int rows = GX ? max(0, min(32, P.n_diag - t0)) : kYRows;
+        const int ns = GX ? min(4, P.n_stripes - r0 / 32) : 1;
+        uint32_t bytes = static_cast<uint32_t>(rows * ns) * 128u * (masked ? 2u : 1u);
+        if (bchunk >= 0) bytes += static_cast<uint32_t>(nf) * kBPitch;
+        if (lane == 0) mbar_expect_tx(bar, bytes);
+        __syncwarp();
+        if (GX) {
+            // Lanes 0 .. ns-1 copy the G blocks of the tile's stripes, lanes
+            // ns .. 2ns-1 the mask blocks.
+            if (rows > 0 && lane < ns * (masked ? 2 : 1)) {
+                const bool is_mask = lane >= ns;
+                const int st = is_mask ? lane - ns : lane;
+                const float* src = (is_mask ? a.Mw : a.Ew) + wl_row(P, b, r0 / 32 + st, t0);
+                const uint32_t d = dst + (is_mask ? a_ring : 0u) + static_cast<uint32_t>(st) * 4096u;
+                bulk_g2s(d, src, static_cast<uint32_t>(rows) * 128u, bar);
+            }
+        } else {
+            // Rows t in [r0, r0 + 159) of stripe k: row (b * n_stripes + k) * n_diag + t of the 2-D view.
+            const int y = (b * P.n_stripes + k) * P.n_diag + r0;
+            if (lane == 1) tensor2d_g2s(dst, &a.tm_e, 0, y, bar);
+            if (lane == 2 && masked) tensor2d_g2s(dst + a_ring, &a.tm_m, 0, y, bar);
+        }
+        if (bchunk >= 0 && lane == 3)
+            bulk_g2s(dst + a_ring_all, Bsrc + (static_cast<size_t>(bchunk) * dim + f0) * (kBPitch / 4),
+                     static_cast<uint32_t>(nf) * kBPitch, bar);
+    };
+
+    // ---- per-thread elements of a chunk, split in registers.  Everything that
+    // does not change from chunk to chunk is computed here, once.
+    float4 ahi[4], alo[4];  // grad_x: 4 vectors; grad_y: 16 scalars in the same registers
+    float4 bhi[4], blo[4];  // B: 16-byte units threadIdx.x + 256 i (nt * 8 of them)
+    // B unit u: row f = 8 * ((u >> 3) % (nt / 8)) + (u & 7), column unit
+    // (u >> 3) / (nt / 8): 8 consecutive lanes, 8 rows of one column unit.
+    uint32_t b_src[4], b_dlo[4], b_dhi[4];
+    uint32_t b_live = 0, b_has = 0;  // bit i: unit i exists; bit i: its row is a feature row
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int u = threadIdx.x + kThreads * i;
+        const int grp = u >> 3;
+        const int f = 8 * (grp % (nt / 8)) + (u & 7), ku = grp / (nt / 8);
+        b_src[i] = static_cast<uint32_t>(f) * kBPitch + static_cast<uint32_t>(ku) * 16u;
+        b_dlo[i] = 2 * a_op + op_off(f, 4 * ku);
+        b_dhi[i] = 2 * a_op + op_off(nt + f, 4 * ku);
+        if (u < nt * 8) b_live |= 1u << i;
+        if (u < nt * 8 && f < nf) b_has |= 1u << i;
+    }
+    // grad_x: row q = r0 + 32 (warp % 4) + lane, column units ku_i = warp / 4 + 2 i.
+    const int gx_rg = warp & 3;
+    const bool gx_row_ok = GX && r0 + 32 * gx_rg + lane < N;
+    const uint32_t gx_src = static_cast<uint32_t>(gx_rg) * 4096u + static_cast<uint32_t>(lane) * 4u;
+    const uint32_t gx_dst = op_off(32 * gx_rg + lane, 0);
+    // grad_y: element e: row jl = 8 (warp + 8 (e & 1)) + (lane & 7), column
+    // ql = 4 (e >> 1) + lane / 8.
+    const int gy_i8 = lane & 7, gy_d = lane >> 3;
+    const bool gy_row_ok0 = !GX && r0 + 8 * warp + gy_i8 < M;
+    const bool gy_row_ok1 = !GX && r0 + 8 * (warp + 8) + gy_i8 < M;
+
+    int s_c = 0;        // ring slot of unit c (and of c + 1: s_c1)
+    uint32_t p_c = 0;   // phase parity of unit c: (c / S) & 1
+    auto gather = [&](int c, int s_c1) {
+        if (GX) {
+            const unsigned char* slot0 = ring + static_cast<uint32_t>(s_c) * slot_bytes + gx_src;
+            const unsigned char* slot1 = ring + static_cast<uint32_t>(s_c1) * slot_bytes + gx_src;
+            const int j_lim = M - 32 * c;  // columns j - 32c below this are in the table
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int ku = (warp >> 2) + 2 * i;
+                float v[4];
+#pragma unroll
+                for (int d = 0; d < 4; ++d) {
+                    const int rel = lane + 4 * ku + d;  // t - 32c, 0 .. 62
+                    const unsigned char* p = (rel < 32 ? slot0 : slot1) + static_cast<uint32_t>(rel & 31) * 128u;
+                    const float x = *reinterpret_cast<const float*>(p);
+                    bool ok = gx_row_ok && 4 * ku + d < j_lim;
+                    if (masked) ok = ok && *reinterpret_cast<const float*>(p + a_ring) > 0.f;
+                    v[d] = ok ? x : 0.f;
+                }
+                ahi[i] = make_float4(split_hi(v[0]), split_hi(v[1]), split_hi(v[2]), split_hi(v[3]));
+                alo[i] = make_float4(v[0] - ahi[i].x, v[1] - ahi[i].y, v[2] - ahi[i].z, v[3] - ahi[i].w);
+            }
+        } else {
+            const unsigned char* slot = ring + static_cast<uint32_t>(s_c) * slot_bytes;
+            const int q_lim = N - 32 * c;
+            float* hs = reinterpret_cast<float*>(ahi);
+            float* ls = reinterpret_cast<float*>(alo);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int ql = 4 * (e >> 1) + gy_d;
+                const int r = ql + 8 * warp + 64 * (e & 1) + gy_i8;  // slot row (t - r0)
+                const uint32_t off = static_cast<uint32_t>(r) * 128u +
+                                     (static_cast<uint32_t>((e >> 1) ^ ((4 * (e >> 1) + gy_d + gy_i8) & 7)) << 4) +
+                                     static_cast<uint32_t>(gy_d) * 4u;
+                float x = *reinterpret_cast<const float*>(slot + off);
+                bool ok = ((e & 1) ? gy_row_ok1 : gy_row_ok0) && ql < q_lim;
+                if (masked) ok = ok && *reinterpret_cast<const float*>(slot + a_ring + off) > 0.f;
+                x = ok ? x : 0.f;
+                hs[e] = split_hi(x);
+                ls[e] = x - hs[e];
+            }
+        }
+        const unsigned char* bslot = ring + static_cast<uint32_t>(GX ? s_c1 : s_c) * slot_bytes + a_ring_all;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (b_has & (1u << i)) v = *reinterpret_cast<const float4*>(bslot + b_src[i]);
+            bhi[i] = make_float4(split_hi(v.x), split_hi(v.y), split_hi(v.z), split_hi(v.w));
+            blo[i] = make_float4(v.x - bhi[i].x, v.y - bhi[i].y, v.z - bhi[i].z, v.w - bhi[i].w);
+        }
+    };
+    auto scatter = [&]() {
+        unsigned char* Ah = smem_raw;
+        unsigned char* Al = smem_raw + a_op;
+        if (GX) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t off = gx_dst + static_cast<uint32_t>((warp >> 2) + 2 * i) * kLBO;
+                *reinterpret_cast<float4*>(Ah + off) = ahi[i];
+                *reinterpret_cast<float4*>(Al + off) = alo[i];
+            }
+        } else {
+            const float* hs = reinterpret_cast<const float*>(ahi);
+            const float* ls = reinterpret_cast<const float*>(alo);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const uint32_t off = static_cast<uint32_t>(warp + 8 * (e & 1)) * kSBO +
+                                     static_cast<uint32_t>(e >> 1) * kLBO + static_cast<uint32_t>(gy_i8) * 16u +
+                                     static_cast<uint32_t>(gy_d) * 4u;
+                *reinterpret_cast<float*>(Ah + off) = hs[e];
+                *reinterpret_cast<float*>(Al + off) = ls[e];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (b_live & (1u << i)) {
+                *reinterpret_cast<float4*>(smem_raw + b_dlo[i]) = blo[i];
+                *reinterpret_cast<float4*>(smem_raw + b_dhi[i]) = bhi[i];
+            }
+        }
+    };
+
+    // MMA shapes: D[0, 2nt+16) += A_hi B'; D[nt, 2nt+16) += A_lo [B_hi; 1].
+    const int n1 = 2 * nt + 16;
+    const int n1a = n1 > 256 ? 256 : n1;
+    const uint32_t idesc1a = idesc_tf32(kTileM, n1a);
+    const uint32_t idesc1b = idesc_tf32(kTileM, n1 > 256 ? n1 - 256 : 16);
+    const uint32_t idesc2 = idesc_tf32(kTileM, nt + 16);
+
+    bool ok = true;
+    if (warp == 0)
+        for (int k = 0; k < S - 1 && k < n_units; ++k) issue(k);
+    for (int c = 0; c < n_chunks; ++c) {
+        const int s_c1 = s_c + 1 == S ? 0 : s_c + 1;
+        const uint32_t p_c1 = s_c1 == 0 ? p_c ^ 1u : p_c;
+        if (warp == 0 && c + S - 1 < n_units) issue(c + S - 1);
+        if (ok) {
+            // Unit c (grad_y) or c + 1 (grad_x; unit c was waited for by chunk c - 1).
+            if (GX && c == 0) ok = mbar_wait_fast(smem_addr(mbar + 0), 0u, wc);
+            if (ok) ok = mbar_wait_fast(smem_addr(mbar + (GX ? s_c1 : s_c)), GX ? p_c1 : p_c, wc);
+        }
+        gather(c, s_c1);
+        if (c >= 1 && ok) ok = mbar_wait_fast(smem_addr(mbar + S), static_cast<uint32_t>((c - 1) & 1), wc);
+        scatter();
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (threadIdx.x == 0 && ok) {
+            const uint32_t aH = smem_base;
+            const uint32_t aL = aH + a_op;
+            const uint32_t bP = aL + a_op;
+            const uint32_t bH = bP + static_cast<uint32_t>(nt / 8) * kSBO;
+#pragma unroll
+            for (int ks = 0; ks < kKT / 8; ++ks) {
+                const uint32_t o = static_cast<uint32_t>(ks) * 2 * kLBO;
+                const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
+                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bP + o), idesc1a, acc);
+                if (n1 > 256)
+                    mma_tf32(tmem + 256u, smem_desc(aH + o), smem_desc(bP + 32u * kSBO + o), idesc1b, acc);
+                mma_tf32(tmem + static_cast<uint32_t>(nt), smem_desc(aL + o), smem_desc(bH + o), idesc2, 1u);
+            }
+            mma_commit(smem_addr(mbar + S));
+        }
+        s_c = s_c1;
+        p_c = p_c1;
+    }
+    if (ok) ok = mbar_wait_fast(smem_addr(mbar + S), static_cast<uint32_t>((n_chunks - 1) & 1), wc);
+    tc_fence_after();
+    const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+
+    if (all_ok) {
+        const int quarter = warp & 3;
+        const int half = warp >> 2;
+        const int r = r0 + quarter * 32 + lane;
+        const float* own = GX ? a.x : a.y;
+        float* g = GX ? a.gx : a.gy;
+        const uint32_t tw = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        float v[16], w[16];
+        tmem_ld16(tw + static_cast<uint32_t>(2 * nt), v);
+        const float sum = v[0];
+        const size_t row_off = (static_cast<size_t>(b) * rows_out + r) * dim + f0;
+        const bool vec = ((dim & 3) == 0) && ((f0 & 3) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(own) | reinterpret_cast<uintptr_t>(g)) & 15u) == 0;
+        for (int c16 = half; c16 * 16 < fb; c16 += 2) {  // warp-uniform
+            tmem_ld16(tw + static_cast<uint32_t>(c16 * 16), v);
+            tmem_ld16(tw + static_cast<uint32_t>(nt + c16 * 16), w);
+            if (r < rows_out) {
+                const int fl = c16 * 16;
+                if (vec && fl + 16 <= fb && f0 + fl + 16 <= dim) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 o = __ldg(reinterpret_cast<const float4*>(own + row_off + fl) + u);
+                        float4 y4;
+                        y4.x = 2.f * (o.x * sum - (v[4 * u + 0] + w[4 * u + 0]));
+                        y4.y = 2.f * (o.y * sum - (v[4 * u + 1] + w[4 * u + 1]));
+                        y4.z = 2.f * (o.z * sum - (v[4 * u + 2] + w[4 * u + 2]));
+                        y4.w = 2.f * (o.w * sum - (v[4 * u + 3] + w[4 * u + 3]));
+                        reinterpret_cast<float4*>(g + row_off + fl)[u] = y4;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int f = fl + i;
+                        if (f < fb && f0 + f < dim)
+                            g[row_off + f] = 2.f * (__ldg(own + row_off + f) * sum - (v[i] + w[i]));
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(a.tmem_cols));
+}
+
+__global__ void __launch_bounds__(kThreads, 1) grad_wl_kernel(const __grid_constant__ GradTcArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    if (static_cast<int>(blockIdx.x) < a.tiles_x * a.n_fblk) grad_wl_tile<true>(a, smem_raw);
+    else grad_wl_tile<false>(a, smem_raw);
+}
+
+static size_t grad_wl_smem(int nt, bool gx, bool masked, int stages) {
+    return wl_ops_bytes(nt) + static_cast<size_t>(stages) * wl_slot_bytes(nt, gx, masked) + 128 + 1024;
+}
+
+bool grad_wl_supported(const WavePlan& P) { return P.K == 1; }
+
+// Feature blocks of at most 128 features, of equal size; ring depths: the most
+// that fit (grad_x needs 3: two resident units and one in flight; grad_y 2).
+void grad_wl_geometry(int dim, bool masked, GradTcArgs* g) {
+    const int nb = (dim + kWlMaxNt - 1) / kWlMaxNt;
+    g->n_fblk = nb;
+    g->fb = (dim + nb - 1) / nb;
+    g->nt = (g->fb + 15) / 16 * 16;
+    int tc = 32;
+    while (tc < 2 * g->nt + 16) tc *= 2;
+    g->tmem_cols = tc;
+    const size_t cap = 227u * 1024u;
+    g->stages_x = 4;
+    while (g->stages_x > 3 && grad_wl_smem(g->nt, true, masked, g->stages_x) > cap) --g->stages_x;
+    g->stages_y = 4;
+    while (g->stages_y > 2 && grad_wl_smem(g->nt, false, masked, g->stages_y) > cap) --g->stages_y;
+}
+
+// 2-D view of a wavefront-layout table for the tensor copies: rows of 32
+// floats (128 bytes), boxes of 159 rows, 128-byte swizzle.
+static cudaError_t encode_rows(CUtensorMap* map, const float* base, const WavePlan& P) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    if (!encode) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {32, static_cast<cuuint64_t>(P.B) * P.n_stripes * P.n_diag};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(kYRows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
+    GradTcArgs args = args_in;
+    const WavePlan& P = args.P;
+    if (P.K != 1 || args.nt < 16 || args.nt > kWlMaxNt || args.nt % 16) return cudaErrorInvalidValue;
+    const bool masked = args.Mw != nullptr;
+    if (((reinterpret_cast<uintptr_t>(args.Ew) | reinterpret_cast<uintptr_t>(args.Mw) |
+          reinterpret_cast<uintptr_t>(args.xTc) | reinterpret_cast<uintptr_t>(args.yTc)) & 15u) != 0)
+        return cudaErrorMisalignedAddress;
+    const size_t smem = std::max(args.tiles_x ? grad_wl_smem(args.nt, true, masked, args.stages_x) : 0,
+                                 args.tiles_y ? grad_wl_smem(args.nt, false, masked, args.stages_y) : 0);
+    if (smem > 227u * 1024u) return cudaErrorInvalidValue;
+    cudaError_t e = cudaSuccess;
+    if (args.tiles_y) {
+        e = encode_rows(&args.tm_e, args.Ew, P);
+        if (e == cudaSuccess && masked) e = encode_rows(&args.tm_m, args.Mw, P);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid((args.tiles_x + args.tiles_y) * args.n_fblk, P.B);
+    e = cudaFuncSetAttribute(grad_wl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    grad_wl_kernel<<<grid, kThreads, smem, stream>>>(args);
+    return cudaGetLastError();
 }
 
 // ============================================================== unfused cost

@@ -39,7 +39,8 @@ def test_sizes_without_gpu():
     assert L.sdtw_cost_elems(4, 64, 64) == cells
     # One band: no wrap ring; the wavefront-layout table of the cost / E.
     assert L.sdtw_workspace_bytes(4, 64, 64) == -(-cells * 4 // 256) * 256
-    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) == L.sdtw_workspace_bytes(4, 64, 64)
+    # x/y backward adds x and y in the chunked transposed layout (B, N/32, dim, 36).
+    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) == L.sdtw_workspace_bytes(4, 64, 64) + 2 * (-(-4 * 2 * 3 * 36 * 4 // 256) * 256)
 
 
 def test_invalid_arguments_rejected():
