@@ -99,6 +99,8 @@ struct GradTcArgs {
     int stages;       // shared-memory pipeline depth (grad_rm)
     int stages_x;     // ring slots of the grad_x tiles (grad_wl)
     int stages_y;     // ring slots of the grad_y tiles (grad_wl)
+    int ops_x;        // operand buffers of the grad_x tiles (grad_wl: 1 or 2)
+    int ops_y;        // operand buffers of the grad_y tiles (grad_wl: 1 or 2)
     WaitCtx wait;
 };
 // From E in the wavefront layout with bulk copies (one row per lane only).

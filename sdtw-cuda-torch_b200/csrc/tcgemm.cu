@@ -450,6 +450,7 @@ cudaError_t launch_grad_rm(const GradTcArgs& args, cudaStream_t stream) {
 // them, and thread 0 issues the MMAs.  Cells outside the table (q >= N,
 // j >= M) and the clamp mask (unfused cost, D <= 0) become zeros in the split.
 constexpr int kWlMaxNt = 128;
+constexpr int kWlSplitWarps = 16;
 constexpr uint32_t kBPitch = 144;  // bytes per row of the chunked transposed x, y
 constexpr int kYRows = 159;        // anti-diagonal rows of one grad_y chunk
 
@@ -464,13 +465,48 @@ __device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const CUtensorMap* ma
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
         : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(mbar) : "memory");
+}
 __device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+// try_wait that lets the hardware suspend the thread (up to about 1 us) until
+// the phase completes, so that waiting warps do not take issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t mbar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(mbar), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __noinline__ bool mbar_wait_sleep(uint32_t mbar, uint32_t parity, const WaitCtx& w) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_sleep(mbar, parity)) return true;
+        const int r = backoff(it << 8, t0, w);  // every poll checks the clock
+        if (r) {
+            if (r == 1) record_error(w, kStatusTimeout, 4, parity, 0);
+            return false;
+        }
+    }
 }
 // Bounded wait with an inline fast path (the slow path is a call).
 __device__ __forceinline__ bool mbar_wait_fast(uint32_t mbar, uint32_t parity, const WaitCtx& w) {
     if (mbar_try_wait(mbar, parity)) return true;
-    return mbar_wait(mbar, parity, w);
+    return mbar_wait_sleep(mbar, parity, w);
+}
+// Warp-uniform bounded wait: lane 0 polls, the result is broadcast, and every
+// lane then observes the completed phase itself (acquire).  ok = false skips.
+__device__ __forceinline__ bool warp_wait(uint32_t mbar, uint32_t parity, const WaitCtx& w, bool ok) {
+    int r = 0;
+    if ((threadIdx.x & 31) == 0) r = ok && mbar_wait_fast(mbar, parity, w) ? 1 : 0;
+    r = __shfl_sync(0xffffffffu, r, 0);
+    if (r) (void)mbar_try_wait(mbar, parity);
+    return r != 0;
 }
 __device__ __forceinline__ float split_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
 
@@ -500,6 +536,7 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
     const int b = blockIdx.y;
     const int nt = a.nt, fb = a.fb;
     const int S = GX ? a.stages_x : a.stages_y;
+    const int NO = GX ? a.ops_x : a.ops_y;  // operand buffers (1 or 2)
     const int local = GX ? blockIdx.x : blockIdx.x - a.tiles_x * a.n_fblk;
     const int tile = local / a.n_fblk;
     const int f0 = (local % a.n_fblk) * fb;
@@ -513,19 +550,23 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* __restrict__ Bsrc = (GX ? a.yTc : a.xTc) + static_cast<size_t>(b) * n_chunks * dim * (kBPitch / 4);
 
-    // Shared memory: [operands: A_hi | A_lo | B' = B_lo ; B_hi ; ones] [S ring
-    // slots: A | mask A | B] [ctrl], operands and slots 1024-byte aligned.
+    // Shared memory: [NO operand buffers: A_hi | A_lo | B' = B_lo ; B_hi ; ones]
+    // [S ring slots: A | mask A | B] [barriers], 1024-byte aligned blocks.
     const uint32_t a_op = kTileM / 8 * kSBO;
     const uint32_t ops_bytes = wl_ops_bytes(nt);
     const uint32_t a_ring = wl_a_ring(GX);
     const uint32_t a_ring_all = masked ? 2 * a_ring : a_ring;
     const uint32_t slot_bytes = wl_slot_bytes(nt, GX, masked);
-    unsigned char* ring = smem_raw + ops_bytes;
-    unsigned char* ctrl = ring + S * slot_bytes;
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(ctrl);  // [0, S): ring slots, S: MMAs
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 64);
+    unsigned char* ring = smem_raw + NO * ops_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + S * slot_bytes);
+    uint64_t* full = bars;            // [S]  unit landed (bytes)
+    uint64_t* empty = bars + 4;       // [S]  slot read by the split warps
+    uint64_t* opfull = bars + 8;      // [2]  operand buffer written by the split warps
+    uint64_t* opempty = bars + 10;    // [2]  operand buffer read by the MMAs (commit)
+    uint64_t* accfull = bars + 12;    //      all MMAs done (commit)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
     const uint32_t smem_base = smem_addr(smem_raw);
-    const uint32_t ring_base = smem_base + ops_bytes;
+    const uint32_t ring_base = smem_base + NO * ops_bytes;
 
     WaitCtx wc = a.wait;
     wc.kernel = 5;
@@ -534,220 +575,250 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
     wc.band = GX ? 1 : 2;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i <= S; ++i) mbar_init(smem_addr(mbar + i), 1);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(smem_addr(full + i), 1);
+            mbar_init(smem_addr(empty + i), kWlSplitWarps);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_addr(opfull + i), kWlSplitWarps);
+            mbar_init(smem_addr(opempty + i), 1);
+        }
+        mbar_init(smem_addr(accfull), 1);
         fence_mbar_init();
     }
     if (warp == 0) {
         tmem_alloc(smem_addr(tmem_slot), static_cast<uint32_t>(a.tmem_cols));
         tmem_relinquish();
     }
-    for (int e = threadIdx.x; e < 16 * kKT; e += kThreads)  // the ones rows of B'
-        *reinterpret_cast<float*>(smem_raw + 2 * a_op + op_off(2 * nt + e / kKT, e % kKT)) = 1.f;
+    for (int e = threadIdx.x; e < NO * 16 * kKT; e += blockDim.x) {  // the ones rows of B'
+        const int o = e / (16 * kKT), r = (e / kKT) % 16, k = e % kKT;
+        *reinterpret_cast<float*>(smem_raw + o * ops_bytes + 2 * a_op + op_off(2 * nt + r, k)) = 1.f;
+    }
+    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
-    // ---- copies of load unit k (warp 0)
-    auto issue = [&](int k) {
-        fence_async_smem();  // the slot's last generic reads before the async writes
-        const int sl = k % S;
-        const uint32_t dst = ring_base + sl * slot_bytes;
-        const uint32_t bar = smem_addr(mbar + sl);
-        const int bchunk = GX ? k - 1 : k;
-        const int t0 = 32 * k;
-        const int rows = GX ? max(0, min(32, P.n_diag - t0)) : kYRows;
-        const int ns = GX ? min(4, P.n_stripes - r0 / 32) : 1;
-        uint32_t bytes = static_cast<uint32_t>(rows * ns) * 128u * (masked ? 2u : 1u);
-        if (bchunk >= 0) bytes += static_cast<uint32_t>(nf) * kBPitch;
-        if (lane == 0) mbar_expect_tx(bar, bytes);
-        __syncwarp();
-        if (GX) {
-            // Lanes 0 .. ns-1 copy the G blocks of the tile's stripes, lanes
-            // ns .. 2ns-1 the mask blocks.
-            if (rows > 0 && lane < ns * (masked ? 2 : 1)) {
-                const bool is_mask = lane >= ns;
-                const int st = is_mask ? lane - ns : lane;
-                const float* src = (is_mask ? a.Mw : a.Ew) + wl_row(P, b, r0 / 32 + st, t0);
-                const uint32_t d = dst + (is_mask ? a_ring : 0u) + static_cast<uint32_t>(st) * 4096u;
-                bulk_g2s(d, src, static_cast<uint32_t>(rows) * 128u, bar);
-            }
-        } else {
-            // Rows t in [r0, r0 + 159) of stripe k: row (b * n_stripes + k) * n_diag + t of the 2-D view.
-            const int y = (b * P.n_stripes + k) * P.n_diag + r0;
-            if (lane == 1) tensor2d_g2s(dst, &a.tm_e, 0, y, bar);
-            if (lane == 2 && masked) tensor2d_g2s(dst + a_ring, &a.tm_m, 0, y, bar);
-        }
-        if (bchunk >= 0 && lane == 3)
-            bulk_g2s(dst + a_ring_all, Bsrc + (static_cast<size_t>(bchunk) * dim + f0) * (kBPitch / 4),
-                     static_cast<uint32_t>(nf) * kBPitch, bar);
-    };
-
-    // ---- per-thread elements of a chunk, split in registers.  Everything that
-    // does not change from chunk to chunk is computed here, once.
-    float4 ahi[4], alo[4];  // grad_x: 4 vectors; grad_y: 16 scalars in the same registers
-    float4 bhi[4], blo[4];  // B: 16-byte units threadIdx.x + 256 i (nt * 8 of them)
-    // B unit u: row f = 8 * ((u >> 3) % (nt / 8)) + (u & 7), column unit
-    // (u >> 3) / (nt / 8): 8 consecutive lanes, 8 rows of one column unit.
-    uint32_t b_src[4], b_dlo[4], b_dhi[4];
-    uint32_t b_live = 0, b_has = 0;  // bit i: unit i exists; bit i: its row is a feature row
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int u = threadIdx.x + kThreads * i;
-        const int grp = u >> 3;
-        const int f = 8 * (grp % (nt / 8)) + (u & 7), ku = grp / (nt / 8);
-        b_src[i] = static_cast<uint32_t>(f) * kBPitch + static_cast<uint32_t>(ku) * 16u;
-        b_dlo[i] = 2 * a_op + op_off(f, 4 * ku);
-        b_dhi[i] = 2 * a_op + op_off(nt + f, 4 * ku);
-        if (u < nt * 8) b_live |= 1u << i;
-        if (u < nt * 8 && f < nf) b_has |= 1u << i;
-    }
-    // grad_x: row q = r0 + 32 (warp % 4) + lane, column units ku_i = warp / 4 + 2 i.
-    const int gx_rg = warp & 3;
-    const bool gx_row_ok = GX && r0 + 32 * gx_rg + lane < N;
-    const uint32_t gx_src = static_cast<uint32_t>(gx_rg) * 4096u + static_cast<uint32_t>(lane) * 4u;
-    const uint32_t gx_dst = op_off(32 * gx_rg + lane, 0);
-    // grad_y: element e: row jl = 8 (warp + 8 (e & 1)) + (lane & 7), column
-    // ql = 4 (e >> 1) + lane / 8.
-    const int gy_i8 = lane & 7, gy_d = lane >> 3;
-    const bool gy_row_ok0 = !GX && r0 + 8 * warp + gy_i8 < M;
-    const bool gy_row_ok1 = !GX && r0 + 8 * (warp + 8) + gy_i8 < M;
-
-    int s_c = 0;        // ring slot of unit c (and of c + 1: s_c1)
-    uint32_t p_c = 0;   // phase parity of unit c: (c / S) & 1
-    auto gather = [&](int c, int s_c1) {
-        if (GX) {
-            const unsigned char* slot0 = ring + static_cast<uint32_t>(s_c) * slot_bytes + gx_src;
-            const unsigned char* slot1 = ring + static_cast<uint32_t>(s_c1) * slot_bytes + gx_src;
-            const int j_lim = M - 32 * c;  // columns j - 32c below this are in the table
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int ku = (warp >> 2) + 2 * i;
-                float v[4];
-#pragma unroll
-                for (int d = 0; d < 4; ++d) {
-                    const int rel = lane + 4 * ku + d;  // t - 32c, 0 .. 62
-                    const unsigned char* p = (rel < 32 ? slot0 : slot1) + static_cast<uint32_t>(rel & 31) * 128u;
-                    const float x = *reinterpret_cast<const float*>(p);
-                    bool ok = gx_row_ok && 4 * ku + d < j_lim;
-                    if (masked) ok = ok && *reinterpret_cast<const float*>(p + a_ring) > 0.f;
-                    v[d] = ok ? x : 0.f;
-                }
-                ahi[i] = make_float4(split_hi(v[0]), split_hi(v[1]), split_hi(v[2]), split_hi(v[3]));
-                alo[i] = make_float4(v[0] - ahi[i].x, v[1] - ahi[i].y, v[2] - ahi[i].z, v[3] - ahi[i].w);
-            }
-        } else {
-            const unsigned char* slot = ring + static_cast<uint32_t>(s_c) * slot_bytes;
-            const int q_lim = N - 32 * c;
-            float* hs = reinterpret_cast<float*>(ahi);
-            float* ls = reinterpret_cast<float*>(alo);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const int ql = 4 * (e >> 1) + gy_d;
-                const int r = ql + 8 * warp + 64 * (e & 1) + gy_i8;  // slot row (t - r0)
-                const uint32_t off = static_cast<uint32_t>(r) * 128u +
-                                     (static_cast<uint32_t>((e >> 1) ^ ((4 * (e >> 1) + gy_d + gy_i8) & 7)) << 4) +
-                                     static_cast<uint32_t>(gy_d) * 4u;
-                float x = *reinterpret_cast<const float*>(slot + off);
-                bool ok = ((e & 1) ? gy_row_ok1 : gy_row_ok0) && ql < q_lim;
-                if (masked) ok = ok && *reinterpret_cast<const float*>(slot + a_ring + off) > 0.f;
-                x = ok ? x : 0.f;
-                hs[e] = split_hi(x);
-                ls[e] = x - hs[e];
-            }
-        }
-        const unsigned char* bslot = ring + static_cast<uint32_t>(GX ? s_c1 : s_c) * slot_bytes + a_ring_all;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (b_has & (1u << i)) v = *reinterpret_cast<const float4*>(bslot + b_src[i]);
-            bhi[i] = make_float4(split_hi(v.x), split_hi(v.y), split_hi(v.z), split_hi(v.w));
-            blo[i] = make_float4(v.x - bhi[i].x, v.y - bhi[i].y, v.z - bhi[i].z, v.w - bhi[i].w);
-        }
-    };
-    auto scatter = [&]() {
-        unsigned char* Ah = smem_raw;
-        unsigned char* Al = smem_raw + a_op;
-        if (GX) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t off = gx_dst + static_cast<uint32_t>((warp >> 2) + 2 * i) * kLBO;
-                *reinterpret_cast<float4*>(Ah + off) = ahi[i];
-                *reinterpret_cast<float4*>(Al + off) = alo[i];
-            }
-        } else {
-            const float* hs = reinterpret_cast<const float*>(ahi);
-            const float* ls = reinterpret_cast<const float*>(alo);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const uint32_t off = static_cast<uint32_t>(warp + 8 * (e & 1)) * kSBO +
-                                     static_cast<uint32_t>(e >> 1) * kLBO + static_cast<uint32_t>(gy_i8) * 16u +
-                                     static_cast<uint32_t>(gy_d) * 4u;
-                *reinterpret_cast<float*>(Ah + off) = hs[e];
-                *reinterpret_cast<float*>(Al + off) = ls[e];
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            if (b_live & (1u << i)) {
-                *reinterpret_cast<float4*>(smem_raw + b_dlo[i]) = blo[i];
-                *reinterpret_cast<float4*>(smem_raw + b_dhi[i]) = bhi[i];
-            }
-        }
-    };
-
-    // MMA shapes: D[0, 2nt+16) += A_hi B'; D[nt, 2nt+16) += A_lo [B_hi; 1].
-    const int n1 = 2 * nt + 16;
-    const int n1a = n1 > 256 ? 256 : n1;
-    const uint32_t idesc1a = idesc_tf32(kTileM, n1a);
-    const uint32_t idesc1b = idesc_tf32(kTileM, n1 > 256 ? n1 - 256 : 16);
-    const uint32_t idesc2 = idesc_tf32(kTileM, nt + 16);
-
     bool ok = true;
-    if (warp == 0)
-        for (int k = 0; k < S - 1 && k < n_units; ++k) issue(k);
-    for (int c = 0; c < n_chunks; ++c) {
-        const int s_c1 = s_c + 1 == S ? 0 : s_c + 1;
-        const uint32_t p_c1 = s_c1 == 0 ? p_c ^ 1u : p_c;
-        if (warp == 0 && c + S - 1 < n_units) issue(c + S - 1);
-        if (ok) {
-            // Unit c (grad_y) or c + 1 (grad_x; unit c was waited for by chunk c - 1).
-            if (GX && c == 0) ok = mbar_wait_fast(smem_addr(mbar + 0), 0u, wc);
-            if (ok) ok = mbar_wait_fast(smem_addr(mbar + (GX ? s_c1 : s_c)), GX ? p_c1 : p_c, wc);
-        }
-        gather(c, s_c1);
-        if (c >= 1 && ok) ok = mbar_wait_fast(smem_addr(mbar + S), static_cast<uint32_t>((c - 1) & 1), wc);
-        scatter();
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (threadIdx.x == 0 && ok) {
-            const uint32_t aH = smem_base;
-            const uint32_t aL = aH + a_op;
-            const uint32_t bP = aL + a_op;
-            const uint32_t bH = bP + static_cast<uint32_t>(nt / 8) * kSBO;
-#pragma unroll
-            for (int ks = 0; ks < kKT / 8; ++ks) {
-                const uint32_t o = static_cast<uint32_t>(ks) * 2 * kLBO;
-                const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
-                mma_tf32(tmem, smem_desc(aH + o), smem_desc(bP + o), idesc1a, acc);
-                if (n1 > 256)
-                    mma_tf32(tmem + 256u, smem_desc(aH + o), smem_desc(bP + 32u * kSBO + o), idesc1b, acc);
-                mma_tf32(tmem + static_cast<uint32_t>(nt), smem_desc(aL + o), smem_desc(bH + o), idesc2, 1u);
+
+    if (warp == kWlSplitWarps) {
+        // ================= copies
+        int issued = 0;
+        for (int k = 0; k < n_units; ++k) {
+            const int sl = k % S;
+            if (k >= S) ok = warp_wait(smem_addr(empty + sl), static_cast<uint32_t>((k / S - 1) & 1), wc, ok);
+            if (!ok) break;
+            const uint32_t dst = ring_base + sl * slot_bytes;
+            const uint32_t bar = smem_addr(full + sl);
+            const int bchunk = GX ? k - 1 : k;
+            const int t0 = 32 * k;
+            const int rows = GX ? max(0, min(32, P.n_diag - t0)) : kYRows;
+            const int ns = GX ? min(4, P.n_stripes - r0 / 32) : 1;
+            uint32_t bytes = static_cast<uint32_t>(rows * ns) * 128u * (masked ? 2u : 1u);
+            if (bchunk >= 0) bytes += static_cast<uint32_t>(nf) * kBPitch;
+            if (lane == 0) mbar_expect_tx(bar, bytes);
+            __syncwarp();
+            if (GX) {
+                // Lanes 0 .. ns-1 copy the G blocks of the tile's stripes,
+                // lanes ns .. 2ns-1 the mask blocks.
+                if (rows > 0 && lane < ns * (masked ? 2 : 1)) {
+                    const bool is_mask = lane >= ns;
+                    const int st = is_mask ? lane - ns : lane;
+                    const float* src = (is_mask ? a.Mw : a.Ew) + wl_row(P, b, r0 / 32 + st, t0);
+                    const uint32_t d = dst + (is_mask ? a_ring : 0u) + static_cast<uint32_t>(st) * 4096u;
+                    bulk_g2s(d, src, static_cast<uint32_t>(rows) * 128u, bar);
+                }
+            } else {
+                // Rows t in [r0, r0 + 159) of stripe k: row (b * n_stripes + k) * n_diag + t of the 2-D view.
+                const int y = (b * P.n_stripes + k) * P.n_diag + r0;
+                if (lane == 1) tensor2d_g2s(dst, &a.tm_e, 0, y, bar);
+                if (lane == 2 && masked) tensor2d_g2s(dst + a_ring, &a.tm_m, 0, y, bar);
             }
-            mma_commit(smem_addr(mbar + S));
+            if (bchunk >= 0 && lane == 3)
+                bulk_g2s(dst + a_ring_all, Bsrc + (static_cast<size_t>(bchunk) * dim + f0) * (kBPitch / 4),
+                         static_cast<uint32_t>(nf) * kBPitch, bar);
+            __syncwarp();
+            issued = k + 1;
         }
-        s_c = s_c1;
-        p_c = p_c1;
+        // In-flight copies land before the CTA can exit: the split warps wait
+        // for every unit on the normal path; after a failure, wait here.
+        if (!ok && lane == 0)
+            for (int k = max(0, issued - S); k < issued; ++k)
+                mbar_wait_fast(smem_addr(full + k % S), static_cast<uint32_t>((k / S) & 1), wc);
+    } else if (warp == kWlSplitWarps + 1) {
+        // ================= MMAs (one thread)
+        const int n1 = 2 * nt + 16;
+        const uint32_t idesc1a = idesc_tf32(kTileM, n1 > 256 ? 256 : n1);
+        const uint32_t idesc1b = idesc_tf32(kTileM, n1 > 256 ? n1 - 256 : 16);
+        const uint32_t idesc2 = idesc_tf32(kTileM, nt + 16);
+        if (lane == 0) {
+            for (int c = 0; c < n_chunks; ++c) {
+                const int o = c % NO;
+                if (ok) ok = mbar_wait_fast(smem_addr(opfull + o), static_cast<uint32_t>((c / NO) & 1), wc);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t aH = smem_base + o * ops_bytes;
+                const uint32_t aL = aH + a_op;
+                const uint32_t bP = aL + a_op;
+                const uint32_t bH = bP + static_cast<uint32_t>(nt / 8) * kSBO;
+#pragma unroll
+                for (int ks = 0; ks < kKT / 8; ++ks) {
+                    const uint32_t off = static_cast<uint32_t>(ks) * 2 * kLBO;
+                    const uint32_t acc = (c > 0 || ks > 0) ? 1u : 0u;
+                    mma_tf32(tmem, smem_desc(aH + off), smem_desc(bP + off), idesc1a, acc);
+                    if (n1 > 256)
+                        mma_tf32(tmem + 256u, smem_desc(aH + off), smem_desc(bP + 32u * kSBO + off), idesc1b, acc);
+                    mma_tf32(tmem + static_cast<uint32_t>(nt), smem_desc(aL + off), smem_desc(bH + off), idesc2, 1u);
+                }
+                mma_commit(smem_addr(opempty + o));
+            }
+            if (ok) mma_commit(smem_addr(accfull));
+        }
+        __syncwarp();
+    } else {
+        // ================= split warps: de-skew, split, store the operands
+        // (kWlSplitWarps = 16 warps, 512 threads; indices below assume it).
+        float4 ahi[2], alo[2];  // grad_x: 2 vectors; grad_y: 8 scalars in the same registers
+        float4 bhi[2], blo[2];  // B: 16-byte units threadIdx.x + 512 i (nt * 8 of them)
+        // B unit u: row f = 8 * ((u >> 3) % (nt / 8)) + (u & 7), column unit
+        // (u >> 3) / (nt / 8): 8 consecutive lanes, 8 rows of one column unit.
+        uint32_t b_src[2], b_dlo[2], b_dhi[2];
+        uint32_t b_live = 0, b_has = 0;  // bit i: unit i exists; bit i: its row is a feature row
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int u = threadIdx.x + 512 * i;
+            const int grp = u >> 3;
+            const int f = 8 * (grp % (nt / 8)) + (u & 7), ku = grp / (nt / 8);
+            b_src[i] = static_cast<uint32_t>(f) * kBPitch + static_cast<uint32_t>(ku) * 16u;
+            b_dlo[i] = 2 * a_op + op_off(f, 4 * ku);
+            b_dhi[i] = 2 * a_op + op_off(nt + f, 4 * ku);
+            if (u < nt * 8) b_live |= 1u << i;
+            if (u < nt * 8 && f < nf) b_has |= 1u << i;
+        }
+        // grad_x: row q = r0 + 32 (warp % 4) + lane, column units ku_i = warp / 4 + 4 i.
+        const int gx_rg = warp & 3;
+        const bool gx_row_ok = GX && r0 + 32 * gx_rg + lane < N;
+        const uint32_t gx_src = static_cast<uint32_t>(gx_rg) * 4096u + static_cast<uint32_t>(lane) * 4u;
+        const uint32_t gx_dst = op_off(32 * gx_rg + lane, 0);
+        // grad_y: element e (0 .. 7): row jl = 8 warp + (lane & 7), column ql = 4 e + lane / 8.
+        const int gy_i8 = lane & 7, gy_d = lane >> 3;
+        const bool gy_row_ok = !GX && r0 + 8 * warp + gy_i8 < M;
+
+        int s_c = 0;       // ring slot of unit c (and of c + 1: s_c1)
+        uint32_t p_c = 0;  // phase parity of unit c: (c / S) & 1
+        int o = 0;         // operand buffer of chunk c: c % NO
+        uint32_t po = 0;   // (c / NO) & 1
+        for (int c = 0; c < n_chunks && ok; ++c) {
+            const int s_c1 = s_c + 1 == S ? 0 : s_c + 1;
+            const uint32_t p_c1 = s_c1 == 0 ? p_c ^ 1u : p_c;
+            // Unit c (grad_y) or c + 1 (grad_x; unit c was waited for by chunk c - 1).
+            if (GX && c == 0) ok = warp_wait(smem_addr(full + 0), 0u, wc, ok);
+            ok = warp_wait(smem_addr(full + (GX ? s_c1 : s_c)), GX ? p_c1 : p_c, wc, ok);
+            if (!ok) break;
+            if (GX) {
+                const unsigned char* slot0 = ring + static_cast<uint32_t>(s_c) * slot_bytes + gx_src;
+                const unsigned char* slot1 = ring + static_cast<uint32_t>(s_c1) * slot_bytes + gx_src;
+                const int j_lim = M - 32 * c;  // columns j - 32c below this are in the table
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int ku = (warp >> 2) + 4 * i;
+                    float v[4];
+#pragma unroll
+                    for (int d = 0; d < 4; ++d) {
+                        const int rel = lane + 4 * ku + d;  // t - 32c, 0 .. 62
+                        const unsigned char* p = (rel < 32 ? slot0 : slot1) + static_cast<uint32_t>(rel & 31) * 128u;
+                        const float x = *reinterpret_cast<const float*>(p);
+                        bool okc = gx_row_ok && 4 * ku + d < j_lim;
+                        if (masked) okc = okc && *reinterpret_cast<const float*>(p + a_ring) > 0.f;
+                        v[d] = okc ? x : 0.f;
+                    }
+                    ahi[i] = make_float4(split_hi(v[0]), split_hi(v[1]), split_hi(v[2]), split_hi(v[3]));
+                    alo[i] = make_float4(v[0] - ahi[i].x, v[1] - ahi[i].y, v[2] - ahi[i].z, v[3] - ahi[i].w);
+                }
+            } else {
+                const unsigned char* slot = ring + static_cast<uint32_t>(s_c) * slot_bytes;
+                const int q_lim = N - 32 * c;
+                float* hs = reinterpret_cast<float*>(ahi);
+                float* ls = reinterpret_cast<float*>(alo);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int ql = 4 * e + gy_d;
+                    const int r = ql + 8 * warp + gy_i8;  // slot row (t - r0)
+                    const uint32_t off = static_cast<uint32_t>(r) * 128u +
+                                         (static_cast<uint32_t>(e ^ ((4 * e + gy_d + gy_i8) & 7)) << 4) +
+                                         static_cast<uint32_t>(gy_d) * 4u;
+                    float x = *reinterpret_cast<const float*>(slot + off);
+                    bool okc = gy_row_ok && ql < q_lim;
+                    if (masked) okc = okc && *reinterpret_cast<const float*>(slot + a_ring + off) > 0.f;
+                    x = okc ? x : 0.f;
+                    hs[e] = split_hi(x);
+                    ls[e] = x - hs[e];
+                }
+            }
+            {
+                const unsigned char* bslot = ring + static_cast<uint32_t>(GX ? s_c1 : s_c) * slot_bytes + a_ring_all;
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (b_has & (1u << i)) v = *reinterpret_cast<const float4*>(bslot + b_src[i]);
+                    bhi[i] = make_float4(split_hi(v.x), split_hi(v.y), split_hi(v.z), split_hi(v.w));
+                    blo[i] = make_float4(v.x - bhi[i].x, v.y - bhi[i].y, v.z - bhi[i].z, v.w - bhi[i].w);
+                }
+            }
+            // Release the slot this chunk was the last reader of (grad_x: unit
+            // c, and unit c + 1 after the last chunk; grad_y: unit c).
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_addr(empty + s_c));
+                if (GX && c + 1 == n_chunks) mbar_arrive(smem_addr(empty + s_c1));
+            }
+            // Operand buffer o, free once the MMAs of chunk c - NO are done.
+            if (c >= NO) ok = warp_wait(smem_addr(opempty + o), po ^ 1u, wc, ok);
+            if (!ok) break;
+            unsigned char* Ob = smem_raw + o * ops_bytes;
+            if (GX) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t off = gx_dst + static_cast<uint32_t>((warp >> 2) + 4 * i) * kLBO;
+                    *reinterpret_cast<float4*>(Ob + off) = ahi[i];
+                    *reinterpret_cast<float4*>(Ob + a_op + off) = alo[i];
+                }
+            } else {
+                const float* hs = reinterpret_cast<const float*>(ahi);
+                const float* ls = reinterpret_cast<const float*>(alo);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t off = static_cast<uint32_t>(warp) * kSBO + static_cast<uint32_t>(e) * kLBO +
+                                         static_cast<uint32_t>(gy_i8) * 16u + static_cast<uint32_t>(gy_d) * 4u;
+                    *reinterpret_cast<float*>(Ob + off) = hs[e];
+                    *reinterpret_cast<float*>(Ob + a_op + off) = ls[e];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                if (b_live & (1u << i)) {
+                    *reinterpret_cast<float4*>(Ob + b_dlo[i]) = blo[i];
+                    *reinterpret_cast<float4*>(Ob + b_dhi[i]) = bhi[i];
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(opfull + o));
+            s_c = s_c1;
+            p_c = p_c1;
+            if (++o == NO) {
+                o = 0;
+                po ^= 1u;
+            }
+        }
+        ok = warp_wait(smem_addr(accfull), 0u, wc, ok);
+        tc_fence_after();
     }
-    if (ok) ok = mbar_wait_fast(smem_addr(mbar + S), static_cast<uint32_t>((n_chunks - 1) & 1), wc);
-    tc_fence_after();
     const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
 
-    if (all_ok) {
+    if (all_ok && warp < kWlSplitWarps) {
         const int quarter = warp & 3;
-        const int half = warp >> 2;
+        const int half = warp >> 2;  // column group (0 .. 3)
         const int r = r0 + quarter * 32 + lane;
         const float* own = GX ? a.x : a.y;
         float* g = GX ? a.gx : a.gy;
@@ -758,7 +829,7 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
         const size_t row_off = (static_cast<size_t>(b) * rows_out + r) * dim + f0;
         const bool vec = ((dim & 3) == 0) && ((f0 & 3) == 0) &&
                          ((reinterpret_cast<uintptr_t>(own) | reinterpret_cast<uintptr_t>(g)) & 15u) == 0;
-        for (int c16 = half; c16 * 16 < fb; c16 += 2) {  // warp-uniform
+        for (int c16 = half; c16 * 16 < fb; c16 += kWlSplitWarps / 4) {  // warp-uniform
             tmem_ld16(tw + static_cast<uint32_t>(c16 * 16), v);
             tmem_ld16(tw + static_cast<uint32_t>(nt + c16 * 16), w);
             if (r < rows_out) {
@@ -790,20 +861,24 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
     if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(a.tmem_cols));
 }
 
-__global__ void __launch_bounds__(kThreads, 1) grad_wl_kernel(const __grid_constant__ GradTcArgs a) {
+constexpr int kWlThreads = 32 * (kWlSplitWarps + 2);  // split warps, the copy warp, the MMA warp
+
+__global__ void __launch_bounds__(kWlThreads, 1) grad_wl_kernel(const __grid_constant__ GradTcArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     if (static_cast<int>(blockIdx.x) < a.tiles_x * a.n_fblk) grad_wl_tile<true>(a, smem_raw);
     else grad_wl_tile<false>(a, smem_raw);
 }
 
-static size_t grad_wl_smem(int nt, bool gx, bool masked, int stages) {
-    return wl_ops_bytes(nt) + static_cast<size_t>(stages) * wl_slot_bytes(nt, gx, masked) + 128 + 1024;
+static size_t grad_wl_smem(int nt, bool gx, bool masked, int stages, int ops) {
+    return static_cast<size_t>(ops) * wl_ops_bytes(nt) + static_cast<size_t>(stages) * wl_slot_bytes(nt, gx, masked) +
+           256 + 1024;
 }
 
 bool grad_wl_supported(const WavePlan& P) { return P.K == 1; }
 
-// Feature blocks of at most 128 features, of equal size; ring depths: the most
-// that fit (grad_x needs 3: two resident units and one in flight; grad_y 2).
+// Feature blocks of at most 128 features, of equal size.  Pipeline depths: the
+// deepest that fits, preferring two operand buffers, then ring slots (grad_x
+// needs 3: two resident units and one in flight; grad_y 2).
 void grad_wl_geometry(int dim, bool masked, GradTcArgs* g) {
     const int nb = (dim + kWlMaxNt - 1) / kWlMaxNt;
     g->n_fblk = nb;
@@ -813,10 +888,26 @@ void grad_wl_geometry(int dim, bool masked, GradTcArgs* g) {
     while (tc < 2 * g->nt + 16) tc *= 2;
     g->tmem_cols = tc;
     const size_t cap = 227u * 1024u;
-    g->stages_x = 4;
-    while (g->stages_x > 3 && grad_wl_smem(g->nt, true, masked, g->stages_x) > cap) --g->stages_x;
-    g->stages_y = 4;
-    while (g->stages_y > 2 && grad_wl_smem(g->nt, false, masked, g->stages_y) > cap) --g->stages_y;
+    for (int gx = 0; gx < 2; ++gx) {
+        const int smin = gx ? 3 : 2;
+        int best_s = smin, best_o = 1;
+        bool found = false;
+        for (int o = 2; o >= 1 && !found; --o)
+            for (int s = 4; s >= smin; --s)
+                if (grad_wl_smem(g->nt, gx, masked, s, o) <= cap) {
+                    best_s = s;
+                    best_o = o;
+                    found = true;
+                    break;
+                }
+        if (gx) {
+            g->stages_x = best_s;
+            g->ops_x = best_o;
+        } else {
+            g->stages_y = best_s;
+            g->ops_y = best_o;
+        }
+    }
 }
 
 // 2-D view of a wavefront-layout table for the tensor copies: rows of 32
@@ -849,8 +940,9 @@ cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
     if (((reinterpret_cast<uintptr_t>(args.Ew) | reinterpret_cast<uintptr_t>(args.Mw) |
           reinterpret_cast<uintptr_t>(args.xTc) | reinterpret_cast<uintptr_t>(args.yTc)) & 15u) != 0)
         return cudaErrorMisalignedAddress;
-    const size_t smem = std::max(args.tiles_x ? grad_wl_smem(args.nt, true, masked, args.stages_x) : 0,
-                                 args.tiles_y ? grad_wl_smem(args.nt, false, masked, args.stages_y) : 0);
+    const size_t smem =
+        std::max(args.tiles_x ? grad_wl_smem(args.nt, true, masked, args.stages_x, args.ops_x) : 0,
+                 args.tiles_y ? grad_wl_smem(args.nt, false, masked, args.stages_y, args.ops_y) : 0);
     if (smem > 227u * 1024u) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
     if (args.tiles_y) {
@@ -861,7 +953,7 @@ cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
     dim3 grid((args.tiles_x + args.tiles_y) * args.n_fblk, P.B);
     e = cudaFuncSetAttribute(grad_wl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    grad_wl_kernel<<<grid, kThreads, smem, stream>>>(args);
+    grad_wl_kernel<<<grid, kWlThreads, smem, stream>>>(args);
     return cudaGetLastError();
 }
 
