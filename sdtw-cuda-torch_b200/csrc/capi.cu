@@ -553,10 +553,8 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
         float* xTc = reinterpret_cast<float*>(region + o.xt);
         float* yTc = reinterpret_cast<float*>(region + o.yt);
         {
-            KernelTimer kt("grad_operands", st, (grad_x ? 1 : 0) + (grad_y ? 1 : 0));
-            e = cudaSuccess;
-            if (grad_x) e = launch_transpose_chunked(y, yTc, B, M, dim, st);
-            if (e == cudaSuccess && grad_y) e = launch_transpose_chunked(x, xTc, B, N, dim, st);
+            KernelTimer kt("grad_operands", st);
+            e = launch_transpose_chunked(grad_y ? x : nullptr, xTc, N, grad_x ? y : nullptr, yTc, M, B, dim, st);
         }
         if (e != cudaSuccess) return cuda_fail(e, "layout launch");
         g.xTc = xTc;

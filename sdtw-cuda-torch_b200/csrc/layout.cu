@@ -307,15 +307,23 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
 }
 
 // 32 x 32 blocks (32 sequence positions x 32 features) through shared memory;
-// grid (ceil(R/32), ceil(C/32), B).  Output rows are 36 floats: 32 positions
-// and 4 zeros.
-__global__ void __launch_bounds__(256) transpose_chunked_kernel(const float* __restrict__ in, float* __restrict__ out,
-                                                                int R, int C) {
+// grid (ceil(max(R0, R1)/32), ceil(C/32), 2B): z < B transposes in0 (rows R0),
+// the rest in1 (rows R1); either may be null.  Output rows are 36 floats: 32
+// positions and 4 zeros.
+__global__ void __launch_bounds__(256) transpose_chunked_kernel(const float* __restrict__ in0, float* __restrict__ out0,
+                                                                int R0, const float* __restrict__ in1,
+                                                                float* __restrict__ out1, int R1, int B, int C) {
     __shared__ float tile[32][33];
+    const bool second = static_cast<int>(blockIdx.z) >= B;
+    const float* __restrict__ in = second ? in1 : in0;
+    float* __restrict__ out = second ? out1 : out0;
+    const int R = second ? R1 : R0;
+    const int b = second ? blockIdx.z - B : blockIdx.z;
     const int c = blockIdx.x, f0 = blockIdx.y * 32;
     const int n_chunks = (R + 31) / 32;
-    const size_t in_off = static_cast<size_t>(blockIdx.z) * R * C;
-    const size_t out_off = (static_cast<size_t>(blockIdx.z) * n_chunks + c) * C * 36;
+    if (!in || c >= n_chunks) return;  // block-uniform
+    const size_t in_off = static_cast<size_t>(b) * R * C;
+    const size_t out_off = (static_cast<size_t>(b) * n_chunks + c) * C * 36;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = warp; i < 32; i += 8) {
         const int r = 32 * c + i, f = f0 + lane;
@@ -416,10 +424,12 @@ cudaError_t launch_wl_to_rm_cm(const float* Aw, const float* maskw, float* A, in
     return cudaGetLastError();
 }
 
-cudaError_t launch_transpose_chunked(const float* in, float* out, int B, int R, int C, cudaStream_t stream) {
-    if (B <= 0 || R <= 0 || C <= 0) return cudaSuccess;
-    const dim3 g((R + 31) / 32, (C + 31) / 32, B);
-    transpose_chunked_kernel<<<g, 256, 0, stream>>>(in, out, R, C);
+cudaError_t launch_transpose_chunked(const float* in0, float* out0, int R0, const float* in1, float* out1, int R1,
+                                     int B, int C, cudaStream_t stream) {
+    if (B <= 0 || C <= 0 || (!in0 && !in1)) return cudaSuccess;
+    const int rows = std::max(in0 ? R0 : 0, in1 ? R1 : 0);
+    const dim3 g((rows + 31) / 32, (C + 31) / 32, 2 * B);
+    transpose_chunked_kernel<<<g, 256, 0, stream>>>(in0, out0, R0, in1, out1, R1, B, C);
     return cudaGetLastError();
 }
 

@@ -57,8 +57,10 @@ cudaError_t launch_wl_to_rm_cm(const float* Aw, const float* maskw, float* A, in
                                const WavePlan& P, cudaStream_t stream);
 // (B,R,C) -> (B,C,ldo), ldo >= R, columns R .. ldo zero.
 // (B,R,C) -> chunked (B, ceil(R/32), C, 36): out[b][c][f][kk] = in[b][32c+kk][f]
-// for kk < 32, zero for 32c+kk >= R and for kk >= 32.
-cudaError_t launch_transpose_chunked(const float* in, float* out, int B, int R, int C, cudaStream_t stream);
+// for kk < 32, zero for 32c+kk >= R and for kk >= 32; two arrays (rows R0 and
+// R1, either input may be null) in one launch.
+cudaError_t launch_transpose_chunked(const float* in0, float* out0, int R0, const float* in1, float* out1, int R1,
+                                     int B, int C, cudaStream_t stream);
 cudaError_t launch_transpose_brc(const float* in, float* out, int B, int R, int C, int ldo, cudaStream_t stream);
 
 // dense.cu
