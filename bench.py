@@ -61,6 +61,9 @@ MUFU_PER_SM_CLK = 16       # ex2/lg2 results per SM per clock
 # read or written once (cost 4 B, score 8 B as a (hi, lo) pair, E 4 B).
 ALG_BYTES = {"cost_wl": 4, "cost_tc": 4, "wavefront_fwd": 12, "wavefront_bwd": 12, "wl_to_rm": 8, "grad_xy": 8,
              "rm_to_wl": 8, "cost_rowmajor": 4}
+# Algorithmic MUFU ops per cell of the reference algorithm: forward softmin
+# (2 ex2 + 1 lg2), reverse log-sum-exp (2 ex2 + 1 lg2) and E = exp(log E) (1 ex2).
+ALG_MUFU = {"wavefront_fwd": 3, "wavefront_bwd": 4}
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum,
 # one launch each, cold L2) for the C2 workload, fused mode (profiles/c2_kernels_full.md).
 TRAFFIC_C2 = {"wavefront_fwd": 56.83e6, "wavefront_bwd": 82.43e6, "cost_wl": 8.48e6, "grad_xy": 54.54e6}

@@ -26,6 +26,24 @@ namespace sdtw {
 
 constexpr int kTB = 32;   // anti-diagonals per tile
 
+// Packed float32 pairs (sm_100 f32x2 arithmetic): a 64-bit register holds two
+// floats, low half first.
+__device__ __forceinline__ unsigned long long sub_f32x2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ float lo_f32x2(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f32x2(unsigned long long v) {
+    return __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
+
 __device__ __forceinline__ size_t wl_row_base(const WavePlan& P, int b, int s, int t) {
     return ((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * (32 * P.K);
 }
@@ -71,10 +89,14 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
     const int ag = threadIdx.x / CG;  // rows 4ag .. 4ag+3
 
     float acc[4][4];
+    unsigned long long acc2[4][4];  // DIRECT: packed (even, odd) partial sums
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[i][c] = 0.f;
+        for (int c = 0; c < 4; ++c) {
+            acc[i][c] = 0.f;
+            acc2[i][c] = 0ull;
+        }
     if (!DIRECT) {
         for (int i = threadIdx.x; i < SR + CJ; i += 256) xn[i] = 0.f;  // xn and yn are adjacent
     }
@@ -111,31 +133,45 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
         }
         const float* xrow = xs + (4 * ag) * PITCH;
         const float* yrow = ys + jb * PITCH;
+        if (DIRECT) {
+            // Packed pairs of features (f32x2): one subtract and one FMA per two
+            // cell-features; acc2 holds the even- and odd-feature partial sums.
 #pragma unroll
-        for (int f = 0; f < FC; f += 4) {
-            float4 xv[4];
+            for (int f = 0; f < FC; f += 4) {
+                ulonglong2 xv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xrow + i * PITCH + f);
+                for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const ulonglong2*>(xrow + i * PITCH + f);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const float4 yv = *reinterpret_cast<const float4*>(yrow + c * CG * PITCH + f);
+                for (int c = 0; c < 4; ++c) {
+                    const ulonglong2 yv = *reinterpret_cast<const ulonglong2*>(yrow + c * CG * PITCH + f);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 a = xv[i];
-                    float r = acc[i][c];
-                    if (DIRECT) {
-                        const float d0 = a.x - yv.x, d1 = a.y - yv.y, d2 = a.z - yv.z, d3 = a.w - yv.w;
-                        r = fmaf(d0, d0, r);
-                        r = fmaf(d1, d1, r);
-                        r = fmaf(d2, d2, r);
-                        r = fmaf(d3, d3, r);
-                    } else {
+                    for (int i = 0; i < 4; ++i) {
+                        const unsigned long long d01 = sub_f32x2(xv[i].x, yv.x);
+                        const unsigned long long d23 = sub_f32x2(xv[i].y, yv.y);
+                        acc2[i][c] = fma_f32x2(d01, d01, acc2[i][c]);
+                        acc2[i][c] = fma_f32x2(d23, d23, acc2[i][c]);
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int f = 0; f < FC; f += 4) {
+                float4 xv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xrow + i * PITCH + f);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float4 yv = *reinterpret_cast<const float4*>(yrow + c * CG * PITCH + f);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 a = xv[i];
+                        float r = acc[i][c];
                         r = fmaf(a.x, yv.x, r);
                         r = fmaf(a.y, yv.y, r);
                         r = fmaf(a.z, yv.z, r);
                         r = fmaf(a.w, yv.w, r);
+                        acc[i][c] = r;
                     }
-                    acc[i][c] = r;
                 }
             }
         }
@@ -151,8 +187,9 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const int jl = jb + CG * c;
-            float v = acc[i][c];
-            if (!DIRECT) v = fmaxf((xn[q] + yn[jl]) - 2.f * v, 0.f);
+            float v;
+            if (DIRECT) v = lo_f32x2(acc2[i][c]) + hi_f32x2(acc2[i][c]);
+            else v = fmaxf((xn[q] + yn[jl]) - 2.f * acc[i][c], 0.f);
             stg[(q + jl) * (SR + 1) + p] = v;
         }
     }
