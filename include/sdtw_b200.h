@@ -178,6 +178,26 @@ int sdtw_cpu_forward_f64(const double *D, double *R, double *out, int B, int N, 
 int sdtw_cpu_backward_f64(const double *R, const double *grad_out, double *E, int B, int N, int M,
                           double gamma, double bandwidth);
 
+/* Float64 CUDA path: the reference's float64 pipeline in double on the device
+ * (one CTA per problem, a barrier per anti-diagonal; a correctness path, e.g.
+ * for gradcheck on the GPU).  D, R, E device pointers; R is the reference
+ * layout (B,N+2,M+2); out (B,).  Runs on `stream`, no workspace.
+ * -- replaces softdtw_cuda/cuda/launcher.py:167-223 (softdtw_forward_cuda) for
+ *    float64 tensors, with the arithmetic of launcher.py:307-324 */
+int sdtw_forward_f64(const double *D, double *R, double *out, int B, int N, int M, double gamma,
+                     double bandwidth, void *stream);
+/* E (B,N,M) = grad_out[b] * dR[N,M]/dD (grad_out NULL = ones).
+ * -- replaces softdtw_cuda/cuda/launcher.py:226-300 (softdtw_backward_cuda_log)
+ *    for float64 tensors, with the arithmetic of launcher.py:327-353 and the
+ *    scaling of softdtw_cuda/autograd.py:46-47 */
+int sdtw_backward_f64(const double *D, const double *R, const double *grad_out, double *E, int B, int N, int M,
+                      double gamma, double bandwidth, void *stream);
+/* D (B,N,M) = sum_k (x_ik - y_jk)^2 in double (the fused cost's direct form),
+ * N <= 65535.
+ * -- the cost of softdtw_cuda/cuda/kernels.py:27-31 for float64 x, y */
+int sdtw_cost_sqeuclid_f64(const double *x, const double *y, double *D, int B, int N, int M, int dim,
+                           void *stream);
+
 /* Allocation-free variant of sdtw_forward_f32 (no counterpart in the
  * reference).  For callers that cannot allocate device memory at call time --
  * a host runtime whose allocator owns all of device memory, a plugin boundary

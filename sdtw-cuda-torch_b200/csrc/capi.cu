@@ -450,6 +450,58 @@ size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim) {
     return wave_ws(B, N, M) + wl_bytes(B, N, M) + grad_operands(B, N, M, dim).total;
 }
 
+static int check_f64(int B, int N, int M, double gamma) {
+    int rc = check_dims(B, N, M);
+    if (rc) return rc;
+    if (!(gamma > 0.0) || !std::isfinite(gamma)) return fail(SDTW_ERR_INVALID_ARGUMENT, "gamma must be finite and > 0");
+    return SDTW_OK;
+}
+
+int sdtw_forward_f64(const double* D, double* R, double* out, int B, int N, int M, double gamma, double bandwidth,
+                     void* stream) {
+    int rc = check_f64(B, N, M, gamma);
+    if (rc) return rc;
+    if (!D || !R || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e;
+    {
+        KernelTimer kt("wavefront_fwd_f64", static_cast<cudaStream_t>(stream));
+        e = launch_forward_f64(D, R, out, B, N, M, gamma, bandwidth > 0.0 ? bandwidth : -1.0,
+                               static_cast<cudaStream_t>(stream));
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "forward launch");
+    return SDTW_OK;
+}
+
+int sdtw_backward_f64(const double* D, const double* R, const double* grad_out, double* E, int B, int N, int M,
+                      double gamma, double bandwidth, void* stream) {
+    int rc = check_f64(B, N, M, gamma);
+    if (rc) return rc;
+    if (!D || !R || !E) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e;
+    {
+        KernelTimer kt("wavefront_bwd_f64", static_cast<cudaStream_t>(stream));
+        e = launch_backward_f64(D, R, grad_out, E, B, N, M, gamma, bandwidth > 0.0 ? bandwidth : -1.0,
+                                static_cast<cudaStream_t>(stream));
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+    return SDTW_OK;
+}
+
+int sdtw_cost_sqeuclid_f64(const double* x, const double* y, double* D, int B, int N, int M, int dim, void* stream) {
+    int rc = check_dims(B, N, M);
+    if (rc) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (N > 65535 || B > 65535) return fail(SDTW_ERR_INVALID_ARGUMENT, "float64 cost: N and B must be <= 65535");
+    if (!x || !y || !D) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e;
+    {
+        KernelTimer kt("cost_f64", static_cast<cudaStream_t>(stream));
+        e = launch_cost_f64(x, y, D, B, N, M, dim, static_cast<cudaStream_t>(stream));
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cost launch");
+    return SDTW_OK;
+}
+
 int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int N, int M, int dim, int direct,
                            void* stream) {
     int rc = check_dims(B, N, M);

@@ -119,4 +119,12 @@ bool cost_tc_supported(const float* x, const float* y, int dim);
 cudaError_t launch_cost_tc(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
                            cudaStream_t stream);
 
+// f64.cu: the float64 pipeline (reference layout R, one CTA per problem).
+cudaError_t launch_forward_f64(const double* D, double* R, double* out, int B, int N, int M, double gamma, double bw,
+                               cudaStream_t stream);
+cudaError_t launch_backward_f64(const double* D, const double* R, const double* grad_out, double* E, int B, int N,
+                                int M, double gamma, double bw, cudaStream_t stream);
+cudaError_t launch_cost_f64(const double* x, const double* y, double* D, int B, int N, int M, int dim,
+                            cudaStream_t stream);
+
 }  // namespace sdtw

@@ -52,6 +52,9 @@ _SIGS = {
     "sdtw_grad_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
     "sdtw_score_to_R_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
     "sdtw_R_to_score_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
+    "sdtw_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
+    "sdtw_backward_f64": ([_P, _P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
+    "sdtw_cost_sqeuclid_f64": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),
     "sdtw_cpu_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
     "sdtw_cpu_backward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
 }
@@ -365,6 +368,57 @@ def R_to_score(R: torch.Tensor, gamma: float) -> torch.Tensor:
     _check(rc, "R_to_score")
     _op_end("R_to_score", R.device, None)
     return score
+
+
+# ----------------------------------------------------------------------------- CUDA float64 ops
+def _f64(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to(dtype=torch.float64).contiguous()
+
+
+def forward_f64(D: torch.Tensor, gamma: float, bandwidth: float):
+    """(out (B,), R (B,N+2,M+2)) in float64 for a CUDA float64 cost tensor."""
+    D = _f64(D)
+    B, N, M = D.shape
+    R = torch.empty((B, N + 2, M + 2), dtype=torch.float64, device=D.device)
+    out = torch.empty(B, dtype=torch.float64, device=D.device)
+    ev = _op_begin(D.device)
+    with torch.cuda.device(D.device):
+        rc = lib().sdtw_forward_f64(_ptr(D), _ptr(R), _ptr(out), B, N, M, float(gamma), float(bandwidth),
+                                    _stream(D.device))
+    _check(rc, "float64 forward")
+    _op_end("forward_f64", D.device, ev)
+    return out, R
+
+
+def backward_f64(D: torch.Tensor, R: torch.Tensor, grad_out: torch.Tensor | None, gamma: float,
+                 bandwidth: float) -> torch.Tensor:
+    """E (B,N,M) = grad_out[b] * dR[N,M]/dD in float64 on the GPU."""
+    D = _f64(D)
+    B, N, M = D.shape
+    E = torch.empty((B, N, M), dtype=torch.float64, device=D.device)
+    g = None if grad_out is None else grad_out.detach().reshape(-1).to(device=D.device, dtype=torch.float64).contiguous()
+    ev = _op_begin(D.device)
+    with torch.cuda.device(D.device):
+        rc = lib().sdtw_backward_f64(_ptr(D), _ptr(R), _ptr(g), _ptr(E), B, N, M, float(gamma), float(bandwidth),
+                                     _stream(D.device))
+    _check(rc, "float64 backward")
+    _op_end("backward_f64", D.device, ev)
+    return E
+
+
+def cost_sqeuclid_f64(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """D = sum_k (x_ik - y_jk)^2 in float64 on the GPU (the fused cost's direct form)."""
+    x = _f64(x)
+    y = _f64(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    D = torch.empty((B, N, M), dtype=torch.float64, device=x.device)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_cost_sqeuclid_f64(_ptr(x), _ptr(y), _ptr(D), B, N, M, dim, _stream(x.device))
+    _check(rc, "float64 cost")
+    _op_end("cost_f64", x.device, ev)
+    return D
 
 
 # ----------------------------------------------------------------------------- CPU ops

@@ -3,7 +3,8 @@
 ``SoftDTWAutograd.apply(D, gamma, bandwidth)`` returns R[N,M] per batch
 element; its backward returns grad_D = grad_out[b] * E[b] where E is the
 expected alignment matrix.  CUDA tensors use the libsdtw_b200 wavefront kernels
-(float32 arithmetic; float16/bfloat16 inputs are computed in float32), CPU
+(float32 arithmetic; float16/bfloat16 inputs are computed in float32; float64
+inputs take the library's float64 device path, in double throughout), CPU
 tensors the library's double-precision host implementation.
 """
 from __future__ import annotations
@@ -32,15 +33,16 @@ class SoftDTWAutograd(Function):
             raise ValueError(f"gamma must be > 0, got {gamma_f}")
         bw = _normalize_bandwidth(bandwidth)
         B, N, M = D.shape
-        if D.is_cuda:
-            if D.dtype == torch.float64:
-                raise NotImplementedError(
-                    "softdtw_cuda: float64 cost matrices on CUDA are not supported by the B200 kernels yet; "
-                    "use float32 (or a CPU tensor for float64)")
+        ctx.f64 = D.is_cuda and D.dtype == torch.float64
+        if ctx.f64:
+            out, table = _native.forward_f64(D, gamma_f, bw)
+            ctx.save_for_backward(table, D.detach())
+        elif D.is_cuda:
             out, table = _native.forward(D, gamma_f, bw)
+            ctx.save_for_backward(table)
         else:
             out, table = _native.cpu_forward(D, gamma_f, bw)
-        ctx.save_for_backward(table)
+            ctx.save_for_backward(table)
         ctx.gamma = gamma_f
         ctx.bandwidth = bw
         ctx.dims = (B, N, M)
@@ -50,8 +52,11 @@ class SoftDTWAutograd(Function):
 
     @staticmethod
     def backward(ctx, grad_output: torch.Tensor):
-        (table,) = ctx.saved_tensors
         B, N, M = ctx.dims
+        if ctx.f64:
+            table, D = ctx.saved_tensors
+            return _native.backward_f64(D, table, grad_output, ctx.gamma, ctx.bandwidth), None, None
+        (table,) = ctx.saved_tensors
         if ctx.cuda:
             E = _native.backward(table, grad_output, B, N, M, ctx.gamma, ctx.bandwidth)
         else:

@@ -4,7 +4,9 @@
 sum_k (x_ik - y_jk)^2 inside the library (no cost tensor is returned to the
 caller) and its backward returns dL/dX and dL/dY directly:
     grad_X = 2 (X * rowsum(G) - G Y),  grad_Y = 2 (Y * colsum(G) - G^T X),
-G = grad_out[b] * E[b].  CUDA only, as in the reference.
+G = grad_out[b] * E[b].  CUDA only, as in the reference.  float64 inputs take
+the library's float64 device path (cost, forward and backward in double);
+their two contractions with G are float64 torch bmm.
 """
 from __future__ import annotations
 
@@ -24,11 +26,16 @@ class SoftDTWXYAutograd(Function):
             raise ValueError(f"Expected X,Y as (B,N,D)/(B,M,D). Got {tuple(X.shape)} and {tuple(Y.shape)}")
         if X.shape[0] != Y.shape[0] or X.shape[2] != Y.shape[2]:
             raise ValueError(f"Batch/features mismatch: {tuple(X.shape)} vs {tuple(Y.shape)}")
-        if X.dtype == torch.float64 or Y.dtype == torch.float64:
-            raise NotImplementedError(
-                "softdtw_cuda: float64 inputs on CUDA are not supported by the B200 kernels yet; use float32")
         gamma_f = float(gamma)
         bw = _normalize_bandwidth(bandwidth)
+        ctx.f64 = X.dtype == torch.float64 or Y.dtype == torch.float64
+        if ctx.f64:
+            D = _native.cost_sqeuclid_f64(X, Y)
+            out, R = _native.forward_f64(D, gamma_f, bw)
+            ctx.save_for_backward(X, Y, D, R)
+            ctx.gamma = gamma_f
+            ctx.bandwidth = bw
+            return out.to(X.dtype)
         out, score = _native.forward_xy(X, Y, gamma_f, bw)
         ctx.save_for_backward(X, Y, score)
         ctx.gamma = gamma_f
@@ -37,6 +44,16 @@ class SoftDTWXYAutograd(Function):
 
     @staticmethod
     def backward(ctx, grad_output: torch.Tensor):
+        if ctx.f64:
+            X, Y, D, R = ctx.saved_tensors
+            G = _native.backward_f64(D, R, grad_output, ctx.gamma, ctx.bandwidth)
+            Xd, Yd = X.detach().double(), Y.detach().double()
+            gx = gy = None
+            if ctx.needs_input_grad[0]:
+                gx = (2.0 * (Xd * G.sum(dim=2, keepdim=True) - torch.bmm(G, Yd))).to(X.dtype)
+            if ctx.needs_input_grad[1]:
+                gy = (2.0 * (Yd * G.sum(dim=1).unsqueeze(2) - torch.bmm(G.transpose(1, 2), Xd))).to(Y.dtype)
+            return gx, gy, None, None
         X, Y, score = ctx.saved_tensors
         gx, gy = _native.backward_xy(X, Y, score, grad_output, ctx.gamma, ctx.bandwidth,
                                      need_x=ctx.needs_input_grad[0], need_y=ctx.needs_input_grad[1])
