@@ -16,7 +16,8 @@ import math
 import torch
 from torch import nn
 
-from .autograd import SoftDTWAutograd, SoftDTWSqEuclidAutograd
+from . import ops  # noqa: F401  (registers torch.ops.softdtw_cuda.*)
+from .autograd import SoftDTWAutograd, SoftDTWSqEuclidAutograd, _normalize_bandwidth
 from .autograd_xy import SoftDTWXYAutograd
 from .distances import _KERNEL_DTYPES, _SQEUCLID_NAMES, pairwise_distance
 
@@ -96,6 +97,15 @@ class SoftDTW(nn.Module):
         return self._pairs(x, y, use_fused)
 
     def _pairs(self, x: torch.Tensor, y: torch.Tensor, use_fused: bool) -> torch.Tensor:
+        if (torch.compiler.is_compiling() and self.dist.lower() in _SQEUCLID_NAMES and x.is_cuda and y.is_cuda
+                and x.device == y.device and x.dtype in _KERNEL_DTYPES and y.dtype == x.dtype):
+            # Under torch.compile: the same library calls as registered custom
+            # operators (softdtw_cuda/ops.py), traceable without a graph break.
+            if x.dim() != 3 or y.dim() != 3 or x.shape[0] != y.shape[0] or x.shape[2] != y.shape[2]:
+                raise ValueError(f"Batch/features mismatch: {tuple(x.shape)} vs {tuple(y.shape)}")
+            bw = _normalize_bandwidth(self.bandwidth)
+            op = torch.ops.softdtw_cuda.xy_forward if use_fused else torch.ops.softdtw_cuda.sq_forward
+            return op(x, y, float(self.gamma), bw)[0]
         if use_fused:
             return SoftDTWXYAutograd.apply(x, y, self.gamma, self.bandwidth)
         if (self.dist.lower() in _SQEUCLID_NAMES and x.is_cuda and y.is_cuda and x.device == y.device
