@@ -216,6 +216,8 @@ def time_oracle(name, budget_s):
         unit_cells = (3 if normalize else 1) * b_s * N * M
         desc = (f"{b_s} of {B} problems ({N}x{M}, D={D}{', normalize' if normalize else ''}) per call, "
                 "unfused reference algorithm")
+    # Every host core, also under torchrun (which sets OMP_NUM_THREADS=1).
+    O.set_num_threads(len(os.sched_getaffinity(0)))
     O.loss_and_grads(x, y, **kw)  # warm
     reps, t0 = 0, time.perf_counter()
     while reps == 0 or (time.perf_counter() - t0 < budget_s and reps < 1000):

@@ -50,6 +50,8 @@ def lib():
         L.oracle_backward_f64.argtypes = [P, P, I, I, I, Dd, Dd, P]
         L.oracle_cost_direct_f32.argtypes = [P, P, I, I, I, I, P]
         L.oracle_num_threads.restype = I
+        L.oracle_set_num_threads.argtypes = [I]
+        L.oracle_set_num_threads.restype = None
         _lib = L
     return _lib
 
@@ -68,6 +70,10 @@ def _bw(bandwidth) -> float:
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    lib().oracle_set_num_threads(int(n))
 
 
 def forward(D: np.ndarray, gamma: float, bandwidth=None):

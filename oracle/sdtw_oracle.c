@@ -192,6 +192,17 @@ void oracle_cost_direct_f32(const float *x, const float *y, int B, int N, int M,
         }
 }
 
+/* Thread count of the oracle's parallel regions (the bench's reference arm uses
+ * every host core even where the launcher set OMP_NUM_THREADS=1). */
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+    extern void omp_set_num_threads(int);
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     extern int omp_get_max_threads(void);
