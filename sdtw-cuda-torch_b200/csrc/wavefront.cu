@@ -147,11 +147,31 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
 
         const int n_steps = M + SR - 1;
         const int n_groups = (n_steps + PF - 1) / PF;
+        // Band-limited launch: only the groups whose anti-diagonals hold an
+        // in-band cell of this stripe run, t in [R0 - ibw - 1, SR - 1 + (R0 + SR - 1 + ibw)]
+        // (one step early, so that the first in-band cell has its diagonal
+        // predecessor from the stripe above); the rows outside are written as -inf.
+        int g_begin = 0, g_end = n_groups;
+        if constexpr (BANDED) {
+            const int t_lo = max(0, R0 - ibw - 1);
+            const int t_hi = min(n_steps - 1, (SR - 1) + min(M - 1, R0 + SR - 1 + ibw));
+            g_begin = (t_lo / PF) / NPH * NPH;
+            g_end = max(g_begin, min(n_groups, t_hi / PF + 1));
+        }
+        const int t_begin = g_begin * PF;
+        // Last column of the row above that is in the band (and so published by
+        // the stripe above); the columns past it read as -inf without the ring.
+        const int c_pub_max = BANDED ? min(M - 1, R0 - 1 + ibw) : M - 1;
         float dq[PD][K];  // cost rows: slot (t mod PD) holds row t
 #pragma unroll
         for (int u = 0; u < PD; ++u)
 #pragma unroll
-            for (int k = 0; k < K; ++k) dq[u][k] = __ldg(Dl + u * SR + k * 32);
+            for (int k = 0; k < K; ++k) dq[u][k] = __ldg(Dl + (t_begin + u) * SR + k * 32);
+        // The columns before t_begin are never read: report them consumed, so
+        // that the stripe above may run up to a full ring ahead of this start.
+        if (t_begin > 0)
+            st_relaxed_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed,
+                                      band_base + static_cast<uint32_t>(min(t_begin, M)));
 
         // Three live anti-diagonals: c* = step t-1, o* = step t-2, as (hi, lo).
         float ch[K], cl[K], oh[K], ol[K];
@@ -174,7 +194,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                 rin_h[u] = NEG;
                 rin_l[u] = 0.f;
             }
-            if (has_in && t0 < M) {  // warp-uniform
+            if (has_in && t0 < M && t0 <= c_pub_max) {  // warp-uniform
                 // Lane u (mod PF) reads slot u: one load instruction for the whole
                 // group (measured on B200: eight loads issued by one lane cost about
                 // 850 cycles per group, one warp-wide load about 200 with the
@@ -188,7 +208,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     const int col = t0 + u;
                     const uint32_t tg = in_wrap ? tg0 : tg0 + static_cast<uint32_t>(u);
                     bool mine = true;
-                    if (col < M) {
+                    if (col <= c_pub_max) {
                         uint64_t eh, el;
                         if (in_wrap) ld_pair(wrap_g + static_cast<uint32_t>(col) * 16u, eh, el);
                         else ld_pair_shared(my_ring_s + (tg % kRing) * 16u, eh, el);
@@ -299,11 +319,11 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         };
         using P0 = std::integral_constant<int, 0>;
         using P1 = std::integral_constant<int, 1>;
-        for (int gi = 0; gi < n_groups; gi += NPH) {
+        for (int gi = g_begin; gi < g_end; gi += NPH) {
             const int t0 = gi * PF;
             group(P0{}, t0);
             if constexpr (NPH == 2) {
-                if (gi + 1 < n_groups) group(P1{}, t0 + PF);
+                if (gi + 1 < g_end) group(P1{}, t0 + PF);
             }
             if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
@@ -311,8 +331,12 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
             }
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
-        // Rows past the last group are padding: -inf, like every cell outside the table.
-        for (int t = n_groups * PF; t < P.n_diag; ++t)
+        // Rows outside the groups that ran (padding, or out of the band): -inf,
+        // like every cell outside the table.
+        for (int t = 0; t < t_begin; ++t)
+#pragma unroll
+            for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = make_float2(NEG, 0.f);
+        for (int t = g_end * PF; t < P.n_diag; ++t)
 #pragma unroll
             for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = make_float2(NEG, 0.f);
         if (!quit && s == P.n_stripes - 1) {
@@ -424,6 +448,25 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         const int n_steps = M + SR - 1;
         const int n_groups = (n_steps + PF - 1) / PF;
         const int t_last = n_groups * PF - 1;  // steps past n_steps - 1 touch cells outside the table
+        // Band-limited launch: only the groups whose anti-diagonals hold an
+        // in-band cell of this stripe run (group gi covers t_last - gi*PF down
+        // to t_last - gi*PF - PF + 1); the rows outside are written as 0.
+        int gi_begin = 0, gi_end = n_groups;
+        if constexpr (BANDED) {
+            const int t_lo = max(0, R0 - ibw);
+            const int t_hi = min(n_steps - 1, (SR - 1) + min(M - 1, R0 + SR - 1 + ibw));
+            gi_begin = ((t_last - t_hi) / PF) / NPH * NPH;
+            gi_end = max(gi_begin, min(n_groups, (t_last - t_lo) / PF + 1));
+        }
+        const int t_top = t_last - gi_begin * PF;  // first (highest) step that runs
+        // Columns of the row below that are in the band (and so sent by the
+        // stripe below); messages for lower columns are zero without the ring.
+        const int c_min = BANDED ? max(0, R0 + SR - ibw) : 0;
+        // The columns above t_top - (SR - 1) are never read: report them
+        // consumed, so that the stripe below may run up to a full ring ahead.
+        if (t_top < t_last)
+            st_relaxed_cluster_u32_if(has_below && !below_wrap && lane == 31, below_consumed,
+                                      band_base + static_cast<uint32_t>(max(0, M - 1 - max(t_top - (SR - 1), -1))));
         // Queued loads: the step due in register slot j reads A(t-2) and
         // PS(t-1), refilled PD steps ahead from clamped (always valid)
         // addresses and used raw: a select on a loaded value would stall on the
@@ -446,17 +489,17 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         float2 pq[PD];     // PS(t-1) for the step due in slot j
 #pragma unroll
         for (int j = 0; j < PD; ++j) {
-            const int t = t_last - j;
+            const int t = t_top - j;
 #pragma unroll
             for (int k = 0; k < K; ++k) aq[j][k] = loadA(t - 2, k);
             pq[j] = loadPS(t - 1);
         }
         float2 A1[K];  // A(t-1)
 #pragma unroll
-        for (int k = 0; k < K; ++k) A1[k] = loadA(t_last - 1, k);
+        for (int k = 0; k < K; ++k) A1[k] = loadA(t_top - 1, k);
         float2 S1;  // row above at anti-diagonal t-1
         {
-            const float2 ps = loadPS(t_last);
+            const float2 ps = loadPS(t_top);
             S1.x = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].x, 1);
             S1.y = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].y, 1);
             if (lane == 0) S1 = ps_live ? ps : make_float2(NEG, 0.f);
@@ -477,7 +520,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
 #pragma unroll
             for (int u = 0; u < PF; ++u) rin[u] = 0.f;
             const int colb0 = t0 - (SR - 1);
-            if (has_below && colb0 - (PF - 1) < M && colb0 >= 0) {  // warp-uniform
+            if (has_below && colb0 - (PF - 1) < M && colb0 >= c_min) {  // warp-uniform
                 bool all = true;
                 float v = 0.f;
                 auto probe = [&]() {
@@ -489,7 +532,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                     const uint32_t tg = below_wrap ? in_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - col);
                     const uint32_t slot = below_wrap ? static_cast<uint32_t>(col) * 2u : (tg % kRing);
                     bool mine = true;
-                    if (col >= 0 && col < M) {
+                    if (col >= c_min && col < M) {
                         const uint64_t e = below_wrap ? ld_one(in_g + slot * 8u) : ld_one_shared(my_ring_s + slot * 8u);
                         mine = tag_of(e) == tg;
                         v = val_of(e);
@@ -601,19 +644,23 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         };
         using P0 = std::integral_constant<int, 0>;
         using P1 = std::integral_constant<int, 1>;
-        for (int gi = 0; gi < n_groups; gi += NPH) {
+        for (int gi = gi_begin; gi < gi_end; gi += NPH) {
             const int t0 = t_last - gi * PF;
             group(P0{}, t0);
             if constexpr (NPH == 2) {
-                if (gi + 1 < n_groups) group(P1{}, t0 - PF);
+                if (gi + 1 < gi_end) group(P1{}, t0 - PF);
             }
             if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
         }
-        // Rows past the last group are padding: zero, like every cell outside the table.
-        for (int t = n_groups * PF; t < P.n_diag; ++t)
+        // Rows outside the groups that ran (padding, or out of the band): zero,
+        // like every cell outside the table.
+        for (int t = 0; t <= t_last - gi_end * PF; ++t)
+#pragma unroll
+            for (int k = 0; k < K; ++k) El[static_cast<size_t>(t) * SR + k * 32] = 0.f;
+        for (int t = t_top + 1; t < P.n_diag; ++t)
 #pragma unroll
             for (int k = 0; k < K; ++k) El[static_cast<size_t>(t) * SR + k * 32] = 0.f;
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
