@@ -1150,19 +1150,27 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 128u);
     if (all_ok) {
+        // Anti-diagonal rows of the staged slices: warp w stores rows tl = w / NSL
+        // + (8 / NSL) i of slice w % NSL; lane p (and p + 32, ... for K > 1) is
+        // position p of the row.  Per slice: the rows' first and last columns
+        // are known in closed form, so the loop body is a load, two compares
+        // and a store.
         const float* stg = reinterpret_cast<const float*>(smem_raw);
-        for (int e = threadIdx.x; e < NSL * TL * SR; e += kThreads) {
-            const int pp = e % SR;
-            const int tl = (e / SR) % TL;
-            const int sl = e / (SR * TL);
-            const int ql = (pp % 32) * K + pp / 32;
-            const int jl = tl - ql;   // column within the tile
-            const int q = q0 + sl * SR + ql;
-            const int j = j0 + jl;
-            if (jl >= 0 && jl < kTileM && j < M && q < N) {
-                const int s = q / SR;
-                const int t = ql + j;
-                Dw[((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * SR + pp] = stg[e];
+        const int sl = warp % NSL;
+        const int q_base = q0 + sl * SR;  // first row of the slice
+        if (q_base < N) {
+            const int s = q_base / SR;
+            const size_t row0 = (static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag;
+            for (int tl = warp / NSL; tl < TL; tl += kThreads / 32 / NSL) {
+#pragma unroll
+                for (int kk = 0; kk < K; ++kk) {
+                    const int pp = kk * 32 + lane;
+                    const int ql = (pp % 32) * K + pp / 32;
+                    const int jl = tl - ql;  // column within the tile
+                    const int j = j0 + jl;
+                    if (jl >= 0 && jl < kTileM && j < M && q_base + ql < N)
+                        Dw[(row0 + ql + j) * SR + pp] = stg[(sl * TL + tl) * SR + pp];
+                }
             }
         }
     }
