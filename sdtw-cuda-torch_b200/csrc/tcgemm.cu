@@ -20,6 +20,7 @@
 // tcgen05.ld (warp w may read tensor-memory lanes 32(w%4)..32(w%4)+31, i.e.
 // those tile rows; the two warp groups take alternate 16-column chunks).
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include <cudaTypedefs.h>
@@ -971,12 +972,14 @@ cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
 // epilogue writes the tile's cells into shared memory by anti-diagonal and
 // stores anti-diagonal rows of the layout (cells of neighbouring tiles in the
 // same rows are left alone).
-constexpr int kCostStages = 2;
-
-template <int K>
+// ST = 1 or 2 operand stages.  One stage serialises copy, split and MMAs of a
+// chunk but halves the shared memory, so that two CTAs share an SM and one's
+// epilogue stores overlap the other's chunks.
+template <int K, int ST>
 __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __restrict__ x, const float* __restrict__ y,
                                                               float* __restrict__ Dw, const WavePlan P, int dim,
                                                               const WaitCtx wait) {
+    constexpr int kCostStages = ST;
     constexpr int SR = 32 * K;
     constexpr int NSL = kTileM / SR;       // stripes in the 128-row tile
     constexpr int TL = SR + kTileM - 1;    // anti-diagonal rows of one stripe slice
@@ -989,7 +992,10 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t op_bytes = kTileM / 8 * kSBO;     // one 128 x 32 operand buffer
     const uint32_t stage_bytes = 4 * op_bytes;       // A_hi, A_lo, B_hi, B_lo
-    unsigned char* ctrl = smem_raw + kCostStages * stage_bytes;
+    // Barriers and norms follow both the operand stages and the epilogue's
+    // staging area, which reuses the stages' space.
+    constexpr uint32_t kStageArea = static_cast<uint32_t>(NSL * TL * SR * sizeof(float));
+    unsigned char* ctrl = smem_raw + (kCostStages * stage_bytes > kStageArea ? kCostStages * stage_bytes : kStageArea);
     uint64_t* mbar = reinterpret_cast<uint64_t*>(ctrl);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 64);
     float* xn = reinterpret_cast<float*>(ctrl + 128);  // [2][128] partial, then [128]
@@ -1077,17 +1083,27 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     };
 
     bool ok = true;
-    issue(0);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (ST == 2) {
+        issue(0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     for (int c = 0; c < n_chunks; ++c) {
         const int st = c % kCostStages;
-        // Refill the other stage with chunk c+1 once the MMAs of chunk c-1 are done.
-        if (c + 1 < n_chunks) {
-            if (c >= 1 && ok) ok = mbar_wait(smem_addr(mbar + (c - 1) % kCostStages), static_cast<uint32_t>(((c - 1) / kCostStages) & 1), wc);
-            issue(c + 1);
+        if (ST == 2) {
+            // Refill the other stage with chunk c+1 once the MMAs of chunk c-1 are done.
+            if (c + 1 < n_chunks) {
+                if (c >= 1 && ok) ok = mbar_wait(smem_addr(mbar + (c - 1) % kCostStages), static_cast<uint32_t>(((c - 1) / kCostStages) & 1), wc);
+                issue(c + 1);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            // The single stage is free once the MMAs of chunk c-1 are done.
+            if (c >= 1 && ok) ok = mbar_wait(smem_addr(mbar), static_cast<uint32_t>((c - 1) & 1), wc);
+            issue(c);
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
         split(c);
         fence_async_smem();
         tc_fence_before();
@@ -1161,6 +1177,7 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
         if (q_base < N) {
             const int s = q_base / SR;
             const size_t row0 = (static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag;
+#pragma unroll 8
             for (int tl = warp / NSL; tl < TL; tl += kThreads / 32 / NSL) {
 #pragma unroll
                 for (int kk = 0; kk < K; ++kk) {
@@ -1176,8 +1193,8 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     }
 }
 
-static size_t cost_tc_smem_bytes(int K) {
-    const size_t ops = static_cast<size_t>(kCostStages) * 4 * (kTileM / 8) * kSBO;
+static size_t cost_tc_smem_bytes(int K, int stages) {
+    const size_t ops = static_cast<size_t>(stages) * 4 * (kTileM / 8) * kSBO;
     const size_t stage = static_cast<size_t>(kTileM / (32 * K)) * (32 * K + kTileM - 1) * (32 * K) * sizeof(float);
     return (ops > stage ? ops : stage) + 128 + 4 * kTileM * sizeof(float);
 }
@@ -1186,29 +1203,30 @@ bool cost_tc_supported(const float* x, const float* y, int dim) {
     return dim >= 16 && dim % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
 }
 
+template <int K, int ST>
+static cudaError_t cost_tc_go(const float* x, const float* y, float* Dw, const WavePlan& P, int dim,
+                              const WaitCtx& wait, cudaStream_t stream) {
+    const dim3 grid((P.M + kTileM - 1) / kTileM, (P.N + kTileM - 1) / kTileM, P.B);
+    const size_t smem = cost_tc_smem_bytes(K, ST);
+    cudaError_t e = cudaFuncSetAttribute(cost_tc_kernel<K, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cost_tc_kernel<K, ST><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_cost_tc(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
                            cudaStream_t stream) {
-    const dim3 grid((P.M + kTileM - 1) / kTileM, (P.N + kTileM - 1) / kTileM, P.B);
-    const size_t smem = cost_tc_smem_bytes(P.K);
-    cudaError_t e = cudaSuccess;
+    // One stage where that lets two CTAs share an SM (K <= 2: the shared memory
+    // is then the epilogue's staging area, under 100 KB).  Measured on B200
+    // (K = 1): C2 unfused cost 50 -> 38 us, 64 x 1024 x 1024 x 128 x 3 problems
+    // 1.27 -> 0.95 ms.
     switch (P.K) {
-        case 1:
-            e = cudaFuncSetAttribute(cost_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-            if (e == cudaSuccess) cost_tc_kernel<1><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
-            break;
-        case 2:
-            e = cudaFuncSetAttribute(cost_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-            if (e == cudaSuccess) cost_tc_kernel<2><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
-            break;
-        case 4:
-            e = cudaFuncSetAttribute(cost_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-            if (e == cudaSuccess) cost_tc_kernel<4><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
-            break;
-        default:
-            return cudaErrorInvalidValue;
+        case 1: return cost_tc_go<1, 1>(x, y, Dw, P, dim, wait, stream);
+        case 2: return cost_tc_go<2, 1>(x, y, Dw, P, dim, wait, stream);
+        case 4: return cost_tc_go<4, 2>(x, y, Dw, P, dim, wait, stream);
+        default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
 }
 
 }  // namespace sdtw
