@@ -510,6 +510,11 @@ __device__ __forceinline__ bool warp_wait(uint32_t mbar, uint32_t parity, const 
     return r != 0;
 }
 __device__ __forceinline__ float split_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+__device__ __forceinline__ float ld_shared_f32(uint32_t saddr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(saddr));
+    return v;
+}
 
 // Offset (floats) of anti-diagonal row t of stripe s of problem b, one row per lane.
 __device__ __forceinline__ size_t wl_row(const WavePlan& P, int b, int s, int t) {
@@ -696,14 +701,38 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
             if (u < nt * 8) b_live |= 1u << i;
             if (u < nt * 8 && f < nf) b_has |= 1u << i;
         }
-        // grad_x: row q = r0 + 32 (warp % 4) + lane, column units ku_i = warp / 4 + 4 i.
+        // grad_x: row q = r0 + 32 (warp % 4) + lane, column units ku_i = warp / 4 + 4 i;
+        // element (i, d) sits at byte gx_off[i][d] of slot c (bit i*4+d of
+        // gx_sel clear) or c + 1 (set).
         const int gx_rg = warp & 3;
         const bool gx_row_ok = GX && r0 + 32 * gx_rg + lane < N;
-        const uint32_t gx_src = static_cast<uint32_t>(gx_rg) * 4096u + static_cast<uint32_t>(lane) * 4u;
         const uint32_t gx_dst = op_off(32 * gx_rg + lane, 0);
-        // grad_y: element e (0 .. 7): row jl = 8 warp + (lane & 7), column ql = 4 e + lane / 8.
+        uint32_t gx_off[2][4];
+        uint32_t gx_sel = 0;
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int d = 0; d < 4; ++d) {
+                const int rel = lane + 4 * ((warp >> 2) + 4 * i) + d;  // t - 32c, 0 .. 62
+                gx_off[i][d] = static_cast<uint32_t>(gx_rg) * 4096u + static_cast<uint32_t>(rel & 31) * 128u +
+                               static_cast<uint32_t>(lane) * 4u;
+                if (rel >= 32) gx_sel |= 1u << (4 * i + d);
+            }
+        // grad_y: element e (0 .. 7): row jl = 8 warp + (lane & 7), column ql = 4 e + lane / 8,
+        // at byte gy_off[e] of the slot (128-byte swizzle).
         const int gy_i8 = lane & 7, gy_d = lane >> 3;
         const bool gy_row_ok = !GX && r0 + 8 * warp + gy_i8 < M;
+        uint32_t gy_off[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int r = 4 * e + gy_d + 8 * warp + gy_i8;  // slot row (t - r0)
+            gy_off[e] = static_cast<uint32_t>(r) * 128u +
+                        (static_cast<uint32_t>(e ^ ((4 * e + gy_d + gy_i8) & 7)) << 4) + static_cast<uint32_t>(gy_d) * 4u;
+        }
+        // Every cell of the tile is in the table except in the last chunk (or
+        // a last, partial row tile): elsewhere no bound checks are needed.
+        const bool rows_full = r0 + kTileM <= rows_out;
+        const uint32_t ring_s = smem_addr(ring);
 
         int s_c = 0;       // ring slot of unit c (and of c + 1: s_c1)
         uint32_t p_c = 0;  // phase parity of unit c: (c / S) & 1
@@ -716,9 +745,10 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
             if (GX && c == 0) ok = warp_wait(smem_addr(full + 0), 0u, wc, ok);
             ok = warp_wait(smem_addr(full + (GX ? s_c1 : s_c)), GX ? p_c1 : p_c, wc, ok);
             if (!ok) break;
+            const bool exact = rows_full && 32 * (c + 1) <= kt && !masked;  // warp-uniform
             if (GX) {
-                const unsigned char* slot0 = ring + static_cast<uint32_t>(s_c) * slot_bytes + gx_src;
-                const unsigned char* slot1 = ring + static_cast<uint32_t>(s_c1) * slot_bytes + gx_src;
+                const uint32_t base0 = ring_s + static_cast<uint32_t>(s_c) * slot_bytes;
+                const uint32_t base1 = ring_s + static_cast<uint32_t>(s_c1) * slot_bytes;
                 const int j_lim = M - 32 * c;  // columns j - 32c below this are in the table
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -726,32 +756,33 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
                     float v[4];
 #pragma unroll
                     for (int d = 0; d < 4; ++d) {
-                        const int rel = lane + 4 * ku + d;  // t - 32c, 0 .. 62
-                        const unsigned char* p = (rel < 32 ? slot0 : slot1) + static_cast<uint32_t>(rel & 31) * 128u;
-                        const float x = *reinterpret_cast<const float*>(p);
-                        bool okc = gx_row_ok && 4 * ku + d < j_lim;
-                        if (masked) okc = okc && *reinterpret_cast<const float*>(p + a_ring) > 0.f;
-                        v[d] = okc ? x : 0.f;
+                        const uint32_t a = ((gx_sel >> (4 * i + d)) & 1u ? base1 : base0) + gx_off[i][d];
+                        const float x = ld_shared_f32(a);
+                        if (exact) {
+                            v[d] = x;
+                        } else {
+                            bool okc = gx_row_ok && 4 * ku + d < j_lim;
+                            if (masked) okc = okc && ld_shared_f32(a + a_ring) > 0.f;
+                            v[d] = okc ? x : 0.f;
+                        }
                     }
                     ahi[i] = make_float4(split_hi(v[0]), split_hi(v[1]), split_hi(v[2]), split_hi(v[3]));
                     alo[i] = make_float4(v[0] - ahi[i].x, v[1] - ahi[i].y, v[2] - ahi[i].z, v[3] - ahi[i].w);
                 }
             } else {
-                const unsigned char* slot = ring + static_cast<uint32_t>(s_c) * slot_bytes;
+                const uint32_t base = ring_s + static_cast<uint32_t>(s_c) * slot_bytes;
                 const int q_lim = N - 32 * c;
                 float* hs = reinterpret_cast<float*>(ahi);
                 float* ls = reinterpret_cast<float*>(alo);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const int ql = 4 * e + gy_d;
-                    const int r = ql + 8 * warp + gy_i8;  // slot row (t - r0)
-                    const uint32_t off = static_cast<uint32_t>(r) * 128u +
-                                         (static_cast<uint32_t>(e ^ ((4 * e + gy_d + gy_i8) & 7)) << 4) +
-                                         static_cast<uint32_t>(gy_d) * 4u;
-                    float x = *reinterpret_cast<const float*>(slot + off);
-                    bool okc = gy_row_ok && ql < q_lim;
-                    if (masked) okc = okc && *reinterpret_cast<const float*>(slot + a_ring + off) > 0.f;
-                    x = okc ? x : 0.f;
+                    const uint32_t a = base + gy_off[e];
+                    float x = ld_shared_f32(a);
+                    if (!exact) {
+                        bool okc = gy_row_ok && 4 * e + gy_d < q_lim;
+                        if (masked) okc = okc && ld_shared_f32(a + a_ring) > 0.f;
+                        x = okc ? x : 0.f;
+                    }
                     hs[e] = split_hi(x);
                     ls[e] = x - hs[e];
                 }
