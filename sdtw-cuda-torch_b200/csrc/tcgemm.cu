@@ -1026,7 +1026,11 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     // Barriers and norms follow both the operand stages and the epilogue's
     // staging area, which reuses the stages' space.
     constexpr uint32_t kStageArea = static_cast<uint32_t>(NSL * TL * SR * sizeof(float));
-    unsigned char* ctrl = smem_raw + (kCostStages * stage_bytes > kStageArea ? kCostStages * stage_bytes : kStageArea);
+    // ST = 1: the operand stage plus separate raw buffers for x and y (the
+    // next chunk's copies land there while this chunk's MMAs run).
+    const uint32_t ops_area = ST == 1 ? 6 * op_bytes : kCostStages * stage_bytes;
+    unsigned char* ctrl = smem_raw + (ops_area > kStageArea ? ops_area : kStageArea);
+    float* npart = reinterpret_cast<float*>(ctrl + 128 + 4 * kTileM * sizeof(float));  // ST = 1: [2][128][8]
     uint64_t* mbar = reinterpret_cast<uint64_t*>(ctrl);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + 64);
     float* xn = reinterpret_cast<float*>(ctrl + 128);  // [2][128] partial, then [128]
@@ -1114,11 +1118,94 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     };
 
     bool ok = true;
+    // ST = 1 unit mapping (rm_row / rm_col): 8 consecutive lanes copy 8 rows of
+    // one 16-byte column (128 contiguous bytes of shared memory), and each row
+    // is read as 64 contiguous bytes of global memory.  Row norms accumulate
+    // per unit and are summed in a fixed order at the end.
+    float nx1[UPT], ny1[UPT];
+#pragma unroll
+    for (int i = 0; i < UPT; ++i) nx1[i] = ny1[i] = 0.f;
+    const uint32_t rawA = smem_base + 4 * op_bytes, rawB = rawA + op_bytes;
+    auto issue1 = [&](int c) {
+        const int f0 = c * kKT;
+#pragma unroll
+        for (int i = 0; i < UPT; ++i) {
+            const int row = rm_row(warp, lane, i), k = rm_col(warp, lane, i);
+            const int f = f0 + k;
+            const bool fx = q0 + row < N && f < dim;
+            const bool fy = j0 + row < M && f < dim;
+            const uint32_t off = op_off(row, k);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(rawA + off),
+                         "l"(fx ? xb + static_cast<size_t>(q0 + row) * dim + f : xb), "r"(fx ? 16u : 0u)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(rawB + off),
+                         "l"(fy ? yb + static_cast<size_t>(j0 + row) * dim + f : yb), "r"(fy ? 16u : 0u)
+                         : "memory");
+        }
+    };
+    auto split1 = [&]() {
+#pragma unroll
+        for (int i = 0; i < UPT; ++i) {
+            const uint32_t off = op_off(rm_row(warp, lane, i), rm_col(warp, lane, i));
+#pragma unroll
+            for (int o = 0; o < 2; ++o) {
+                const float4 v = *reinterpret_cast<const float4*>(smem_raw + (4 + o) * op_bytes + off);
+                float4 h, l;
+                h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+                h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+                h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+                h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+                l.x = v.x - h.x;
+                l.y = v.y - h.y;
+                l.z = v.z - h.z;
+                l.w = v.w - h.w;
+                unsigned char* hi = smem_raw + 2 * o * op_bytes;
+                *reinterpret_cast<float4*>(hi + off) = h;
+                *reinterpret_cast<float4*>(hi + op_bytes + off) = l;
+                float& acc = o == 0 ? nx1[i] : ny1[i];
+                acc = fmaf(v.x, v.x, acc);
+                acc = fmaf(v.y, v.y, acc);
+                acc = fmaf(v.z, v.z, acc);
+                acc = fmaf(v.w, v.w, acc);
+            }
+        }
+    };
+    if (ST == 1) {
+        issue1(0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        for (int c = 0; c < n_chunks; ++c) {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            // The operand stage is free once the MMAs of chunk c-1 are done.
+            if (c >= 1 && ok) ok = mbar_wait(smem_addr(mbar), static_cast<uint32_t>((c - 1) & 1), wc);
+            split1();
+            // Each thread refills only the raw units it has just read.
+            if (c + 1 < n_chunks) {
+                issue1(c + 1);
+                asm volatile("cp.async.commit_group;" ::: "memory");
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (threadIdx.x == 0 && ok) {
+                const uint32_t aH = smem_base, aL = aH + op_bytes, bH = aL + op_bytes, bL = bH + op_bytes;
+#pragma unroll
+                for (int ks = 0; ks < kKT / 8; ++ks) {
+                    const uint32_t o = static_cast<uint32_t>(ks) * 2 * kLBO;
+                    const uint32_t acc0 = (c > 0 || ks > 0) ? 1u : 0u;
+                    mma_tf32(tmem, smem_desc(aH + o), smem_desc(bH + o), idesc, acc0);
+                    mma_tf32(tmem, smem_desc(aH + o), smem_desc(bL + o), idesc, 1u);
+                    mma_tf32(tmem, smem_desc(aL + o), smem_desc(bH + o), idesc, 1u);
+                }
+                mma_commit(smem_addr(mbar));
+            }
+        }
+    }
     if (ST == 2) {
         issue(0);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    for (int c = 0; c < n_chunks; ++c) {
+    for (int c = 0; ST == 2 && c < n_chunks; ++c) {
         const int st = c % kCostStages;
         if (ST == 2) {
             // Refill the other stage with chunk c+1 once the MMAs of chunk c-1 are done.
@@ -1156,9 +1243,19 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
             mma_commit(smem_addr(mbar + st));
         }
     }
-    // Squared norms: threads r and r + 128 hold the two halves of row r.
-    xn[(threadIdx.x >> 7) * kTileM + urow] = xs2;
-    yn[(threadIdx.x >> 7) * kTileM + urow] = ys2;
+    if (ST == 1) {
+        // Squared norms: the 8 column units of row r, in column order.
+#pragma unroll
+        for (int i = 0; i < UPT; ++i) {
+            const int row = rm_row(warp, lane, i), ug = rm_col(warp, lane, i) / 4;
+            npart[row * 8 + ug] = nx1[i];
+            npart[kTileM * 8 + row * 8 + ug] = ny1[i];
+        }
+    } else {
+        // Squared norms: threads r and r + 128 hold the two halves of row r.
+        xn[(threadIdx.x >> 7) * kTileM + urow] = xs2;
+        yn[(threadIdx.x >> 7) * kTileM + urow] = ys2;
+    }
     if (n_chunks > 0 && ok) {
         const int cl = n_chunks - 1;
         ok = mbar_wait(smem_addr(mbar + cl % kCostStages), static_cast<uint32_t>((cl / kCostStages) & 1), wc);
@@ -1167,8 +1264,19 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     tc_fence_after();
     const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
     if (threadIdx.x < kTileM) {
-        xn[threadIdx.x] = xn[threadIdx.x] + xn[kTileM + threadIdx.x];
-        yn[threadIdx.x] = yn[threadIdx.x] + yn[kTileM + threadIdx.x];
+        if (ST == 1) {
+            float ax = 0.f, ay = 0.f;
+#pragma unroll
+            for (int ug = 0; ug < 8; ++ug) {
+                ax += npart[threadIdx.x * 8 + ug];
+                ay += npart[kTileM * 8 + threadIdx.x * 8 + ug];
+            }
+            xn[threadIdx.x] = ax;
+            yn[threadIdx.x] = ay;
+        } else {
+            xn[threadIdx.x] = xn[threadIdx.x] + xn[kTileM + threadIdx.x];
+            yn[threadIdx.x] = yn[threadIdx.x] + yn[kTileM + threadIdx.x];
+        }
     }
     __syncthreads();
 
@@ -1225,9 +1333,10 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
 }
 
 static size_t cost_tc_smem_bytes(int K, int stages) {
-    const size_t ops = static_cast<size_t>(stages) * 4 * (kTileM / 8) * kSBO;
+    const size_t op = (kTileM / 8) * kSBO;
+    const size_t ops = stages == 1 ? 6 * op : static_cast<size_t>(stages) * 4 * op;
     const size_t stage = static_cast<size_t>(kTileM / (32 * K)) * (32 * K + kTileM - 1) * (32 * K) * sizeof(float);
-    return (ops > stage ? ops : stage) + 128 + 4 * kTileM * sizeof(float);
+    return (ops > stage ? ops : stage) + 128 + 4 * kTileM * sizeof(float) + 2 * kTileM * 8 * sizeof(float);
 }
 
 bool cost_tc_supported(const float* x, const float* y, int dim) {
