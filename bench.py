@@ -57,6 +57,7 @@ PUBLISHED = {  # reference, B=32 N=M=512 D=64 fwd+bwd (unstated GPU
 }
 MUFU_PER_CELL = 7          # algorithmic ex2/lg2 per DP cell, forward + backward (reference algorithm)
 MUFU_PER_SM_CLK = 16       # ex2/lg2 results per SM per clock
+DEP_CYCLES = 105           # dependency chain of one cell (SHFL, max, adds, EX2, LG2, TwoSum, select)
 # Algorithmic HBM bytes per DP cell of each library kernel: every table entry
 # read or written once (cost 4 B, score 8 B as a (hi, lo) pair, E 4 B).
 ALG_BYTES = {"cost_wl": 4, "cost_tc": 4, "wavefront_fwd": 12, "wavefront_bwd": 12, "wl_to_rm": 8, "grad_xy": 8,
@@ -474,6 +475,21 @@ def main():
                      "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms_per_step": breakdown[k],
                                      "alg_ops_per_cell": ALG_MUFU[k]} for k, v in wf.items()},
                      "alg_ops_per_cell": MUFU_PER_CELL}
+    # Latency floor of the wavefronts: a problem needs N + M - 1 dependent
+    # anti-diagonal steps (n_bands * (M + 32) when its stripes loop over bands),
+    # each at least one cell's dependency chain (DEP_CYCLES, measured with
+    # clock64 microbenchmarks on B200); problems beyond what fits at once run
+    # in further waves.
+    n_prob = (hi - lo) if is_bary else (3 if normalize else 1) * B
+    Mp = N if is_bary else M
+    pinfo = _native.plan_info(n_prob, N, Mp)
+    steps = max(N + Mp - 1, pinfo["bands"] * (Mp + 32))
+    waves = -(-n_prob // max(1, pinfo["clusters_fit"]))
+    floor_ms = waves * steps * DEP_CYCLES / (sm_mhz * 1e6) * 1e3
+    roofline_latency = {"bound": "dependent chain", "unit": "ms", "cycles_per_step": DEP_CYCLES,
+                        "steps": steps, "waves": waves, "floor_ms": floor_ms,
+                        "kernels": {k: {"ms_per_step": breakdown[k], "frac": floor_ms / breakdown[k]}
+                                    for k in ALG_MUFU if k in breakdown}}
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -502,6 +518,7 @@ def main():
         "kernel_ms_per_step": breakdown,
         "roofline": roofline,
         "roofline_mufu": roofline_mufu,
+        "roofline_latency": roofline_latency,
         "cpu_baseline": cpu_baseline,
         "e2e": e2e,
         "gpu_launches": launches,
