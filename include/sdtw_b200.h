@@ -18,7 +18,8 @@
  * of float32 (hi, lo) with T = hi + lo, in the anti-diagonal ("wavefront")
  * layout the kernels write with coalesced stores.  It must be 8-byte aligned;
  * workspaces 256-byte aligned.  The cost table of the unfused x/y entry points
- * (sdtw_cost_elems floats) uses the same anti-diagonal layout.
+ * (sdtw_cost_elems floats) uses the same anti-diagonal layout and must be
+ * 16-byte aligned.
  * sdtw_score_to_R_f32 / sdtw_R_to_score_f32 convert to and from the
  * reference layout.
  */

@@ -242,9 +242,9 @@ WavePlan plan(int B, int N, int M) {
 //   D-input forward/backward : [wrap ring][WL table]
 //   x/y forward              : [wrap ring][WL cost]
 //   x/y backward, sqeuclid bwd: [wrap ring][WL E][gradient operands]
-//     one row per lane: x, y in the chunked transposed layout (B, ceil(N/32),
-//     dim, 36) and (B, ceil(M/32), dim, 36);
-//     more rows per lane: G, G^T, x^T, y^T row-major, rows padded to a
+//     grad_wl (one row per lane, N or M above 128): x, y in the chunked
+//     transposed layout (B, ceil(N/32), dim, 36) and (B, ceil(M/32), dim, 36);
+//     grad_rm (otherwise): G, G^T, x^T, y^T row-major, rows padded to a
 //     multiple of 32 floats
 size_t wave_ws(int B, int N, int M) {
     WavePlan p = plan(B, N, M);
@@ -252,13 +252,20 @@ size_t wave_ws(int B, int N, int M) {
 }
 size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
 size_t pad32(int n) { return (static_cast<size_t>(n) + 31) & ~static_cast<size_t>(31); }
+// The gradient from the wavefront layout (grad_wl, one row per lane) or from
+// row-major operands (grad_rm): the latter for more rows per lane, and for
+// problems of at most one 128-row tile each way, where each grad_wl CTA runs
+// a single tile and its warp-specialised pipeline never fills.
+bool grad_rm_path(int N, int M) {
+    return rows_per_lane(N, g_k_override.load()) != 1 || (N <= 128 && M <= 128);
+}
 struct GradOperands {
     size_t g, gt, xt, yt, total;  // byte offsets from the start of the region
 };
 GradOperands grad_operands(int B, int N, int M, int dim) {
     GradOperands o;
     const size_t b = static_cast<size_t>(B);
-    if (rows_per_lane(N, g_k_override.load()) == 1) {  // xTc, yTc: rows of 36 floats per 32 positions
+    if (!grad_rm_path(N, M)) {  // xTc, yTc: rows of 36 floats per 32 positions
         o.g = o.gt = 0;
         o.xt = 0;
         o.yt = align_up(b * (pad32(N) / 32) * dim * 36 * sizeof(float), 256);
@@ -600,7 +607,9 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     cudaError_t e;
     char* region = static_cast<char*>(workspace) + w0 + wl_bytes(B, N, M);
     const GradOperands o = grad_operands(B, N, M, dim);
-    if (grad_wl_supported(g.P) && (reinterpret_cast<uintptr_t>(mask_w) & 15u) == 0) {
+    if (!grad_rm_path(N, M)) {
+        if ((reinterpret_cast<uintptr_t>(mask_w) & 15u) != 0)
+            return fail(SDTW_ERR_INVALID_ARGUMENT, "cost table must be 16-byte aligned");
         // G straight from the wavefront layout; x, y in the chunked transposed layout.
         float* xTc = reinterpret_cast<float*>(region + o.xt);
         float* yTc = reinterpret_cast<float*>(region + o.yt);

@@ -39,8 +39,12 @@ def test_sizes_without_gpu():
     assert L.sdtw_cost_elems(4, 64, 64) == cells
     # One band: no wrap ring; the wavefront-layout table of the cost / E.
     assert L.sdtw_workspace_bytes(4, 64, 64) == -(-cells * 4 // 256) * 256
-    # x/y backward adds x and y in the chunked transposed layout (B, N/32, dim, 36).
-    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) == L.sdtw_workspace_bytes(4, 64, 64) + 2 * (-(-4 * 2 * 3 * 36 * 4 // 256) * 256)
+    # x/y backward adds the gradient operands.
+    up = lambda v: -(-v // 256) * 256
+    # One 128-row tile each way: G, G^T, x^T, y^T row-major with rows padded to 32.
+    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) == L.sdtw_workspace_bytes(4, 64, 64) + 2 * up(4 * 64 * 64 * 4) + 2 * up(4 * 3 * 64 * 4)
+    # Longer: x, y chunked and transposed, rows of 36 floats per 32 positions.
+    assert L.sdtw_workspace_bytes_xy(4, 200, 64, 3) == L.sdtw_workspace_bytes(4, 200, 64) + up(4 * 7 * 3 * 36 * 4) + up(4 * 2 * 3 * 36 * 4)
 
 
 def test_invalid_arguments_rejected():

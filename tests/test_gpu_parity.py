@@ -105,12 +105,15 @@ def test_shapes_vs_oracle(shape, fused):
 
 @pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("dim", [1, 33, 128, 241, 300, 513])
-def test_feature_dims(dim, fused):
+@pytest.mark.parametrize("NM", [(70, 90), (150, 190)], ids=["rm", "wl"])
+def test_feature_dims(dim, fused, NM):
     """Gradients on the tensor cores (3xTF32): feature blocks of up to 240
-    columns plus the row-sum column, partial 128-row tiles and K chunks."""
+    columns plus the row-sum column, partial 128-row tiles and K chunks.
+    Lengths of at most 128 take the row-major operand kernel, longer ones the
+    kernel that reads E from the wavefront layout."""
     rng = np.random.default_rng(dim)
-    x = (rng.standard_normal((2, 70, dim)) / np.sqrt(dim)).astype(np.float32)
-    y = (rng.standard_normal((2, 90, dim)) / np.sqrt(dim)).astype(np.float32)
+    x = (rng.standard_normal((2, NM[0], dim)) / np.sqrt(dim)).astype(np.float32)
+    y = (rng.standard_normal((2, NM[1], dim)) / np.sqrt(dim)).astype(np.float32)
     out, gx, gy = _gpu_run(x, y, gamma=1.0, fused=fused)
     _check_against_oracle(x, y, out, gx, gy, gamma=1.0, fused=fused)
 
