@@ -184,6 +184,13 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         float upl_prev = 0.f;
         const int q0 = lane * K;  // row offset of k = 0 in the stripe
         const int rows_left = N - R0;
+        // Band-wrap input (global memory, an L2 round trip per load): the slots
+        // of the next group are loaded one group ahead.  The data is normally
+        // long written by then (the band above ran M + SR - 1 steps earlier);
+        // a slot read too early shows an older tag and is polled again.
+        uint64_t wpf_h = 0, wpf_l = 0;
+        if (has_in && in_wrap && t_begin < M && t_begin + (lane & (PF - 1)) <= c_pub_max)
+            ld_pair(wrap_g + static_cast<uint32_t>(t_begin + (lane & (PF - 1))) * 16u, wpf_h, wpf_l);
 
         auto group = [&](auto phase_c, int t0) {
             constexpr int PH = decltype(phase_c)::value;
@@ -218,7 +225,19 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     }
                     all = __all_sync(SDTW_FULL_MASK, mine);
                 };
-                probe();
+                if (in_wrap) {  // warp-uniform: the prefetched slots, then the next group's
+                    const int col = t0 + (lane & (PF - 1));
+                    bool mine = true;
+                    if (col <= c_pub_max) {
+                        mine = tag_of(wpf_h) == tg0 && tag_of(wpf_l) == tg0;
+                        vh = val_of(wpf_h);
+                        vl = val_of(wpf_l);
+                    }
+                    all = __all_sync(SDTW_FULL_MASK, mine);
+                    if (col + PF <= c_pub_max) ld_pair(wrap_g + static_cast<uint32_t>(col + PF) * 16u, wpf_h, wpf_l);
+                } else {
+                    probe();
+                }
                 if (!all && ok) {  // uniform (vote)
                     uint64_t w0 = 0;
                     for (uint32_t it = 1;; ++it) {
@@ -511,6 +530,13 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         const int q0 = lane * K;
         const int rows_left = N - R0;
         float* El = Es + lane;
+        // Band-wrap input (global memory): the slots of the next group are
+        // loaded one group ahead, as in the forward.
+        uint64_t wpf = 0;
+        {
+            const int col = t_top - (SR - 1) - (lane & (PF - 1));
+            if (has_below && below_wrap && col >= c_min && col < M) wpf = ld_one(in_g + static_cast<uint32_t>(col) * 16u);
+        }
 
         auto group = [&](auto phase_c, int t0) {
             constexpr int PH = decltype(phase_c)::value;
@@ -539,7 +565,18 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                     }
                     all = __all_sync(SDTW_FULL_MASK, mine);
                 };
-                probe();
+                if (below_wrap) {  // warp-uniform: the prefetched slots, then the next group's
+                    const int col = colb0 - (lane & (PF - 1));
+                    bool mine = true;
+                    if (col >= c_min && col < M) {
+                        mine = tag_of(wpf) == in_tag_wrap;
+                        v = val_of(wpf);
+                    }
+                    all = __all_sync(SDTW_FULL_MASK, mine);
+                    if (col - PF >= c_min && col - PF < M) wpf = ld_one(in_g + static_cast<uint32_t>(col - PF) * 16u);
+                } else {
+                    probe();
+                }
                 if (!all && ok) {  // uniform: the tag vote is warp-wide
                     uint64_t w0 = 0;
                     for (uint32_t it = 1;; ++it) {
