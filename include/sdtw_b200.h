@@ -20,8 +20,12 @@
  * workspaces 256-byte aligned.  The cost table of the unfused x/y entry points
  * (sdtw_cost_elems floats) uses the same anti-diagonal layout and must be
  * 16-byte aligned.
- * sdtw_score_to_R_f32 / sdtw_R_to_score_f32 convert to and from the
- * reference layout.
+ * sdtw_score_to_R_f32 / sdtw_R_to_score_f32 convert the table of
+ * sdtw_forward_f32 to and from the reference layout.  The x/y pairs
+ * (sdtw_forward_xy_f32 / sdtw_backward_xy_f32 and the sqeuclid pair) keep, in a
+ * buffer of the same size, the state their backward needs: with one row per
+ * lane, each cell's softmax weights of its diagonal and upper predecessors
+ * instead of its score.  Pass that buffer only to the matching backward.
  */
 #ifndef SDTW_B200_H
 #define SDTW_B200_H

@@ -323,10 +323,15 @@ GradOperands grad_operands(int B, int N, int M, int dim) {
     return o;
 }
 
+// weights: the table keeps each cell's predecessor weights (the state of the
+// x/y pairs' backward, one row per lane) instead of its score.
+bool weight_store(int B, int N, int M) { return plan(B, N, M).K == 1; }
+
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
-                uint64_t* wrap, cudaStream_t stream) {
+                uint64_t* wrap, cudaStream_t stream, bool weights = false) {
     FwdArgs a{};
     a.P = plan(B, N, M);
+    a.weights = weights ? 1 : 0;
     a.Dw = Dw;
     a.score = reinterpret_cast<float2*>(score);
     a.out = out;
@@ -348,9 +353,10 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
 }
 
 int run_backward(const float* score, const float* grad_out, float* Ew, int B, int N, int M, float bw,
-                 uint64_t* wrap, cudaStream_t stream) {
+                 uint64_t* wrap, cudaStream_t stream, bool weights = false) {
     BwdArgs a{};
     a.P = plan(B, N, M);
+    a.weights = weights ? 1 : 0;
     a.score = reinterpret_cast<const float2*>(score);
     a.grad_out = grad_out;
     a.Ew = Ew;
@@ -622,7 +628,8 @@ int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out
         e = launch_cost_wl(x, y, Dw, plan(B, N, M), dim, true, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
-    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
+    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st,
+                       weight_store(B, N, M));
 }
 
 // Backward through the x/y chain rule; mask_w (WL cost) applies the clamp mask
@@ -632,7 +639,8 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
                        cudaStream_t st) {
     const size_t w0 = wave_ws(B, N, M);
     float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
-    int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st);
+    int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st,
+                          weight_store(B, N, M));
     if (rc) return rc;
     if (!grad_x && !grad_y) return SDTW_OK;
     GradTcArgs g{};
@@ -728,7 +736,8 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
         e = launch_cost_wl(x, y, cost, plan(B, N, M), dim, false, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
-    return run_forward(cost, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st);
+    return run_forward(cost, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st,
+                       weight_store(B, N, M));
 }
 
 int sdtw_backward_sqeuclid_f32(const float* x, const float* y, const float* score, const float* cost,

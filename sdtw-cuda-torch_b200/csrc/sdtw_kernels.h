@@ -24,6 +24,7 @@ struct FwdArgs {
     int ibw;          // integer band: cell (i, j) is kept when |i - j| <= ibw (floor(bw), or 2^29 when disabled)
     uint32_t seq;     // launch sequence number (tags of the global ring)
     int debug_stall;  // stripe whose output is withheld (failure-detection tests); -1 = none
+    int weights;      // nonzero: store each cell's predecessor weights instead of its score (one row per lane)
     WaitCtx wait;
 };
 
@@ -37,6 +38,7 @@ struct BwdArgs {
     int ibw;
     uint32_t seq;
     int debug_stall;
+    int weights;  // nonzero: `score` holds the forward's predecessor weights (one row per lane)
     WaitCtx wait;
 };
 

@@ -24,7 +24,11 @@
 //   * the backward weight exp((R[c] - D[c] - R[p]) / gamma) equals the softmax
 //     weight of predecessor p among c's three predecessors, so the reverse pass
 //     recomputes it from the stored scores of c's predecessors, normalised to
-//     sum to one.  It needs no cost values and no log-space E table.
+//     sum to one.  It needs no cost values and no log-space E table.  With the
+//     weight store (W, one row per lane: the x/y entry points) the forward
+//     writes those weights itself -- it has the three exponentials at hand --
+//     as (diagonal, upper), the left one being 1 minus both, and the reverse
+//     step is three multiply-adds and a shuffle.
 //   * one warp per stripe of 32*K rows, three live anti-diagonals in registers,
 //     neighbour rows exchanged with one warp shuffle per step, stripe-to-stripe
 //     rows handed over through tagged u64 ring slots in the consumer's shared
@@ -43,6 +47,10 @@ constexpr int kRing = 128;  // ring slots per warp (power of two)
 // for interior groups without the edge masks measured slower (the bodies no
 // longer fit the instruction cache), so every group runs the masked body.
 constexpr int kFwdPhases = 2;
+// Prefetch distance of the reverse pass with the weight store, in groups:
+// measured on B200 (C2 / C3 / C5 shapes), 2 beats 1 by 9-18 % (the loads were
+// exposed) and 4 (four step bodies) is slower than both.
+constexpr int kBwdWeightPhases = 2;
 
 __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
     return (seq << 12) | (static_cast<uint32_t>(band) & 0xfffu);
@@ -82,8 +90,9 @@ __device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
 // addresses.  Cells outside the table (left of column 0, right of column M-1,
 // rows past N) or the band are stored as -inf.  The last cell's score is read
 // back from the store after the stripe.
-template <int K, bool BANDED>
+template <int K, bool BANDED, bool W>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a) {
+    static_assert(!W || K == 1, "the weight store is built for one row per lane");
     constexpr int PF = StepCfg<K>::PF;
     constexpr int NPH = kFwdPhases;  // prefetch distance in groups
     constexpr int PD = NPH * PF;     // prefetch distance (steps)
@@ -184,6 +193,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         float upl_prev = 0.f;
         const int q0 = lane * K;  // row offset of k = 0 in the stripe
         const int rows_left = N - R0;
+        // Weight store: the lane of the last row keeps the last cell's score
+        // (step t_last) as it passes, instead of reading it back.
+        const int t_last = (W && s == P.n_stripes - 1 && lane == N - 1 - R0) ? N - 1 - R0 + M - 1 : -1;
+        float last_h = 0.f, last_l = 0.f;
         // Band-wrap input (global memory, an L2 round trip per load): the slots
         // of the next group are loaded one group ahead.  The data is normally
         // long written by then (the band above ran M + SR - 1 steps earlier);
@@ -306,7 +319,8 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     const float p = c[k] * kk;
                     const float e = fmaf(c[k], kk, -p);
                     const float m = max3f(dh, uh, lh);
-                    const float sm = ex2f((dh - m) + dl) + ex2f((uh - m) + ul) + ex2f((lh - m) + ll);
+                    const float ed = ex2f((dh - m) + dl), eu = ex2f((uh - m) + ul), el = ex2f((lh - m) + ll);
+                    const float sm = ed + eu + el;
                     const float delta = (lg2f(sm) - p) - e;
                     // TwoSum: m + delta = hi + lo exactly.
                     const float hi = m + delta;
@@ -319,7 +333,17 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                         live = live && static_cast<unsigned>(R0 + q0 + k - col + ibw) <= static_cast<unsigned>(2 * ibw);
                     nh[k] = live ? hi : NEG;
                     nl[k] = live ? lo : 0.f;
-                    Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
+                    if constexpr (W) {
+                        // The softmax weights of the diagonal and upper
+                        // predecessors (the left one is 1 minus both): all the
+                        // reverse pass needs of this cell.  Zero outside.
+                        const float inv = rcpf(sm);
+                        Tg[u * SR] = make_float2(live ? ed * inv : 0.f, live ? eu * inv : 0.f);
+                        last_h = (t == t_last) ? nh[k] : last_h;
+                        last_l = (t == t_last) ? nl[k] : last_l;
+                    } else {
+                        Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
+                    }
                 }
                 // Bottom row of the stripe goes to the next stripe's warp.
                 const int colb = colb0 + u;
@@ -351,14 +375,16 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
         // Rows outside the groups that ran (padding, or out of the band): -inf,
-        // like every cell outside the table.
+        // like every cell outside the table (weights: zero).
+        const float2 fill = W ? make_float2(0.f, 0.f) : make_float2(NEG, 0.f);
         for (int t = 0; t < t_begin; ++t)
 #pragma unroll
-            for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = make_float2(NEG, 0.f);
+            for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = fill;
         for (int t = g_end * PF; t < P.n_diag; ++t)
 #pragma unroll
-            for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = make_float2(NEG, 0.f);
-        if (!quit && s == P.n_stripes - 1) {
+            for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = fill;
+        if (W && !quit && t_last >= 0) a.out[b] = fmaf(-last_h, a.inv_k, -last_l * a.inv_k);
+        if (!W && !quit && s == P.n_stripes - 1) {
             // Last cell (N-1, M-1): row q of this stripe, step q + M - 1; the
             // owning lane reads back its own store.
             const int q = N - 1 - R0;
@@ -392,12 +418,14 @@ __device__ __forceinline__ float2 load_score(const float2* __restrict__ S, const
 // loads, PF steps ahead), the row above from the neighbour lane by shuffle,
 // and for lane 0 the last row of the previous stripe (one prefetched load).
 // E is written in the wavefront layout.
-template <int K, bool BANDED>
+template <int K, bool BANDED, bool W>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a) {
+    static_assert(!W || K == 1, "the weight store is built for one row per lane");
     constexpr int PF = StepCfg<K>::PF;
     // Prefetch distance: one group (K = 1, whose 512-thread launches leave 128
-    // registers per thread) or two groups (K > 1).
-    constexpr int NPH = K == 1 ? 1 : 2;
+    // registers per thread), two groups (K > 1), or with the weight store,
+    // whose steps are short and load one float2 each, kBwdWeightPhases groups.
+    constexpr int NPH = W ? kBwdWeightPhases : (K == 1 ? 1 : 2);
     constexpr int PD = NPH * PF;
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -504,20 +532,25 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
             return __ldg(Tp + static_cast<size_t>(cc) * SR);
         };
 
-        float2 aq[PD][K];  // A(t-2) for the step due in slot j
+        // Weight store (W): the step due in slot j reads its own cell's
+        // weights, row t, queued PD steps ahead; nothing else is loaded.
+        float2 aq[PD][K];  // A(t-2) for the step due in slot j (W: the weights of row t)
         float2 pq[PD];     // PS(t-1) for the step due in slot j
+        float2 A1[K];      // A(t-1)
+        float2 S1;         // row above at anti-diagonal t-1
+        if constexpr (W) {
 #pragma unroll
-        for (int j = 0; j < PD; ++j) {
-            const int t = t_top - j;
+            for (int j = 0; j < PD; ++j) aq[j][0] = loadA(t_top - j, 0);
+        } else {
 #pragma unroll
-            for (int k = 0; k < K; ++k) aq[j][k] = loadA(t - 2, k);
-            pq[j] = loadPS(t - 1);
-        }
-        float2 A1[K];  // A(t-1)
+            for (int j = 0; j < PD; ++j) {
+                const int t = t_top - j;
 #pragma unroll
-        for (int k = 0; k < K; ++k) A1[k] = loadA(t_top - 1, k);
-        float2 S1;  // row above at anti-diagonal t-1
-        {
+                for (int k = 0; k < K; ++k) aq[j][k] = loadA(t - 2, k);
+                pq[j] = loadPS(t - 1);
+            }
+#pragma unroll
+            for (int k = 0; k < K; ++k) A1[k] = loadA(t_top - 1, k);
             const float2 ps = loadPS(t_top);
             S1.x = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].x, 1);
             S1.y = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].y, 1);
@@ -615,68 +648,92 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 - u;
                 constexpr int J0 = PH * PF;
-                float2 A2[K];
-#pragma unroll
-                for (int k = 0; k < K; ++k) {
-                    A2[k] = aq[J0 + u][k];
-                    aq[J0 + u][k] = loadA(t - 2 - PD, k);
-                }
-                float2 S2;
-                {
-                    const float2 ps = pq[J0 + u];
-                    pq[J0 + u] = loadPS(t - 1 - PD);
-                    S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
-                    S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
-                    S2.x = (lane == 0) ? (ps_live ? ps.x : NEG) : S2.x;
-                    S2.y = (lane == 0) ? (ps_live ? ps.y : 0.f) : S2.y;
-                }
-                float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
-                below = (lane == 31) ? rin[u] : below;
-                float nmsg[K];
-#pragma unroll
-                for (int k = K - 1; k >= 0; --k) {
-                    const int q = q0 + k;
-                    const int col = t - q;
-                    const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
-                    float e = accl[k] + in_below;
-                    float2 tl = A1[k];
-                    float2 tu = (k == 0) ? S1 : A1[k > 0 ? k - 1 : 0];
-                    float2 td = (k == 0) ? S2 : A2[k > 0 ? k - 1 : 0];
-                    bool live = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                if constexpr (W) {
+                    const float2 w = aq[J0 + u][0];  // (diagonal, upper) weights of cell (q0, t - q0)
+                    aq[J0 + u][0] = loadA(t - PD, 0);
+                    float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
+                    below = (lane == 31) ? rin[u] : below;
+                    const int col = t - q0;
+                    bool live = q0 < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
                     if constexpr (BANDED)
-                        live = live && static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                    e = (q == rows_left - 1 && col == M - 1) ? gb : e;
+                        live = live && static_cast<unsigned>(R0 + q0 - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    float e = accl[0] + below;
+                    e = (q0 == rows_left - 1 && col == M - 1) ? gb : e;
                     e = live ? e : 0.f;
-                    // Predecessor scores; column -1 is the border (+inf R),
-                    // except the corner (-1, -1) of row 0 (R = 0).
-                    const bool c0 = (col == 0);
-                    tl.x = c0 ? NEG : tl.x;
-                    tl.y = c0 ? 0.f : tl.y;
-                    td.x = c0 ? ((R0 + q == 0) ? 0.f : NEG) : td.x;
-                    td.y = c0 ? 0.f : td.y;
-                    Eg[-static_cast<ptrdiff_t>(u) * SR + k * 32] = e;
-                    // Softmax of the predecessors' scores; the lo of the max cancels.
-                    const float m = max3f(td.x, tu.x, tl.x);
-                    const float ed = ex2f((td.x - m) + td.y);
-                    const float eu = ex2f((tu.x - m) + tu.y);
-                    const float el = ex2f((tl.x - m) + tl.y);
-                    const float inv = live ? rcpf(ed + eu + el) : 0.f;
-                    const float ei = e * inv;
-                    accl[k] = ei * el;
-                    nmsg[k] = fmaf(ei, eu, dprev[k]);
-                    dprev[k] = ei * ed;
-                }
-                // Message of row 0 to the stripe above, column t.
-                const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
-                const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
-                const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
-                st_one_if(pub, out_g + slot * 8u, pack_tagged(nmsg[0], tgo));
+                    Eg[-static_cast<ptrdiff_t>(u) * SR] = e;
+                    const float wl = (1.f - w.x) - w.y;
+                    accl[0] = e * wl;
+                    const float nm = fmaf(e, w.y, dprev[0]);
+                    dprev[0] = e * w.x;
+                    const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
+                    const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
+                    const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
+                    st_one_if(pub, out_g + slot * 8u, pack_tagged(nm, tgo));
+                    msg[0] = nm;
+                } else {
+                    float2 A2[K];
 #pragma unroll
-                for (int k = 0; k < K; ++k) {
-                    msg[k] = nmsg[k];
-                    A1[k] = A2[k];
+                    for (int k = 0; k < K; ++k) {
+                        A2[k] = aq[J0 + u][k];
+                        aq[J0 + u][k] = loadA(t - 2 - PD, k);
+                    }
+                    float2 S2;
+                    {
+                        const float2 ps = pq[J0 + u];
+                        pq[J0 + u] = loadPS(t - 1 - PD);
+                        S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
+                        S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
+                        S2.x = (lane == 0) ? (ps_live ? ps.x : NEG) : S2.x;
+                        S2.y = (lane == 0) ? (ps_live ? ps.y : 0.f) : S2.y;
+                    }
+                    float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
+                    below = (lane == 31) ? rin[u] : below;
+                    float nmsg[K];
+#pragma unroll
+                    for (int k = K - 1; k >= 0; --k) {
+                        const int q = q0 + k;
+                        const int col = t - q;
+                        const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
+                        float e = accl[k] + in_below;
+                        float2 tl = A1[k];
+                        float2 tu = (k == 0) ? S1 : A1[k > 0 ? k - 1 : 0];
+                        float2 td = (k == 0) ? S2 : A2[k > 0 ? k - 1 : 0];
+                        bool live = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                        if constexpr (BANDED)
+                            live = live && static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                        e = (q == rows_left - 1 && col == M - 1) ? gb : e;
+                        e = live ? e : 0.f;
+                        // Predecessor scores; column -1 is the border (+inf R),
+                        // except the corner (-1, -1) of row 0 (R = 0).
+                        const bool c0 = (col == 0);
+                        tl.x = c0 ? NEG : tl.x;
+                        tl.y = c0 ? 0.f : tl.y;
+                        td.x = c0 ? ((R0 + q == 0) ? 0.f : NEG) : td.x;
+                        td.y = c0 ? 0.f : td.y;
+                        Eg[-static_cast<ptrdiff_t>(u) * SR + k * 32] = e;
+                        // Softmax of the predecessors' scores; the lo of the max cancels.
+                        const float m = max3f(td.x, tu.x, tl.x);
+                        const float ed = ex2f((td.x - m) + td.y);
+                        const float eu = ex2f((tu.x - m) + tu.y);
+                        const float el = ex2f((tl.x - m) + tl.y);
+                        const float inv = live ? rcpf(ed + eu + el) : 0.f;
+                        const float ei = e * inv;
+                        accl[k] = ei * el;
+                        nmsg[k] = fmaf(ei, eu, dprev[k]);
+                        dprev[k] = ei * ed;
+                    }
+                    // Message of row 0 to the stripe above, column t.
+                    const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
+                    const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
+                    const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
+                    st_one_if(pub, out_g + slot * 8u, pack_tagged(nmsg[0], tgo));
+#pragma unroll
+                    for (int k = 0; k < K; ++k) {
+                        msg[k] = nmsg[k];
+                        A1[k] = A2[k];
+                    }
+                    S1 = S2;
                 }
-                S1 = S2;
             }
         };
         using P0 = std::integral_constant<int, 0>;
@@ -684,8 +741,12 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         for (int gi = gi_begin; gi < gi_end; gi += NPH) {
             const int t0 = t_last - gi * PF;
             group(P0{}, t0);
-            if constexpr (NPH == 2) {
+            if constexpr (NPH >= 2) {
                 if (gi + 1 < gi_end) group(P1{}, t0 - PF);
+            }
+            if constexpr (NPH >= 4) {
+                if (gi + 2 < gi_end) group(std::integral_constant<int, 2>{}, t0 - 2 * PF);
+                if (gi + 3 < gi_end) group(std::integral_constant<int, 3>{}, t0 - 3 * PF);
             }
             if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
@@ -791,15 +852,21 @@ int max_active_clusters(const WavePlan& P) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const void* fns[2] = {nullptr, nullptr};
+    const void* fns[4] = {nullptr, nullptr, nullptr, nullptr};
     switch (P.K) {
-        case 1: fns[0] = (const void*)fwd_kernel<1, false>; fns[1] = (const void*)bwd_kernel<1, false>; break;
-        case 2: fns[0] = (const void*)fwd_kernel<2, false>; fns[1] = (const void*)bwd_kernel<2, false>; break;
-        case 4: fns[0] = (const void*)fwd_kernel<4, false>; fns[1] = (const void*)bwd_kernel<4, false>; break;
+        case 1:
+            fns[0] = (const void*)fwd_kernel<1, false, false>;
+            fns[1] = (const void*)bwd_kernel<1, false, false>;
+            fns[2] = (const void*)fwd_kernel<1, false, true>;
+            fns[3] = (const void*)bwd_kernel<1, false, true>;
+            break;
+        case 2: fns[0] = (const void*)fwd_kernel<2, false, false>; fns[1] = (const void*)bwd_kernel<2, false, false>; break;
+        case 4: fns[0] = (const void*)fwd_kernel<4, false, false>; fns[1] = (const void*)bwd_kernel<4, false, false>; break;
         default: return -1;
     }
     int best = -1;
     for (const void* fn : fns) {
+        if (!fn) continue;
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
             (void)cudaGetLastError();
@@ -816,15 +883,18 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
     const bool banded = args.ibw < P.N + P.M;
     dim3 grid(P.B * P.csize), block(P.wpc * 32);
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
+    const void* fn = nullptr;
     switch (P.K) {
-        case 1: return launch_cluster(banded ? (const void*)fwd_kernel<1, true> : (const void*)fwd_kernel<1, false>, grid, block,
-                                      ring_smem_bytes(P), P.csize, stream, kargs);
-        case 2: return launch_cluster(banded ? (const void*)fwd_kernel<2, true> : (const void*)fwd_kernel<2, false>, grid, block,
-                                      ring_smem_bytes(P), P.csize, stream, kargs);
-        case 4: return launch_cluster(banded ? (const void*)fwd_kernel<4, true> : (const void*)fwd_kernel<4, false>, grid, block,
-                                      ring_smem_bytes(P), P.csize, stream, kargs);
+        case 1:
+            fn = args.weights ? (banded ? (const void*)fwd_kernel<1, true, true> : (const void*)fwd_kernel<1, false, true>)
+                              : (banded ? (const void*)fwd_kernel<1, true, false> : (const void*)fwd_kernel<1, false, false>);
+            break;
+        case 2: fn = banded ? (const void*)fwd_kernel<2, true, false> : (const void*)fwd_kernel<2, false, false>; break;
+        case 4: fn = banded ? (const void*)fwd_kernel<4, true, false> : (const void*)fwd_kernel<4, false, false>; break;
         default: return cudaErrorInvalidValue;
     }
+    if (args.weights && P.K != 1) return cudaErrorInvalidValue;
+    return launch_cluster(fn, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
 }
 
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
@@ -832,15 +902,18 @@ cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
     const bool banded = args.ibw < P.N + P.M;
     dim3 grid(P.B * P.csize), block(P.wpc * 32);
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
+    const void* fn = nullptr;
     switch (P.K) {
-        case 1: return launch_cluster(banded ? (const void*)bwd_kernel<1, true> : (const void*)bwd_kernel<1, false>, grid, block,
-                                      ring_smem_bytes(P), P.csize, stream, kargs);
-        case 2: return launch_cluster(banded ? (const void*)bwd_kernel<2, true> : (const void*)bwd_kernel<2, false>, grid, block,
-                                      ring_smem_bytes(P), P.csize, stream, kargs);
-        case 4: return launch_cluster(banded ? (const void*)bwd_kernel<4, true> : (const void*)bwd_kernel<4, false>, grid, block,
-                                      ring_smem_bytes(P), P.csize, stream, kargs);
+        case 1:
+            fn = args.weights ? (banded ? (const void*)bwd_kernel<1, true, true> : (const void*)bwd_kernel<1, false, true>)
+                              : (banded ? (const void*)bwd_kernel<1, true, false> : (const void*)bwd_kernel<1, false, false>);
+            break;
+        case 2: fn = banded ? (const void*)bwd_kernel<2, true, false> : (const void*)bwd_kernel<2, false, false>; break;
+        case 4: fn = banded ? (const void*)bwd_kernel<4, true, false> : (const void*)bwd_kernel<4, false, false>; break;
         default: return cudaErrorInvalidValue;
     }
+    if (args.weights && P.K != 1) return cudaErrorInvalidValue;
+    return launch_cluster(fn, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
 }
 
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream) {

@@ -4,7 +4,8 @@
 They return and accept the R table in the reference layout (B, N+2, M+2),
 converting from/to the library's score table, so code that called the
 reference launchers directly keeps working.  The autograd Functions do not go
-through here: they keep the score table and skip the conversion.
+through here: the x/y pairs they call keep each cell's predecessor weights
+instead, which is all their backward needs.
 """
 from __future__ import annotations
 
@@ -28,7 +29,10 @@ def softdtw_forward_cuda_fused_sqeuclid(X: torch.Tensor, Y: torch.Tensor, gamma:
         raise ValueError(f"Batch/features mismatch: {tuple(X.shape)} vs {tuple(Y.shape)}")
     B, N, _ = X.shape
     M = Y.shape[1]
-    out, score = _native.forward_xy(X, Y, gamma, _bw(bandwidth))
+    # The x/y forward keeps predecessor weights, not scores, for its backward;
+    # the R table comes from the scores of the same direct-form cost.
+    D = _native.cost_sqeuclid(X, Y, direct=True)
+    out, score = _native.forward(D, gamma, _bw(bandwidth))
     R = _native.score_to_R(score, B, N, M, gamma)
     return out.to(X.dtype), R.to(X.dtype)
 
