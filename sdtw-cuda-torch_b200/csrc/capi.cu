@@ -285,6 +285,7 @@ WavePlan plan(int B, int N, int M) {
 //   D-input forward/backward : [wrap ring][WL table]
 //   x/y forward              : [wrap ring][WL cost]
 //   x/y backward, sqeuclid bwd: [wrap ring][WL E][gradient operands]
+//     grad_small (one row per lane, dim <= 16): per-split column sums;
 //     grad_wl (one row per lane, N or M above 128): x, y in the chunked
 //     transposed layout (B, ceil(N/32), dim, 36) and (B, ceil(M/32), dim, 36);
 //     grad_rm (otherwise): G, G^T, x^T, y^T row-major, rows padded to a
@@ -308,6 +309,12 @@ struct GradOperands {
 GradOperands grad_operands(int B, int N, int M, int dim) {
     GradOperands o;
     const size_t b = static_cast<size_t>(B);
+    const WavePlan p = plan(B, N, M);
+    if (grad_small_supported(p, dim)) {  // per-split column sums of grad_small
+        o.g = o.gt = o.xt = o.yt = 0;
+        o.total = align_up(grad_small_part_bytes(p, dim), 256);
+        return o;
+    }
     if (!grad_rm_path(N, M)) {  // xTc, yTc: rows of 36 floats per 32 positions
         o.g = o.gt = 0;
         o.xt = 0;
@@ -658,6 +665,13 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     cudaError_t e;
     char* region = static_cast<char*>(workspace) + w0 + wl_bytes(B, N, M);
     const GradOperands o = grad_operands(B, N, M, dim);
+    if (grad_small_supported(g.P, dim)) {
+        // Few features: the contraction on the FP32 pipes, one read of E.
+        KernelTimer kt("grad_xy", st, grad_y ? 2 : 1);
+        e = launch_grad_small(Ew, mask_w, x, y, grad_x, grad_y, reinterpret_cast<float*>(region), g.P, dim, st);
+        if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+        return SDTW_OK;
+    }
     if (!grad_rm_path(N, M)) {
         if ((reinterpret_cast<uintptr_t>(mask_w) & 15u) != 0)
             return fail(SDTW_ERR_INVALID_ARGUMENT, "cost table must be 16-byte aligned");

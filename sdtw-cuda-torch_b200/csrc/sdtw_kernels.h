@@ -114,6 +114,13 @@ cudaError_t launch_grad_wl(const GradTcArgs& args, cudaStream_t stream);
 // The same from row-major G, G^T, x^T and y^T (16-byte operand copies).
 void grad_rm_geometry(int dim, int* fb, int* nt, int* n_fblk, int* tmem_cols, int* stages);
 cudaError_t launch_grad_rm(const GradTcArgs& args, cudaStream_t stream);
+// grad_small.cu: both gradients on the FP32 pipes for dim <= 16, from E in the
+// wavefront layout (one row per lane); `part` holds grad_small_part_bytes of
+// per-split column sums (needed when gy is set).
+bool grad_small_supported(const WavePlan& P, int dim);
+size_t grad_small_part_bytes(const WavePlan& P, int dim);
+cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
+                              float* part, const WavePlan& P, int dim, cudaStream_t st);
 // tcgemm.cu: the unfused (expanded, clamped) cost on the tensor cores, written
 // in the wavefront layout.  Requires dim >= 16, dim % 4 == 0 and 16-byte
 // aligned x, y (cost_tc_supported).

@@ -41,10 +41,14 @@ def test_sizes_without_gpu():
     assert L.sdtw_workspace_bytes(4, 64, 64) == -(-cells * 4 // 256) * 256
     # x/y backward adds the gradient operands.
     up = lambda v: -(-v // 256) * 256
-    # One 128-row tile each way: G, G^T, x^T, y^T row-major with rows padded to 32.
-    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) == L.sdtw_workspace_bytes(4, 64, 64) + 2 * up(4 * 64 * 64 * 4) + 2 * up(4 * 3 * 64 * 4)
+    # Up to 16 features: column sums per split of 8 stripes (B x splits x M x
+    # (4 + 1) floats for dim <= 4).
+    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 3) == L.sdtw_workspace_bytes(4, 64, 64) + up(4 * 1 * 64 * 5 * 4)
+    assert L.sdtw_workspace_bytes_xy(2, 300, 40, 9) == L.sdtw_workspace_bytes(2, 300, 40) + up(2 * 2 * 40 * 17 * 4)
+    # More features, one 128-row tile each way: G, G^T, x^T, y^T row-major with rows padded to 32.
+    assert L.sdtw_workspace_bytes_xy(4, 64, 64, 20) == L.sdtw_workspace_bytes(4, 64, 64) + 2 * up(4 * 64 * 64 * 4) + 2 * up(4 * 20 * 64 * 4)
     # Longer: x, y chunked and transposed, rows of 36 floats per 32 positions.
-    assert L.sdtw_workspace_bytes_xy(4, 200, 64, 3) == L.sdtw_workspace_bytes(4, 200, 64) + up(4 * 7 * 3 * 36 * 4) + up(4 * 2 * 3 * 36 * 4)
+    assert L.sdtw_workspace_bytes_xy(4, 200, 64, 20) == L.sdtw_workspace_bytes(4, 200, 64) + up(4 * 7 * 20 * 36 * 4) + up(4 * 2 * 20 * 36 * 4)
 
 
 def test_invalid_arguments_rejected():
