@@ -121,7 +121,12 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
     if (g > 0) prev_consumed = mapa_shared(smem_addr(consumed + (g - 1) % wpc), (g - 1) / wpc);
 
     const float kk = a.kk;
-    const float NEG = neg_inf();
+    // Cells outside the table or the band.  The weight store uses a large
+    // finite value instead of -inf: ex2 of (it - m) is still 0 next to any
+    // live score, and a cell whose predecessors are all outside gets finite
+    // weights (1/3 each, with lo = 0) instead of NaN, so its weights need no
+    // mask (the reverse pass multiplies them by E = 0).
+    const float NEG = W ? -1.0e30f : neg_inf();
     const int ibw = a.ibw;
     WaitCtx wc = a.wait;
     wc.kernel = 1;
@@ -323,11 +328,12 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     const float m = max3f(dh, uh, lh);
                     const float ed = ex2f((dh - m) + dl), eu = ex2f((uh - m) + ul), el = ex2f((lh - m) + ll);
                     const float sm = ed + eu + el;
-                    const float delta = (lg2f(sm) - p) - e;
-                    // TwoSum: m + delta = hi + lo exactly.
+                    const float delta = lg2f(sm) - p;
+                    // TwoSum: m + delta = hi + lo exactly; the product's error e
+                    // joins lo (off the dependent chain).
                     const float hi = m + delta;
                     const float bb = hi - m;
-                    const float lo = (m - (hi - bb)) + (delta - bb);
+                    const float lo = ((m - (hi - bb)) + (delta - bb)) - e;
                     // Cells outside the table (or the band) read as -inf.
                     const int col = t - (q0 + k);
                     bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && q0 + k < rows_left;
@@ -338,9 +344,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     if constexpr (W) {
                         // The softmax weights of the diagonal and upper
                         // predecessors (the left one is 1 minus both): all the
-                        // reverse pass needs of this cell.  Zero outside.
+                        // reverse pass needs of this cell.  Finite for every
+                        // cell (see NEG); outside the table E is 0.
                         const float inv = rcpf(sm);
-                        Tg[u * SR] = make_float2(live ? ed * inv : 0.f, live ? eu * inv : 0.f);
+                        Tg[u * SR] = make_float2(ed * inv, eu * inv);
                         last_h = (t == t_last) ? nh[k] : last_h;
                         last_l = (t == t_last) ? nl[k] : last_l;
                     } else {
@@ -385,7 +392,8 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         for (int t = g_end * PF; t < P.n_diag; ++t)
 #pragma unroll
             for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = fill;
-        if (W && !quit && t_last >= 0) a.out[b] = fmaf(-last_h, a.inv_k, -last_l * a.inv_k);
+        if (W && !quit && t_last >= 0)
+            a.out[b] = last_h <= -1.0e29f ? pos_inf() : fmaf(-last_h, a.inv_k, -last_l * a.inv_k);
         if (!W && !quit && s == P.n_stripes - 1) {
             // Last cell (N-1, M-1): row q of this stripe, step q + M - 1; the
             // owning lane reads back its own store.
