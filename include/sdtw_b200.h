@@ -16,7 +16,7 @@
  * The "score" table takes the place of the reference's R table
  * (B, N+2, M+2): it holds T = -R * log2(e) / gamma for every cell, as a pair
  * of float32 (hi, lo) with T = hi + lo, in the anti-diagonal ("wavefront")
- * layout the kernels write with coalesced stores.  It must be 8-byte aligned;
+ * layout the kernels write with bulk copies of whole rows.  It must be 16-byte aligned;
  * workspaces 256-byte aligned.  The cost table of the unfused x/y entry points
  * (sdtw_cost_elems floats) uses the same anti-diagonal layout and must be
  * 16-byte aligned.

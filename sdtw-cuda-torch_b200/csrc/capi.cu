@@ -398,7 +398,8 @@ int check_ws(void* ws, size_t have, size_t need) {
 
 int check_score(const float* score) {
     if (!score) return fail(SDTW_ERR_INVALID_ARGUMENT, "null score");
-    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
+    // The forward writes it with bulk copies of whole anti-diagonal rows.
+    if (reinterpret_cast<uintptr_t>(score) % 16u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 16-byte aligned");
     return SDTW_OK;
 }
 
@@ -785,7 +786,8 @@ int sdtw_score_to_R_f32(const float* score, float* R, int B, int N, int M, float
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    if (reinterpret_cast<uintptr_t>(score) % 8u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 8-byte aligned");
+    // The forward writes it with bulk copies of whole anti-diagonal rows.
+    if (reinterpret_cast<uintptr_t>(score) % 16u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 16-byte aligned");
     WavePlan p = plan(B, N, M);
     const float kk = kLog2e / gamma;
     cudaError_t e = launch_score_to_R(reinterpret_cast<const float2*>(score), R, p, static_cast<float>(1.0 / (double)kk),

@@ -42,6 +42,12 @@
 namespace sdtw {
 
 constexpr int kRing = 128;  // ring slots per warp (power of two)
+// Byte offset of the forward's staging buffers: after the rings ([wpc][kRing][2]
+// u64) and the consumption counters ([wpc] u32), 16-byte aligned for the bulk
+// copies.
+__host__ __device__ constexpr size_t fwd_stage_offset(int wpc) {
+    return (static_cast<size_t>(wpc) * (2 * kRing * 8 + 4) + 15) / 16 * 16;
+}
 // Prefetch distance of the forward in groups.  Two register phases (the
 // step body compiled twice) measured faster than one on B200; a third body
 // for interior groups without the edge masks measured slower (the bodies no
@@ -109,6 +115,11 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][kRing][2]
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
+    // Table rows of a group are staged here ([2][PF][SR] float2 per warp, one
+    // buffer per phase) and written by one bulk copy (the rows of a group are
+    // contiguous): the warp never waits on global stores.
+    float2* stage = reinterpret_cast<float2*>(smem_raw + fwd_stage_offset(wpc)) + warp * 2 * PF * SR;
+    const uint32_t stage_s = smem_addr(stage);
     for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
@@ -198,9 +209,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         float upl_prev = 0.f;
         const int q0 = lane * K;  // row offset of k = 0 in the stripe
         const int rows_left = N - R0;
-        // Weight store: the lane of the last row keeps the last cell's score
-        // (step t_last) as it passes, instead of reading it back.
-        const int t_last = (W && s == P.n_stripes - 1 && lane == N - 1 - R0) ? N - 1 - R0 + M - 1 : -1;
+        // The lane of the last row keeps the last cell's score (step t_last)
+        // as it passes (the table rows go out by bulk copies).
+        const int t_last = (s == P.n_stripes - 1 && (N - 1 - R0) / K == lane) ? N - 1 - R0 + M - 1 : -1;
+        const int k_last = (N - 1 - R0) % K;
         float last_h = 0.f, last_l = 0.f;
         // Band-wrap input (global memory, an L2 round trip per load): the slots
         // of the next group are loaded one group ahead.  The data is normally
@@ -294,7 +306,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                 }
             }
             // ---- PF steps.
-            float2* Tg = Tl + static_cast<size_t>(t0) * SR;
+            // This phase's staging buffer was last read by the copy two groups ago.
+            if (lane == 0) bulk_wait_read_1();
+            __syncwarp();
+            float2* Tg = stage + PH * PF * SR + lane;
             const float* Dg = Dl + static_cast<size_t>(t0 + PD) * SR;
             const int colb0 = t0 - (SR - 1);  // bottom-row column of step t0
             const uint32_t tgo0 = out_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(colb0);
@@ -348,10 +363,12 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                         // cell (see NEG); outside the table E is 0.
                         const float inv = rcpf(sm);
                         Tg[u * SR] = make_float2(ed * inv, eu * inv);
-                        last_h = (t == t_last) ? nh[k] : last_h;
-                        last_l = (t == t_last) ? nl[k] : last_l;
                     } else {
                         Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
+                    }
+                    if (K == 1 || k == k_last) {
+                        last_h = (t == t_last) ? nh[k] : last_h;
+                        last_l = (t == t_last) ? nl[k] : last_l;
                     }
                 }
                 // Bottom row of the stripe goes to the next stripe's warp.
@@ -368,6 +385,13 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                     cl[k] = nl[k];
                 }
             }
+            // Rows t0 .. t0 + PF - 1 of the table: one bulk copy.
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                bulk_s2g(Tl - lane + static_cast<size_t>(t0) * SR, stage_s + PH * PF * SR * 8u, PF * SR * 8u);
+                bulk_commit();
+            }
         };
         using P0 = std::integral_constant<int, 0>;
         using P1 = std::integral_constant<int, 1>;
@@ -383,6 +407,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
             }
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
+        // The band's copies are complete before the fill stores below and the
+        // next band's first group (which reuses phase 0's buffer).
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band): -inf,
         // like every cell outside the table (weights: zero).
         const float2 fill = W ? make_float2(0.f, 0.f) : make_float2(NEG, 0.f);
@@ -392,17 +420,8 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         for (int t = g_end * PF; t < P.n_diag; ++t)
 #pragma unroll
             for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = fill;
-        if (W && !quit && t_last >= 0)
+        if (!quit && t_last >= 0)
             a.out[b] = last_h <= -1.0e29f ? pos_inf() : fmaf(-last_h, a.inv_k, -last_l * a.inv_k);
-        if (!W && !quit && s == P.n_stripes - 1) {
-            // Last cell (N-1, M-1): row q of this stripe, step q + M - 1; the
-            // owning lane reads back its own store.
-            const int q = N - 1 - R0;
-            if (lane == q / K) {
-                const float2 v = Tl[static_cast<size_t>(q + M - 1) * SR + (q % K) * 32];
-                a.out[b] = fmaf(-v.x, a.inv_k, -v.y * a.inv_k);
-            }
-        }
     }
     // No CTA may leave while a peer can still write into its shared memory.
     cluster_sync_all();
@@ -839,11 +858,20 @@ static cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
+}
+// The forward adds its staging buffers ([wpc][2][PF][32K] float2) after the ring.
+static size_t fwd_smem_bytes(const WavePlan& P) {
+    const int PF = P.K >= 4 ? 4 : 8;
+    return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * 2 * PF * 32 * P.K * 8u;
 }
 
 // Clusters of this geometry that can be resident at once on the current
@@ -875,8 +903,16 @@ int max_active_clusters(const WavePlan& P) {
         default: return -1;
     }
     int best = -1;
-    for (const void* fn : fns) {
+    for (int i = 0; i < 4; ++i) {
+        const void* fn = fns[i];
         if (!fn) continue;
+        cfg.dynamicSmemBytes = (i % 2 == 0) ? fwd_smem_bytes(P) : ring_smem_bytes(P);  // forwards: even slots
+        if (cfg.dynamicSmemBytes > 48 * 1024 &&
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(cfg.dynamicSmemBytes)) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return -1;
+        }
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
             (void)cudaGetLastError();
@@ -904,7 +940,7 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
         default: return cudaErrorInvalidValue;
     }
     if (args.weights && P.K != 1) return cudaErrorInvalidValue;
-    return launch_cluster(fn, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+    return launch_cluster(fn, grid, block, fwd_smem_bytes(P), P.csize, stream, kargs);
 }
 
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
