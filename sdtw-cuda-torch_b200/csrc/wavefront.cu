@@ -49,9 +49,11 @@ __host__ __device__ constexpr size_t fwd_stage_offset(int wpc) {
     return (static_cast<size_t>(wpc) * (2 * kRing * 8 + 4) + 15) / 16 * 16;
 }
 // Prefetch distance of the forward in groups.  Two register phases (the
-// step body compiled twice) measured faster than one on B200; a third body
-// for interior groups without the edge masks measured slower (the bodies no
-// longer fit the instruction cache), so every group runs the masked body.
+// step body compiled twice) measured faster than one on B200, and faster
+// than three or four (C2 forward 0.177 / 0.219 / 0.298 ms: the deeper cost
+// queues spill at the 128 registers of a 512-thread CTA); a third body for
+// interior groups without the edge masks measured slower (the bodies no longer
+// fit the instruction cache), so every group runs the masked body.
 constexpr int kFwdPhases = 2;
 // Prefetch distance of the reverse pass with the weight store, in groups:
 // measured on B200 (C2 / C3 / C5 shapes), 2 beats 1 by 9-18 % (the loads were
@@ -115,10 +117,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][kRing][2]
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
-    // Table rows of a group are staged here ([2][PF][SR] float2 per warp, one
+    // Table rows of a group are staged here ([NPH][PF][SR] float2 per warp, one
     // buffer per phase) and written by one bulk copy (the rows of a group are
     // contiguous): the warp never waits on global stores.
-    float2* stage = reinterpret_cast<float2*>(smem_raw + fwd_stage_offset(wpc)) + warp * 2 * PF * SR;
+    float2* stage = reinterpret_cast<float2*>(smem_raw + fwd_stage_offset(wpc)) + warp * NPH * PF * SR;
     const uint32_t stage_s = smem_addr(stage);
     for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
@@ -306,8 +308,8 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                 }
             }
             // ---- PF steps.
-            // This phase's staging buffer was last read by the copy two groups ago.
-            if (lane == 0) bulk_wait_read_1();
+            // This phase's staging buffer was last read by the copy NPH groups ago.
+            if (lane == 0) bulk_wait_read<NPH - 1>();
             __syncwarp();
             float2* Tg = stage + PH * PF * SR + lane;
             const float* Dg = Dl + static_cast<size_t>(t0 + PD) * SR;
@@ -398,8 +400,14 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         for (int gi = g_begin; gi < g_end; gi += NPH) {
             const int t0 = gi * PF;
             group(P0{}, t0);
-            if constexpr (NPH == 2) {
+            if constexpr (NPH >= 2) {
                 if (gi + 1 < g_end) group(P1{}, t0 + PF);
+            }
+            if constexpr (NPH >= 3) {
+                if (gi + 2 < g_end) group(std::integral_constant<int, 2>{}, t0 + 2 * PF);
+            }
+            if constexpr (NPH >= 4) {
+                if (gi + 3 < g_end) group(std::integral_constant<int, 3>{}, t0 + 3 * PF);
             }
             if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
@@ -868,10 +876,10 @@ static cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t 
 static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
-// The forward adds its staging buffers ([wpc][2][PF][32K] float2) after the ring.
+// The forward adds its staging buffers ([wpc][phases][PF][32K] float2) after the ring.
 static size_t fwd_smem_bytes(const WavePlan& P) {
     const int PF = P.K >= 4 ? 4 : 8;
-    return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * 2 * PF * 32 * P.K * 8u;
+    return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * kFwdPhases * PF * 32 * P.K * 8u;
 }
 
 // Clusters of this geometry that can be resident at once on the current
