@@ -44,6 +44,15 @@ __device__ __forceinline__ float hi_f32x2(unsigned long long v) {
     return __uint_as_float(static_cast<uint32_t>(v >> 32));
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ size_t wl_row_base(const WavePlan& P, int b, int s, int t) {
     return ((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * (32 * P.K);
 }
@@ -77,8 +86,8 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
     extern __shared__ __align__(16) float cs[];
     float* xn = cs;                      // [SR]
     float* yn = xn + SR;                 // [CJ]
-    float* xs = cs + NOFF;               // [SR][PITCH]
-    float* ys = xs + SR * PITCH;         // [CJ][PITCH]
+    float* xs0 = cs + NOFF;                  // [SR + CJ][PITCH]: x rows then y rows
+    float* xs1 = xs0 + (SR + CJ) * PITCH;    // second buffer (16-byte async copies)
     const int j0 = blockIdx.x * CJ;
     const int s = blockIdx.y;
     const int b = blockIdx.z;
@@ -100,19 +109,40 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
     if (!DIRECT) {
         for (int i = threadIdx.x; i < SR + CJ; i += 256) xn[i] = 0.f;  // xn and yn are adjacent
     }
-    for (int f0 = 0; f0 < dim; f0 += FC) {
-        __syncthreads();
-        if (VEC) {  // dim % 4 == 0 and 16-byte aligned rows: float4 loads
-            for (int e = threadIdx.x; e < (SR + CJ) * (FC / 4); e += 256) {
-                const int r = e / (FC / 4), f = (e % (FC / 4)) * 4;
-                const bool isx = r < SR;
-                const int row = isx ? R0 + r : j0 + r - SR;
-                const bool in = (isx ? row < P.N : row < P.M) && f0 + f < dim;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (in) v = __ldg(reinterpret_cast<const float4*>((isx ? xb : yb) + static_cast<size_t>(row) * dim + f0 + f));
-                *reinterpret_cast<float4*>(xs + r * PITCH + f) = v;  // ys follows xs: row r of [xs; ys]
+    // VEC (dim % 4 == 0, 16-byte aligned rows): feature chunks staged with
+    // 16-byte cp.async into two buffers, the next chunk's copies in flight
+    // while this one is computed.
+    auto stage_async = [&](float* dstb, int f0) {
+        for (int e = threadIdx.x; e < (SR + CJ) * (FC / 4); e += 256) {
+            const int r = e / (FC / 4), f = (e % (FC / 4)) * 4;
+            const bool isx = r < SR;
+            const int row = isx ? R0 + r : j0 + r - SR;
+            const bool in = (isx ? row < P.N : row < P.M) && f0 + f < dim;
+            float* dst = dstb + r * PITCH + f;
+            if (in)
+                cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dst)),
+                           (isx ? xb : yb) + static_cast<size_t>(row) * dim + f0 + f);
+            else
+                *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        cp_async_commit();
+    };
+    const int n_chunks = (dim + FC - 1) / FC;
+    if (VEC) stage_async(xs0, 0);
+    for (int ci = 0; ci < n_chunks; ++ci) {
+        const int f0 = ci * FC;
+        float* const xs = (VEC && (ci & 1)) ? xs1 : xs0;
+        float* const ys = xs + SR * PITCH;
+        if (VEC) {
+            if (ci + 1 < n_chunks) {
+                stage_async((ci & 1) ? xs0 : xs1, f0 + FC);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
             }
+            __syncthreads();
         } else {
+            __syncthreads();
             for (int e = threadIdx.x; e < (SR + CJ) * FC; e += 256) {
                 const int r = e / FC, f = e % FC;
                 const bool isx = r < SR;
@@ -120,8 +150,8 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
                 const bool in = (isx ? row < P.N : row < P.M) && f0 + f < dim;
                 xs[r * PITCH + f] = in ? __ldg((isx ? xb : yb) + static_cast<size_t>(row) * dim + f0 + f) : 0.f;
             }
+            __syncthreads();
         }
-        __syncthreads();
         if (!DIRECT) {
             for (int i = threadIdx.x; i < SR + CJ; i += 256) {
                 const float* row = xs + i * PITCH;
@@ -175,11 +205,13 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
                 }
             }
         }
+        // The next iteration's copies overwrite the buffer read above.
+        if (VEC) __syncthreads();
     }
     __syncthreads();
     // Stage by local anti-diagonal tl = q + (j - j0) in [0, SR + CJ - 1), row
-    // pitch SR + 1 (aliases xs/ys, not the norms), then store.
-    float* stg = xs;
+    // pitch SR + 1 (aliases the staging buffers, not the norms), then store.
+    float* stg = xs0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int q = 4 * ag + i;
@@ -385,7 +417,7 @@ template <int K, int FC>
 static size_t cost_wl_smem() {
     constexpr int SR = 32 * K, CJ = 4096 / SR;
     constexpr int NOFF = (SR + CJ + 3) / 4 * 4;
-    const size_t in = static_cast<size_t>(SR + CJ) * CostPitch<FC>::v;
+    const size_t in = 2 * static_cast<size_t>(SR + CJ) * CostPitch<FC>::v;  // two buffers
     const size_t stage = static_cast<size_t>(SR + CJ - 1) * (SR + 1);
     return (NOFF + (in > stage ? in : stage)) * sizeof(float);
 }
