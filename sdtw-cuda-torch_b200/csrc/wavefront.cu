@@ -96,8 +96,9 @@ __device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
 // PF whole steps and the cost rows are prefetched PD = 2*PF steps ahead (two
 // register phases, each a compile-time half of dq) without clamping
 // addresses.  Cells outside the table (left of column 0, right of column M-1,
-// rows past N) or the band are stored as -inf.  The last cell's score is read
-// back from the store after the stripe.
+// rows past N) or the band are stored as -inf.  The rows of a group go out as
+// one bulk copy from shared memory; the last cell's score is kept in registers
+// by its lane as it passes.
 template <int K, bool BANDED, bool W>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a) {
     static_assert(!W || K == 1, "the weight store is built for one row per lane");
@@ -477,6 +478,11 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * kRing);
+    // E rows of a group are staged here ([NPH][PF][SR] floats per warp, one
+    // buffer per phase, after the space the forward's rings take) and written
+    // by one bulk copy (the rows of a group are contiguous).
+    float* bstage = reinterpret_cast<float*>(smem_raw + fwd_stage_offset(wpc)) + warp * NPH * PF * SR;
+    const uint32_t bstage_s = smem_addr(bstage);
     for (int i = threadIdx.x; i < wpc * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
@@ -677,8 +683,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                     }
                 }
             }
-            // ---- PF reverse steps.
-            float* Eg = El + static_cast<size_t>(t0) * SR;
+            // ---- PF reverse steps (step u fills staged row PF - 1 - u, i.e. t0 - u).
+            if (lane == 0) bulk_wait_read<NPH - 1>();
+            __syncwarp();
+            float* Eg = bstage + PH * PF * SR + (PF - 1) * SR + lane;
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 - u;
@@ -772,6 +780,13 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                     S1 = S2;
                 }
             }
+            // Rows t0 - PF + 1 .. t0 of E: one bulk copy.
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                bulk_s2g(El - lane + static_cast<size_t>(t0 - PF + 1) * SR, bstage_s + PH * PF * SR * 4u, PF * SR * 4u);
+                bulk_commit();
+            }
         };
         using P0 = std::integral_constant<int, 0>;
         using P1 = std::integral_constant<int, 1>;
@@ -790,6 +805,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                 break;
             }
         }
+        // The band's copies are complete before the zero fill below and the
+        // next band's first group.
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band): zero,
         // like every cell outside the table.
         for (int t = 0; t <= t_last - gi_end * PF; ++t)
@@ -876,6 +895,12 @@ static cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t 
 static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
+// The reverse pass stages E rows ([wpc][phases][PF][32K] floats) at the same offset.
+static size_t bwd_smem_bytes(const WavePlan& P, bool weights) {
+    const int PF = P.K >= 4 ? 4 : 8;
+    const int nph = weights ? kBwdWeightPhases : (P.K == 1 ? 1 : 2);
+    return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * nph * PF * 32 * P.K * 4u;
+}
 // The forward adds its staging buffers ([wpc][phases][PF][32K] float2) after the ring.
 static size_t fwd_smem_bytes(const WavePlan& P) {
     const int PF = P.K >= 4 ? 4 : 8;
@@ -914,7 +939,8 @@ int max_active_clusters(const WavePlan& P) {
     for (int i = 0; i < 4; ++i) {
         const void* fn = fns[i];
         if (!fn) continue;
-        cfg.dynamicSmemBytes = (i % 2 == 0) ? fwd_smem_bytes(P) : ring_smem_bytes(P);  // forwards: even slots
+        // Forwards in even slots, reverse passes in odd ones; slots 2 and 3 use the weight store.
+        cfg.dynamicSmemBytes = (i % 2 == 0) ? fwd_smem_bytes(P) : bwd_smem_bytes(P, i == 3);
         if (cfg.dynamicSmemBytes > 48 * 1024 &&
             cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(cfg.dynamicSmemBytes)) != cudaSuccess) {
@@ -967,7 +993,7 @@ cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
         default: return cudaErrorInvalidValue;
     }
     if (args.weights && P.K != 1) return cudaErrorInvalidValue;
-    return launch_cluster(fn, grid, block, ring_smem_bytes(P), P.csize, stream, kargs);
+    return launch_cluster(fn, grid, block, bwd_smem_bytes(P, args.weights != 0), P.csize, stream, kargs);
 }
 
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream) {
