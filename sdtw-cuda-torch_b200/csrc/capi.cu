@@ -740,6 +740,7 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
     if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !cost || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(cost) % 16u) return fail(SDTW_ERR_INVALID_ARGUMENT, "cost table must be 16-byte aligned");
     if ((rc = check_ws(workspace, workspace_bytes, wave_ws(B, N, M)))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e;

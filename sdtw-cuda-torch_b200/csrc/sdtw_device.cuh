@@ -156,6 +156,16 @@ __device__ __forceinline__ uint64_t ld_one_shared(uint32_t saddr) {
     asm volatile("ld.relaxed.cluster.shared::cta.u64 %0, [%1];" : "=l"(a) : "r"(saddr));
     return a;
 }
+// 16-byte global -> shared asynchronous copies (per-thread groups).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Shared -> global bulk copies (async proxy), for staged table rows.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void bulk_s2g(void* gdst, uint32_t ssrc, uint32_t bytes) {

@@ -55,6 +55,12 @@ __host__ __device__ constexpr size_t fwd_stage_offset(int wpc) {
 // interior groups without the edge masks measured slower (the bodies no longer
 // fit the instruction cache), so every group runs the masked body.
 constexpr int kFwdPhases = 2;
+// The forward's cost rows are staged after its store buffers: [wpc][3][PF][32K]
+// floats (three groups: the current one and two in flight).
+__host__ __device__ constexpr int fwd_pf(int K) { return K >= 4 ? 4 : 8; }
+__host__ __device__ constexpr size_t fwd_cost_offset(int wpc, int K) {
+    return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * kFwdPhases * fwd_pf(K) * 32 * K * 8;
+}
 // Prefetch distance of the reverse pass with the weight store, in groups:
 // measured on B200 (C2 / C3 / C5 shapes), 2 beats 1 by 9-18 % (the loads were
 // exposed) and 4 (four step bodies) is slower than both.
@@ -93,9 +99,8 @@ __device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
 // sequentially across band boundaries.
 //
 // Step code.  The anti-diagonal rows are padded (wl_diag), so every group runs
-// PF whole steps and the cost rows are prefetched PD = 2*PF steps ahead (two
-// register phases, each a compile-time half of dq) without clamping
-// addresses.  Cells outside the table (left of column 0, right of column M-1,
+// PF whole steps; the cost rows of a group are copied into shared memory two
+// groups ahead.  Cells outside the table (left of column 0, right of column M-1,
 // rows past N) or the band are stored as -inf.  The rows of a group go out as
 // one bulk copy from shared memory; the last cell's score is kept in registers
 // by its lane as it passes.
@@ -103,8 +108,7 @@ template <int K, bool BANDED, bool W>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a) {
     static_assert(!W || K == 1, "the weight store is built for one row per lane");
     constexpr int PF = StepCfg<K>::PF;
-    constexpr int NPH = kFwdPhases;  // prefetch distance in groups
-    constexpr int PD = NPH * PF;     // prefetch distance (steps)
+    constexpr int NPH = kFwdPhases;  // step bodies (phases): store staging buffer per phase
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
@@ -123,6 +127,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
     // contiguous): the warp never waits on global stores.
     float2* stage = reinterpret_cast<float2*>(smem_raw + fwd_stage_offset(wpc)) + warp * NPH * PF * SR;
     const uint32_t stage_s = smem_addr(stage);
+    // Cost rows of group g are copied (16-byte cp.async) two groups ahead into
+    // buffer (g - g_begin) % 3 of [3][PF][SR] floats.
+    const float* cost = reinterpret_cast<const float*>(smem_raw + fwd_cost_offset(wpc, K)) + warp * 3 * PF * SR;
+    const uint32_t cost_s = smem_addr(cost);
     for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
@@ -190,11 +198,19 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         // Last column of the row above that is in the band (and so published by
         // the stripe above); the columns past it read as -inf without the ring.
         const int c_pub_max = BANDED ? min(M - 1, R0 - 1 + ibw) : M - 1;
-        float dq[PD][K];  // cost rows: slot (t mod PD) holds row t
+        // Group gg's cost rows (PF * SR contiguous floats), or an empty commit
+        // past the last group, so that every group finds its rows two commits back.
+        auto cost_copy = [&](int gg) {
+            if (gg < g_end) {
+                const float* src = Dl - lane + static_cast<size_t>(gg) * PF * SR;
+                const uint32_t dst = cost_s + static_cast<uint32_t>((gg - g_begin) % 3) * PF * SR * 4u;
 #pragma unroll
-        for (int u = 0; u < PD; ++u)
-#pragma unroll
-            for (int k = 0; k < K; ++k) dq[u][k] = __ldg(Dl + (t_begin + u) * SR + k * 32);
+                for (int i = 0; i < PF * SR / 128; ++i) cp_async16(dst + (lane + 32 * i) * 16u, src + (lane + 32 * i) * 4);
+            }
+            cp_async_commit();
+        };
+        cost_copy(g_begin);
+        cost_copy(g_begin + 1);
         // The columns before t_begin are never read: report them consumed, so
         // that the stripe above may run up to a full ring ahead of this start.
         if (t_begin > 0)
@@ -309,11 +325,15 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                 }
             }
             // ---- PF steps.
-            // This phase's staging buffer was last read by the copy NPH groups ago.
+            // This phase's staging buffer was last read by the copy NPH groups
+            // ago; this group's cost rows (two commits back) have landed.
             if (lane == 0) bulk_wait_read<NPH - 1>();
+            cp_async_wait<1>();
             __syncwarp();
+            const int gg = t0 / PF;
+            const float* cb = cost + ((gg - g_begin) % 3) * PF * SR + lane;
+            cost_copy(gg + 2);  // into the buffer the previous group read
             float2* Tg = stage + PH * PF * SR + lane;
-            const float* Dg = Dl + static_cast<size_t>(t0 + PD) * SR;
             const int colb0 = t0 - (SR - 1);  // bottom-row column of step t0
             const uint32_t tgo0 = out_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(colb0);
 #pragma unroll
@@ -321,10 +341,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                 const int t = t0 + u;
                 float c[K];
 #pragma unroll
-                for (int k = 0; k < K; ++k) {
-                    c[k] = dq[PH * PF + u][k];
-                    dq[PH * PF + u][k] = __ldg(Dg + u * SR + k * 32);  // row t + PD
-                }
+                for (int k = 0; k < K; ++k) c[k] = cb[u * SR + k * 32];
                 float uph = __shfl_up_sync(SDTW_FULL_MASK, ch[K - 1], 1);
                 float upl = __shfl_up_sync(SDTW_FULL_MASK, cl[K - 1], 1);
                 uph = (lane == 0) ? rin_h[u] : uph;
@@ -417,8 +434,9 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
         // The band's copies are complete before the fill stores below and the
-        // next band's first group (which reuses phase 0's buffer).
+        // next band's first group (which reuses phase 0's buffer and the cost buffers).
         if (lane == 0) bulk_wait_all();
+        cp_async_wait<0>();
         __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band): -inf,
         // like every cell outside the table (weights: zero).
@@ -901,10 +919,10 @@ static size_t bwd_smem_bytes(const WavePlan& P, bool weights) {
     const int nph = weights ? kBwdWeightPhases : (P.K == 1 ? 1 : 2);
     return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * nph * PF * 32 * P.K * 4u;
 }
-// The forward adds its staging buffers ([wpc][phases][PF][32K] float2) after the ring.
+// The forward adds its store staging ([wpc][phases][PF][32K] float2) and cost
+// staging ([wpc][3][PF][32K] floats) after the ring.
 static size_t fwd_smem_bytes(const WavePlan& P) {
-    const int PF = P.K >= 4 ? 4 : 8;
-    return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * kFwdPhases * PF * 32 * P.K * 8u;
+    return fwd_cost_offset(P.wpc, P.K) + static_cast<size_t>(P.wpc) * 3 * fwd_pf(P.K) * 32 * P.K * 4u;
 }
 
 // Clusters of this geometry that can be resident at once on the current
