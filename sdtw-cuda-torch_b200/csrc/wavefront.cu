@@ -61,6 +61,10 @@ __host__ __device__ constexpr int fwd_pf(int K) { return K >= 4 ? 4 : 8; }
 __host__ __device__ constexpr size_t fwd_cost_offset(int wpc, int K) {
     return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * kFwdPhases * fwd_pf(K) * 32 * K * 8;
 }
+// The reverse pass's weight staging follows its E staging ([wpc][nph][PF][32K] floats).
+__host__ __device__ constexpr size_t bwd_weight_offset(int wpc, int K, int nph) {
+    return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * nph * fwd_pf(K) * 32 * K * 4;
+}
 // Prefetch distance of the reverse pass with the weight store, in groups:
 // measured on B200 (C2 / C3 / C5 shapes), 2 beats 1 by 9-18 % (the loads were
 // exposed) and 4 (four step bodies) is slower than both.
@@ -501,6 +505,10 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
     // by one bulk copy (the rows of a group are contiguous).
     float* bstage = reinterpret_cast<float*>(smem_raw + fwd_stage_offset(wpc)) + warp * NPH * PF * SR;
     const uint32_t bstage_s = smem_addr(bstage);
+    // Weight store: the weights of group g's rows are copied (16-byte cp.async)
+    // two groups ahead into buffer (g - gi_begin) % 3 of [3][PF][SR] float2.
+    const float2* wbuf = reinterpret_cast<const float2*>(smem_raw + bwd_weight_offset(wpc, K, NPH)) + warp * 3 * PF * SR;
+    const uint32_t wbuf_s = smem_addr(wbuf);
     for (int i = threadIdx.x; i < wpc * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
@@ -599,9 +607,20 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         float2 pq[PD];     // PS(t-1) for the step due in slot j
         float2 A1[K];      // A(t-1)
         float2 S1;         // row above at anti-diagonal t-1
-        if constexpr (W) {
+        // Group gi's weights: rows t0 - PF + 1 .. t0 (t0 = t_last - gi * PF), or
+        // an empty commit past the last group.
+        auto wcopy = [&](int gi) {
+            if (gi < gi_end) {
+                const float2* src = Ts + static_cast<size_t>(t_last - gi * PF - PF + 1) * SR;
+                const uint32_t dst = wbuf_s + static_cast<uint32_t>((gi - gi_begin) % 3) * PF * SR * 8u;
 #pragma unroll
-            for (int j = 0; j < PD; ++j) aq[j][0] = loadA(t_top - j, 0);
+                for (int i = 0; i < PF * SR / 64; ++i) cp_async16(dst + (lane + 32 * i) * 16u, src + (lane + 32 * i) * 2);
+            }
+            cp_async_commit();
+        };
+        if constexpr (W) {
+            wcopy(gi_begin);
+            wcopy(gi_begin + 1);
         } else {
 #pragma unroll
             for (int j = 0; j < PD; ++j) {
@@ -703,15 +722,24 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
             }
             // ---- PF reverse steps (step u fills staged row PF - 1 - u, i.e. t0 - u).
             if (lane == 0) bulk_wait_read<NPH - 1>();
+            const float2* wb = wbuf;  // this group's weights (weight store)
+            (void)wb;
+            if constexpr (W) {
+                cp_async_wait<1>();  // committed two groups back
+                __syncwarp();
+                const int gi = (t_last - t0) / PF;
+                wb = wbuf + ((gi - gi_begin) % 3) * PF * SR + (PF - 1) * SR + lane;
+                wcopy(gi + 2);  // into the buffer the previous group read
+            }
             __syncwarp();
             float* Eg = bstage + PH * PF * SR + (PF - 1) * SR + lane;
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 - u;
                 constexpr int J0 = PH * PF;
+                (void)J0;
                 if constexpr (W) {
-                    const float2 w = aq[J0 + u][0];  // (diagonal, upper) weights of cell (q0, t - q0)
-                    aq[J0 + u][0] = loadA(t - PD, 0);
+                    const float2 w = wb[-u * SR];  // (diagonal, upper) weights of cell (q0, t - q0)
                     float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
                     const float rv = __shfl_sync(SDTW_FULL_MASK, v, u);
                     below = (lane == 31) ? rv : below;
@@ -826,6 +854,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
         // The band's copies are complete before the zero fill below and the
         // next band's first group.
         if (lane == 0) bulk_wait_all();
+        cp_async_wait<0>();
         __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band): zero,
         // like every cell outside the table.
@@ -913,11 +942,12 @@ static cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t 
 static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
-// The reverse pass stages E rows ([wpc][phases][PF][32K] floats) at the same offset.
+// The reverse pass stages E rows ([wpc][phases][PF][32K] floats) at the same
+// offset, then (weight store) its weights ([wpc][3][PF][32K] float2).
 static size_t bwd_smem_bytes(const WavePlan& P, bool weights) {
-    const int PF = P.K >= 4 ? 4 : 8;
     const int nph = weights ? kBwdWeightPhases : (P.K == 1 ? 1 : 2);
-    return fwd_stage_offset(P.wpc) + static_cast<size_t>(P.wpc) * nph * PF * 32 * P.K * 4u;
+    const size_t w = weights ? static_cast<size_t>(P.wpc) * 3 * fwd_pf(P.K) * 32 * P.K * 8u : 0;
+    return bwd_weight_offset(P.wpc, P.K, nph) + w;
 }
 // The forward adds its store staging ([wpc][phases][PF][32K] float2) and cost
 // staging ([wpc][3][PF][32K] floats) after the ring.
