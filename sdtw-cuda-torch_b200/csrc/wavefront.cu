@@ -48,13 +48,11 @@ constexpr int kRing = 128;  // ring slots per warp (power of two)
 __host__ __device__ constexpr size_t fwd_stage_offset(int wpc) {
     return (static_cast<size_t>(wpc) * (2 * kRing * 8 + 4) + 15) / 16 * 16;
 }
-// Prefetch distance of the forward in groups.  Two register phases (the
-// step body compiled twice) measured faster than one on B200, and faster
-// than three or four (C2 forward 0.177 / 0.219 / 0.298 ms: the deeper cost
-// queues spill at the 128 registers of a 512-thread CTA); a third body for
-// interior groups without the edge masks measured slower (the bodies no longer
-// fit the instruction cache), so every group runs the masked body.
-constexpr int kFwdPhases = 2;
+// Step bodies of the forward (compile-time phases, one store staging buffer
+// each).  With the cost rows staged in shared memory one body measured as fast
+// as two at C2 and 3.5 % faster at C3 (N = M = 4096: the smaller code); with
+// the costs in a register queue, two had beaten one and three or four spilled.
+constexpr int kFwdPhases = 1;
 // The forward's cost rows are staged after its store buffers: [wpc][3][PF][32K]
 // floats (three groups: the current one and two in flight).
 __host__ __device__ constexpr int fwd_pf(int K) { return K >= 4 ? 4 : 8; }
