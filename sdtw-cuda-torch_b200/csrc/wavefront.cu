@@ -63,9 +63,10 @@ __host__ __device__ constexpr size_t fwd_cost_offset(int wpc, int K) {
 __host__ __device__ constexpr size_t bwd_weight_offset(int wpc, int K, int nph) {
     return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * nph * fwd_pf(K) * 32 * K * 4;
 }
-// Prefetch distance of the reverse pass with the weight store, in groups:
-// measured on B200 (C2 / C3 / C5 shapes), 2 beats 1 by 9-18 % (the loads were
-// exposed) and 4 (four step bodies) is slower than both.
+// Step bodies of the reverse pass with the weight store (one E staging buffer
+// each).  Two measured faster than one and than four on B200 (C2 / C3 / C5
+// shapes), both while its weights sat in a register queue (two groups of
+// prefetch: 9-18 % faster than one) and with the shared-memory staging.
 constexpr int kBwdWeightPhases = 2;
 
 __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
@@ -76,9 +77,12 @@ __device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
 // Steps run in groups of PF.  Per group (warp-uniform code): the consumer lane
 // reads and checks the PF ring slots it will need, the producer lane checks
 // flow control once, and every 32 columns a relaxed store reports progress.
-// Per step: shuffles, the cell math, coalesced loads/stores of one
-// anti-diagonal row, one predicated ring store -- no branches.  The cost
-// (forward) or score rows (backward) of step t are loaded PF steps ahead.
+// Per step: shuffles, the cell math, one shared-memory read of the step's cost
+// (forward) or weights (reverse pass, weight store) and one staged table
+// store, one predicated ring store -- no branches.  A group's input rows are
+// copied into shared memory two groups ahead, its output rows leave as one
+// bulk copy (the score-store reverse pass loads its score rows one group ahead
+// into registers).
 template <int K>
 struct StepCfg {
     static constexpr int PF = (K >= 4) ? 4 : 8;
@@ -599,9 +603,9 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
             return __ldg(Tp + static_cast<size_t>(cc) * SR);
         };
 
-        // Weight store (W): the step due in slot j reads its own cell's
-        // weights, row t, queued PD steps ahead; nothing else is loaded.
-        float2 aq[PD][K];  // A(t-2) for the step due in slot j (W: the weights of row t)
+        // Weight store (W): each step reads its own cell's weights, row t,
+        // staged in shared memory (wcopy); nothing else is loaded.
+        float2 aq[PD][K];  // A(t-2) for the step due in slot j (score store)
         float2 pq[PD];     // PS(t-1) for the step due in slot j
         float2 A1[K];      // A(t-1)
         float2 S1;         // row above at anti-diagonal t-1
