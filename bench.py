@@ -52,7 +52,7 @@ WORKLOADS = {
            "BASELINE config 5: barycenter of 4096 sequences x 100 x 3, gamma=1, Adam lr=0.1, "
            "one step = one iteration over the whole set, sharded over the ranks"),
 }
-PUBLISHED = {  # reference, B=32 N=M=512 D=64 fwd+bwd (unstated GPU)
+PUBLISHED = {  # the reference's published numbers: B=32 N=M=512 D=64 fwd+bwd (unstated GPU)
     "c2": {"fused": 32 * 512 * 512 / 0.14136, "unfused": 32 * 512 * 512 / 0.02010},
 }
 MUFU_PER_CELL = 7          # algorithmic ex2/lg2 per DP cell, forward + backward (reference algorithm)
@@ -527,7 +527,7 @@ def main():
                                    else f"dp{world} (batch-sharded, no collective)"),
                    "l2": ("per-iteration working set (about 1 GB of tables) larger than the 126 MB L2" if is_bary else
                           "flushed before every timed step (256 MiB write, outside the events)"),
-                   "vs_baseline_basis": "per-GPU value / BASELINE.md published number (unstated GPU)"},
+                   "vs_baseline_basis": "per-GPU value / the reference's published number (unstated GPU)"},
         "modes": modes,
         "kernel_ms_per_step": breakdown,
         "roofline": roofline,

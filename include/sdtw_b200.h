@@ -53,7 +53,9 @@ const char *sdtw_last_error_message(void);
 /* Reads and clears the device status word written by the kernels' bounded
  * waits (0 = no failure; on failure sdtw_last_error_message says which wait
  * gave up).  It does not synchronise: call it after the stream has been
- * synchronised to observe the kernels enqueued before. */
+ * synchronised to observe the kernels enqueued before.  Once the current
+ * device has run sdtw_forward_noalloc_f32, it also reads that entry point's
+ * device status word (a small synchronous copy). */
 int sdtw_status(void);
 
 /* Wall-clock limit of one device-side wait, in nanoseconds (default 2e9). */
@@ -219,7 +221,11 @@ int sdtw_cost_sqeuclid_f64(const double *x, const double *y, double *D, int B, i
  * device's array, which keeps the previous call's contents (each call resets
  * what must start fresh): calls on one device that overlap on the GPU -- issued
  * on different streams without ordering -- race on it, so the caller must
- * order them, e.g. by issuing them on one stream. */
+ * order them, e.g. by issuing them on one stream.  A device-side wait of this
+ * entry point that gives up records the failure in a device word inside the
+ * library (it cannot use the mapped host record the other entry points
+ * create); sdtw_status() reads and clears it, so call sdtw_status() after
+ * synchronising the stream to learn whether the results are valid. */
 int sdtw_forward_noalloc_f32(const float *D, float *score, float *out, int B, int N, int M, float gamma,
                              float bandwidth, void *stream);
 

@@ -137,8 +137,8 @@ void clear_status() {
     cudaMemcpyToSymbol(g_abort_flag, &zero, sizeof(int));
 }
 
-std::string diag_text() {
-    const volatile int* d = g_status_host + 8;
+// Diagnostics of a failed wait: d points at a WaitDiag record (8 ints).
+std::string diag_text_of(const volatile int* d) {
     char buf[256];
     std::snprintf(buf, sizeof buf,
                   "%s pass, %s wait, problem %d, warp %d, band %d: expected %d, last seen %d",
@@ -147,10 +147,13 @@ std::string diag_text() {
                                          : (d[0] == 5 ? "tensor-core gradient" : (d[0] == 6 ? "tensor-core cost" : "?"))),
                   d[1] == 1 ? "shared-memory ring"
                             : (d[1] == 2 ? "global ring"
-                                         : (d[1] == 3 ? "flow-control" : (d[1] == 4 ? "MMA completion" : "?"))),
+                                         : (d[1] == 3 ? "flow-control"
+                                                      : (d[1] == 4 ? "MMA completion"
+                                                                   : (d[1] == 5 ? "aborted (another wait failed)" : "?")))),
                   d[2], d[3], d[4], d[5], d[6]);
     return buf;
 }
+std::string diag_text() { return diag_text_of(g_status_host + 8); }
 
 // A failure recorded by an earlier launch surfaces at the next call.
 int pending_status() {
@@ -335,7 +338,7 @@ GradOperands grad_operands(int B, int N, int M, int dim) {
 bool weight_store(int B, int N, int M) { return plan(B, N, M).K == 1; }
 
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
-                uint64_t* wrap, cudaStream_t stream, bool weights = false) {
+                uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr) {
     FwdArgs a{};
     a.P = plan(B, N, M);
     a.weights = weights ? 1 : 0;
@@ -349,7 +352,7 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
     a.ibw = int_band(bw);
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
-    a.wait = wait_ctx();
+    a.wait = wait ? *wait : wait_ctx();
     cudaError_t e;
     {
         KernelTimer kt("wavefront_fwd", stream);
@@ -405,6 +408,67 @@ int check_score(const float* score) {
 
 }  // namespace
 
+// ----------------------------------------------------------------------------
+// Allocation-free forward.
+//
+// Some callers cannot allocate device memory when they call us: a host runtime
+// whose allocator owns all of device memory and lends out no scratch, a plugin
+// boundary that hands over only input and output buffers, or a latency-critical
+// loop in which cudaMalloc (which can synchronise the device) is not allowed.
+// For them the D-input forward has a variant whose scratch (band-wrap ring and
+// the anti-diagonal copy of D) lives in a fixed device array compiled into the
+// library.  Every GPU that loads the library holds this array until the process
+// exits.  The caller still passes D, score and out.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+// Status word ([0]) and the failed wait's diagnostics ([8..15], a WaitDiag) of
+// the launches of the allocation-free forward: device memory, since that entry
+// point may not create the mapped host status record the others use.
+static __device__ int g_noalloc_status[16];
+static std::atomic<unsigned long long> g_noalloc_used{0};  // bit d: device d ran it
+
+// Host code cannot use a __device__ array's name as a device address; look the
+// addresses up with the device current.  Done at every call (it allocates
+// nothing), so an address is never kept past a device reset.
+static int noalloc_addrs(int* dev, void** scratch, int** status) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (*dev < 0 || *dev >= 64) return fail(SDTW_ERR_INVALID_ARGUMENT, "device index out of range");
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    void* q = nullptr;
+    e = cudaGetSymbolAddress(&q, g_noalloc_status);
+    if (e != cudaSuccess || !q) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc status)");
+    *scratch = p;
+    *status = static_cast<int*>(q);
+    return SDTW_OK;
+}
+
+// Status of the allocation-free forward on the current device: its device
+// word, read and cleared; 0 if that entry point never ran here.
+static int noalloc_take_status(std::string* why) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (!(g_noalloc_used.load() & (1ull << dev))) return 0;
+    int rec[16] = {0};
+    // A synchronous copy: sdtw_status is called after the caller synchronised.
+    if (cudaMemcpyFromSymbol(rec, g_noalloc_status, sizeof rec) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (rec[0] == 0) return 0;
+    *why = diag_text_of(rec + 8);
+    const int zero[16] = {0};
+    cudaMemcpyToSymbol(g_noalloc_status, zero, sizeof zero);
+    const int z = 0;
+    cudaMemcpyToSymbol(g_abort_flag, &z, sizeof(int));
+    return rec[0];
+}
+
 extern "C" {
 
 const char* sdtw_version(void) { return "sdtw-b200 0.1.0 (sm_100a)"; }
@@ -422,11 +486,17 @@ const char* sdtw_error_string(int code) {
 const char* sdtw_last_error_message(void) { return g_last_error.c_str(); }
 
 int sdtw_status(void) {
-    if (!g_status_host) return 0;
-    int s = *reinterpret_cast<volatile int*>(g_status_host);
+    int s = g_status_host ? *reinterpret_cast<volatile int*>(g_status_host) : 0;
     if (s != 0) {
         g_last_error = "device-side wait timed out: " + diag_text();
         clear_status();
+    }
+    // The allocation-free forward records its failures in a device word.
+    std::string why;
+    const int s2 = noalloc_take_status(&why);
+    if (s2 != 0 && s == 0) {
+        g_last_error = "device-side wait timed out (allocation-free forward): " + why;
+        s = s2;
     }
     return s;
 }
@@ -808,40 +878,6 @@ int sdtw_R_to_score_f32(const float* R, float* score, int B, int N, int M, float
 }
 
 
-// ----------------------------------------------------------------------------
-// Allocation-free forward.
-//
-// Some callers cannot allocate device memory when they call us: a host runtime
-// whose allocator owns all of device memory and lends out no scratch, a plugin
-// boundary that hands over only input and output buffers, or a latency-critical
-// loop in which cudaMalloc (which can synchronise the device) is not allowed.
-// For them the D-input forward has a variant whose scratch (band-wrap ring and
-// the anti-diagonal copy of D) lives in a fixed device array compiled into the
-// library.  Every GPU that loads the library holds this array until the process
-// exits.  The caller still passes D, score and out.
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-static void* g_noalloc_base[64];  // device address of g_noalloc_scratch, per device
-static std::mutex g_noalloc_mu;
-
-// Host code cannot use the array's name as a device address; look the address
-// up once per device, with that device current.
-static int noalloc_base(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if (dev < 0 || dev >= 64) return fail(SDTW_ERR_INVALID_ARGUMENT, "device index out of range");
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_base[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
-        g_noalloc_base[dev] = p;
-    }
-    *out = g_noalloc_base[dev];
-    return SDTW_OK;
-}
-
 int sdtw_forward_noalloc_f32(const float* D, float* score, float* out, int B, int N, int M, float gamma,
                              float bandwidth, void* stream) {
     int rc;
@@ -854,11 +890,14 @@ int sdtw_forward_noalloc_f32(const float* D, float* score, float* out, int B, in
                     "problem too large for the allocation-free forward: needs " + std::to_string(need) +
                         " bytes of scratch, the fixed array holds " + std::to_string(kNoAllocScratchBytes) +
                         " (use sdtw_forward_f32 with a workspace)");
-    // A failure recorded by an earlier launch still surfaces here; the status
-    // word is only read if another entry point already created it.
+    // A failure recorded by an earlier launch of another entry point still
+    // surfaces here (its status record exists only if one of them ran).
     if ((rc = pending_status())) return rc;
+    int dev = 0;
     void* base = nullptr;
-    if ((rc = noalloc_base(&base))) return rc;
+    int* status = nullptr;
+    if ((rc = noalloc_addrs(&dev, &base, &status))) return rc;
+    g_noalloc_used.fetch_or(1ull << dev);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // The array keeps the previous call's contents.  The anti-diagonal copy of D
     // is fully rewritten below; the band-wrap ring's slots are reset so that no
@@ -874,7 +913,10 @@ int sdtw_forward_noalloc_f32(const float* D, float* score, float* out, int B, in
         e = launch_rm_to_wl(D, Dw, plan(B, N, M), st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "layout launch");
-    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(base), st);
+    WaitCtx w = wait_ctx();
+    w.status = status;
+    w.diag = reinterpret_cast<volatile WaitDiag*>(status + 8);
+    return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(base), st, false, &w);
 }
 
 }  // extern "C"

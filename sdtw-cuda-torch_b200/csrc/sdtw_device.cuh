@@ -238,6 +238,32 @@ __device__ __forceinline__ void record_error(const WaitCtx& w, int code, int kin
     if (w.status) *w.status = code;
 }
 
+// A wait that gave up because another wait had failed (the abort flag) also
+// marks its launch as failed, so that no launch can finish with a wrong
+// result and an ok status, whichever status word the first failure went to.
+// The first failure's diagnostics are kept; kind 5 marks an abort.
+__device__ __forceinline__ void record_abort(const WaitCtx& w) {
+    if (w.status && *w.status == 0) {
+        if (w.diag) {
+            w.diag->kernel = w.kernel;
+            w.diag->kind = 5;
+            w.diag->problem = w.problem;
+            w.diag->warp = w.warp;
+            w.diag->band = w.band;
+            w.diag->expect = 0;
+            w.diag->seen = 0;
+        }
+        __threadfence_system();
+        *w.status = kStatusTimeout;
+    }
+}
+
+// r as returned by backoff(): 1 = this wait ran out of time, 2 = aborted.
+__device__ __forceinline__ void record_giveup(const WaitCtx& w, int r, int kind, uint32_t expect, uint32_t seen) {
+    if (r == 1) record_error(w, kStatusTimeout, kind, expect, seen);
+    else if (r == 2) record_abort(w);
+}
+
 // Shared back-off policy of the slow paths: poll tightly, look at the clock
 // every 256 polls, at the device abort flag every 4096 polls once the wait is
 // older than 20 us, and sleep between polls once it is older than 1 ms.
@@ -269,7 +295,7 @@ static __device__ __noinline__ uint64_t wait_tag_generic(uint64_t ga, uint32_t t
         e = ld_one(ga);
         if (tag_of(e) == tag) return e;
         const int r = backoff(it, t0, w);
-        if (r == 1) record_error(w, kStatusTimeout, 1, tag, tag_of(e));
+        record_giveup(w, r, 1, tag, tag_of(e));
         if (r) return e;
     }
 }
@@ -283,7 +309,7 @@ static __device__ __noinline__ uint32_t wait_counter_ge(uint32_t saddr, uint32_t
         seen = ld_acquire_cluster_u32(saddr);
         if (static_cast<int32_t>(seen - need) >= 0) return seen;
         const int r = backoff(it, t0, w);
-        if (r == 1) record_error(w, kStatusTimeout, 3, need, seen);
+        record_giveup(w, r, 3, need, seen);
         if (r) return seen;
     }
 }

@@ -154,7 +154,7 @@ __device__ __noinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, const Wai
         if (mbar_try_wait(mbar, parity)) return true;
         const int r = backoff(it, t0, w);
         if (r) {
-            if (r == 1) record_error(w, kStatusTimeout, 4, parity, 0);
+            record_giveup(w, r, 4, parity, 0);
             return false;
         }
     }
@@ -490,7 +490,7 @@ __device__ __noinline__ bool mbar_wait_sleep(uint32_t mbar, uint32_t parity, con
         if (mbar_try_wait_sleep(mbar, parity)) return true;
         const int r = backoff(it << 8, t0, w);  // every poll checks the clock
         if (r) {
-            if (r == 1) record_error(w, kStatusTimeout, 4, parity, 0);
+            record_giveup(w, r, 4, parity, 0);
             return false;
         }
     }

@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                         if (all) break;
                         const int r = backoff(it, w0, wc);
                         if (r) {
-                            if (r == 1 && lane == 0) record_error(wc, kStatusTimeout, 1, tg0, 0);
+                            if (lane == 0) record_giveup(wc, r, 1, tg0, 0);
                             ok = false;
                             break;
                         }
@@ -699,7 +699,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                         if (all) break;
                         const int r = backoff(it, w0, wc);
                         if (r) {
-                            if (r == 1 && lane == 0) record_error(wc, kStatusTimeout, 1, static_cast<uint32_t>(colb0), 0);
+                            if (lane == 0) record_giveup(wc, r, 1, static_cast<uint32_t>(colb0), 0);
                             ok = false;
                             break;
                         }

@@ -28,7 +28,6 @@ back to the step-by-step loop.
 from __future__ import annotations
 
 import math
-import time
 
 import torch
 
@@ -125,7 +124,6 @@ def _graph_barycenter(X, w, bary0, loss_fn, max_iter, lr, early_stopping, patien
     host_losses = torch.empty(max_iter, dtype=X.dtype, pin_memory=True)
     done = 0
     stop = None
-    t0 = time.time()
     while done < max_iter and stop is None:
         n = min(_READBACK_EVERY, max_iter - done)
         for _ in range(n):
@@ -149,7 +147,6 @@ def _graph_barycenter(X, w, bary0, loss_fn, max_iter, lr, early_stopping, patien
                 print(f"Early stopping at iteration {it + 1} (no improvement for {patience} iterations)")
                 break
             if (it + 1) % 20 == 0:
-                _ = time.time() - t0
                 imp = f"{improvement:9.6f}" if early_stopping else "     N/A "
                 print(f"Iteration {it + 1:3d}/{max_iter} | Loss: {losses[it]:9.6f} | Improvement: {imp} | "
                       f"LR: {lrs[it + 1]:.2e}")
@@ -208,7 +205,6 @@ def softdtw_barycenter(
     opt = torch.optim.Adam([bary], lr=lr)
     sched = torch.optim.lr_scheduler.CosineAnnealingLR(opt, T_max=max_iter, eta_min=lr * 0.1)
 
-    t0 = time.time()
     best = float("inf")
     stale = 0
     for it in range(max_iter):
@@ -237,7 +233,6 @@ def softdtw_barycenter(
         if verbose and (it + 1) % 20 == 0:
             if torch.cuda.is_available():
                 torch.cuda.synchronize()
-            _ = time.time() - t0
             lr_val = opt.param_groups[0]["lr"]
             imp = f"{improvement:9.6f}" if early_stopping else "     N/A "
             print(f"Iteration {it + 1:3d}/{max_iter} | Loss: {loss_val:9.6f} | Improvement: {imp} | LR: {lr_val:.2e}")
