@@ -41,6 +41,9 @@ extern "C" {
 #define SDTW_ERR_INVALID_ARGUMENT 1 /* bad size, pointer, gamma or workspace */
 #define SDTW_ERR_CUDA 2             /* a CUDA runtime call failed (see sdtw_last_error_message) */
 #define SDTW_ERR_TIMEOUT 3          /* a device-side wait ran out of time; results are invalid */
+#define SDTW_ERR_RANGE 4            /* the forward's values left the float32 exponential-domain range
+                                       (|R|/gamma >= 3.7e8, |cost|*log2(e)/gamma >= 4.2e6, or a NaN
+                                       cost); results are invalid */
 
 /* Library version string. */
 const char *sdtw_version(void);

@@ -149,11 +149,22 @@ std::string diag_text_of(const volatile int* d) {
                             : (d[1] == 2 ? "global ring"
                                          : (d[1] == 3 ? "flow-control"
                                                       : (d[1] == 4 ? "MMA completion"
-                                                                   : (d[1] == 5 ? "aborted (another wait failed)" : "?")))),
+                                                                   : (d[1] == 5 ? "aborted (another wait failed)"
+                                                                                : (d[1] == 6 ? "value range" : "?"))))),
                   d[2], d[3], d[4], d[5], d[6]);
     return buf;
 }
 std::string diag_text() { return diag_text_of(g_status_host + 8); }
+
+// Text of a nonzero device status (the wait diagnostics `why` for a timeout).
+std::string status_text(int s, const std::string& why) {
+    if (s == kStatusRange)
+        return "the forward's scores left the representable range: |R| / gamma must stay below 3.7e8 and "
+               "|cost| * log2(e) / gamma below 4.2e6 per cell, and no cost may be NaN (use float64 inputs "
+               "for larger ranges)";
+    return "a device-side wait timed out (" + why + ")";
+}
+int status_code(int s) { return s == kStatusRange ? SDTW_ERR_RANGE : SDTW_ERR_TIMEOUT; }
 
 // A failure recorded by an earlier launch surfaces at the next call.
 int pending_status() {
@@ -162,7 +173,7 @@ int pending_status() {
         if (s != 0) {
             std::string why = diag_text();
             clear_status();
-            return fail(SDTW_ERR_TIMEOUT, "a device-side wait of an earlier launch timed out (" + why + ")");
+            return fail(status_code(s), "an earlier launch failed: " + status_text(s, why));
         }
     }
     return SDTW_OK;
@@ -348,6 +359,7 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
     a.wrap = wrap;
     a.kk = kLog2e / gamma;
     a.inv_k = static_cast<float>(1.0 / static_cast<double>(a.kk));
+    a.inv_k_d = static_cast<double>(gamma) * 0.6931471805599453;
     a.bw = bw > 0.f ? bw : -1.f;
     a.ibw = int_band(bw);
     a.seq = g_seq.fetch_add(1);
@@ -479,6 +491,7 @@ const char* sdtw_error_string(int code) {
         case SDTW_ERR_INVALID_ARGUMENT: return "invalid argument";
         case SDTW_ERR_CUDA: return "CUDA runtime error";
         case SDTW_ERR_TIMEOUT: return "device-side wait timed out";
+        case SDTW_ERR_RANGE: return "value range exceeded";
         default: return "unknown error";
     }
 }
@@ -488,14 +501,14 @@ const char* sdtw_last_error_message(void) { return g_last_error.c_str(); }
 int sdtw_status(void) {
     int s = g_status_host ? *reinterpret_cast<volatile int*>(g_status_host) : 0;
     if (s != 0) {
-        g_last_error = "device-side wait timed out: " + diag_text();
+        g_last_error = status_text(s, diag_text());
         clear_status();
     }
     // The allocation-free forward records its failures in a device word.
     std::string why;
     const int s2 = noalloc_take_status(&why);
     if (s2 != 0 && s == 0) {
-        g_last_error = "device-side wait timed out (allocation-free forward): " + why;
+        g_last_error = "allocation-free forward: " + status_text(s2, why);
         s = s2;
     }
     return s;

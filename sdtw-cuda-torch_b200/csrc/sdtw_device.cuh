@@ -201,6 +201,7 @@ __device__ __forceinline__ float val_of(uint64_t e) { return __uint_as_float(sta
 enum : int {
     kStatusOk = 0,
     kStatusTimeout = 3,
+    kStatusRange = 4,  // a value left the range of the exponential-domain forward
 };
 
 // Where a wait gave up (written next to the status word, for diagnostics).
@@ -255,6 +256,25 @@ __device__ __forceinline__ void record_abort(const WaitCtx& w) {
         }
         __threadfence_system();
         *w.status = kStatusTimeout;
+    }
+}
+
+// A forward whose scores left the representable range (or met a NaN cost)
+// marks its launch failed with kStatusRange; kind 6 in the diagnostics.  It
+// does not raise the abort flag: no wait is affected.
+__device__ __forceinline__ void record_range(const WaitCtx& w) {
+    if (w.status && *w.status == 0) {
+        if (w.diag) {
+            w.diag->kernel = w.kernel;
+            w.diag->kind = 6;
+            w.diag->problem = w.problem;
+            w.diag->warp = w.warp;
+            w.diag->band = w.band;
+            w.diag->expect = 0;
+            w.diag->seen = 0;
+        }
+        __threadfence_system();
+        *w.status = kStatusRange;
     }
 }
 

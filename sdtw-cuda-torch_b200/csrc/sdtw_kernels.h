@@ -20,6 +20,7 @@ struct FwdArgs {
     uint64_t* wrap;   // (B*M) band-wrap ring, null when n_bands == 1
     float kk;         // log2(e) / gamma
     float inv_k;      // gamma * ln(2)
+    double inv_k_d;   // gamma * ln(2) in double (the loss of the exponential-domain forward)
     float bw;         // Sakoe-Chiba bandwidth, <= 0 disables
     int ibw;          // integer band: cell (i, j) is kept when |i - j| <= ibw (floor(bw), or 2^29 when disabled)
     uint32_t seq;     // launch sequence number (tags of the global ring)
@@ -43,6 +44,15 @@ struct BwdArgs {
 };
 
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
+// wavefront_exp.cu: the one-row-per-lane forward (exponential domain) and the
+// reverse pass over its stored shares; launch_forward / launch_backward route
+// K = 1 to them.
+cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream);
+cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream);
+size_t fwdx_smem(const WavePlan& P);
+size_t bwdw_smem(const WavePlan& P);
+const void* fwdx_fn(bool banded, bool weights);
+const void* bwdw_fn(bool banded);
 int max_active_clusters(const WavePlan& P);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);

@@ -38,16 +38,10 @@
 #include "sdtw_device.cuh"
 #include "sdtw_kernels.h"
 #include "sdtw_plan.h"
+#include "wavefront_ring.cuh"
 
 namespace sdtw {
 
-constexpr int kRing = 128;  // ring slots per warp (power of two)
-// Byte offset of the forward's staging buffers: after the rings ([wpc][kRing][2]
-// u64) and the consumption counters ([wpc] u32), 16-byte aligned for the bulk
-// copies.
-__host__ __device__ constexpr size_t fwd_stage_offset(int wpc) {
-    return (static_cast<size_t>(wpc) * (2 * kRing * 8 + 4) + 15) / 16 * 16;
-}
 // Step bodies of the forward (compile-time phases, one store staging buffer
 // each).  With the cost rows staged in shared memory one body measured as fast
 // as two at C2 and 3.5 % faster at C3 (N = M = 4096: the smaller code); with
@@ -69,10 +63,6 @@ __host__ __device__ constexpr size_t bwd_weight_offset(int wpc, int K, int nph) 
 // prefetch: 9-18 % faster than one) and with the shared-memory staging.
 constexpr int kBwdWeightPhases = 2;
 
-__device__ __forceinline__ uint32_t wrap_tag(uint32_t seq, int band) {
-    return (seq << 12) | (static_cast<uint32_t>(band) & 0xfffu);
-}
-
 // ============================================================== step groups
 // Steps run in groups of PF.  Per group (warp-uniform code): the consumer lane
 // reads and checks the PF ring slots it will need, the producer lane checks
@@ -88,15 +78,6 @@ struct StepCfg {
     static constexpr int PF = (K >= 4) ? 4 : 8;
 };
 
-__device__ __forceinline__ bool report_due(int done, int PF, int M) {
-    // `done` columns consumed, PF more than after the previous group: report
-    // when a multiple of 32 was crossed, and at the end of the row.
-    return (done & 31) < PF || done >= M;
-}
-
-__device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b, int s) {
-    return (static_cast<size_t>(b) * P.n_stripes + s) * static_cast<size_t>(P.n_diag) * (32 * P.K);
-}
 
 // ============================================================== forward
 // Ring slot pair layout (per consumer warp): kRing x {hi, lo} tagged u64;
@@ -920,27 +901,6 @@ __global__ void R_to_score_kernel(const float* __restrict__ R, float2* __restric
 }
 
 // ============================================================== launchers
-static cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t smem, int csize,
-                                  cudaStream_t stream, void** args) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = csize;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-    }
-    return cudaLaunchKernelExC(&cfg, fn, args);
-}
-
 static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
@@ -973,24 +933,39 @@ int max_active_clusters(const WavePlan& P) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    // (kernel, dynamic shared memory) of every pass this geometry may launch.
     const void* fns[4] = {nullptr, nullptr, nullptr, nullptr};
+    size_t smem[4] = {0, 0, 0, 0};
     switch (P.K) {
         case 1:
-            fns[0] = (const void*)fwd_kernel<1, false, false>;
+            fns[0] = fwdx_fn(false, false);
+            smem[0] = fwdx_smem(P);
             fns[1] = (const void*)bwd_kernel<1, false, false>;
-            fns[2] = (const void*)fwd_kernel<1, false, true>;
-            fns[3] = (const void*)bwd_kernel<1, false, true>;
+            smem[1] = bwd_smem_bytes(P, false);
+            fns[2] = fwdx_fn(false, true);
+            smem[2] = fwdx_smem(P);
+            fns[3] = bwdw_fn(false);
+            smem[3] = bwdw_smem(P);
             break;
-        case 2: fns[0] = (const void*)fwd_kernel<2, false, false>; fns[1] = (const void*)bwd_kernel<2, false, false>; break;
-        case 4: fns[0] = (const void*)fwd_kernel<4, false, false>; fns[1] = (const void*)bwd_kernel<4, false, false>; break;
+        case 2:
+            fns[0] = (const void*)fwd_kernel<2, false, false>;
+            smem[0] = fwd_smem_bytes(P);
+            fns[1] = (const void*)bwd_kernel<2, false, false>;
+            smem[1] = bwd_smem_bytes(P, false);
+            break;
+        case 4:
+            fns[0] = (const void*)fwd_kernel<4, false, false>;
+            smem[0] = fwd_smem_bytes(P);
+            fns[1] = (const void*)bwd_kernel<4, false, false>;
+            smem[1] = bwd_smem_bytes(P, false);
+            break;
         default: return -1;
     }
     int best = -1;
     for (int i = 0; i < 4; ++i) {
         const void* fn = fns[i];
         if (!fn) continue;
-        // Forwards in even slots, reverse passes in odd ones; slots 2 and 3 use the weight store.
-        cfg.dynamicSmemBytes = (i % 2 == 0) ? fwd_smem_bytes(P) : bwd_smem_bytes(P, i == 3);
+        cfg.dynamicSmemBytes = smem[i];
         if (cfg.dynamicSmemBytes > 48 * 1024 &&
             cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(cfg.dynamicSmemBytes)) != cudaSuccess) {
@@ -1009,41 +984,35 @@ int max_active_clusters(const WavePlan& P) {
 
 cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
+    if (P.K == 1) return launch_forward_x(args, stream);
+    if (args.weights) return cudaErrorInvalidValue;
     // The band check runs only when a band can exclude a cell of the table.
     const bool banded = args.ibw < P.N + P.M;
     dim3 grid(P.B * P.csize), block(P.wpc * 32);
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
     const void* fn = nullptr;
     switch (P.K) {
-        case 1:
-            fn = args.weights ? (banded ? (const void*)fwd_kernel<1, true, true> : (const void*)fwd_kernel<1, false, true>)
-                              : (banded ? (const void*)fwd_kernel<1, true, false> : (const void*)fwd_kernel<1, false, false>);
-            break;
         case 2: fn = banded ? (const void*)fwd_kernel<2, true, false> : (const void*)fwd_kernel<2, false, false>; break;
         case 4: fn = banded ? (const void*)fwd_kernel<4, true, false> : (const void*)fwd_kernel<4, false, false>; break;
         default: return cudaErrorInvalidValue;
     }
-    if (args.weights && P.K != 1) return cudaErrorInvalidValue;
     return launch_cluster(fn, grid, block, fwd_smem_bytes(P), P.csize, stream, kargs);
 }
 
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
+    if (args.weights) return launch_backward_w(args, stream);
     const bool banded = args.ibw < P.N + P.M;
     dim3 grid(P.B * P.csize), block(P.wpc * 32);
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
     const void* fn = nullptr;
     switch (P.K) {
-        case 1:
-            fn = args.weights ? (banded ? (const void*)bwd_kernel<1, true, true> : (const void*)bwd_kernel<1, false, true>)
-                              : (banded ? (const void*)bwd_kernel<1, true, false> : (const void*)bwd_kernel<1, false, false>);
-            break;
+        case 1: fn = banded ? (const void*)bwd_kernel<1, true, false> : (const void*)bwd_kernel<1, false, false>; break;
         case 2: fn = banded ? (const void*)bwd_kernel<2, true, false> : (const void*)bwd_kernel<2, false, false>; break;
         case 4: fn = banded ? (const void*)bwd_kernel<4, true, false> : (const void*)bwd_kernel<4, false, false>; break;
         default: return cudaErrorInvalidValue;
     }
-    if (args.weights && P.K != 1) return cudaErrorInvalidValue;
-    return launch_cluster(fn, grid, block, bwd_smem_bytes(P, args.weights != 0), P.csize, stream, kargs);
+    return launch_cluster(fn, grid, block, bwd_smem_bytes(P, false), P.csize, stream, kargs);
 }
 
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream) {
