@@ -77,8 +77,7 @@ int sdtw_timing_read(char *names, size_t names_len, double *total_ms, long *coun
  * -1 disables.  Never set outside tests. */
 void sdtw_debug_stall_stripe(int stripe);
 
-/* Tuning/test hook: force the warps per CTA (1..16 with one DP row per lane,
- * 1..8 with more), the thread-block cluster
+/* Tuning/test hook: force the stripes (chain warps) per CTA (1..8), the thread-block cluster
  * size (1..8) and the DP rows per lane (1, 2 or 4) of the wavefront launches;
  * 0 restores the automatic choice.  The score layout depends on the rows per
  * lane, so a forward and its backward must run under the same setting. */

@@ -50,6 +50,7 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream);
 size_t fwdx_smem(const WavePlan& P);
+int fwdx_threads(const WavePlan& P);
 size_t bwdw_smem(const WavePlan& P);
 const void* fwdx_fn(bool banded, bool weights);
 const void* bwdw_fn(bool banded);

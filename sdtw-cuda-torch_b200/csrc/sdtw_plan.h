@@ -67,9 +67,10 @@ inline size_t score_elems(int B, int N, int M, int k_override = 0) {
     return 2u * wl_cells(B, N, M, k_override);
 }
 
-// Warps per CTA the wavefront kernels are compiled for: 16 with one DP row per
-// lane, 8 with more (their registers then need 255 per thread).
-inline int wpc_max(int K) { return K == 1 ? 16 : 8; }
+// Stripes (chain warps) per CTA the wavefront kernels are compiled for: 8
+// (with one DP row per lane the forward pairs each chain warp with a helper
+// warp, 512 threads; with more rows per lane the registers need 255 per thread).
+inline int wpc_max(int K) { (void)K; return 8; }
 
 // wpc_override / cs_override / k_override (> 0) force the warps per CTA, the
 // cluster size and the rows per lane (tests use them to exercise many bands

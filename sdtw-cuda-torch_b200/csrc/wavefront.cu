@@ -933,17 +933,20 @@ int max_active_clusters(const WavePlan& P) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    // (kernel, dynamic shared memory) of every pass this geometry may launch.
+    // (kernel, dynamic shared memory, threads) of every pass this geometry may launch.
     const void* fns[4] = {nullptr, nullptr, nullptr, nullptr};
     size_t smem[4] = {0, 0, 0, 0};
+    int threads[4] = {P.wpc * 32, P.wpc * 32, P.wpc * 32, P.wpc * 32};
     switch (P.K) {
         case 1:
             fns[0] = fwdx_fn(false, false);
             smem[0] = fwdx_smem(P);
+            threads[0] = fwdx_threads(P);
             fns[1] = (const void*)bwd_kernel<1, false, false>;
             smem[1] = bwd_smem_bytes(P, false);
             fns[2] = fwdx_fn(false, true);
             smem[2] = fwdx_smem(P);
+            threads[2] = fwdx_threads(P);
             fns[3] = bwdw_fn(false);
             smem[3] = bwdw_smem(P);
             break;
@@ -966,6 +969,7 @@ int max_active_clusters(const WavePlan& P) {
         const void* fn = fns[i];
         if (!fn) continue;
         cfg.dynamicSmemBytes = smem[i];
+        cfg.blockDim = dim3(threads[i]);
         if (cfg.dynamicSmemBytes > 48 * 1024 &&
             cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(cfg.dynamicSmemBytes)) != cudaSuccess) {

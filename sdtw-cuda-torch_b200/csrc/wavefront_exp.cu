@@ -68,8 +68,7 @@ constexpr int kShiftMin = -96;           // terms below 2^-96 of the largest are
 constexpr int kErange = 1 << 29;         // valid exponents lie in (-2^29, 2^29)
 constexpr float kPmax = 4194304.f;       // |D| * log2(e) / gamma per cell must stay below 2^22
 constexpr float kMagic = 12582912.f;     // 1.5 * 2^23: adding it rounds to an integer in the low bits
-constexpr int kFwdStages = 2;            // forward: table-row staging buffers
-constexpr int kBwdPhases = 2;            // reverse pass: E staging buffers (step bodies)
+constexpr int kBwdPhases = 2;            // reverse pass: step bodies per loop iteration
 }  // namespace
 
 // m * 2^s for s <= 0 by an add to the exponent field.  m is a normal float
@@ -101,23 +100,60 @@ __device__ __forceinline__ float2 to_score(float m, int e) {
 }
 
 // ------------------------------------------------------------------ forward
+// Warp roles.  Warps [0, wpc) of a CTA carry the dependent chains, one stripe
+// each; warp wpc + h is the helper of chain warp h (warps are placed on SM
+// sub-partitions by index mod 4, so with wpc a multiple of 4 a pair shares a
+// sub-partition and the helper issues in the chain warp's idle cycles).  Per
+// group of PF steps the helper
+//   * copies the cost rows two groups ahead into shared memory (cp.async),
+//   * turns every cost into K = km * 2^ke (one ex2 per cell),
+//   * reads the ring slots of the row above (the tag vote, and any wait for
+//     the stripe above, happen here) and reports their consumption,
+// and hands both over in one of kNB buffers guarded by mbarriers (full:
+// helper to chain, empty: chain to helper).  The chain warp runs the steps,
+// stores each cell's shares (or score) with one coalesced row store per step,
+// and publishes its stripe's bottom row.
+//
 // Shared memory: rings [wpc][kRing][2] u64 and counters [wpc] u32 (as in
-// wavefront.cu), then per warp: the staged table rows of two groups
-// [2][PF][32] float2 (a group's rows are written while the previous group's
-// bulk copy still reads its buffer), the cost rows of three groups [3][PF][32]
-// float, and the ring input and bottom-row output of one group [2][PF] uint2.
-__host__ __device__ constexpr size_t fx_cost_off(int wpc) {
-    return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * kFwdStages * kPF * 32 * 8;
-}
-__host__ __device__ constexpr size_t fx_stash_off(int wpc) {
+// wavefront.cu), then per pair: the helper's cost rows [3][PF][32] float, the
+// handed-over K [kNB][PF][32] (km, ke), the ring input [kNB][PF] (m, e), the
+// chain's bottom-row output [PF] (m, e), and the mbarriers [2][kNB].
+constexpr int kNB = 3;
+__host__ __device__ constexpr size_t fx_cost_off(int wpc) { return fwd_stage_offset(wpc); }
+__host__ __device__ constexpr size_t fx_k_off(int wpc) {
     return fx_cost_off(wpc) + static_cast<size_t>(wpc) * 3 * kPF * 32 * 4;
 }
+__host__ __device__ constexpr size_t fx_rin_off(int wpc) {
+    return fx_k_off(wpc) + static_cast<size_t>(wpc) * kNB * kPF * 32 * 8;
+}
+__host__ __device__ constexpr size_t fx_pub_off(int wpc) {
+    return fx_rin_off(wpc) + static_cast<size_t>(wpc) * kNB * kPF * 8;
+}
+__host__ __device__ constexpr size_t fx_mbar_off(int wpc) {
+    return fx_pub_off(wpc) + static_cast<size_t>(wpc) * kPF * 8;
+}
 __host__ __device__ constexpr size_t fx_smem_bytes(int wpc) {
-    return fx_stash_off(wpc) + static_cast<size_t>(wpc) * 2 * kPF * 8;
+    return fx_mbar_off(wpc) + static_cast<size_t>(wpc) * 2 * kNB * 8;
 }
 
 __device__ __forceinline__ uint64_t pack_tagged_bits(uint32_t v, uint32_t tag) {
     return (static_cast<uint64_t>(tag) << 32) | static_cast<uint64_t>(v);
+}
+
+// Bounded wait for an mbarrier phase (kind 4 in the diagnostics).
+__device__ __noinline__ bool mbar_wait_bounded(uint32_t mbar, uint32_t parity, const WaitCtx& w) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(mbar, parity)) return true;
+        const int r = backoff(it, t0, w);
+        if (r) {
+            record_giveup(w, r, 4, parity, 0);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ bool mbar_wait_fx(uint32_t mbar, uint32_t parity, const WaitCtx& w) {
+    return mbar_try_wait(mbar, parity) || mbar_wait_bounded(mbar, parity, w);
 }
 
 template <bool BANDED, bool W>
@@ -126,7 +162,9 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
     const int wpc = P.wpc;
-    const int warp = threadIdx.x >> 5;
+    const int wid = threadIdx.x >> 5;
+    const bool helper = wid >= wpc;
+    const int warp = helper ? wid - wpc : wid;  // the chain warp of this pair
     const int lane = threadIdx.x & 31;
     const int crank = static_cast<int>(cluster_ctarank());
     const int b = blockIdx.x / P.csize;
@@ -135,14 +173,18 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][kRing][2]
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
-    float2* stage = reinterpret_cast<float2*>(smem_raw + fwd_stage_offset(wpc)) + warp * kFwdStages * PF * 32;
-    const uint32_t stage_s = smem_addr(stage);
     const float* cost = reinterpret_cast<const float*>(smem_raw + fx_cost_off(wpc)) + warp * 3 * PF * 32;
     const uint32_t cost_s = smem_addr(cost);
-    uint2* rin_s = reinterpret_cast<uint2*>(smem_raw + fx_stash_off(wpc)) + warp * 2 * PF;  // ring input (m, e)
-    uint2* pub_s = rin_s + PF;                                                                  // bottom row (m, e)
+    uint2* kbuf = reinterpret_cast<uint2*>(smem_raw + fx_k_off(wpc)) + warp * kNB * PF * 32;
+    uint2* rin = reinterpret_cast<uint2*>(smem_raw + fx_rin_off(wpc)) + warp * kNB * PF;
+    uint2* pub_s = reinterpret_cast<uint2*>(smem_raw + fx_pub_off(wpc)) + warp * PF;
+    const uint32_t mb_full = smem_addr(reinterpret_cast<uint64_t*>(smem_raw + fx_mbar_off(wpc)) + warp * 2 * kNB);
+    const uint32_t mb_empty = mb_full + kNB * 8u;
     for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
+    if (threadIdx.x < wpc * 2 * kNB)
+        mbar_init(smem_addr(reinterpret_cast<uint64_t*>(smem_raw + fx_mbar_off(wpc)) + threadIdx.x), 32);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     cluster_sync_all();
 
     const uint32_t my_consumed = smem_addr(consumed + warp);
@@ -160,9 +202,10 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
     wc.warp = g;
     bool ok = true;          // false once a wait of this lane failed
     bool quit = false;       // warp-uniform
-    bool bad = false;        // a valid exponent left its range
-    float pmax = 0.f;        // largest |D| * log2(e) / gamma of a live cell (NaN if one was NaN)
-    uint32_t cons_seen = 0;  // consumer progress last observed
+    bool bad = false;        // chain: a valid exponent left its range
+    float pmax = 0.f;        // helper: largest |D| * log2(e) / gamma of a live cell (NaN if one was NaN)
+    uint32_t cons_seen = 0;  // chain: consumer progress last observed
+    uint32_t seqg = 0;       // groups run so far (both roles count alike): buffer seqg % kNB
 
     for (int band = 0; band < P.n_bands && !quit; ++band) {
         const int s = band * P.G + g;
@@ -175,16 +218,7 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
         const bool out_wrap = (g == P.G - 1);
         const uint32_t band_base = static_cast<uint32_t>(band) * static_cast<uint32_t>(M);
         const size_t sb = stripe_base(P, b, s);
-        float2* Tl = a.score + sb + lane;  // this lane's position of anti-diagonal row 0
-        const float* Dl = a.Dw + sb;
         const uint64_t wrap_g = reinterpret_cast<uint64_t>(a.wrap + static_cast<size_t>(b) * 2 * M);
-        const uint64_t out_g = out_wrap ? wrap_g : next_ring_g;
-        const uint32_t in_tag_wrap = wrap_tag(a.seq, band - 1);
-        const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
-
-        // Everything before this band counts as consumed.
-        st_release_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed, band_base);
-
         const int n_steps = M + 31;
         const int n_groups = (n_steps + PF - 1) / PF;
         // Band-limited launch: only the groups whose anti-diagonals hold an
@@ -199,49 +233,82 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
             g_end = max(g_begin, min(n_groups, t_hi / PF + 1));
         }
         const int t_begin = g_begin * PF;
-        // Last column of the row above that is in the band (and so published
-        // by the stripe above); the columns past it read as P = 0.
-        const int c_pub_max = BANDED ? min(M - 1, R0 - 1 + ibw) : M - 1;
-        // Group gg's cost rows (PF * 32 contiguous floats), or an empty commit
-        // past the last group, so that every group finds its rows two commits back.
-        auto cost_copy = [&](int gg) {
-            if (gg < g_end) {
-                const float* src = Dl + static_cast<size_t>(gg) * PF * 32;
-                const uint32_t dst = cost_s + static_cast<uint32_t>((gg - g_begin) % 3) * PF * 32 * 4u;
-#pragma unroll
-                for (int i = 0; i < PF * 32 / 128; ++i) cp_async16(dst + (lane + 32 * i) * 16u, src + (lane + 32 * i) * 4);
-            }
-            cp_async_commit();
-        };
-        cost_copy(g_begin);
-        cost_copy(g_begin + 1);
-        if (t_begin > 0)
-            st_relaxed_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed,
-                                      band_base + static_cast<uint32_t>(min(t_begin, M)));
-
-        // Cell state: own previous cell (left neighbour of the next step) and
-        // the upper neighbour of the previous step (diagonal of the next).
-        float m_l = 1.f;
-        int e_l = kEneg;
-        float m_d = 1.f;
-        int e_d = (R0 == 0 && lane == 0) ? 0 : kEneg;  // R[0,0] = 0 above-left of cell (0, 0)
         const int rows_left = N - R0;
         const bool full_rows = rows_left >= 32;
-        const int l_last = N - 1 - R0;
-        const int t_last = (s == P.n_stripes - 1 && lane == l_last) ? l_last + M - 1 : -1;
-        float last_m = 1.f;
-        int last_e = kEneg;
-        // Band-wrap input (global memory, an L2 round trip per load): the slots
-        // of the next group are loaded one group ahead.
-        uint64_t wpf_h = 0, wpf_l = 0;
-        if (has_in && in_wrap && t_begin < M && t_begin + (lane & (PF - 1)) <= c_pub_max)
-            ld_pair(wrap_g + static_cast<uint32_t>(t_begin + (lane & (PF - 1))) * 16u, wpf_h, wpf_l);
+        auto interior_group = [&](int t0) { return !BANDED && full_rows && t0 >= 32 && t0 + PF <= M; };
 
-        auto group = [&](auto masked_c, int t0) {
-            constexpr bool MASKED = decltype(masked_c)::value;
-            // ---- ring input: the row above for columns t0 .. t0+PF-1, slot u
-            // read by lane u (mod PF), kept in shared memory for lane 0's steps.
-            {
+        if (helper) {
+            // ================================================ helper
+            const float* Dl = a.Dw + sb;
+            const uint32_t in_tag_wrap = wrap_tag(a.seq, band - 1);
+            // Last column of the row above that is in the band (published by
+            // the stripe above); the columns past it read as P = 0.
+            const int c_pub_max = BANDED ? min(M - 1, R0 - 1 + ibw) : M - 1;
+            // Everything before this band counts as consumed.
+            st_release_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed, band_base);
+            auto cost_copy = [&](int gg) {
+                if (gg < g_end) {
+                    const float* src = Dl + static_cast<size_t>(gg) * PF * 32;
+                    const uint32_t dst = cost_s + static_cast<uint32_t>((gg - g_begin) % 3) * PF * 32 * 4u;
+#pragma unroll
+                    for (int i = 0; i < PF * 32 / 128; ++i)
+                        cp_async16(dst + (lane + 32 * i) * 16u, src + (lane + 32 * i) * 4);
+                }
+                cp_async_commit();
+            };
+            cost_copy(g_begin);
+            cost_copy(g_begin + 1);
+            if (t_begin > 0)
+                st_relaxed_cluster_u32_if(has_in && !in_wrap && lane == 0, prev_consumed,
+                                          band_base + static_cast<uint32_t>(min(t_begin, M)));
+            // Band-wrap input (global memory, an L2 round trip per load): the
+            // slots of the next group are loaded one group ahead.
+            uint64_t wpf_h = 0, wpf_l = 0;
+            if (has_in && in_wrap && t_begin < M && t_begin + (lane & (PF - 1)) <= c_pub_max)
+                ld_pair(wrap_g + static_cast<uint32_t>(t_begin + (lane & (PF - 1))) * 16u, wpf_h, wpf_l);
+
+            for (int gi = g_begin; gi < g_end; ++gi, ++seqg) {
+                const int t0 = gi * PF;
+                const uint32_t slot = seqg % kNB, use = seqg / kNB;
+                // The chain warp has finished with this buffer's previous use.
+                if (use > 0 && ok) ok = mbar_wait_fx(mb_empty + slot * 8u, (use - 1) & 1u, wc);
+                // ---- K of the group's cells, from its cost rows (two commits back).
+                cp_async_wait<1>();
+                __syncwarp();
+                const float* cb = cost + ((gi - g_begin) % 3) * PF * 32 + lane;
+                uint2* kb = kbuf + slot * PF * 32 + lane;
+                const bool masked = !interior_group(t0);
+#pragma unroll
+                for (int u = 0; u < PF; ++u) {
+                    const float c = cb[u * 32];
+                    const float p = c * kk;
+                    const float r = __fadd_rd(-p, kMagic);
+                    const float fl = r - kMagic;
+                    const int ke = __float_as_int(r) - __float_as_int(kMagic);
+                    float km = ex2f(fmaf(-c, kk, -fl));
+                    int kx = ke;
+                    float pa = fabsf(p);
+                    if constexpr (!W) {
+                        // Caller-supplied costs may be +inf (a forbidden cell,
+                        // P = 0): handed over as exponent kEneg.
+                        const bool cinf = c == pos_inf();
+                        pa = cinf ? 0.f : pa;
+                        km = cinf ? 1.f : km;
+                        kx = cinf ? kEneg : kx;
+                    }
+                    if (masked) {
+                        const int col = t0 + u - lane;
+                        bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && lane < rows_left;
+                        if constexpr (BANDED)
+                            live = live && static_cast<unsigned>(R0 + lane - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                        pa = live ? pa : 0.f;
+                    }
+                    pmax = max_nan(pmax, pa);
+                    kb[u * 32] = make_uint2(__float_as_uint(km), static_cast<uint32_t>(kx));
+                }
+                cost_copy(gi + 2);  // into the buffer just read
+                // ---- ring input: the row above for columns t0 .. t0+PF-1, slot u
+                // read by lane u (mod PF).
                 uint32_t vm = __float_as_uint(1.f), ve = static_cast<uint32_t>(kEneg);
                 if (has_in && t0 < M && t0 <= c_pub_max) {  // warp-uniform
                     const int u = lane & (PF - 1);
@@ -290,8 +357,37 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                     st_relaxed_cluster_u32_if(!in_wrap && report_due(done, PF, M) && lane == 0, prev_consumed,
                                               band_base + static_cast<uint32_t>(done));
                 }
-                if (lane < PF) rin_s[lane] = make_uint2(vm, ve);
+                if (lane < PF) rin[slot * PF + lane] = make_uint2(vm, ve);
+                mbar_arrive(mb_full + slot * 8u);  // release: the K and ring rows above
+                if ((gi & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
+                    quit = true;
+                    ++seqg;
+                    break;
+                }
             }
+            cp_async_wait<0>();
+            __syncwarp();
+            if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
+            continue;
+        }
+
+        // ==================================================== chain warp
+        float2* Tl = a.score + sb + lane;  // this lane's position of anti-diagonal row 0
+        const uint64_t out_g = out_wrap ? wrap_g : next_ring_g;
+        const uint32_t out_tag_wrap = wrap_tag(a.seq, band);
+        // Cell state: own previous cell (left neighbour of the next step) and
+        // the upper neighbour of the previous step (diagonal of the next).
+        float m_l = 1.f;
+        int e_l = kEneg;
+        float m_d = 1.f;
+        int e_d = (R0 == 0 && lane == 0) ? 0 : kEneg;  // R[0,0] = 0 above-left of cell (0, 0)
+        const int l_last = N - 1 - R0;
+        const int t_last = (s == P.n_stripes - 1 && lane == l_last) ? l_last + M - 1 : -1;
+        float last_m = 1.f;
+        int last_e = kEneg;
+
+        auto group = [&](auto masked_c, int t0, uint32_t slot) {
+            constexpr bool MASKED = decltype(masked_c)::value;
             // ---- flow control for the columns this group publishes.
             if (has_out && !out_wrap) {  // warp-uniform
                 const int col_last = min(t0 + PF - 1 - 31, M - 1);
@@ -304,27 +400,15 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                     }
                 }
             }
-            // ---- PF steps.  This group's staging buffer was last read by the
-            // bulk copy of two groups ago; its cost rows (two commits back) have landed.
-            const int gg = t0 / PF;
-            const int sbuf = gg & (kFwdStages - 1);
-            if (lane == 0) bulk_wait_read<kFwdStages - 1>();
-            cp_async_wait<1>();
-            __syncwarp();
-            const float* cb = cost + ((gg - g_begin) % 3) * PF * 32 + lane;
-            cost_copy(gg + 2);  // into the buffer the previous group read
-            float2* Tg = stage + sbuf * PF * 32 + lane;
+            const uint2* kb = kbuf + slot * PF * 32 + lane;
+            const uint2* ri_s = rin + slot * PF;
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 + u;
-                // K = 2^(-c * kk) = km * 2^ke, off the dependent chain.
-                const float c = cb[u * 32];
-                const float p = c * kk;
-                const float r = __fadd_rd(-p, kMagic);
-                const float fl = r - kMagic;
-                const int ke = __float_as_int(r) - __float_as_int(kMagic);
-                const float km = ex2f(fmaf(-c, kk, -fl));
-                const uint2 ri = rin_s[u];
+                const uint2 kp = kb[u * 32];
+                const float km = __uint_as_float(kp.x);
+                const int ke = static_cast<int>(kp.y);
+                const uint2 ri = ri_s[u];
                 float mu = __shfl_up_sync(SDTW_FULL_MASK, m_l, 1);
                 int eu = __shfl_up_sync(SDTW_FULL_MASK, e_l, 1);
                 mu = (lane == 0) ? __uint_as_float(ri.x) : mu;
@@ -336,13 +420,11 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                 const float sum = (vl + vd) + vu;
                 float mn = sum;
                 int en = emax + ke;
-                float pa = fabsf(p);
                 if constexpr (!W) {
-                    // Caller-supplied costs may be +inf (a forbidden cell): P = 0.
-                    const bool cinf = c == pos_inf();
+                    // A cell of cost +inf (marked by the helper): P = 0.
+                    const bool cinf = ke == kEneg;
                     mn = cinf ? 1.f : mn;
                     en = cinf ? kEneg : en;
-                    pa = cinf ? 0.f : pa;
                 }
                 float2 rec;
                 if constexpr (W) {
@@ -362,13 +444,10 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                     mn = live ? mn : 1.f;
                     en = live ? en : kEneg;
                     rec = live ? rec : (W ? make_float2(0.f, 0.f) : make_float2(neg_inf(), 0.f));
-                    pmax = live ? max_nan(pmax, pa) : pmax;
                     last_m = (t == t_last) ? mn : last_m;
                     last_e = (t == t_last) ? en : last_e;
-                } else {
-                    pmax = max_nan(pmax, pa);
                 }
-                Tg[u * 32] = rec;
+                Tl[static_cast<size_t>(t) * 32] = rec;  // one coalesced row store per step
                 if (lane == 31) pub_s[u] = make_uint2(__float_as_uint(mn), static_cast<uint32_t>(en));
                 m_d = mu;
                 e_d = eu;
@@ -390,7 +469,6 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                 m_d = __int_as_float((bd & 0x007fffff) | 0x3f800000);
             }
             bad = bad || (e_l != kEneg && static_cast<unsigned>(e_l + kErange) > static_cast<unsigned>(2 * kErange));
-            fence_proxy_async_smem();
             __syncwarp();
             // ---- the stripe's bottom row for columns t0-31 .. t0-31+PF-1: lane u
             // stores column t0 - 31 + u (both halves tagged).
@@ -399,35 +477,29 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                 const bool pub = lane < PF && static_cast<unsigned>(colb) < static_cast<unsigned>(M);
                 const uint2 pv = pub_s[lane & (PF - 1)];
                 const uint32_t tgo = out_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(colb);
-                const uint32_t slot = out_wrap ? static_cast<uint32_t>(colb) : (tgo % kRing);
-                st_pair_if(pub, out_g + slot * 16u, pack_tagged_bits(pv.x, tgo), pack_tagged_bits(pv.y, tgo));
-            }
-            // Rows t0 .. t0 + PF - 1 of the table: one bulk copy.
-            if (lane == 0) {
-                bulk_s2g(Tl - lane + static_cast<size_t>(t0) * 32, stage_s + sbuf * PF * 32 * 8u, PF * 32 * 8u);
-                bulk_commit();
+                const uint32_t sl = out_wrap ? static_cast<uint32_t>(colb) : (tgo % kRing);
+                st_pair_if(pub, out_g + sl * 16u, pack_tagged_bits(pv.x, tgo), pack_tagged_bits(pv.y, tgo));
             }
         };
-        for (int gi = g_begin; gi < g_end; ++gi) {
+        for (int gi = g_begin; gi < g_end; ++gi, ++seqg) {
             const int t0 = gi * PF;
+            const uint32_t slot = seqg % kNB, use = seqg / kNB;
+            // The helper has filled this buffer (K and the row above).
+            if (ok) ok = mbar_wait_fx(mb_full + slot * 8u, use & 1u, wc);
             if constexpr (!BANDED) {
-                const bool interior = full_rows && t0 >= 32 && t0 + PF <= M;
-                if (interior) group(std::false_type{}, t0);
-                else group(std::true_type{}, t0);
+                if (interior_group(t0)) group(std::false_type{}, t0, slot);
+                else group(std::true_type{}, t0, slot);
             } else {
-                group(std::true_type{}, t0);
+                group(std::true_type{}, t0, slot);
             }
+            mbar_arrive(mb_empty + slot * 8u);
             if ((gi & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
+                ++seqg;
                 break;
             }
         }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
-        // The band's copies are complete before the fill stores below and the
-        // next band's first group (which reuses the staging and cost buffers).
-        if (lane == 0) bulk_wait_all();
-        cp_async_wait<0>();
-        __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band).
         const float2 fill = W ? make_float2(0.f, 0.f) : make_float2(neg_inf(), 0.f);
         for (int t = 0; t < t_begin; ++t) Tl[static_cast<size_t>(t) * 32] = fill;
@@ -444,11 +516,12 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
 
 // ------------------------------------------------------------------ reverse pass (weights)
 // Shared memory: rings [wpc][kRing] u64 and counters [wpc] u32, then (at the
-// forward's staging offset) per warp the E rows of kBwdPhases groups [ph][PF][32]
-// float, the weights of three groups [3][PF][32] float2 and the messages of
-// one group [PF] float.
+// forward's staging offset) per warp the weights of three groups [3][PF][32]
+// float2 and the messages of one group [PF] float.  E leaves by one coalesced
+// 128-byte row store per step (measured on B200 faster than staging a group's
+// rows in shared memory for one bulk copy: C2 reverse pass 0.131 -> 0.117 ms).
 __host__ __device__ constexpr size_t bw_w_off(int wpc) {
-    return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * kBwdPhases * kPF * 32 * 4;
+    return fwd_stage_offset(wpc);
 }
 __host__ __device__ constexpr size_t bw_stash_off(int wpc) {
     return bw_w_off(wpc) + static_cast<size_t>(wpc) * 3 * kPF * 32 * 8;
@@ -479,8 +552,6 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * kRing);
-    float* bstage = reinterpret_cast<float*>(smem_raw + fwd_stage_offset(wpc)) + warp * NPH * PF * 32;
-    const uint32_t bstage_s = smem_addr(bstage);
     const float2* wbuf = reinterpret_cast<const float2*>(smem_raw + bw_w_off(wpc)) + warp * 3 * PF * 32;
     const uint32_t wbuf_s = smem_addr(wbuf);
     float* pub_s = reinterpret_cast<float*>(smem_raw + bw_stash_off(wpc)) + warp * PF;
@@ -574,7 +645,7 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
         }
 
         auto group = [&](auto phase_c, auto masked_c, int t0) {
-            constexpr int PH = decltype(phase_c)::value;
+            (void)phase_c;  // two step bodies per loop iteration (compile-time unrolled)
             constexpr bool MASKED = decltype(masked_c)::value;
             // ---- messages for lane 31 (columns colb0 .. colb0-PF+1); lane u
             // (mod PF) holds column colb0 - u, handed to lane 31 at step u.
@@ -637,13 +708,11 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
                 }
             }
             // ---- PF reverse steps (step u fills staged row PF - 1 - u, i.e. t0 - u).
-            if (lane == 0) bulk_wait_read<NPH - 1>();
             cp_async_wait<1>();  // this group's shares, committed two groups back
             __syncwarp();
             const int gi = (t_last - t0) / PF;
             const float2* wb = wbuf + ((gi - gi_begin) % 3) * PF * 32 + (PF - 1) * 32 + lane;
             wcopy(gi + 2);  // into the buffer the previous group read
-            float* Eg = bstage + PH * PF * 32 + (PF - 1) * 32 + lane;
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
                 const int t = t0 - u;
@@ -660,7 +729,7 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
                     e = (lane == rows_left - 1 && col == M - 1) ? gb : e;
                     e = live ? e : 0.f;
                 }
-                Eg[-u * 32] = e;
+                El[static_cast<size_t>(t) * 32] = e;  // one coalesced row store per step
                 const float dn = e * w.x;            // to the diagonal predecessor (two steps on)
                 msg = fmaf(e, w.y, dprev);           // to the row above: upper share + previous diagonal
                 accl = fmaf(-e, w.y, e - dn);        // left share: e * (1 - wd - wu)
@@ -677,13 +746,7 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
                 const uint32_t slot = up_wrap ? static_cast<uint32_t>(col) * 2u : (tgo % kRing);
                 st_one_if(pub, out_g + slot * 8u, pack_tagged(pv, tgo));
             }
-            // Rows t0 - PF + 1 .. t0 of E: one bulk copy.
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                bulk_s2g(El - lane + static_cast<size_t>(t0 - PF + 1) * 32, bstage_s + PH * PF * 32 * 4u, PF * 32 * 4u);
-                bulk_commit();
-            }
+
         };
         using P0 = std::integral_constant<int, 0>;
         using P1 = std::integral_constant<int, 1>;
@@ -705,9 +768,7 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
                 break;
             }
         }
-        // The band's copies are complete before the zero fill below and the
-        // next band's first group.
-        if (lane == 0) bulk_wait_all();
+        // The band's copies are complete before the next band's first group.
         cp_async_wait<0>();
         __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band): zero.
@@ -720,6 +781,7 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
 
 // ------------------------------------------------------------------ launchers
 size_t fwdx_smem(const WavePlan& P) { return fx_smem_bytes(P.wpc); }
+int fwdx_threads(const WavePlan& P) { return 2 * P.wpc * 32; }  // a chain warp and its helper per stripe
 size_t bwdw_smem(const WavePlan& P) { return bw_smem_bytes(P.wpc); }
 
 const void* fwdx_fn(bool banded, bool weights) {
@@ -732,10 +794,10 @@ const void* bwdw_fn(bool banded) {
 
 cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
-    if (P.K != 1) return cudaErrorInvalidValue;
+    if (P.K != 1 || P.wpc > 8) return cudaErrorInvalidValue;
     const bool banded = args.ibw < P.N + P.M;
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
-    return launch_cluster(fwdx_fn(banded, args.weights != 0), dim3(P.B * P.csize), dim3(P.wpc * 32), fwdx_smem(P),
+    return launch_cluster(fwdx_fn(banded, args.weights != 0), dim3(P.B * P.csize), dim3(fwdx_threads(P)), fwdx_smem(P),
                           P.csize, stream, kargs);
 }
 
