@@ -211,18 +211,18 @@ int int_band(float bw) {
 
 // Resident clusters per geometry, cached per device (the occupancy query is a
 // host call; the plan is computed at every launch).
-int cached_cluster_fit(const WavePlan& p) {
+int cached_cluster_fit(const WavePlan& p, int pass) {
     static std::mutex mu;
     static std::map<std::tuple<int, int, int, int>, int> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return -1;
-    const auto key = std::make_tuple(dev, p.K, p.wpc, p.csize);
+    const auto key = std::make_tuple(dev * 4 + pass, p.K, p.wpc, p.csize);
     {
         std::lock_guard<std::mutex> lk(mu);
         auto it = cache.find(key);
         if (it != cache.end()) return it->second;
     }
-    const int n = max_active_clusters(p);
+    const int n = max_active_clusters(p, pass);
     std::lock_guard<std::mutex> lk(mu);
     cache[key] = n;
     return n;
@@ -252,25 +252,27 @@ double plan_cost(const WavePlan& q, int B, int M, int fit, int sms) {
     return waves * steps * step;
 }
 
-// Launch geometry.  make_plan's choice unless its clusters do not all fit on
+// Launch geometry of a pass (0 forward, 1 reverse; each pass has its own
+// kernels and occupancy, and the table layout depends only on the rows per
+// lane, which both passes share).  make_plan's choice unless its clusters do not all fit on
 // the GPU at once (a second wave would double the time): then the candidate
 // with fewer waves, then fewer bands.  With one row per lane, the geometry of
 // plan_cost's minimum replaces that choice when it is estimated at least 15 %
 // faster.
-WavePlan plan(int B, int N, int M) {
+WavePlan plan(int B, int N, int M, int pass) {
     const int wo = g_wpc_override.load(), co = g_cs_override.load(), ko = g_k_override.load();
     const int sms = num_sms();
     const WavePlan p = make_plan(B, N, M, sms, wo, co, ko);
     if (wo > 0 || co > 0) return p;
     WavePlan base = p;
-    const int fit = cached_cluster_fit(p);
+    const int fit = cached_cluster_fit(p, pass);
     if (fit > 0 && B > fit) {
         auto waves = [&](int f) { return f > 0 ? (B + f - 1) / f : 1 << 30; };
         int best_w = waves(fit);
         for (int cs = 8; cs >= 1; cs /= 2) {
             if (cs == p.csize) continue;
             const WavePlan q = make_plan(B, N, M, sms, 0, cs, ko);
-            const int w = waves(cached_cluster_fit(q));
+            const int w = waves(cached_cluster_fit(q, pass));
             if (w < best_w || (w == best_w && q.n_bands < base.n_bands)) {
                 base = q;
                 best_w = w;
@@ -278,7 +280,7 @@ WavePlan plan(int B, int N, int M) {
         }
     }
     if (p.K != 1) return base;
-    const double base_c = plan_cost(base, B, M, cached_cluster_fit(base), sms);
+    const double base_c = plan_cost(base, B, M, cached_cluster_fit(base, pass), sms);
     WavePlan best = base;
     double best_c = base_c;
     for (int cs = 1; cs <= 8; cs *= 2)
@@ -286,7 +288,7 @@ WavePlan plan(int B, int N, int M) {
             const WavePlan q = make_plan(B, N, M, sms, wpc, cs, ko);
             if (q.wpc != wpc || q.csize != cs) continue;
             if ((wpc / 2) * cs >= q.n_stripes) continue;  // half the warps would still hold every stripe
-            const double c = plan_cost(q, B, M, cached_cluster_fit(q), sms);
+            const double c = plan_cost(q, B, M, cached_cluster_fit(q, pass), sms);
             if (c < best_c) {
                 best = q;
                 best_c = c;
@@ -305,8 +307,7 @@ WavePlan plan(int B, int N, int M) {
 //     grad_rm (otherwise): G, G^T, x^T, y^T row-major, rows padded to a
 //     multiple of 32 floats
 size_t wave_ws(int B, int N, int M) {
-    WavePlan p = plan(B, N, M);
-    return align_up(wrap_bytes(p), 256);
+    return align_up(std::max(wrap_bytes(plan(B, N, M, 0)), wrap_bytes(plan(B, N, M, 1))), 256);
 }
 size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
 size_t pad32(int n) { return (static_cast<size_t>(n) + 31) & ~static_cast<size_t>(31); }
@@ -323,7 +324,7 @@ struct GradOperands {
 GradOperands grad_operands(int B, int N, int M, int dim) {
     GradOperands o;
     const size_t b = static_cast<size_t>(B);
-    const WavePlan p = plan(B, N, M);
+    const WavePlan p = plan(B, N, M, 0);
     if (grad_small_supported(p, dim)) {  // per-split column sums of grad_small
         o.g = o.gt = o.xt = o.yt = 0;
         o.total = align_up(grad_small_part_bytes(p, dim), 256);
@@ -346,12 +347,12 @@ GradOperands grad_operands(int B, int N, int M, int dim) {
 
 // weights: the table keeps each cell's predecessor weights (the state of the
 // x/y pairs' backward, one row per lane) instead of its score.
-bool weight_store(int B, int N, int M) { return plan(B, N, M).K == 1; }
+bool weight_store(int B, int N, int M) { return plan(B, N, M, 0).K == 1; }
 
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr) {
     FwdArgs a{};
-    a.P = plan(B, N, M);
+    a.P = plan(B, N, M, 0);
     a.weights = weights ? 1 : 0;
     a.Dw = Dw;
     a.score = reinterpret_cast<float2*>(score);
@@ -377,7 +378,7 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
 int run_backward(const float* score, const float* grad_out, float* Ew, int B, int N, int M, float bw,
                  uint64_t* wrap, cudaStream_t stream, bool weights = false) {
     BwdArgs a{};
-    a.P = plan(B, N, M);
+    a.P = plan(B, N, M, 1);
     a.weights = weights ? 1 : 0;
     a.score = reinterpret_cast<const float2*>(score);
     a.grad_out = grad_out;
@@ -567,13 +568,13 @@ int sdtw_plan_info(int B, int N, int M, int* info) {
     if (!info) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     int rc = check_dims(B, N, M);
     if (rc) return rc;
-    const WavePlan p = plan(B, N, M);
+    const WavePlan p = plan(B, N, M, 0);
     info[0] = p.K;
     info[1] = p.wpc;
     info[2] = p.csize;
     info[3] = p.n_bands;
     info[4] = p.n_stripes;
-    info[5] = cached_cluster_fit(p);
+    info[5] = cached_cluster_fit(p, 0);
     return SDTW_OK;
 }
 
@@ -673,7 +674,7 @@ int sdtw_forward_f32(const float* D, float* score, float* out, int B, int N, int
     if ((rc = check_ws(workspace, workspace_bytes, w0 + wl_bytes(B, N, M)))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* Dw = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
-    const WavePlan p = plan(B, N, M);
+    const WavePlan p = plan(B, N, M, 0);
     cudaError_t e;
     {
         KernelTimer kt("rm_to_wl", st);
@@ -697,7 +698,7 @@ int sdtw_backward_f32(const float* score, const float* grad_out, float* E, int B
     cudaError_t e;
     {
         KernelTimer kt("wl_to_rm", st);
-        e = launch_wl_to_rm(Ew, nullptr, E, plan(B, N, M), st);
+        e = launch_wl_to_rm(Ew, nullptr, E, plan(B, N, M, 0), st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "layout launch");
     return SDTW_OK;
@@ -716,7 +717,7 @@ int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out
     cudaError_t e;
     {
         KernelTimer kt("cost_wl", st);
-        e = launch_cost_wl(x, y, Dw, plan(B, N, M), dim, true, st);
+        e = launch_cost_wl(x, y, Dw, plan(B, N, M, 0), dim, true, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
     return run_forward(Dw, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st,
@@ -735,7 +736,7 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     if (rc) return rc;
     if (!grad_x && !grad_y) return SDTW_OK;
     GradTcArgs g{};
-    g.P = plan(B, N, M);
+    g.P = plan(B, N, M, 0);
     g.Ew = Ew;
     g.Mw = mask_w;
     g.x = x;
@@ -829,10 +830,10 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
     cudaError_t e;
     if (cost_tc_supported(x, y, dim)) {
         KernelTimer kt("cost_tc", st);
-        e = launch_cost_tc(x, y, cost, plan(B, N, M), dim, wait_ctx(), st);
+        e = launch_cost_tc(x, y, cost, plan(B, N, M, 0), dim, wait_ctx(), st);
     } else {
         KernelTimer kt("cost_wl", st);
-        e = launch_cost_wl(x, y, cost, plan(B, N, M), dim, false, st);
+        e = launch_cost_wl(x, y, cost, plan(B, N, M, 0), dim, false, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
     return run_forward(cost, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st,
@@ -872,7 +873,7 @@ int sdtw_score_to_R_f32(const float* score, float* R, int B, int N, int M, float
     if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     // The forward writes it with bulk copies of whole anti-diagonal rows.
     if (reinterpret_cast<uintptr_t>(score) % 16u) return fail(SDTW_ERR_INVALID_ARGUMENT, "score must be 16-byte aligned");
-    WavePlan p = plan(B, N, M);
+    WavePlan p = plan(B, N, M, 0);
     const float kk = kLog2e / gamma;
     cudaError_t e = launch_score_to_R(reinterpret_cast<const float2*>(score), R, p, static_cast<float>(1.0 / (double)kk),
                                       static_cast<cudaStream_t>(stream));
@@ -884,7 +885,7 @@ int sdtw_R_to_score_f32(const float* R, float* score, int B, int N, int M, float
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
     if (!score || !R) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    WavePlan p = plan(B, N, M);
+    WavePlan p = plan(B, N, M, 0);
     cudaError_t e = launch_R_to_score(R, reinterpret_cast<float2*>(score), p, kLog2e / gamma, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "R_to_score launch");
     return SDTW_OK;
@@ -923,7 +924,7 @@ int sdtw_forward_noalloc_f32(const float* D, float* score, float* out, int B, in
     cudaError_t e;
     {
         KernelTimer kt("rm_to_wl", st);
-        e = launch_rm_to_wl(D, Dw, plan(B, N, M), st);
+        e = launch_rm_to_wl(D, Dw, plan(B, N, M, 0), st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "layout launch");
     WaitCtx w = wait_ctx();

@@ -54,7 +54,7 @@ int fwdx_threads(const WavePlan& P);
 size_t bwdw_smem(const WavePlan& P);
 const void* fwdx_fn(bool banded, bool weights);
 const void* bwdw_fn(bool banded);
-int max_active_clusters(const WavePlan& P);
+int max_active_clusters(const WavePlan& P, int pass);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
 cudaError_t launch_R_to_score(const float* R, float2* S, const WavePlan& P, float kk, cudaStream_t stream);

@@ -918,10 +918,11 @@ static size_t fwd_smem_bytes(const WavePlan& P) {
 }
 
 // Clusters of this geometry that can be resident at once on the current
-// device (the smaller of the forward's and the backward's figure), or -1 if
-// the runtime cannot tell.  Clusters are placed within one GPC, so on B200 the
-// figure can be below (SMs / cluster size).
-int max_active_clusters(const WavePlan& P) {
+// device for a pass (0: the forward kernels, 1: the reverse passes; the
+// smaller figure of the pass's variants), or -1 if the runtime cannot tell.
+// Clusters are placed within one GPC, so on B200 the figure can be below
+// (SMs / cluster size).
+int max_active_clusters(const WavePlan& P, int pass) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(P.csize);
     cfg.blockDim = dim3(P.wpc * 32);
@@ -939,28 +940,27 @@ int max_active_clusters(const WavePlan& P) {
     int threads[4] = {P.wpc * 32, P.wpc * 32, P.wpc * 32, P.wpc * 32};
     switch (P.K) {
         case 1:
-            fns[0] = fwdx_fn(false, false);
-            smem[0] = fwdx_smem(P);
-            threads[0] = fwdx_threads(P);
-            fns[1] = (const void*)bwd_kernel<1, false, false>;
-            smem[1] = bwd_smem_bytes(P, false);
-            fns[2] = fwdx_fn(false, true);
-            smem[2] = fwdx_smem(P);
-            threads[2] = fwdx_threads(P);
-            fns[3] = bwdw_fn(false);
-            smem[3] = bwdw_smem(P);
+            if (pass == 0) {
+                fns[0] = fwdx_fn(false, false);
+                smem[0] = fwdx_smem(P);
+                threads[0] = fwdx_threads(P);
+                fns[2] = fwdx_fn(false, true);
+                smem[2] = fwdx_smem(P);
+                threads[2] = fwdx_threads(P);
+            } else {
+                fns[1] = (const void*)bwd_kernel<1, false, false>;
+                smem[1] = bwd_smem_bytes(P, false);
+                fns[3] = bwdw_fn(false);
+                smem[3] = bwdw_smem(P);
+            }
             break;
         case 2:
-            fns[0] = (const void*)fwd_kernel<2, false, false>;
-            smem[0] = fwd_smem_bytes(P);
-            fns[1] = (const void*)bwd_kernel<2, false, false>;
-            smem[1] = bwd_smem_bytes(P, false);
+            fns[pass] = pass == 0 ? (const void*)fwd_kernel<2, false, false> : (const void*)bwd_kernel<2, false, false>;
+            smem[pass] = pass == 0 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
             break;
         case 4:
-            fns[0] = (const void*)fwd_kernel<4, false, false>;
-            smem[0] = fwd_smem_bytes(P);
-            fns[1] = (const void*)bwd_kernel<4, false, false>;
-            smem[1] = bwd_smem_bytes(P, false);
+            fns[pass] = pass == 0 ? (const void*)fwd_kernel<4, false, false> : (const void*)bwd_kernel<4, false, false>;
+            smem[pass] = pass == 0 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
             break;
         default: return -1;
     }

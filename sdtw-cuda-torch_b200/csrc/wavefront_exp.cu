@@ -157,7 +157,7 @@ __device__ __forceinline__ bool mbar_wait_fx(uint32_t mbar, uint32_t parity, con
 }
 
 template <bool BANDED, bool W>
-__global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
+__global__ void __launch_bounds__(512, 2) fwdx_kernel(const FwdArgs a) {
     constexpr int PF = kPF;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
@@ -278,9 +278,15 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                 const float* cb = cost + ((gi - g_begin) % 3) * PF * 32 + lane;
                 uint2* kb = kbuf + slot * PF * 32 + lane;
                 const bool masked = !interior_group(t0);
+                // All loads before the first store: the compiler cannot tell the
+                // cost rows from the K buffer apart, and a load placed after a
+                // store would serialise the cells.
+                float cv[PF];
+#pragma unroll
+                for (int u = 0; u < PF; ++u) cv[u] = cb[u * 32];
 #pragma unroll
                 for (int u = 0; u < PF; ++u) {
-                    const float c = cb[u * 32];
+                    const float c = cv[u];
                     const float p = c * kk;
                     const float r = __fadd_rd(-p, kMagic);
                     const float fl = r - kMagic;
@@ -400,15 +406,27 @@ __global__ void __launch_bounds__(512) fwdx_kernel(const FwdArgs a) {
                     }
                 }
             }
+            // The group's K and ring input in registers before the stores of the
+            // steps that use them (a shared load placed after a store would
+            // wait for it).
             const uint2* kb = kbuf + slot * PF * 32 + lane;
             const uint2* ri_s = rin + slot * PF;
+            // Half a group at a time keeps the registers of two CTAs per SM.
+            constexpr int PH = PF / 2;
+            uint2 kq[PH], rq[PH];
 #pragma unroll
             for (int u = 0; u < PF; ++u) {
+                if (u % PH == 0) {
+#pragma unroll
+                    for (int v = 0; v < PH; ++v) {
+                        kq[v] = kb[(u + v) * 32];
+                        rq[v] = ri_s[u + v];
+                    }
+                }
                 const int t = t0 + u;
-                const uint2 kp = kb[u * 32];
-                const float km = __uint_as_float(kp.x);
-                const int ke = static_cast<int>(kp.y);
-                const uint2 ri = ri_s[u];
+                const float km = __uint_as_float(kq[u % PH].x);
+                const int ke = static_cast<int>(kq[u % PH].y);
+                const uint2 ri = rq[u % PH];
                 float mu = __shfl_up_sync(SDTW_FULL_MASK, m_l, 1);
                 int eu = __shfl_up_sync(SDTW_FULL_MASK, e_l, 1);
                 mu = (lane == 0) ? __uint_as_float(ri.x) : mu;
