@@ -216,7 +216,7 @@ int cached_cluster_fit(const WavePlan& p, int pass) {
     static std::map<std::tuple<int, int, int, int>, int> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return -1;
-    const auto key = std::make_tuple(dev * 4 + pass, p.K, p.wpc, p.csize);
+    const auto key = std::make_tuple(dev * 128 + pass, p.K, p.wpc, p.csize);
     {
         std::lock_guard<std::mutex> lk(mu);
         auto it = cache.find(key);
@@ -306,8 +306,20 @@ WavePlan plan(int B, int N, int M, int pass) {
 //     transposed layout (B, ceil(N/32), dim, 36) and (B, ceil(M/32), dim, 36);
 //     grad_rm (otherwise): G, G^T, x^T, y^T row-major, rows padded to a
 //     multiple of 32 floats
+// The band-wrap ring (needed when a pass's plan has more than one band; its
+// size does not depend on the plan) of the D-input passes, and of the x/y
+// passes (whose forward may compute its costs from x and y: plan 2 + dp).
 size_t wave_ws(int B, int N, int M) {
     return align_up(std::max(wrap_bytes(plan(B, N, M, 0)), wrap_bytes(plan(B, N, M, 1))), 256);
+}
+size_t wave_ws_xy(int B, int N, int M, int dim) {
+    size_t w = std::max(wrap_bytes(plan(B, N, M, 0)), wrap_bytes(plan(B, N, M, 1)));
+    if (rows_per_lane(N, g_k_override.load()) == 1 && (dim < 4 || (dim <= 16 && dim % 4 == 0))) {
+        int dp = 4;  // as fused_dp (alignment aside)
+        while (dp < dim) dp *= 2;
+        w = std::max(w, wrap_bytes(plan(B, N, M, 2 + dp)));
+    }
+    return align_up(w, 256);
 }
 size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
 size_t pad32(int n) { return (static_cast<size_t>(n) + 31) & ~static_cast<size_t>(31); }
@@ -349,10 +361,16 @@ GradOperands grad_operands(int B, int N, int M, int dim) {
 // x/y pairs' backward, one row per lane) instead of its score.
 bool weight_store(int B, int N, int M) { return plan(B, N, M, 0).K == 1; }
 
+// Dw: the cost table, or null with x, y, dim, dp (> 0) for the fused costs.
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
-                uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr) {
+                uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr,
+                const float* x = nullptr, const float* y = nullptr, int dim = 0, int dp = 0) {
     FwdArgs a{};
-    a.P = plan(B, N, M, 0);
+    a.P = plan(B, N, M, dp ? 2 + dp : 0);
+    a.x = x;
+    a.y = y;
+    a.dim = dim;
+    a.dp = dp;
     a.weights = weights ? 1 : 0;
     a.Dw = Dw;
     a.score = reinterpret_cast<float2*>(score);
@@ -595,7 +613,7 @@ size_t sdtw_workspace_bytes(int B, int N, int M) {
 
 size_t sdtw_workspace_bytes_xy(int B, int N, int M, int dim) {
     if (B <= 0 || N <= 0 || M <= 0 || dim <= 0) return 0;
-    return wave_ws(B, N, M) + wl_bytes(B, N, M) + grad_operands(B, N, M, dim).total;
+    return wave_ws_xy(B, N, M, dim) + wl_bytes(B, N, M) + grad_operands(B, N, M, dim).total;
 }
 
 static int check_f64(int B, int N, int M, double gamma) {
@@ -710,9 +728,15 @@ int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out
     if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
-    const size_t w0 = wave_ws(B, N, M);
+    const size_t w0 = wave_ws_xy(B, N, M, dim);
     if ((rc = check_ws(workspace, workspace_bytes, w0 + wl_bytes(B, N, M)))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Up to 16 features: the costs are computed inside the forward from x and
+    // y (no cost table); more features: a cost table first (see fused_dp).
+    const int dp = weight_store(B, N, M) ? fused_dp(dim, x, y) : 0;
+    if (dp)
+        return run_forward(nullptr, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st, true,
+                           nullptr, x, y, dim, dp);
     float* Dw = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
     cudaError_t e;
     {
@@ -729,7 +753,7 @@ int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out
 int backward_xy_common(const float* x, const float* y, const float* score, const float* mask_w, const float* grad_out,
                        float* grad_x, float* grad_y, int B, int N, int M, int dim, float bandwidth, void* workspace,
                        cudaStream_t st) {
-    const size_t w0 = wave_ws(B, N, M);
+    const size_t w0 = wave_ws_xy(B, N, M, dim);
     float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
     int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st,
                           weight_store(B, N, M));

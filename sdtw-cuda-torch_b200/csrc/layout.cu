@@ -26,23 +26,6 @@ namespace sdtw {
 
 constexpr int kTB = 32;   // anti-diagonals per tile
 
-// Packed float32 pairs (sm_100 f32x2 arithmetic): a 64-bit register holds two
-// floats, low half first.
-__device__ __forceinline__ unsigned long long sub_f32x2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
-                                                        unsigned long long c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ float lo_f32x2(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
-__device__ __forceinline__ float hi_f32x2(unsigned long long v) {
-    return __uint_as_float(static_cast<uint32_t>(v >> 32));
-}
 
 __device__ __forceinline__ size_t wl_row_base(const WavePlan& P, int b, int s, int t) {
     return ((static_cast<size_t>(b) * P.n_stripes + s) * P.n_diag + t) * (32 * P.K);

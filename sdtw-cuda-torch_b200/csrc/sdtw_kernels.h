@@ -26,6 +26,12 @@ struct FwdArgs {
     uint32_t seq;     // launch sequence number (tags of the global ring)
     int debug_stall;  // stripe whose output is withheld (failure-detection tests); -1 = none
     int weights;      // nonzero: store each cell's predecessor weights instead of its score (one row per lane)
+    // Fused costs (wavefront_exp.cu, dp > 0): sum_k (x_ik - y_jk)^2 computed in
+    // the kernel from x (B,N,dim) and y (B,M,dim); Dw is then unused.
+    const float* x;
+    const float* y;
+    int dim;
+    int dp;           // 0: costs from Dw; else the feature padding (fused_dp)
     WaitCtx wait;
 };
 
@@ -49,11 +55,13 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
 // K = 1 to them.
 cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream);
-size_t fwdx_smem(const WavePlan& P);
+size_t fwdx_smem(const WavePlan& P, int dp);
 int fwdx_threads(const WavePlan& P);
+int fused_dp(int dim, const float* x, const float* y);
 size_t bwdw_smem(const WavePlan& P);
-const void* fwdx_fn(bool banded, bool weights);
+const void* fwdx_fn(bool banded, bool weights, int dp);
 const void* bwdw_fn(bool banded);
+// pass: 0 forward with costs from a table, 1 reverse pass, 2 + dp the fused forward.
 int max_active_clusters(const WavePlan& P, int pass);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);

@@ -440,19 +440,11 @@ constexpr int kWlSplitWarps = 16;
 constexpr uint32_t kBPitch = 144;  // bytes per row of the chunked transposed x, y
 constexpr int kYRows = 159;        // anti-diagonal rows of one grad_y chunk
 
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(mbar)
-                 : "memory");
-}
 __device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
         : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
 }
 // try_wait that lets the hardware suspend the thread (up to about 1 us) until
 // the phase completes, so that waiting warps do not take issue slots.

@@ -941,12 +941,16 @@ int max_active_clusters(const WavePlan& P, int pass) {
     switch (P.K) {
         case 1:
             if (pass == 0) {
-                fns[0] = fwdx_fn(false, false);
-                smem[0] = fwdx_smem(P);
+                fns[0] = fwdx_fn(false, false, 0);
+                smem[0] = fwdx_smem(P, 0);
                 threads[0] = fwdx_threads(P);
-                fns[2] = fwdx_fn(false, true);
-                smem[2] = fwdx_smem(P);
+                fns[2] = fwdx_fn(false, true, 0);
+                smem[2] = fwdx_smem(P, 0);
                 threads[2] = fwdx_threads(P);
+            } else if (pass >= 2) {
+                fns[0] = fwdx_fn(false, true, pass - 2);
+                smem[0] = fwdx_smem(P, pass - 2);
+                threads[0] = fwdx_threads(P);
             } else {
                 fns[1] = (const void*)bwd_kernel<1, false, false>;
                 smem[1] = bwd_smem_bytes(P, false);
@@ -955,12 +959,12 @@ int max_active_clusters(const WavePlan& P, int pass) {
             }
             break;
         case 2:
-            fns[pass] = pass == 0 ? (const void*)fwd_kernel<2, false, false> : (const void*)bwd_kernel<2, false, false>;
-            smem[pass] = pass == 0 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
+            fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<2, false, false> : (const void*)bwd_kernel<2, false, false>;
+            smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
             break;
         case 4:
-            fns[pass] = pass == 0 ? (const void*)fwd_kernel<4, false, false> : (const void*)bwd_kernel<4, false, false>;
-            smem[pass] = pass == 0 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
+            fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<4, false, false> : (const void*)bwd_kernel<4, false, false>;
+            smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
             break;
         default: return -1;
     }
