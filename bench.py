@@ -20,6 +20,9 @@ value distributions):
        iteration over the whole set, cells = 4096*100*100.  The set is sharded
        over the ranks (strong scaling, one NCCL all-reduce per step); the other
        workloads run B problems per rank (weak scaling, no collective).
+The default run (c2) also times c3 and c5 and reports them under "workloads"
+(their own ms per step, kernel breakdown, MUFU fraction and latency floor; the
+all-reduce time per step for c5).
 Metric: DP cells per second summed over all GPUs.  `--impl reference` times the
 reference's CPU algorithm (the oracle restatement in oracle/, all host
 threads) on a bounded sample of the same workload.
@@ -288,223 +291,253 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    name = args.workload
-    B, N, M, Dm, gamma, normalize, head_mode, other_modes, desc = WORKLOADS[name]
-    if args.only_mode:
-        if args.only_mode not in (head_mode,) + tuple(other_modes):
-            raise SystemExit(f"workload {name} has no mode {args.only_mode}")
-        head_mode, other_modes = args.only_mode, ()
-    is_bary = name == "c5"
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
-    stream = torch.cuda.current_stream(dev)
+    def run_one(name, steps, warmup, fused_only, only_mode, sampler):
+        """Times one workload; returns its measurements (all ranks)."""
+        args_steps, args_warmup = steps, warmup
+        B, N, M, Dm, gamma, normalize, head_mode, other_modes, desc = WORKLOADS[name]
+        if only_mode:
+            if only_mode not in (head_mode,) + tuple(other_modes):
+                raise SystemExit(f"workload {name} has no mode {only_mode}")
+            head_mode, other_modes = only_mode, ()
+        is_bary = name == "c5"
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+        stream = torch.cuda.current_stream(dev)
 
-    if is_bary:
-        Xn, _ = make_data(name, B, N, M, Dm, seed=1234)
-        lo, hi = shard_bounds(B, rank, world)
-        X_h = torch.from_numpy(Xn[lo:hi]).pin_memory()
-        X_d = X_h.to(dev)
-        cells = B * N * N  # whole job per iteration
-        my_cells = (hi - lo) * N * N
-    else:
-        xn, yn = make_data(name, B, N, M, Dm, seed=1234 + rank)
-        x_h = torch.from_numpy(xn).pin_memory()
-        y_h = torch.from_numpy(yn).pin_memory()
-        x = x_h.to(dev)
-        y = y_h.to(dev)
-        cells = world * cells_of(name)
-        my_cells = cells_of(name)
+        if is_bary:
+            Xn, _ = make_data(name, B, N, M, Dm, seed=1234)
+            lo, hi = shard_bounds(B, rank, world)
+            X_h = torch.from_numpy(Xn[lo:hi]).pin_memory()
+            X_d = X_h.to(dev)
+            cells = B * N * N  # whole job per iteration
+            my_cells = (hi - lo) * N * N
+        else:
+            xn, yn = make_data(name, B, N, M, Dm, seed=1234 + rank)
+            x_h = torch.from_numpy(xn).pin_memory()
+            y_h = torch.from_numpy(yn).pin_memory()
+            x = x_h.to(dev)
+            y = y_h.to(dev)
+            cells = world * cells_of(name)
+            my_cells = cells_of(name)
 
-    def step(mode):
-        xr = x.detach().requires_grad_(True)
-        yr = y.detach().requires_grad_(True)
-        out = SoftDTW(gamma=gamma, normalize=normalize, fused=(None if mode == "fused" else False))(xr, yr)
-        out.mean().backward()
-        return xr.grad, yr.grad
+        def step(mode):
+            xr = x.detach().requires_grad_(True)
+            yr = y.detach().requires_grad_(True)
+            out = SoftDTW(gamma=gamma, normalize=normalize, fused=(None if mode == "fused" else False))(xr, yr)
+            out.mean().backward()
+            return xr.grad, yr.grad
 
-    def timed(fn, k):
-        times = []
-        for _ in range(k):
-            flush.zero_()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            fn()
-            e1.record(stream)
-            times.append((e0, e1))
-        torch.cuda.synchronize(dev)
-        return [a.elapsed_time(b) for a, b in times]
-
-    sampler = ClockSampler(local)
-    modes = {}
-    launches = 0
-    breakdown = {}
-    per_launch = {}
-    all_modes = (head_mode,) + (() if args.fused_only else tuple(other_modes))
-    with sampler:
-        for mode in all_modes:
-            allreduce_ms = None
-            if is_bary:
-                # One call of K iterations (the optimiser state carries over),
-                # timed as a whole; the per-step figure is the average.
-                sharded_barycenter(X_d, gamma=gamma, max_iter=args.warmup, lr=0.1, early_stopping=False)
-                torch.cuda.synchronize(dev)
-                barrier()
-                torch.cuda.synchronize(dev)
-                l0 = _native.launches()
-                _native.timing_enable(True)
-                stats = {}
+        def timed(fn, k):
+            times = []
+            for _ in range(k):
                 flush.zero_()
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                sharded_barycenter(X_d, gamma=gamma, max_iter=args.steps, lr=0.1, early_stopping=False, stats=stats)
+                fn()
+                e1.record(stream)
+                times.append((e0, e1))
+            torch.cuda.synchronize(dev)
+            return [a.elapsed_time(b) for a, b in times]
+
+        sampler = ClockSampler(local)
+        modes = {}
+        launches = 0
+        breakdown = {}
+        per_launch = {}
+        all_modes = (head_mode,) + (() if fused_only else tuple(other_modes))
+        with sampler:
+            for mode in all_modes:
+                allreduce_ms = None
+                if is_bary:
+                    # One call of K iterations (the optimiser state carries over),
+                    # timed as a whole; the per-step figure is the average.
+                    sharded_barycenter(X_d, gamma=gamma, max_iter=args_warmup, lr=0.1, early_stopping=False)
+                    torch.cuda.synchronize(dev)
+                    barrier()
+                    torch.cuda.synchronize(dev)
+                    l0 = _native.launches()
+                    _native.timing_enable(True)
+                    stats = {}
+                    flush.zero_()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    sharded_barycenter(X_d, gamma=gamma, max_iter=args_steps, lr=0.1, early_stopping=False, stats=stats)
+                    e1.record(stream)
+                    torch.cuda.synchronize(dev)
+                    ms = [e0.elapsed_time(e1) / args_steps] * args_steps
+                    n_launch = _native.launches() - l0
+                    kt = _native.timing_read()
+                    _native.timing_enable(False)
+                    allreduce_ms = 1e3 * stats.get("allreduce_s", 0.0) / max(args_steps, 1)
+                else:
+                    for _ in range(args_warmup):
+                        step(mode)
+                    torch.cuda.synchronize(dev)
+                    barrier()
+                    torch.cuda.synchronize(dev)
+                    l0 = _native.launches()
+                    _native.timing_enable(True)  # per-kernel CUDA events on the launching stream
+                    ms = timed(lambda: step(mode), args_steps)
+                    n_launch = _native.launches() - l0
+                    kt = _native.timing_read()
+                    _native.timing_enable(False)
+                bd = {k: v[0] / args_steps for k, v in kt.items()}
+                pl = {k: v[0] / max(v[1], 1) for k, v in kt.items()}
+                if mode == head_mode:
+                    breakdown, per_launch, launches = bd, pl, n_launch
+                torch.cuda.synchronize(dev)
+                barrier()
+                _native.check_status(dev)
+                mean_ms = max_over_ranks(statistics.mean(ms))
+                modes[mode] = {"value": cells / (mean_ms / 1e3), "ms_per_step": mean_ms,
+                               "median_ms": statistics.median(ms), "kernel_ms_per_step": bd, "gpu_launches": n_launch}
+                if allreduce_ms is not None:
+                    modes[mode]["allreduce_ms_per_step"] = max_over_ranks(allreduce_ms)
+                pub = PUBLISHED.get(name, {}).get(mode)
+                modes[mode]["vs_published"] = (modes[mode]["value"] / world / pub) if pub else None
+
+        # End to end through the public API with host buffers.
+        e2e = None
+        if not fused_only:
+            if is_bary:
+                out_h = torch.empty(N, Dm).pin_memory()
+
+                def e2e_run(k):
+                    Xd = X_h.to(dev, non_blocking=True)
+                    bary = sharded_barycenter(Xd, gamma=gamma, max_iter=k, lr=0.1, early_stopping=False)
+                    out_h.copy_(bary, non_blocking=True)
+
+                e2e_run(args_warmup)
+                torch.cuda.synchronize(dev)
+                barrier()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                e2e_run(args_steps)
                 e1.record(stream)
                 torch.cuda.synchronize(dev)
-                ms = [e0.elapsed_time(e1) / args.steps] * args.steps
-                n_launch = _native.launches() - l0
-                kt = _native.timing_read()
-                _native.timing_enable(False)
-                allreduce_ms = 1e3 * stats.get("allreduce_s", 0.0) / max(args.steps, 1)
+                e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args_steps)
+                h2d = X_h.numel() * 4 / args_steps
+                d2h = out_h.numel() * 4 / args_steps
+                api = ("softdtw_cuda.distributed.sharded_barycenter (pinned host sequences in, barycenter out; "
+                       "per-step bytes = one call's copies / steps)")
             else:
-                for _ in range(args.warmup):
-                    step(mode)
-                torch.cuda.synchronize(dev)
-                barrier()
-                torch.cuda.synchronize(dev)
-                l0 = _native.launches()
-                _native.timing_enable(True)  # per-kernel CUDA events on the launching stream
-                ms = timed(lambda: step(mode), args.steps)
-                n_launch = _native.launches() - l0
-                kt = _native.timing_read()
-                _native.timing_enable(False)
-            bd = {k: v[0] / args.steps for k, v in kt.items()}
-            pl = {k: v[0] / max(v[1], 1) for k, v in kt.items()}
-            if mode == head_mode:
-                breakdown, per_launch, launches = bd, pl, n_launch
-            torch.cuda.synchronize(dev)
-            barrier()
-            _native.check_status(dev)
-            mean_ms = max_over_ranks(statistics.mean(ms))
-            modes[mode] = {"value": cells / (mean_ms / 1e3), "ms_per_step": mean_ms,
-                           "median_ms": statistics.median(ms), "kernel_ms_per_step": bd, "gpu_launches": n_launch}
-            if allreduce_ms is not None:
-                modes[mode]["allreduce_ms_per_step"] = max_over_ranks(allreduce_ms)
-            pub = PUBLISHED.get(name, {}).get(mode)
-            modes[mode]["vs_published"] = (modes[mode]["value"] / world / pub) if pub else None
+                gx_h = torch.empty_like(x_h).pin_memory()
+                gy_h = torch.empty_like(y_h).pin_memory()
+                loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+                fused = None if head_mode == "fused" else False
 
-    # End to end through the public API with host buffers.
-    e2e = None
-    if not args.fused_only:
-        if is_bary:
-            out_h = torch.empty(N, Dm).pin_memory()
+                def e2e_step(grads_out):
+                    xd = x_h.to(dev, non_blocking=True).requires_grad_(True)
+                    yd = y_h.to(dev, non_blocking=True).requires_grad_(True)
+                    loss = SoftDTW(gamma=gamma, normalize=normalize, fused=fused)(xd, yd).mean()
+                    loss.backward()
+                    loss_h.copy_(loss.detach(), non_blocking=True)
+                    if grads_out:
+                        gx_h.copy_(xd.grad, non_blocking=True)
+                        gy_h.copy_(yd.grad, non_blocking=True)
 
-            def e2e_run(k):
-                Xd = X_h.to(dev, non_blocking=True)
-                bary = sharded_barycenter(Xd, gamma=gamma, max_iter=k, lr=0.1, early_stopping=False)
-                out_h.copy_(bary, non_blocking=True)
+                # Headline: a training step's result (the loss) comes back to the
+                # host; dL/dx, dL/dy are computed in the timed region and stay on
+                # the device for the optimizer.  Also timed: the same step with both
+                # gradients copied to host memory as well.
+                res = {}
+                for grads_out in (False, True):
+                    for _ in range(args_warmup):
+                        e2e_step(grads_out)
+                    torch.cuda.synchronize(dev)
+                    barrier()
+                    res[grads_out] = max_over_ranks(statistics.mean(timed(lambda: e2e_step(grads_out), args_steps)))
+                e2e_ms = res[False]
+                h2d = x_h.numel() * 4 + y_h.numel() * 4
+                d2h = 4
+                d2h_grads = 4 + gx_h.numel() * 4 + gy_h.numel() * 4
+                api = (f"softdtw_cuda.SoftDTW ({head_mode}; pinned host x,y in; loss out, dL/dx and dL/dy computed "
+                       "and left on the device)")
+                e2e_grads = {"value": cells / (res[True] / 1e3), "ms_per_step": res[True], "d2h_bytes_per_step": d2h_grads,
+                             "api": f"as above, plus dL/dx and dL/dy copied to pinned host memory"}
+            e2e = {"value": cells / (e2e_ms / 1e3), "unit": "cells/s", "ms_per_step": e2e_ms,
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
+            if not is_bary:
+                e2e["grads_to_host"] = e2e_grads
 
-            e2e_run(args.warmup)
-            torch.cuda.synchronize(dev)
-            barrier()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            e2e_run(args.steps)
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-            e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-            h2d = X_h.numel() * 4 / args.steps
-            d2h = out_h.numel() * 4 / args.steps
-            api = ("softdtw_cuda.distributed.sharded_barycenter (pinned host sequences in, barycenter out; "
-                   "per-step bytes = one call's copies / steps)")
-        else:
-            gx_h = torch.empty_like(x_h).pin_memory()
-            gy_h = torch.empty_like(y_h).pin_memory()
-            loss_h = torch.empty((), dtype=torch.float32).pin_memory()
-            fused = None if head_mode == "fused" else False
+        clocks = sampler.summary()
+        head = modes[head_mode]
 
-            def e2e_step(grads_out):
-                xd = x_h.to(dev, non_blocking=True).requires_grad_(True)
-                yd = y_h.to(dev, non_blocking=True).requires_grad_(True)
-                loss = SoftDTW(gamma=gamma, normalize=normalize, fused=fused)(xd, yd).mean()
-                loss.backward()
-                loss_h.copy_(loss.detach(), non_blocking=True)
-                if grads_out:
-                    gx_h.copy_(xd.grad, non_blocking=True)
-                    gy_h.copy_(yd.grad, non_blocking=True)
+        # Roofline of the dominant kernel (largest device time per step).
+        dom = max(breakdown, key=breakdown.get)
+        dom_ms = per_launch[dom]
+        launches_per_step = breakdown[dom] / dom_ms
+        alg_bytes = ALG_BYTES.get(dom, 0) * my_cells / launches_per_step  # per launch
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        hbm_peak = peaks.get("hbm_gbs", 6650.0)
+        achieved = alg_bytes / (dom_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": achieved / hbm_peak,
+                    "traffic": TRAFFIC_C2.get(dom) if name == "c2" else None,
+                    "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                    "alg_bytes_per_cell": ALG_BYTES.get(dom, 0)}
+        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
+        mufu_peak = n_sm * MUFU_PER_SM_CLK * sm_mhz * 1e6
+        step_mufu = MUFU_PER_CELL * my_cells / (head["ms_per_step"] / 1e3)
+        wf = {k: ALG_MUFU[k] * my_cells / (breakdown[k] / 1e3) for k in ALG_MUFU if k in breakdown}
+        roofline_mufu = {"bound": "mufu", "unit": "Gop/s", "peak": mufu_peak / 1e9,
+                         "peak_basis": f"{n_sm} SMs x {MUFU_PER_SM_CLK} ex2/lg2 per clk x {sm_mhz:.0f} MHz (median under load)",
+                         "step_achieved": step_mufu / 1e9, "step_frac": step_mufu / mufu_peak,
+                         "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms_per_step": breakdown[k],
+                                         "alg_ops_per_cell": ALG_MUFU[k]} for k, v in wf.items()},
+                         "alg_ops_per_cell": MUFU_PER_CELL}
+        # Latency floor of the wavefronts: a problem needs N + M - 1 dependent
+        # anti-diagonal steps (n_bands * (M + 32) when its stripes loop over bands),
+        # each at least one cell's dependency chain (DEP_CYCLES, measured with
+        # clock64 microbenchmarks on B200); problems beyond what fits at once run
+        # in further waves.
+        n_prob = (hi - lo) if is_bary else (3 if normalize else 1) * B
+        Mp = N if is_bary else M
+        pinfo = _native.plan_info(n_prob, N, Mp)
+        steps = max(N + Mp - 1, pinfo["bands"] * (Mp + 32))
+        waves = -(-n_prob // max(1, pinfo["clusters_fit"]))
+        floor_ms = waves * steps * DEP_CYCLES / (sm_mhz * 1e6) * 1e3
+        roofline_latency = {"bound": "dependent chain", "unit": "ms", "cycles_per_step": DEP_CYCLES,
+                            "steps": steps, "waves": waves, "floor_ms": floor_ms,
+                            "kernels": {k: {"ms_per_step": breakdown[k], "frac": floor_ms / breakdown[k]}
+                                        for k in ALG_MUFU if k in breakdown}}
 
-            # Headline: a training step's result (the loss) comes back to the
-            # host; dL/dx, dL/dy are computed in the timed region and stay on
-            # the device for the optimizer.  Also timed: the same step with both
-            # gradients copied to host memory as well.
-            res = {}
-            for grads_out in (False, True):
-                for _ in range(args.warmup):
-                    e2e_step(grads_out)
-                torch.cuda.synchronize(dev)
-                barrier()
-                res[grads_out] = max_over_ranks(statistics.mean(timed(lambda: e2e_step(grads_out), args.steps)))
-            e2e_ms = res[False]
-            h2d = x_h.numel() * 4 + y_h.numel() * 4
-            d2h = 4
-            d2h_grads = 4 + gx_h.numel() * 4 + gy_h.numel() * 4
-            api = (f"softdtw_cuda.SoftDTW ({head_mode}; pinned host x,y in; loss out, dL/dx and dL/dy computed "
-                   "and left on the device)")
-            e2e_grads = {"value": cells / (res[True] / 1e3), "ms_per_step": res[True], "d2h_bytes_per_step": d2h_grads,
-                         "api": f"as above, plus dL/dx and dL/dy copied to pinned host memory"}
-        e2e = {"value": cells / (e2e_ms / 1e3), "unit": "cells/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
-        if not is_bary:
-            e2e["grads_to_host"] = e2e_grads
 
-    clocks = sampler.summary()
+        return {"name": name, "B": B, "N": N, "M": M, "Dm": Dm, "desc": desc, "head_mode": head_mode,
+                "is_bary": is_bary, "cells": cells, "modes": modes, "breakdown": breakdown, "launches": launches,
+                "e2e": e2e, "roofline": roofline, "roofline_mufu": roofline_mufu,
+                "roofline_latency": roofline_latency, "clocks": clocks}
+
+    sampler = ClockSampler(local)
+    res = run_one(args.workload, args.steps, args.warmup, args.fused_only, args.only_mode, sampler)
+    name, B, N, Dm, desc = res["name"], res["B"], res["N"], res["Dm"], res["desc"]
+    head_mode, is_bary, modes, breakdown = res["head_mode"], res["is_bary"], res["modes"], res["breakdown"]
+    e2e, roofline, roofline_mufu, roofline_latency = res["e2e"], res["roofline"], res["roofline_mufu"], res["roofline_latency"]
+    launches, clocks = res["launches"], res["clocks"]
     head = modes[head_mode]
-
-    # Roofline of the dominant kernel (largest device time per step).
-    dom = max(breakdown, key=breakdown.get)
-    dom_ms = per_launch[dom]
-    launches_per_step = breakdown[dom] / dom_ms
-    alg_bytes = ALG_BYTES.get(dom, 0) * my_cells / launches_per_step  # per launch
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
-    hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    achieved = alg_bytes / (dom_ms / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak,
-                "traffic": TRAFFIC_C2.get(dom) if name == "c2" else None,
-                "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                "alg_bytes_per_cell": ALG_BYTES.get(dom, 0)}
-    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
-    sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
-    mufu_peak = n_sm * MUFU_PER_SM_CLK * sm_mhz * 1e6
-    step_mufu = MUFU_PER_CELL * my_cells / (head["ms_per_step"] / 1e3)
-    wf = {k: ALG_MUFU[k] * my_cells / (breakdown[k] / 1e3) for k in ALG_MUFU if k in breakdown}
-    roofline_mufu = {"bound": "mufu", "unit": "Gop/s", "peak": mufu_peak / 1e9,
-                     "peak_basis": f"{n_sm} SMs x {MUFU_PER_SM_CLK} ex2/lg2 per clk x {sm_mhz:.0f} MHz (median under load)",
-                     "step_achieved": step_mufu / 1e9, "step_frac": step_mufu / mufu_peak,
-                     "kernels": {k: {"achieved": v / 1e9, "frac": v / mufu_peak, "ms_per_step": breakdown[k],
-                                     "alg_ops_per_cell": ALG_MUFU[k]} for k, v in wf.items()},
-                     "alg_ops_per_cell": MUFU_PER_CELL}
-    # Latency floor of the wavefronts: a problem needs N + M - 1 dependent
-    # anti-diagonal steps (n_bands * (M + 32) when its stripes loop over bands),
-    # each at least one cell's dependency chain (DEP_CYCLES, measured with
-    # clock64 microbenchmarks on B200); problems beyond what fits at once run
-    # in further waves.
-    n_prob = (hi - lo) if is_bary else (3 if normalize else 1) * B
-    Mp = N if is_bary else M
-    pinfo = _native.plan_info(n_prob, N, Mp)
-    steps = max(N + Mp - 1, pinfo["bands"] * (Mp + 32))
-    waves = -(-n_prob // max(1, pinfo["clusters_fit"]))
-    floor_ms = waves * steps * DEP_CYCLES / (sm_mhz * 1e6) * 1e3
-    roofline_latency = {"bound": "dependent chain", "unit": "ms", "cycles_per_step": DEP_CYCLES,
-                        "steps": steps, "waves": waves, "floor_ms": floor_ms,
-                        "kernels": {k: {"ms_per_step": breakdown[k], "frac": floor_ms / breakdown[k]}
-                                    for k in ALG_MUFU if k in breakdown}}
-
+    # The default run also reports the other north-star shapes: the tiled
+    # N = M = 4096 problem (C3) and the barycenter (C5), each timed on its own
+    # (3 warm-up steps; C3 at most 10 timed steps, C5 at most 20).
+    subs = {}
+    if args.workload == "c2" and not args.fused_only:
+        for sub, k in (("c3", 10), ("c5", 20)):
+            r = run_one(sub, min(args.steps, k), 3, True, None, ClockSampler(local))
+            hm = r["modes"][r["head_mode"]]
+            subs[sub] = {"workload": f"{sub}: {r['desc']}; mode = {r['head_mode']}",
+                         "value": hm["value"], "unit": "cells/s", "ms_per_step": hm["ms_per_step"],
+                         "scaling": "strong" if r["is_bary"] else "weak", "kernel_ms_per_step": r["breakdown"],
+                         "gpu_launches": r["launches"], "roofline_mufu": r["roofline_mufu"],
+                         "roofline_latency": r["roofline_latency"], "clocks": r["clocks"]}
+            if "allreduce_ms_per_step" in hm:
+                subs[sub]["allreduce_ms_per_step"] = hm["allreduce_ms_per_step"]
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(name, 10.0)
@@ -538,6 +571,8 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if subs:
+        line["workloads"] = subs
     print(json.dumps(line), flush=True)
 
 
