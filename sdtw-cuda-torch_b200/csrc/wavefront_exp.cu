@@ -431,14 +431,14 @@ __global__ void __launch_bounds__(512, DP >= 8 ? 1 : 2) fwdx_kernel(const FwdArg
                         km = cinf ? 1.f : km;
                         kx = cinf ? kEneg : kx;
                     }
-                    if (masked) {
-                        const int col = t0 + u - lane;
-                        bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && lane < rows_left;
-                        if constexpr (BANDED)
-                            live = live && static_cast<unsigned>(R0 + lane - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                        pa = live ? pa : 0.f;
-                    }
-                    pmax = max_nan(pmax, pa);
+                    // Only cells inside the table (and the band) count for the
+                    // range check; computed for every cell (a branch here would
+                    // keep the compiler from interleaving the group's cells).
+                    const int col = t0 + u - lane;
+                    bool live = static_cast<unsigned>(col) < static_cast<unsigned>(M) && lane < rows_left;
+                    if constexpr (BANDED)
+                        live = live && static_cast<unsigned>(R0 + lane - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    pmax = max_nan(pmax, (live || !masked) ? pa : 0.f);
                     kb[u * 32] = make_uint2(__float_as_uint(km), static_cast<uint32_t>(kx));
                 }
                 if constexpr (DP == 0) cost_copy(gi + 2);  // into the buffer just read
