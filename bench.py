@@ -274,6 +274,7 @@ def main():
 
     from softdtw_cuda import SoftDTW, _native
     from softdtw_cuda.distributed import shard_bounds, sharded_barycenter
+    import softdtw_cuda.barycenters as _bc
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -349,14 +350,38 @@ def main():
             for mode in all_modes:
                 allreduce_ms = None
                 if is_bary:
-                    # One call of K iterations (the optimiser state carries over),
-                    # timed as a whole; the per-step figure is the average.
+                    # Kernel breakdown and launch count from one step-by-step
+                    # call (per-kernel CUDA events cannot run inside a graph);
+                    # a graph replay launches the same kernels.
+                    _bc.USE_CUDA_GRAPH = False
                     sharded_barycenter(X_d, gamma=gamma, max_iter=args_warmup, lr=0.1, early_stopping=False)
                     torch.cuda.synchronize(dev)
                     barrier()
-                    torch.cuda.synchronize(dev)
                     l0 = _native.launches()
                     _native.timing_enable(True)
+                    sharded_barycenter(X_d, gamma=gamma, max_iter=args_steps, lr=0.1, early_stopping=False)
+                    torch.cuda.synchronize(dev)
+                    n_launch = _native.launches() - l0
+                    kt = _native.timing_read()
+                    _native.timing_enable(False)
+                    _bc.USE_CUDA_GRAPH = True
+                    # The all-reduce of [gradient | loss] on its own, as the
+                    # iteration issues it.
+                    allreduce_ms = 0.0
+                    if world > 1:
+                        buf = torch.zeros(N * Dm + 1, device=dev)
+                        for _ in range(5):
+                            dist.all_reduce(buf)
+                        torch.cuda.synchronize(dev)
+                        barrier()
+                        allreduce_ms = statistics.median(timed(lambda: dist.all_reduce(buf), 20))
+                    # The timed call: K iterations of the replayed CUDA graph
+                    # (the untimed call of the same length captures it); the
+                    # per-step figure is the average.
+                    sharded_barycenter(X_d, gamma=gamma, max_iter=args_steps, lr=0.1, early_stopping=False)
+                    torch.cuda.synchronize(dev)
+                    barrier()
+                    torch.cuda.synchronize(dev)
                     stats = {}
                     flush.zero_()
                     e0 = torch.cuda.Event(enable_timing=True)
@@ -365,11 +390,9 @@ def main():
                     sharded_barycenter(X_d, gamma=gamma, max_iter=args_steps, lr=0.1, early_stopping=False, stats=stats)
                     e1.record(stream)
                     torch.cuda.synchronize(dev)
+                    if not stats.get("graph") or stats.get("captured"):
+                        raise SystemExit(f"barycenter timing did not replay a cached graph: {stats}")
                     ms = [e0.elapsed_time(e1) / args_steps] * args_steps
-                    n_launch = _native.launches() - l0
-                    kt = _native.timing_read()
-                    _native.timing_enable(False)
-                    allreduce_ms = 1e3 * stats.get("allreduce_s", 0.0) / max(args_steps, 1)
                 else:
                     for _ in range(args_warmup):
                         step(mode)
@@ -402,13 +425,14 @@ def main():
         if not fused_only:
             if is_bary:
                 out_h = torch.empty(N, Dm).pin_memory()
+                Xd = torch.empty_like(X_d)  # the device buffer the sequences are loaded into
 
                 def e2e_run(k):
-                    Xd = X_h.to(dev, non_blocking=True)
+                    Xd.copy_(X_h, non_blocking=True)
                     bary = sharded_barycenter(Xd, gamma=gamma, max_iter=k, lr=0.1, early_stopping=False)
                     out_h.copy_(bary, non_blocking=True)
 
-                e2e_run(args_warmup)
+                e2e_run(args_steps)  # captures the graph the timed call replays
                 torch.cuda.synchronize(dev)
                 barrier()
                 e0 = torch.cuda.Event(enable_timing=True)

@@ -66,7 +66,10 @@ struct KernelTimer {
     cudaEvent_t e0 = nullptr;
     KernelTimer(const char* n, cudaStream_t s, int kernels = 1) : name(n), st(s) {
         g_launches.fetch_add(static_cast<unsigned long long>(kernels));
-        if (g_timing.load()) {
+        // No timing events inside a stream capture (a CUDA graph): they would
+        // be recorded at every replay, not now.
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (g_timing.load() && cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
             std::lock_guard<std::mutex> lk(g_timing_mu);
             e0 = pool_event();
             cudaEventRecord(e0, st);
@@ -361,6 +364,16 @@ GradOperands grad_operands(int B, int N, int M, int dim) {
 // x/y pairs' backward, one row per lane) instead of its score.
 bool weight_store(int B, int N, int M) { return plan(B, N, M, 0).K == 1; }
 
+// A launch with more than one band hands rows between bands through a ring in
+// the workspace, checked by tags that carry the launch's sequence number.  The
+// ring is reset before every such launch, so that a launch replayed from a
+// CUDA graph (same sequence number, same workspace) never meets a previous
+// replay's entries.
+cudaError_t reset_wrap(const WavePlan& P, uint64_t* wrap, cudaStream_t stream) {
+    if (P.n_bands <= 1) return cudaSuccess;
+    return cudaMemsetAsync(wrap, 0xff, wrap_bytes(P), stream);
+}
+
 // Dw: the cost table, or null with x, y, dim, dp (> 0) for the fused costs.
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr,
@@ -384,7 +397,8 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
     a.wait = wait ? *wait : wait_ctx();
-    cudaError_t e;
+    cudaError_t e = reset_wrap(a.P, wrap, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(band-wrap ring)");
     {
         KernelTimer kt("wavefront_fwd", stream);
         e = launch_forward(a, stream);
@@ -407,7 +421,8 @@ int run_backward(const float* score, const float* grad_out, float* Ew, int B, in
     a.seq = g_seq.fetch_add(1);
     a.debug_stall = g_debug_stall.load();
     a.wait = wait_ctx();
-    cudaError_t e;
+    cudaError_t e = reset_wrap(a.P, wrap, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(band-wrap ring)");
     {
         KernelTimer kt("wavefront_bwd", stream);
         e = launch_backward(a, stream);

@@ -17,13 +17,14 @@ the loss history back asynchronously every few replays, applies the early-stop
 rule to it, and returns the barycenter of the stopping iteration from the
 history, so the result is the one the step-by-step loop returns.
 
-The graph pays off where an iteration is bound by launch overhead: measured on
-B200, 8 sequences of 32 x 3 take 0.09 ms per iteration replayed against 0.66 ms
-step by step (6.7 ms to capture); at 4096 x 100 x 3 an iteration is 1.3 ms of
-GPU work either way and capturing costs 80 ms.  So the graph is used up to
-GRAPH_MAX_CELLS DP cells per iteration (B * N^2).  Shapes the graph cannot
-serve (more than one wavefront band per problem) and any capture failure fall
-back to the step-by-step loop.
+The captured graph is kept (a few per process, keyed by the sequences'
+address and shape and by gamma, lr, max_iter and the fused flag), so a second
+call with the same configuration only resets the state and replays.  A launch
+whose wavefront needs more than one band resets its band-wrap ring inside the
+graph, so every shape can be replayed.  Runs shorter than GRAPH_MIN_ITERS
+iterations, and any capture failure, use the step-by-step loop.  The same
+engine serves ``softdtw_cuda.distributed.sharded_barycenter``, whose captured
+iteration includes the NCCL all-reduce of [gradient | loss].
 """
 from __future__ import annotations
 
@@ -36,8 +37,10 @@ from .module import SoftDTW
 
 # Use the CUDA-graph loop for CUDA tensors when it applies.
 USE_CUDA_GRAPH = True
-GRAPH_MAX_CELLS = 1 << 22
+GRAPH_MIN_ITERS = 8  # shorter runs are not worth a capture
 _READBACK_EVERY = 8  # replays between asynchronous loss read-backs
+_GRAPH_CACHE_SIZE = 4
+_graphs: dict = {}  # key -> _BaryGraph (insertion order = age)
 
 
 def _cosine_lrs(lr: float, max_iter: int) -> list[float]:
@@ -73,86 +76,145 @@ def _early_stop_at(losses, max_iter, patience, tol):
     return None
 
 
-def _graph_barycenter(X, w, bary0, loss_fn, max_iter, lr, early_stopping, patience, tol, verbose):
-    """The loop as a replayed CUDA graph (see the module docstring).  Returns
-    None when the shape needs more than one wavefront band per problem."""
-    B, N, Dm = X.shape
-    if _native.plan_info(B, N, N)["bands"] != 1:
-        return None
-    dev = X.device
-    lrs = _cosine_lrs(lr, max_iter)
-    lr_table = torch.tensor(lrs[:max_iter], dtype=torch.float32, device=dev)
-    lr_t = lr_table[0].clone()
-    it_t = torch.zeros(1, dtype=torch.long, device=dev)
-    loss_hist = torch.zeros(max_iter, dtype=X.dtype, device=dev)
-    bary_hist = torch.zeros((max_iter, N, Dm), dtype=X.dtype, device=dev)
-    bary = bary0.clone().requires_grad_(True)
-    bary.grad = torch.zeros_like(bary)
-    opt = torch.optim.Adam([bary], lr=lr_t, capturable=True)
+class _BaryGraph:
+    """One captured Adam iteration and the state it reads and writes.
 
-    def body():
-        lr_t.copy_(torch.index_select(lr_table, 0, it_t)[0])
-        bary.grad.zero_()
-        d = loss_fn(bary.unsqueeze(0).expand(B, -1, -1), X)
-        loss = (w * d).sum()
-        loss.backward()
-        torch.nn.utils.clip_grad_norm_([bary], max_norm=1.0)
-        opt.step()
-        loss_hist.index_copy_(0, it_t, loss.detach().reshape(1))
-        bary_hist.index_copy_(0, it_t, bary.detach().unsqueeze(0))
-        it_t.add_(1)
+    X (B, N, D) is read in place; the weights, the starting point, the Adam
+    state, the iteration counter and the histories are persistent tensors that
+    ``run`` resets before replaying.  ``reduce``, if given, is called on the
+    contiguous [gradient (N*D) | loss] buffer inside the iteration (the
+    sharded barycenter's all-reduce); clipping and Adam follow it."""
 
-    # Warm up on a side stream (allocator, cuBLAS, the optimizer's state), then
-    # put every state tensor back to the start before capturing.
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for _ in range(2):
+    def __init__(self, X, gamma, fused, max_iter, lr, reduce):
+        B, N, Dm = X.shape
+        dev = X.device
+        self.B, self.N, self.D, self.max_iter = B, N, Dm, max_iter
+        self.X = X  # held so that its memory is not reused while the graph reads it
+        self.iterations = 0
+        self.lrs = _cosine_lrs(lr, max_iter)
+        self.w = torch.zeros(B, dtype=X.dtype, device=dev)
+        self.bary0 = torch.zeros((N, Dm), dtype=X.dtype, device=dev)
+        self.lr_table = torch.tensor(self.lrs[:max_iter], dtype=torch.float32, device=dev)
+        self.lr_t = self.lr_table[0].clone()
+        self.it_t = torch.zeros(1, dtype=torch.long, device=dev)
+        self.loss_hist = torch.zeros(max_iter, dtype=X.dtype, device=dev)
+        self.bary_hist = torch.zeros((max_iter, N, Dm), dtype=X.dtype, device=dev)
+        self.bary = torch.zeros((N, Dm), dtype=X.dtype, device=dev, requires_grad=True)
+        self.bary.grad = torch.zeros_like(self.bary)
+        self.buf = torch.zeros(N * Dm + 1, dtype=X.dtype, device=dev)
+        self.opt = torch.optim.Adam([self.bary], lr=self.lr_t, capturable=True)
+        loss_fn = SoftDTW(gamma=gamma, normalize=False, fused=fused)
+        bary, w, buf, opt = self.bary, self.w, self.buf, self.opt
+
+        def body():
+            self.lr_t.copy_(torch.index_select(self.lr_table, 0, self.it_t)[0])
+            bary.grad.zero_()
+            loss = None
+            if B > 0:
+                d = loss_fn(bary.unsqueeze(0).expand(B, -1, -1), X)
+                loss = (w * d).sum()
+                loss.backward()
+            if reduce is not None:
+                if loss is not None:
+                    buf[:-1].copy_(bary.grad.reshape(-1))
+                    buf[-1:].copy_(loss.detach().reshape(1))
+                else:
+                    buf.zero_()
+                reduce(buf)
+                bary.grad.copy_(buf[:-1].view(N, Dm))
+                loss_now = buf[-1:]
+            else:
+                loss_now = loss.detach().reshape(1)
+            torch.nn.utils.clip_grad_norm_([bary], max_norm=1.0)
+            opt.step()
+            self.loss_hist.index_copy_(0, self.it_t, loss_now)
+            self.bary_hist.index_copy_(0, self.it_t, bary.detach().unsqueeze(0))
+            self.it_t.add_(1)
+
+        # Warm up on a side stream (allocator, workspaces, the optimizer's
+        # state, the communicator), then capture one iteration.
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self._reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
             body()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    with torch.no_grad():
-        bary.copy_(bary0)
-        bary.grad.zero_()
-        it_t.zero_()
-        for st in opt.state[bary].values():
-            if torch.is_tensor(st):
-                st.zero_()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        body()
 
-    host_losses = torch.empty(max_iter, dtype=X.dtype, pin_memory=True)
-    done = 0
-    stop = None
-    while done < max_iter and stop is None:
-        n = min(_READBACK_EVERY, max_iter - done)
-        for _ in range(n):
-            graph.replay()
-        done += n
-        if early_stopping or verbose:
-            host_losses[:done].copy_(loss_hist[:done], non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
-            if early_stopping:
-                stop = _early_stop_at(host_losses[:done].tolist(), max_iter, patience, tol)
-    last = stop if stop is not None else max_iter - 1
-    if verbose:
-        losses = host_losses[:last + 1].tolist()
-        best = float("inf")
-        for it in range(last + 1):
-            improvement = float("nan")
-            if early_stopping:
-                improvement = best - losses[it]
-                best = losses[it] if improvement > tol else best
-            if stop is not None and it == stop:
-                print(f"Early stopping at iteration {it + 1} (no improvement for {patience} iterations)")
-                break
-            if (it + 1) % 20 == 0:
-                imp = f"{improvement:9.6f}" if early_stopping else "     N/A "
-                print(f"Iteration {it + 1:3d}/{max_iter} | Loss: {losses[it]:9.6f} | Improvement: {imp} | "
-                      f"LR: {lrs[it + 1]:.2e}")
-    result = bary_hist[last].clone()
-    del graph
-    return result
+    def _reset(self):
+        with torch.no_grad():
+            self.bary.copy_(self.bary0)
+            self.bary.grad.zero_()
+            self.it_t.zero_()
+            for st in self.opt.state[self.bary].values():
+                if torch.is_tensor(st):
+                    st.zero_()
+
+    def run(self, w, bary0, max_iter, early_stopping, patience, tol, verbose):
+        dev = self.bary.device
+        with torch.no_grad():
+            self.w.copy_(w)
+            self.bary0.copy_(bary0)
+        self._reset()
+        host_losses = torch.empty(max_iter, dtype=self.loss_hist.dtype, pin_memory=True)
+        done = 0
+        stop = None
+        while done < max_iter and stop is None:
+            n = min(_READBACK_EVERY, max_iter - done)
+            for _ in range(n):
+                self.graph.replay()
+            done += n
+            if early_stopping or verbose:
+                host_losses[:done].copy_(self.loss_hist[:done], non_blocking=True)
+                torch.cuda.current_stream(dev).synchronize()
+                if early_stopping:
+                    stop = _early_stop_at(host_losses[:done].tolist(), max_iter, patience, tol)
+        last = stop if stop is not None else max_iter - 1
+        self.iterations = last + 1
+        if verbose:
+            losses = host_losses[:last + 1].tolist()
+            best = float("inf")
+            for it in range(last + 1):
+                improvement = float("nan")
+                if early_stopping:
+                    improvement = best - losses[it]
+                    best = losses[it] if improvement > tol else best
+                if stop is not None and it == stop:
+                    print(f"Early stopping at iteration {it + 1} (no improvement for {patience} iterations)")
+                    break
+                if (it + 1) % 20 == 0:
+                    imp = f"{improvement:9.6f}" if early_stopping else "     N/A "
+                    print(f"Iteration {it + 1:3d}/{max_iter} | Loss: {losses[it]:9.6f} | Improvement: {imp} | "
+                          f"LR: {self.lrs[it + 1]:.2e}")
+        return self.bary_hist[last].clone()
+
+
+def _graph_barycenter(X, w, bary0, gamma, fused, max_iter, lr, early_stopping, patience, tol, verbose,
+                      reduce=None, reduce_key=None, stats=None):
+    """The loop as a replayed CUDA graph (see the module docstring), captured
+    once per configuration.  ``stats``, if a dict, receives the number of
+    iterations run and whether this call captured the graph."""
+    key = (X.device.index, X.data_ptr(), tuple(X.shape), X.dtype, float(gamma), fused, int(max_iter), float(lr),
+           reduce_key)
+    g = _graphs.pop(key, None)
+    captured = g is None
+    if captured:
+        g = _BaryGraph(X, gamma, fused, max_iter, lr, reduce)
+        while len(_graphs) >= _GRAPH_CACHE_SIZE:
+            _graphs.pop(next(iter(_graphs)))
+    _graphs[key] = g  # newest last
+    out = g.run(w, bary0, max_iter, early_stopping, patience, tol, verbose)
+    if stats is not None:
+        stats.update(iterations=g.iterations, captured=captured)
+    return out
+
+
+def clear_graph_cache() -> None:
+    """Release the captured barycenter graphs (and their memory pools)."""
+    _graphs.clear()
 
 
 def softdtw_barycenter(
@@ -193,14 +255,12 @@ def softdtw_barycenter(
     else:
         bary = init.clone().to(device)
     loss_fn = SoftDTW(gamma=gamma, normalize=False, fused=fused)
-    if USE_CUDA_GRAPH and X.is_cuda and max_iter > 0 and B * N * N <= GRAPH_MAX_CELLS:
+    if USE_CUDA_GRAPH and X.is_cuda and max_iter >= GRAPH_MIN_ITERS and B > 0:
         try:
-            res = _graph_barycenter(X, w, bary.detach(), loss_fn, max_iter, lr, early_stopping, patience, tol,
-                                    verbose)
+            return _graph_barycenter(X, w, bary.detach(), gamma, fused, max_iter, lr, early_stopping, patience,
+                                     tol, verbose)
         except RuntimeError:
-            res = None
-        if res is not None:
-            return res
+            pass
     bary.requires_grad_(True)
     opt = torch.optim.Adam([bary], lr=lr)
     sched = torch.optim.lr_scheduler.CosineAnnealingLR(opt, T_max=max_iter, eta_min=lr * 0.1)

@@ -18,7 +18,10 @@ is single-device; these functions are new and keep its single-device results:
   weight normalisation and the initial weighted mean take one all-reduce each,
   before the loop.  The loop follows softdtw_cuda/barycenters.py:17-180 of the
   reference (Adam, cosine annealing to lr/10, clip-norm 1, early stopping after
-  max_iter // 2 on the global loss).
+  max_iter // 2 on the global loss).  On CUDA one iteration, all-reduce
+  included, is captured in a CUDA graph and replayed (barycenters.py's graph
+  engine), so a step costs no host launch overhead; every rank captures and
+  replays the same collective sequence.
 """
 from __future__ import annotations
 
@@ -143,6 +146,24 @@ def sharded_barycenter(
     else:
         bary = init.clone().to(device=device, dtype=X.dtype)
     bary.requires_grad_(True)
+
+    from . import barycenters as _bc
+    if _bc.USE_CUDA_GRAPH and X.is_cuda and max_iter >= _bc.GRAPH_MIN_ITERS:
+        reduce = None
+        if world > 1:
+            def reduce(t):
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+        t0 = time.time()
+        info = {}
+        res = _bc._graph_barycenter(X, w, bary.detach(), gamma, fused, max_iter, lr, early_stopping, patience, tol,
+                                    verbose and rank == 0, reduce=reduce, reduce_key=("sum", id(group), world),
+                                    stats=info)
+        if stats is not None:
+            # The all-reduce runs inside the graph, where it cannot be timed
+            # apart from the iteration: allreduce_s is None.
+            stats.update(iterations=info["iterations"], allreduce_s=None, wall_s=time.time() - t0, world=world,
+                         graph=True, captured=info["captured"])
+        return res
 
     loss_fn = SoftDTW(gamma=gamma, normalize=False, fused=fused)
     opt = torch.optim.Adam([bary], lr=lr)

@@ -36,9 +36,9 @@ def _run(graph, X, **kw):
 @pytest.mark.parametrize("early,weighted,fused", [(False, False, None), (True, True, None), (True, False, False)])
 def test_graph_loop_matches_step_loop(early, weighted, fused):
     X, w = _data(16, 40, 3, seed=3)
-    assert 16 * 40 * 40 <= bc.GRAPH_MAX_CELLS
     kw = dict(gamma=1.0, max_iter=60, lr=0.1, early_stopping=early, patience=3, tol=1e-2, verbose=True,
               weights=w if weighted else None, fused=fused)
+    assert kw["max_iter"] >= bc.GRAPH_MIN_ITERS
     b_graph, out_graph = _run(True, X, **kw)
     b_eager, out_eager = _run(False, X, **kw)
     torch.testing.assert_close(b_graph, b_eager, rtol=1e-4, atol=1e-5)
@@ -46,3 +46,32 @@ def test_graph_loop_matches_step_loop(early, weighted, fused):
     # float rounding of the last digit, so compare the message skeletons.
     strip = lambda s: [ln.split("| Loss")[0] if ln.startswith("Iteration") else ln for ln in s.splitlines()]
     assert strip(out_graph) == strip(out_eager)
+
+
+def test_graph_cache_reuse_and_multiband():
+    """A second call with the same configuration replays the cached graph with
+    the new weights and starting point; a shape whose wavefront runs in many
+    bands (forced plan) replays correctly (its band-wrap ring is reset inside
+    the graph)."""
+    from softdtw_cuda import _native
+    bc.clear_graph_cache()
+    X, w = _data(12, 70, 3, seed=5)
+    kw = dict(gamma=1.0, max_iter=24, lr=0.1, early_stopping=False)
+    b1, _ = _run(True, X, weights=w, **kw)
+    n_cached = len(bc._graphs)
+    b2, _ = _run(True, X, weights=w.flip(0), init=X[0], **kw)
+    assert len(bc._graphs) == n_cached  # replayed, not captured again
+    torch.testing.assert_close(b1, _run(False, X, weights=w, **kw)[0], rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(b2, _run(False, X, weights=w.flip(0), init=X[0], **kw)[0], rtol=1e-4, atol=1e-5)
+    _native.set_plan_override(1, 1, 1)  # one stripe per CTA, one CTA per cluster: 3 bands at N = 70
+    try:
+        assert _native.plan_info(12, 70, 70)["bands"] > 1
+        bc.clear_graph_cache()
+        b3, _ = _run(True, X, weights=w, **kw)
+        b4, _ = _run(True, X, weights=w, **kw)
+        b5, _ = _run(False, X, weights=w, **kw)
+    finally:
+        _native.set_plan_override(0, 0, 0)
+        bc.clear_graph_cache()
+    torch.testing.assert_close(b3, b5, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(b4, b5, rtol=1e-4, atol=1e-5)
