@@ -568,6 +568,10 @@ def main():
         cpu_baseline = {"value": v, "unit": "cells/s", "cores": cores, "kind": "port", "sample": sample}
 
     if world > 1:
+        # The cached barycenter graphs hold captured NCCL calls: release them
+        # before the process group, whose teardown otherwise waits on them.
+        torch.cuda.synchronize(dev)
+        _bc.clear_graph_cache()
         dist.destroy_process_group()
     if rank != 0:
         return

@@ -16,7 +16,7 @@
  * The "score" table takes the place of the reference's R table
  * (B, N+2, M+2): it holds T = -R * log2(e) / gamma for every cell, as a pair
  * of float32 (hi, lo) with T = hi + lo, in the anti-diagonal ("wavefront")
- * layout the kernels write with bulk copies of whole rows.  It must be 16-byte aligned;
+ * layout the kernels write by whole anti-diagonal rows.  It must be 16-byte aligned;
  * workspaces 256-byte aligned.  The cost table of the unfused x/y entry points
  * (sdtw_cost_elems floats) uses the same anti-diagonal layout and must be
  * 16-byte aligned.
@@ -168,6 +168,34 @@ int sdtw_backward_sqeuclid_f32(const float *x, const float *y, const float *scor
  * -- replaces torch autograd of softdtw_cuda/distances.py:20-28 */
 int sdtw_grad_sqeuclid_f32(const float *G, const float *D_mask, const float *x, const float *y,
                            float *grad_x, float *grad_y, int B, int N, int M, int dim, void *stream);
+
+/* One iteration of the Soft-DTW barycenter, split at the point where the
+ * multi-GPU barycenter all-reduces [gradient | loss] across ranks.
+ *
+ * sdtw_barycenter_grad_f32: for the barycenter bary (N,dim), the sequences
+ * X (B,M,dim) and the weights w (B,), writes grad_loss (N*dim + 1 floats):
+ *   grad_loss[0 : N*dim] = sum_b w[b] * d SoftDTW_gamma(bary, X[b]) / d bary,
+ *   grad_loss[N*dim]     = sum_b w[b] * SoftDTW_gamma(bary, X[b]),
+ * both reduced in a fixed order (bit-reproducible).  The fused (direct-form)
+ * squared-Euclidean cost, no band.  Workspace: sdtw_barycenter_workspace_bytes.
+ * -- replaces softdtw_cuda/barycenters.py:122-131 (expand, SoftDTW loss,
+ *    weighted sum, backward)
+ *
+ * sdtw_barycenter_adam_f32: clips grad_loss[0:n] to 2-norm max_norm (factor
+ * min(1, max_norm / (norm + 1e-6))), then one Adam step on bary (n floats)
+ * with the moments exp_avg, exp_avg_sq and the learning rate
+ * lr_table[*step]; records loss_hist[*step] = grad_loss[n] and
+ * bary_hist[*step * n : ...] = the new bary, and increments *step (a device
+ * int).  Does nothing once *step >= max_iter.  Every operand is a device
+ * pointer, so the pair can be captured in a CUDA graph and replayed.
+ * -- replaces softdtw_cuda/barycenters.py:134-137 (clip_grad_norm_, Adam
+ *    step, cosine-annealing scheduler step) */
+size_t sdtw_barycenter_workspace_bytes(int B, int N, int M, int dim);
+int sdtw_barycenter_grad_f32(const float *bary, const float *X, const float *w, float *grad_loss, int B, int N,
+                             int M, int dim, float gamma, void *workspace, size_t workspace_bytes, void *stream);
+int sdtw_barycenter_adam_f32(float *bary, float *exp_avg, float *exp_avg_sq, const float *grad_loss, size_t n,
+                             const float *lr_table, int max_iter, int *step, float *loss_hist, float *bary_hist,
+                             float beta1, float beta2, float eps, float max_norm, void *stream);
 
 /* Score table <-> reference R layout (B,N+2,M+2): R[:,0,0] = 0, other borders
  * +inf, interior R = -T*gamma*ln 2.

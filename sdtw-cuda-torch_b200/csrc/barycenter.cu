@@ -1,0 +1,161 @@
+// barycenter.cu -- the device side of one Soft-DTW barycenter iteration
+// around the wavefronts (softdtw_cuda/barycenters.py:114-137 of the
+// reference):
+//
+//   barycenter_batch = barycenter.unsqueeze(0).expand(B, -1, -1)   (122)
+//   loss = (weights * SoftDTW(barycenter_batch, X)).sum()           (125-128)
+//   loss.backward()                                                 (131)
+//   clip_grad_norm_([barycenter], max_norm=1.0)                     (134)
+//   optimizer.step()  (Adam), scheduler.step() (cosine annealing)   (136-137)
+//
+// The wavefronts and the gradient kernels read the barycenter once for every
+// problem (x batch stride 0), and their per-problem results are reduced here:
+//   bary_reduce   grad_loss[v] = sum_b gx[b, v] for v < n (the expand's
+//                 backward) and grad_loss[n] = sum_b w[b] * out[b] (the loss),
+//                 in a fixed order: slices of problems to partials, then the
+//                 partials in slice order -- deterministic, no atomics;
+//   bary_adam     one CTA: the gradient's 2-norm, the clip factor
+//                 min(1, max_norm / (norm + 1e-6)), and Adam (Kingma & Ba,
+//                 2015) with torch's update form: m <- lerp(m, g, 1 - beta1),
+//                 v <- beta2 v + (1 - beta2) g^2, p <- p - lr / (1 - beta1^t)
+//                 * m / (sqrt(v) / sqrt(1 - beta2^t) + eps), t = step + 1, lr =
+//                 lr_table[step] (the cosine schedule, precomputed); then the
+//                 loss and the new barycenter are recorded at index step and
+//                 step is incremented.  Everything the iteration needs stays on
+//                 the device, so the iteration can be captured in a CUDA graph.
+#include <algorithm>
+#include <cmath>
+
+#include "sdtw_kernels.h"
+
+namespace sdtw {
+
+namespace {
+constexpr int kReduceThreads = 256;
+constexpr int kReduceSlices = 64;  // problem slices of the first reduction stage
+constexpr int kAdamThreads = 512;
+
+int reduce_slices(int B) { return B < kReduceSlices ? B : kReduceSlices; }
+}  // namespace
+
+__global__ void bary_broadcast_kernel(const float* __restrict__ bary, float* __restrict__ xb, int B, size_t n) {
+    const size_t total = static_cast<size_t>(B) * n;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        xb[i] = __ldg(bary + i % n);
+}
+
+// Stage 1: slice s of the problems, values v = blockIdx.x * 256 + thread (v ==
+// n is the weighted loss).
+__global__ void __launch_bounds__(kReduceThreads) bary_reduce_part_kernel(const float* __restrict__ gx,
+                                                                         const float* __restrict__ w,
+                                                                         const float* __restrict__ out,
+                                                                         float* __restrict__ part, int B, size_t n) {
+    const size_t v = static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
+    if (v > n) return;
+    const int S = gridDim.y, s = blockIdx.y;
+    const int b0 = static_cast<int>(static_cast<long long>(B) * s / S);
+    const int b1 = static_cast<int>(static_cast<long long>(B) * (s + 1) / S);
+    float acc = 0.f;
+    if (v < n) {
+#pragma unroll 8
+        for (int b = b0; b < b1; ++b) acc += __ldg(gx + static_cast<size_t>(b) * n + v);
+    } else {
+#pragma unroll 8
+        for (int b = b0; b < b1; ++b) acc = fmaf(__ldg(w + b), __ldg(out + b), acc);
+    }
+    part[static_cast<size_t>(s) * (n + 1) + v] = acc;
+}
+
+// Stage 2: the slices' partials in slice order.
+__global__ void __launch_bounds__(kReduceThreads) bary_reduce_final_kernel(const float* __restrict__ part,
+                                                                          float* __restrict__ grad_loss, int S,
+                                                                          size_t n) {
+    const size_t v = static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
+    if (v > n) return;
+    float acc = 0.f;
+    for (int s = 0; s < S; ++s) acc += __ldg(part + static_cast<size_t>(s) * (n + 1) + v);
+    grad_loss[v] = acc;
+}
+
+// Block-wide sum in a fixed order (per-thread partials, then a tree).
+__device__ float block_sum(float v, float* red) {
+    red[threadIdx.x] = v;
+    __syncthreads();
+    for (int h = blockDim.x / 2; h > 0; h >>= 1) {
+        if (threadIdx.x < h) red[threadIdx.x] += red[threadIdx.x + h];
+        __syncthreads();
+    }
+    const float r = red[0];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(kAdamThreads) bary_adam_kernel(float* __restrict__ bary, float* __restrict__ m,
+                                                                float* __restrict__ v,
+                                                                const float* __restrict__ grad_loss, size_t n,
+                                                                const float* __restrict__ lr_table, int max_iter,
+                                                                int* __restrict__ step, float* __restrict__ loss_hist,
+                                                                float* __restrict__ bary_hist, float beta1, float beta2,
+                                                                float eps, float max_norm) {
+    __shared__ float red[kAdamThreads];
+    const int it = *step;
+    if (it < 0 || it >= max_iter) return;  // more replays than iterations: nothing to do
+    float sq = 0.f;
+    for (size_t i = threadIdx.x; i < n; i += kAdamThreads) {
+        const float g = grad_loss[i];
+        sq = fmaf(g, g, sq);
+    }
+    const float norm = sqrtf(block_sum(sq, red));
+    const float clip = fminf(max_norm / (norm + 1e-6f), 1.f);
+    const float lr = lr_table[it];
+    const double t = static_cast<double>(it) + 1.0;
+    const float bc1 = static_cast<float>(1.0 - pow(static_cast<double>(beta1), t));
+    const float bc2_sqrt = sqrtf(static_cast<float>(1.0 - pow(static_cast<double>(beta2), t)));
+    const float step_size = lr / bc1;
+    float* hist = bary_hist + static_cast<size_t>(it) * n;
+    for (size_t i = threadIdx.x; i < n; i += kAdamThreads) {
+        const float g = grad_loss[i] * clip;
+        float mi = m[i], vi = v[i];
+        mi = fmaf(1.f - beta1, g - mi, mi);
+        vi = fmaf(1.f - beta2, g * g, vi * beta2);
+        const float p = bary[i] - step_size * (mi / (sqrtf(vi) / bc2_sqrt + eps));
+        m[i] = mi;
+        v[i] = vi;
+        bary[i] = p;
+        hist[i] = p;
+    }
+    if (threadIdx.x == 0) loss_hist[it] = grad_loss[n];
+    __syncthreads();
+    if (threadIdx.x == 0) *step = it + 1;
+}
+
+cudaError_t launch_bary_broadcast(const float* bary, float* xb, int B, size_t n, cudaStream_t st) {
+    const size_t total = static_cast<size_t>(B) * n;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 148 * 8));
+    bary_broadcast_kernel<<<blocks, 256, 0, st>>>(bary, xb, B, n);
+    return cudaGetLastError();
+}
+
+size_t bary_reduce_part_floats(int B, size_t n) { return static_cast<size_t>(reduce_slices(B)) * (n + 1); }
+
+cudaError_t launch_bary_reduce(const float* gx, const float* w, const float* out, float* part, float* grad_loss, int B,
+                               size_t n, cudaStream_t st) {
+    const int S = reduce_slices(B);
+    const unsigned bx = static_cast<unsigned>((n + 1 + kReduceThreads - 1) / kReduceThreads);
+    bary_reduce_part_kernel<<<dim3(bx, S), kReduceThreads, 0, st>>>(gx, w, out, part, B, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    bary_reduce_final_kernel<<<bx, kReduceThreads, 0, st>>>(part, grad_loss, S, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bary_adam(float* bary, float* exp_avg, float* exp_avg_sq, const float* grad_loss, size_t n,
+                             const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
+                             float beta1, float beta2, float eps, float max_norm, cudaStream_t st) {
+    bary_adam_kernel<<<1, kAdamThreads, 0, st>>>(bary, exp_avg, exp_avg_sq, grad_loss, n, lr_table, max_iter, step,
+                                                 loss_hist, bary_hist, beta1, beta2, eps, max_norm);
+    return cudaGetLastError();
+}
+
+}  // namespace sdtw

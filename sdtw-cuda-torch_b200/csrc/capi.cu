@@ -377,10 +377,12 @@ cudaError_t reset_wrap(const WavePlan& P, uint64_t* wrap, cudaStream_t stream) {
 // Dw: the cost table, or null with x, y, dim, dp (> 0) for the fused costs.
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr,
-                const float* x = nullptr, const float* y = nullptr, int dim = 0, int dp = 0) {
+                const float* x = nullptr, const float* y = nullptr, int dim = 0, int dp = 0,
+                bool x_shared = false) {
     FwdArgs a{};
     a.P = plan(B, N, M, dp ? 2 + dp : 0);
     a.x = x;
+    a.x_bstride = x_shared ? 0 : static_cast<size_t>(N) * dim;
     a.y = y;
     a.dim = dim;
     a.dp = dp;
@@ -792,7 +794,8 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     if (grad_small_supported(g.P, dim)) {
         // Few features: the contraction on the FP32 pipes, one read of E.
         KernelTimer kt("grad_xy", st, grad_y ? 2 : 1);
-        e = launch_grad_small(Ew, mask_w, x, y, grad_x, grad_y, reinterpret_cast<float*>(region), g.P, dim, st);
+        e = launch_grad_small(Ew, mask_w, x, y, grad_x, grad_y, reinterpret_cast<float*>(region), g.P, dim, st,
+                              static_cast<size_t>(N) * dim);
         if (e != cudaSuccess) return cuda_fail(e, "grad launch");
         return SDTW_OK;
     }
@@ -854,6 +857,116 @@ int sdtw_backward_xy_f32(const float* x, const float* y, const float* score, con
     if ((rc = check_ws(workspace, workspace_bytes, sdtw_workspace_bytes_xy(B, N, M, dim)))) return rc;
     return backward_xy_common(x, y, score, nullptr, grad_out, grad_x, grad_y, B, N, M, dim, bandwidth, workspace,
                               static_cast<cudaStream_t>(stream));
+}
+
+// ----------------------------------------------------------------------------
+// Barycenter iteration (barycenters.py:122-137 of the reference): the weighted
+// loss and its gradient with respect to the barycenter, and the clipped Adam
+// step.  Workspace: the x/y workspace, then the shares table, the broadcast
+// barycenter (used when the forward cannot read one x for every problem), the
+// per-problem gradients, the per-problem losses and the reduction partials.
+namespace {
+struct BaryLayout {
+    size_t score, xb, gx, out, part, total;
+};
+BaryLayout bary_layout(int B, int N, int M, int dim) {
+    BaryLayout L;
+    const size_t nd = static_cast<size_t>(N) * dim;
+    size_t o = sdtw_workspace_bytes_xy(B, N, M, dim);
+    L.score = o;
+    o += align_up(score_elems(B, N, M, g_k_override.load()) * sizeof(float), 256);
+    L.xb = o;
+    o += align_up(static_cast<size_t>(B) * nd * sizeof(float), 256);
+    L.gx = o;
+    o += align_up(static_cast<size_t>(B) * nd * sizeof(float), 256);
+    L.out = o;
+    o += align_up(static_cast<size_t>(B) * sizeof(float), 256);
+    L.part = o;
+    o += align_up(bary_reduce_part_floats(B, nd) * sizeof(float), 256);
+    L.total = o;
+    return L;
+}
+}  // namespace
+
+size_t sdtw_barycenter_workspace_bytes(int B, int N, int M, int dim) {
+    if (B <= 0 || N <= 0 || M <= 0 || dim <= 0) return 0;
+    return bary_layout(B, N, M, dim).total;
+}
+
+int sdtw_barycenter_grad_f32(const float* bary, const float* X, const float* w, float* grad_loss, int B, int N, int M,
+                             int dim, float gamma, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_common(B, N, M, gamma))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!bary || !X || !w || !grad_loss) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const BaryLayout L = bary_layout(B, N, M, dim);
+    if ((rc = check_ws(workspace, workspace_bytes, L.total))) return rc;
+    char* ws = static_cast<char*>(workspace);
+    float* score = reinterpret_cast<float*>(ws + L.score);
+    float* gx = reinterpret_cast<float*>(ws + L.gx);
+    float* out = reinterpret_cast<float*>(ws + L.out);
+    float* part = reinterpret_cast<float*>(ws + L.part);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t nd = static_cast<size_t>(N) * dim;
+    const WavePlan P0 = plan(B, N, M, 0);
+    const int dp = weight_store(B, N, M) ? fused_dp(dim, bary, X) : 0;
+    cudaError_t e;
+    if (dp && grad_small_supported(P0, dim)) {
+        // The forward and the gradient read the one barycenter for every
+        // problem (x batch stride 0); the costs are computed in the forward.
+        uint64_t* wrap = static_cast<uint64_t*>(workspace);
+        if ((rc = run_forward(nullptr, score, out, B, N, M, gamma, 0.f, wrap, st, true, nullptr, bary, X, dim, dp,
+                              true)))
+            return rc;
+        const size_t w0 = wave_ws_xy(B, N, M, dim);
+        float* Ew = reinterpret_cast<float*>(ws + w0);
+        if ((rc = run_backward(score, w, Ew, B, N, M, 0.f, wrap, st, true))) return rc;
+        {
+            KernelTimer kt("grad_xy", st);
+            e = launch_grad_small(Ew, nullptr, bary, X, gx, nullptr, reinterpret_cast<float*>(ws + w0 + wl_bytes(B, N, M)),
+                                  P0, dim, st, 0);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+    } else {
+        // General path: the barycenter broadcast to every problem, then the
+        // x/y pair.
+        float* xb = reinterpret_cast<float*>(ws + L.xb);
+        {
+            KernelTimer kt("bary_broadcast", st);
+            e = launch_bary_broadcast(bary, xb, B, nd, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "broadcast launch");
+        if ((rc = sdtw_forward_xy_f32(xb, X, score, out, B, N, M, dim, gamma, 0.f, workspace, workspace_bytes, stream)))
+            return rc;
+        if ((rc = backward_xy_common(xb, X, score, nullptr, w, gx, nullptr, B, N, M, dim, 0.f, workspace, st))) return rc;
+    }
+    {
+        KernelTimer kt("bary_reduce", st, 2);
+        e = launch_bary_reduce(gx, w, out, part, grad_loss, B, nd, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "reduce launch");
+    return SDTW_OK;
+}
+
+int sdtw_barycenter_adam_f32(float* bary, float* exp_avg, float* exp_avg_sq, const float* grad_loss, size_t n,
+                             const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
+                             float beta1, float beta2, float eps, float max_norm, void* stream) {
+    int rc;
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    if (!bary || !exp_avg || !exp_avg_sq || !grad_loss || !lr_table || !step || !loss_hist || !bary_hist)
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (n == 0 || max_iter <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "n and max_iter must be > 0");
+    if (!(beta1 >= 0.f && beta1 < 1.f) || !(beta2 >= 0.f && beta2 < 1.f) || !(eps >= 0.f) || !(max_norm > 0.f))
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "need 0 <= beta1, beta2 < 1, eps >= 0 and max_norm > 0");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        KernelTimer kt("bary_adam", st);
+        e = launch_bary_adam(bary, exp_avg, exp_avg_sq, grad_loss, n, lr_table, max_iter, step, loss_hist, bary_hist,
+                             beta1, beta2, eps, max_norm, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "adam launch");
+    return SDTW_OK;
 }
 
 int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, float* cost, float* out, int B, int N,

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
                                                                       const float* __restrict__ y,
                                                                       float* __restrict__ gx,
                                                                       float* __restrict__ part, WavePlan P, int dim,
-                                                                      int n_split) {
+                                                                      int n_split, size_t xbs) {
     extern __shared__ __align__(16) float sm[];
     const int warps = blockDim.x >> 5;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
     float* red = sm + warps * (SmallSmem<DP>::E + SmallSmem<DP>::X);
     float* Yt = red + warps * SmallSmem<DP>::RED;
     const int N = P.N, M = P.M;
-    const int b = blockIdx.y, split = blockIdx.x;
+    const int b = blockIdx.y, split = blockIdx.x;  // problem, split of 8 stripes
     const int s = split * warps + warp;
     const bool live = s < P.n_stripes;  // warp-uniform
     const int R0 = s * 32;
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
 #pragma unroll
     for (int d = 0; d < DP; ++d)
         Xt[lane * DP + d] =
-            (live && R0 + lane < N && d < dim) ? __ldg(x + (static_cast<size_t>(b) * N + R0 + lane) * dim + d) : 0.f;
+            (live && R0 + lane < N && d < dim) ? __ldg(x + b * xbs + static_cast<size_t>(R0 + lane) * dim + d) : 0.f;
     float racc[DP + 1];  // row R0 + lane: sum_j G y_j (DP), sum_j G
 #pragma unroll
     for (int d = 0; d <= DP; ++d) racc[d] = 0.f;
@@ -187,7 +187,7 @@ size_t grad_small_part_bytes(const WavePlan& P, int dim) {
 
 template <int DP>
 static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
-                            float* part, const WavePlan& P, int dim, cudaStream_t st) {
+                            float* part, const WavePlan& P, int dim, cudaStream_t st, size_t xbs) {
     const int n_split = grad_small_splits(P);
     const int warps = small_warps(P);
     const size_t smem = static_cast<size_t>(SmallSmem<DP>::floats(warps)) * sizeof(float);
@@ -197,9 +197,9 @@ static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, co
     const dim3 grid(n_split, P.B);
     float* pp = gy ? part : nullptr;
     if (Mw)
-        grad_small_kernel<DP, true><<<grid, 32 * warps, smem, st>>>(Ew, Mw, x, y, gx, pp, P, dim, n_split);
+        grad_small_kernel<DP, true><<<grid, 32 * warps, smem, st>>>(Ew, Mw, x, y, gx, pp, P, dim, n_split, xbs);
     else
-        grad_small_kernel<DP, false><<<grid, 32 * warps, smem, st>>>(Ew, Mw, x, y, gx, pp, P, dim, n_split);
+        grad_small_kernel<DP, false><<<grid, 32 * warps, smem, st>>>(Ew, Mw, x, y, gx, pp, P, dim, n_split, xbs);
     e = cudaGetLastError();
     if (e != cudaSuccess || !gy) return e;
     const size_t n = static_cast<size_t>(P.B) * P.M * dim;
@@ -209,13 +209,13 @@ static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, co
 }
 
 cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
-                              float* part, const WavePlan& P, int dim, cudaStream_t st) {
+                              float* part, const WavePlan& P, int dim, cudaStream_t st, size_t xbs) {
     if (!grad_small_supported(P, dim)) return cudaErrorInvalidValue;
     if (!gx && !gy) return cudaSuccess;
     switch (small_dp(dim)) {
-        case 4: return go_small<4>(Ew, Mw, x, y, gx, gy, part, P, dim, st);
-        case 8: return go_small<8>(Ew, Mw, x, y, gx, gy, part, P, dim, st);
-        default: return go_small<16>(Ew, Mw, x, y, gx, gy, part, P, dim, st);
+        case 4: return go_small<4>(Ew, Mw, x, y, gx, gy, part, P, dim, st, xbs);
+        case 8: return go_small<8>(Ew, Mw, x, y, gx, gy, part, P, dim, st, xbs);
+        default: return go_small<16>(Ew, Mw, x, y, gx, gy, part, P, dim, st, xbs);
     }
 }
 

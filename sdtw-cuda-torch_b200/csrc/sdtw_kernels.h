@@ -32,6 +32,7 @@ struct FwdArgs {
     const float* y;
     int dim;
     int dp;           // 0: costs from Dw; else the feature padding (fused_dp)
+    size_t x_bstride;  // floats between problems' x (N * dim; 0 = one x for every problem)
     WaitCtx wait;
 };
 
@@ -138,8 +139,23 @@ cudaError_t launch_grad_rm(const GradTcArgs& args, cudaStream_t stream);
 // per-split column sums (needed when gy is set).
 bool grad_small_supported(const WavePlan& P, int dim);
 size_t grad_small_part_bytes(const WavePlan& P, int dim);
+// x_bstride: floats between problems' x (N * dim; 0 = one x shared by all).
 cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
-                              float* part, const WavePlan& P, int dim, cudaStream_t st);
+                              float* part, const WavePlan& P, int dim, cudaStream_t st, size_t x_bstride);
+// barycenter.cu: the reductions and the optimiser step of the barycenter loop.
+//   bary_broadcast: xb[b] = bary for every problem b (materialised x).
+//   bary_reduce: grad_loss[v] = sum_b gx[b, v] (v < n), grad_loss[n] =
+//     sum_b w[b] * out[b], in a fixed order (two kernels, `part` holds
+//     bary_reduce_part_floats).
+//   bary_adam: clip the gradient to norm max_norm, one Adam step with the
+//     learning rate lr_table[*step], record loss and barycenter, ++*step.
+cudaError_t launch_bary_broadcast(const float* bary, float* xb, int B, size_t n, cudaStream_t st);
+size_t bary_reduce_part_floats(int B, size_t n);
+cudaError_t launch_bary_reduce(const float* gx, const float* w, const float* out, float* part, float* grad_loss, int B,
+                               size_t n, cudaStream_t st);
+cudaError_t launch_bary_adam(float* bary, float* exp_avg, float* exp_avg_sq, const float* grad_loss, size_t n,
+                             const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
+                             float beta1, float beta2, float eps, float max_norm, cudaStream_t st);
 // tcgemm.cu: the unfused (expanded, clamped) cost on the tensor cores, written
 // in the wavefront layout.  Requires dim >= 16, dim % 4 == 0 and 16-byte
 // aligned x, y (cost_tc_supported).

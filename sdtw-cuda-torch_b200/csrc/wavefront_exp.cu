@@ -48,10 +48,10 @@
 // bands).  Steps run in groups of 8: per group the consumer checks the 8 ring
 // slots it needs with one warp-wide load and a vote, the producer checks flow
 // control once and publishes the stripe's bottom row for the group's 8
-// columns with one warp-wide store, the cost rows of the group after next are
-// copied into shared memory (cp.async), and the group's table rows leave as
-// one bulk copy (cp.async.bulk).  Groups whose cells all lie inside the table
-// run without masks.
+// columns with one warp-wide store, the inputs of the group after next are
+// copied into shared memory (cp.async), and every step's table row leaves as
+// one coalesced 128- or 256-byte store.  Groups whose cells all lie inside the
+// table run without masks.
 #include <type_traits>
 
 #include "sdtw_device.cuh"
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(512, DP >= 8 ? 1 : 2) fwdx_kernel(const FwdArg
             unsigned long long xq[DP > 0 ? DP / 2 : 1];
             if constexpr (DP > 0) {
                 float xv[DP];
-                const float* xr = a.x + (static_cast<size_t>(b) * N + R0 + lane) * D;
+                const float* xr = a.x + static_cast<size_t>(b) * a.x_bstride + static_cast<size_t>(R0 + lane) * D;
 #pragma unroll
                 for (int f = 0; f < DP; ++f) xv[f] = (lane < rows_left && f < D) ? __ldg(xr + f) : 0.f;
 #pragma unroll

@@ -18,7 +18,7 @@ CSRC = os.path.join(ROOT, "csrc")
 LIB_DIR = os.path.join(PKG, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libsdtw_b200.so")
 
-SOURCES = ["capi.cu", "wavefront.cu", "wavefront_exp.cu", "layout.cu", "dense.cu", "tcgemm.cu", "grad_small.cu", "f64.cu", "cpu.cpp"]
+SOURCES = ["capi.cu", "wavefront.cu", "wavefront_exp.cu", "layout.cu", "dense.cu", "tcgemm.cu", "grad_small.cu", "barycenter.cu", "f64.cu", "cpu.cpp"]
 HEADERS = ["sdtw_device.cuh", "sdtw_kernels.h", "sdtw_plan.h", "wavefront_ring.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

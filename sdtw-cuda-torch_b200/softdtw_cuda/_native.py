@@ -55,6 +55,9 @@ _SIGS = {
     "sdtw_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
     "sdtw_backward_f64": ([_P, _P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
     "sdtw_cost_sqeuclid_f64": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "sdtw_barycenter_workspace_bytes": ([_I, _I, _I, _I], _SZ),
+    "sdtw_barycenter_grad_f32": ([_P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _SZ, _P], _I),
+    "sdtw_barycenter_adam_f32": ([_P, _P, _P, _P, _SZ, _P, _I, _P, _P, _P, _F, _F, _F, _F, _P], _I),
     "sdtw_cpu_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
     "sdtw_cpu_backward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
 }
@@ -208,6 +211,44 @@ def _f32(t: torch.Tensor) -> torch.Tensor:
 
 
 # ----------------------------------------------------------------------------- CUDA ops
+def barycenter_workspace(B: int, N: int, M: int, dim: int, device) -> torch.Tensor:
+    n = lib().sdtw_barycenter_workspace_bytes(B, N, M, dim)
+    return torch.empty(max(int(n), 256), dtype=torch.uint8, device=device)
+
+
+def barycenter_grad(bary: torch.Tensor, X: torch.Tensor, w: torch.Tensor, grad_loss: torch.Tensor, gamma: float,
+                    ws: torch.Tensor) -> None:
+    """grad_loss (N*D + 1,) <- [sum_b w_b dSoftDTW(bary, X_b)/dbary | sum_b w_b SoftDTW(bary, X_b)].
+    All operands contiguous float32 on one device (not copied: the call can
+    be captured in a CUDA graph)."""
+    B, M, dim = X.shape
+    N = bary.shape[0]
+    for t in (bary, X, w, grad_loss):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.device != X.device:
+            raise ValueError("barycenter_grad: operands must be contiguous float32 tensors on one device")
+    if bary.shape != (N, dim) or w.shape != (B,) or grad_loss.numel() != N * dim + 1:
+        raise ValueError("barycenter_grad: shape mismatch")
+    with torch.cuda.device(X.device):
+        rc = lib().sdtw_barycenter_grad_f32(_ptr(bary), _ptr(X), _ptr(w), _ptr(grad_loss), B, N, M, dim,
+                                            float(gamma), _ptr(ws), ws.numel(), _stream(X.device))
+    _check(rc, "barycenter gradient")
+
+
+def barycenter_adam(bary, exp_avg, exp_avg_sq, grad_loss, lr_table, step, loss_hist, bary_hist,
+                    beta1=0.9, beta2=0.999, eps=1e-8, max_norm=1.0) -> None:
+    """Clip grad_loss[:n] to max_norm, one Adam step on bary with lr_table[step],
+    record the loss and the new bary at index step, step += 1 (all on the device)."""
+    n = bary.numel()
+    if step.dtype != torch.int32:
+        raise ValueError("barycenter_adam: step must be an int32 tensor")
+    with torch.cuda.device(bary.device):
+        rc = lib().sdtw_barycenter_adam_f32(_ptr(bary), _ptr(exp_avg), _ptr(exp_avg_sq), _ptr(grad_loss), n,
+                                            _ptr(lr_table), lr_table.numel(), _ptr(step), _ptr(loss_hist),
+                                            _ptr(bary_hist), float(beta1), float(beta2), float(eps), float(max_norm),
+                                            _stream(bary.device))
+    _check(rc, "barycenter Adam step")
+
+
 def cost_sqeuclid(x: torch.Tensor, y: torch.Tensor, direct: bool = False) -> torch.Tensor:
     x = _f32(x)
     y = _f32(y)

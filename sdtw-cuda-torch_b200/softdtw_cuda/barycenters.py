@@ -9,10 +9,14 @@ progress messages follow the reference.  The multi-GPU version is
 
 On CUDA the loop runs as one CUDA graph of one iteration, replayed
 (barycenters.py:114-158 of the reference is a host loop with a device sync per
-step): Soft-DTW forward and backward, the weighted loss, gradient clipping, a
-capturable Adam step with the learning rate read from a precomputed
-cosine-annealing table indexed by a device iteration counter, and copies of the
-loss and of the barycenter into per-iteration history buffers.  The host reads
+step): Soft-DTW forward and backward, the weighted loss, gradient clipping, an
+Adam step with the learning rate read from a precomputed cosine-annealing table
+indexed by a device iteration counter, and copies of the loss and of the
+barycenter into per-iteration history buffers.  For float32 sequences and the
+fused cost the iteration is the library's: the wavefronts read the one
+barycenter for every sequence, the gradient and the loss are reduced over the
+sequences on the device, and clipping, Adam and the histories are one kernel
+(``_native.barycenter_grad`` / ``_native.barycenter_adam``).  The host reads
 the loss history back asynchronously every few replays, applies the early-stop
 rule to it, and returns the barycenter of the stopping iteration from the
 history, so the result is the one the step-by-step loop returns.
@@ -79,14 +83,22 @@ def _early_stop_at(losses, max_iter, patience, tol):
 class _BaryGraph:
     """One captured Adam iteration and the state it reads and writes.
 
-    X (B, N, D) is read in place; the weights, the starting point, the Adam
-    state, the iteration counter and the histories are persistent tensors that
-    ``run`` resets before replaying.  ``reduce``, if given, is called on the
-    contiguous [gradient (N*D) | loss] buffer inside the iteration (the
-    sharded barycenter's all-reduce); clipping and Adam follow it."""
+    X (B, M, D) is read in place; the weights, the starting point (N, D), the
+    Adam state, the iteration counter and the histories are persistent tensors
+    that ``run`` resets before replaying.  ``reduce``, if given, is called on
+    the contiguous [gradient (N*D) | loss] buffer inside the iteration (the
+    sharded barycenter's all-reduce); clipping and Adam follow it.
 
-    def __init__(self, X, gamma, fused, max_iter, lr, reduce):
-        B, N, Dm = X.shape
+    float32 with the fused cost (fused None or True) runs the library's
+    barycenter entry points: the loss and gradient with the barycenter read
+    once for all sequences and reduced over them on the device
+    (``_native.barycenter_grad``), then clipping, Adam and the histories in
+    one kernel (``_native.barycenter_adam``) -- a handful of launches per
+    iteration.  Other configurations capture the torch loop body
+    (SoftDTW module, autograd, clip_grad_norm_, capturable Adam)."""
+
+    def __init__(self, X, N, gamma, fused, max_iter, lr, reduce):
+        B, M, Dm = X.shape
         dev = X.device
         self.B, self.N, self.D, self.max_iter = B, N, Dm, max_iter
         self.X = X  # held so that its memory is not reused while the graph reads it
@@ -95,13 +107,56 @@ class _BaryGraph:
         self.w = torch.zeros(B, dtype=X.dtype, device=dev)
         self.bary0 = torch.zeros((N, Dm), dtype=X.dtype, device=dev)
         self.lr_table = torch.tensor(self.lrs[:max_iter], dtype=torch.float32, device=dev)
-        self.lr_t = self.lr_table[0].clone()
-        self.it_t = torch.zeros(1, dtype=torch.long, device=dev)
         self.loss_hist = torch.zeros(max_iter, dtype=X.dtype, device=dev)
         self.bary_hist = torch.zeros((max_iter, N, Dm), dtype=X.dtype, device=dev)
+        self.host_losses = torch.empty(max_iter, dtype=X.dtype, pin_memory=True)
+        self.buf = torch.zeros(N * Dm + 1, dtype=X.dtype, device=dev)
+        self.native = fused is not False and X.dtype == torch.float32 and X.is_contiguous()
+        if self.native:
+            body = self._native_body(X, gamma, reduce)
+        else:
+            body = self._torch_body(X, gamma, fused, reduce)
+
+        # Warm up on a side stream (allocator, workspaces, the optimizer's
+        # state, the communicator), then capture one iteration.
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self._reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            body()
+
+    def _native_body(self, X, gamma, reduce):
+        B, N, Dm, dev = self.B, self.N, self.D, X.device
+        self.bary = torch.zeros((N, Dm), dtype=torch.float32, device=dev)
+        self.exp_avg = torch.zeros_like(self.bary)
+        self.exp_avg_sq = torch.zeros_like(self.bary)
+        self.step = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ws = _native.barycenter_workspace(B, N, X.shape[1], Dm, dev) if B > 0 else None
+        bary, buf, w, ws = self.bary, self.buf, self.w, self.ws
+
+        def body():
+            if B > 0:
+                _native.barycenter_grad(bary, X, w, buf, gamma, ws)
+            else:
+                buf.zero_()
+            if reduce is not None:
+                reduce(buf)
+            _native.barycenter_adam(bary, self.exp_avg, self.exp_avg_sq, buf, self.lr_table, self.step,
+                                    self.loss_hist, self.bary_hist)
+
+        return body
+
+    def _torch_body(self, X, gamma, fused, reduce):
+        B, N, Dm, dev = self.B, self.N, self.D, X.device
+        self.lr_t = self.lr_table[0].clone()
+        self.it_t = torch.zeros(1, dtype=torch.long, device=dev)
         self.bary = torch.zeros((N, Dm), dtype=X.dtype, device=dev, requires_grad=True)
         self.bary.grad = torch.zeros_like(self.bary)
-        self.buf = torch.zeros(N * Dm + 1, dtype=X.dtype, device=dev)
         self.opt = torch.optim.Adam([self.bary], lr=self.lr_t, capturable=True)
         loss_fn = SoftDTW(gamma=gamma, normalize=False, fused=fused)
         bary, w, buf, opt = self.bary, self.w, self.buf, self.opt
@@ -131,22 +186,16 @@ class _BaryGraph:
             self.bary_hist.index_copy_(0, self.it_t, bary.detach().unsqueeze(0))
             self.it_t.add_(1)
 
-        # Warm up on a side stream (allocator, workspaces, the optimizer's
-        # state, the communicator), then capture one iteration.
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                body()
-        torch.cuda.current_stream(dev).wait_stream(side)
-        self._reset()
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            body()
+        return body
 
     def _reset(self):
         with torch.no_grad():
             self.bary.copy_(self.bary0)
+            if self.native:
+                self.exp_avg.zero_()
+                self.exp_avg_sq.zero_()
+                self.step.zero_()
+                return
             self.bary.grad.zero_()
             self.it_t.zero_()
             for st in self.opt.state[self.bary].values():
@@ -159,7 +208,7 @@ class _BaryGraph:
             self.w.copy_(w)
             self.bary0.copy_(bary0)
         self._reset()
-        host_losses = torch.empty(max_iter, dtype=self.loss_hist.dtype, pin_memory=True)
+        host_losses = self.host_losses
         done = 0
         stop = None
         while done < max_iter and stop is None:
@@ -197,12 +246,13 @@ def _graph_barycenter(X, w, bary0, gamma, fused, max_iter, lr, early_stopping, p
     """The loop as a replayed CUDA graph (see the module docstring), captured
     once per configuration.  ``stats``, if a dict, receives the number of
     iterations run and whether this call captured the graph."""
-    key = (X.device.index, X.data_ptr(), tuple(X.shape), X.dtype, float(gamma), fused, int(max_iter), float(lr),
+    N = bary0.shape[0]
+    key = (X.device.index, X.data_ptr(), tuple(X.shape), X.dtype, N, float(gamma), fused, int(max_iter), float(lr),
            reduce_key)
     g = _graphs.pop(key, None)
     captured = g is None
     if captured:
-        g = _BaryGraph(X, gamma, fused, max_iter, lr, reduce)
+        g = _BaryGraph(X, N, gamma, fused, max_iter, lr, reduce)
         while len(_graphs) >= _GRAPH_CACHE_SIZE:
             _graphs.pop(next(iter(_graphs)))
     _graphs[key] = g  # newest last

@@ -21,7 +21,10 @@ is single-device; these functions are new and keep its single-device results:
   max_iter // 2 on the global loss).  On CUDA one iteration, all-reduce
   included, is captured in a CUDA graph and replayed (barycenters.py's graph
   engine), so a step costs no host launch overhead; every rank captures and
-  replays the same collective sequence.
+  replays the same collective sequence.  The cached graphs hold captured NCCL
+  calls: call ``release_graphs()`` (after a device synchronize) before
+  ``torch.distributed.destroy_process_group()``, whose teardown otherwise waits
+  on them.
 """
 from __future__ import annotations
 
@@ -103,6 +106,13 @@ class ShardedSoftDTW(torch.nn.Module):
         if x.shape[0] == 0:
             return (x.sum() + y.sum()) * 0.0
         return sharded_mean(self.loss(x, y), n)
+
+
+def release_graphs() -> None:
+    """Release the cached barycenter graphs (and the NCCL calls captured in
+    them); to be called before destroying the process group."""
+    from . import barycenters as _bc
+    _bc.clear_graph_cache()
 
 
 def sharded_barycenter(

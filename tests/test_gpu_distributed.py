@@ -40,23 +40,26 @@ def _worker(rank, world, port, out_dir, early):
     try:
         X, w = _data(20, 48, 3, seed=11)
         lo, hi = shard_bounds(X.shape[0], rank, world)
+        Xr, wr = X[lo:hi].to(dev), w[lo:hi].to(dev)
         kw = dict(gamma=1.0, max_iter=40, lr=0.1, early_stopping=early, patience=3, tol=1e-2)
         res = {}
         for graph in (True, False):
             bc.USE_CUDA_GRAPH = graph
             stats = {}
-            b = sharded_barycenter(X[lo:hi].to(dev), weights=w[lo:hi].to(dev), stats=stats, **kw)
+            b = sharded_barycenter(Xr, weights=wr, stats=stats, **kw)
             torch.cuda.synchronize(dev)
             res[graph] = (b.cpu(), stats["iterations"], bool(stats.get("graph")))
         bc.USE_CUDA_GRAPH = True
-        # A second graph call replays the cached graph.
+        # A second graph call on the same sequences replays the cached graph.
         stats = {}
-        b2 = sharded_barycenter(X[lo:hi].to(dev), weights=w[lo:hi].to(dev), stats=stats, **kw)
+        b2 = sharded_barycenter(Xr, weights=wr, stats=stats, **kw)
         torch.cuda.synchronize(dev)
         res["replay"] = (b2.cpu(), stats["iterations"], stats.get("captured"))
-        bc.clear_graph_cache()
         torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
+        # Graphs holding captured NCCL calls go before the process group.
+        torch.cuda.synchronize(dev)
+        bc.clear_graph_cache()
         dist.destroy_process_group()
 
 
