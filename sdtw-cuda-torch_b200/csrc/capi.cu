@@ -433,6 +433,37 @@ int run_backward(const float* score, const float* grad_out, float* Ew, int B, in
     return SDTW_OK;
 }
 
+// The reverse pass that applies the squared-Euclidean chain rule for grad_x
+// itself (no E table), see bwdw_kernel.
+int run_backward_grad(const float* score, const float* grad_out, int B, int N, int M, uint64_t* wrap,
+                      cudaStream_t stream, const float* x, size_t x_bstride, const float* y, int dim, int gd, float* gx) {
+    BwdArgs a{};
+    a.P = plan(B, N, M, 64 + gd);
+    a.weights = 1;
+    a.score = reinterpret_cast<const float2*>(score);
+    a.grad_out = grad_out;
+    a.wrap = wrap;
+    a.bw = -1.f;
+    a.ibw = int_band(0.f);
+    a.seq = g_seq.fetch_add(1);
+    a.debug_stall = g_debug_stall.load();
+    a.wait = wait_ctx();
+    a.x = x;
+    a.y = y;
+    a.dim = dim;
+    a.gd = gd;
+    a.x_bstride = x_bstride;
+    a.gx = gx;
+    cudaError_t e = reset_wrap(a.P, wrap, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(band-wrap ring)");
+    {
+        KernelTimer kt("wavefront_bwd", stream);
+        e = launch_backward(a, stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+    return SDTW_OK;
+}
+
 int check_common(int B, int N, int M, float gamma) {
     int rc;
     if ((rc = check_dims(B, N, M)) || (rc = check_gamma(gamma))) return rc;
@@ -772,6 +803,14 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
                        cudaStream_t st) {
     const size_t w0 = wave_ws_xy(B, N, M, dim);
     float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
+    // Only grad_x, fused cost, up to 16 features, no band: the reverse pass
+    // applies the chain rule as it goes and E never reaches memory.
+    const int gd = (!mask_w && grad_x && !grad_y && weight_store(B, N, M) && int_band(bandwidth) >= N + M)
+                       ? grad_fused_gd(dim, y)
+                       : 0;
+    if (gd)
+        return run_backward_grad(score, grad_out, B, N, M, static_cast<uint64_t*>(workspace), st, x,
+                                 static_cast<size_t>(N) * dim, y, dim, gd, grad_x);
     int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st,
                           weight_store(B, N, M));
     if (rc) return rc;
@@ -908,25 +947,17 @@ int sdtw_barycenter_grad_f32(const float* bary, const float* X, const float* w, 
     float* part = reinterpret_cast<float*>(ws + L.part);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t nd = static_cast<size_t>(N) * dim;
-    const WavePlan P0 = plan(B, N, M, 0);
     const int dp = weight_store(B, N, M) ? fused_dp(dim, bary, X) : 0;
     cudaError_t e;
-    if (dp && grad_small_supported(P0, dim)) {
+    if (dp && grad_fused_gd(dim, X) == dp) {
         // The forward and the gradient read the one barycenter for every
         // problem (x batch stride 0); the costs are computed in the forward.
         uint64_t* wrap = static_cast<uint64_t*>(workspace);
         if ((rc = run_forward(nullptr, score, out, B, N, M, gamma, 0.f, wrap, st, true, nullptr, bary, X, dim, dp,
                               true)))
             return rc;
-        const size_t w0 = wave_ws_xy(B, N, M, dim);
-        float* Ew = reinterpret_cast<float*>(ws + w0);
-        if ((rc = run_backward(score, w, Ew, B, N, M, 0.f, wrap, st, true))) return rc;
-        {
-            KernelTimer kt("grad_xy", st);
-            e = launch_grad_small(Ew, nullptr, bary, X, gx, nullptr, reinterpret_cast<float*>(ws + w0 + wl_bytes(B, N, M)),
-                                  P0, dim, st, 0);
-        }
-        if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+        // grad_x of every problem straight from the reverse pass.
+        if ((rc = run_backward_grad(score, w, B, N, M, wrap, st, bary, 0, X, dim, dp, gx))) return rc;
     } else {
         // General path: the barycenter broadcast to every problem, then the
         // x/y pair.

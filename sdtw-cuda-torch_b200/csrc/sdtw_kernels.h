@@ -47,6 +47,15 @@ struct BwdArgs {
     uint32_t seq;
     int debug_stall;
     int weights;  // nonzero: `score` holds the forward's predecessor weights (one row per lane)
+    // grad_x in the reverse pass (gd > 0; the fused cost, weight store, no
+    // band): E is not stored; each lane accumulates its row's sum_j E y_j and
+    // sum_j E and writes grad_x.
+    const float* x;
+    const float* y;
+    int dim;
+    int gd;             // features padded to 4, 8 or 16; 0 = store E
+    size_t x_bstride;   // floats between problems' x (N * dim; 0 = one x for all)
+    float* gx;          // (B,N,dim) grad_x
     WaitCtx wait;
 };
 
@@ -59,10 +68,13 @@ cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream);
 size_t fwdx_smem(const WavePlan& P, int dp);
 int fwdx_threads(const WavePlan& P);
 int fused_dp(int dim, const float* x, const float* y);
-size_t bwdw_smem(const WavePlan& P);
+size_t bwdw_smem(const WavePlan& P, int gd = 0);
 const void* fwdx_fn(bool banded, bool weights, int dp);
-const void* bwdw_fn(bool banded);
-// pass: 0 forward with costs from a table, 1 reverse pass, 2 + dp the fused forward.
+const void* bwdw_fn(bool banded, int gd = 0);
+// Feature padding of the reverse pass with grad_x (4, 8, 16), or 0.
+int grad_fused_gd(int dim, const float* y);
+// pass: 0 forward with costs from a table, 1 reverse pass, 2 + dp the fused
+// forward, 64 + gd the reverse pass with grad_x.
 int max_active_clusters(const WavePlan& P, int pass);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);
@@ -142,6 +154,7 @@ size_t grad_small_part_bytes(const WavePlan& P, int dim);
 // x_bstride: floats between problems' x (N * dim; 0 = one x shared by all).
 cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
                               float* part, const WavePlan& P, int dim, cudaStream_t st, size_t x_bstride);
+
 // barycenter.cu: the reductions and the optimiser step of the barycenter loop.
 //   bary_broadcast: xb[b] = bary for every problem b (materialised x).
 //   bary_reduce: grad_loss[v] = sum_b gx[b, v] (v < n), grad_loss[n] =

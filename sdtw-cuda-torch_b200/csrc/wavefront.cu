@@ -947,6 +947,9 @@ int max_active_clusters(const WavePlan& P, int pass) {
                 fns[2] = fwdx_fn(false, true, 0);
                 smem[2] = fwdx_smem(P, 0);
                 threads[2] = fwdx_threads(P);
+            } else if (pass >= 64) {
+                fns[0] = bwdw_fn(false, pass - 64);
+                smem[0] = bwdw_smem(P, pass - 64);
             } else if (pass >= 2) {
                 fns[0] = fwdx_fn(false, true, pass - 2);
                 smem[0] = fwdx_smem(P, pass - 2);

@@ -673,8 +673,14 @@ __host__ __device__ constexpr size_t bw_w_off(int wpc) {
 __host__ __device__ constexpr size_t bw_stash_off(int wpc) {
     return bw_w_off(wpc) + static_cast<size_t>(wpc) * 3 * kPF * 32 * 8;
 }
-__host__ __device__ constexpr size_t bw_smem_bytes(int wpc) {
+// With grad_x (gd > 0) per warp also a window of y rows [kYRows][y_pitch(gd)]
+// (ring of segments of PF rows, cp.async two groups ahead, like the fused
+// forward's).
+__host__ __device__ constexpr size_t bw_ywin_off(int wpc) {
     return bw_stash_off(wpc) + static_cast<size_t>(wpc) * kPF * 4;
+}
+__host__ __device__ constexpr size_t bw_smem_bytes(int wpc, int gd = 0) {
+    return bw_ywin_off(wpc) + (gd == 0 ? 0 : static_cast<size_t>(wpc) * kYRows * y_pitch(gd) * 4);
 }
 
 // Reverse wavefront over the forward's shares.  At reverse step t the lane of
@@ -683,10 +689,21 @@ __host__ __device__ constexpr size_t bw_smem_bytes(int wpc) {
 //     + message from the row below: E(q+1, j) * upper share of (q+1, j)
 //                                  + E(q+1, j+1) * diagonal share of (q+1, j+1)
 // E(N-1, M-1) = grad_out[b] (autograd.py:46-47 multiplies it in).
-template <bool BANDED>
-__global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
+//
+// GD > 0 (grad_x only): the squared-Euclidean chain rule (autograd_xy.py:41-49)
+// is applied as E is produced, and E is not stored.  Lane q (row i = R0 + q)
+// keeps sum_j E_ij and sum_j E_ij y_j (y_j from the warp's y window) and
+// writes grad_x[i] = 2 (x_i sum_j E_ij - sum_j E_ij y_j) at the end of its
+// stripe.  (grad_y the same way -- column partials passed down the lanes by
+// shuffles, one per feature per step -- measured slower on B200 than the E
+// table and grad_small: C3 reverse pass 1.42 -> 2.96 ms against a 0.79 ms
+// gradient kernel; the extra shuffles delay the chain's own.)
+template <bool BANDED, int GD>
+__global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kernel(const BwdArgs a) {
     constexpr int PF = kPF;
-    constexpr int NPH = kBwdPhases;
+    constexpr int NPH = GD > 0 ? 1 : kBwdPhases;
+    constexpr int YP = y_pitch(GD > 0 ? GD : 4);
+    static_assert(GD == 0 || !BANDED, "the gradient mode runs without a band");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
     const int wpc = P.wpc;
@@ -702,8 +719,15 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
     const float2* wbuf = reinterpret_cast<const float2*>(smem_raw + bw_w_off(wpc)) + warp * 3 * PF * 32;
     const uint32_t wbuf_s = smem_addr(wbuf);
     float* pub_s = reinterpret_cast<float*>(smem_raw + bw_stash_off(wpc)) + warp * PF;
+    float* ywin = reinterpret_cast<float*>(smem_raw + bw_ywin_off(wpc)) + warp * kYRows * YP;
     for (int i = threadIdx.x; i < wpc * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
+    if constexpr (GD > 0) {
+        // Window rows that are never copied (outside y) stay finite: they meet
+        // only cells with E = 0.
+        float* yw_all = reinterpret_cast<float*>(smem_raw + bw_ywin_off(wpc));
+        for (int i = threadIdx.x; i < wpc * kYRows * YP; i += blockDim.x) yw_all[i] = 0.f;
+    }
     cluster_sync_all();
 
     // Messages flow upward: this warp's input comes from warp g+1 (the stripe
@@ -766,14 +790,53 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
         if (t_top < t_last)
             st_relaxed_cluster_u32_if(has_below && !below_wrap && lane == 31, below_consumed,
                                       band_base + static_cast<uint32_t>(max(0, M - 1 - max(t_top - 31, -1))));
+        const int rows_left = N - R0;
+        const bool full_rows = rows_left >= 32;
+        // ---- gradient mode: the row accumulators.
+        const int D = a.dim;
+        float racc[GD > 0 ? GD : 1], rsum = 0.f;  // row: sum_j E y_j, sum_j E
+#pragma unroll
+        for (int f = 0; f < (GD > 0 ? GD : 1); ++f) racc[f] = 0.f;
+        const float* yb = GD > 0 ? a.y + static_cast<size_t>(b) * M * D : nullptr;
+        // y rows 8 seg .. 8 seg + 7 (those inside y) into window slot seg mod
+        // kYSeg: 16-byte copies, or 4-byte copies into padded rows for D < 4.
+        auto y_issue = [&](int seg) {
+            if constexpr (GD > 0) {
+                const int r0 = seg * PF;
+                const int nr = (seg >= 0) ? max(0, min(PF, M - r0)) : 0;
+                float* dst = ywin + (seg & (kYSeg - 1)) * PF * YP;
+                if (D < 4) {
+                    for (int e = lane; e < nr * D; e += 32) {
+                        const int r = e / D, f = e - r * D;
+                        cp_async4(smem_addr(dst + r * YP + f), yb + static_cast<size_t>(r0) * D + e);
+                    }
+                } else {
+                    const int cpr = D / 4;
+                    for (int e = lane; e < nr * cpr; e += 32) {
+                        const int r = e / cpr, k = e - r * cpr;
+                        cp_async16(smem_addr(dst + r * YP + 4 * k), yb + static_cast<size_t>(r0 + r) * D + 4 * k);
+                    }
+                }
+            }
+        };
         // Group gi's shares: rows t0 - PF + 1 .. t0 (t0 = t_last - gi * PF),
-        // or an empty commit past the last group.
+        // or an empty commit past the last group.  In the gradient mode the
+        // same commit carries the lowest y segment group gi reads (its cells
+        // read segments k - 4 .. k, k = n_groups - 1 - gi; the first commit
+        // carries all five).
         auto wcopy = [&](int gi) {
             if (gi < gi_end) {
                 const float2* src = Ts + static_cast<size_t>(t_last - gi * PF - PF + 1) * 32;
                 const uint32_t dst = wbuf_s + static_cast<uint32_t>((gi - gi_begin) % 3) * PF * 32 * 8u;
 #pragma unroll
                 for (int i = 0; i < PF * 32 / 64; ++i) cp_async16(dst + (lane + 32 * i) * 16u, src + (lane + 32 * i) * 2);
+                if constexpr (GD > 0) {
+                    const int k = n_groups - 1 - gi;
+                    if (gi == gi_begin)
+                        for (int sg = k; sg >= k - 4; --sg) y_issue(sg);
+                    else
+                        y_issue(k - 4);
+                }
             }
             cp_async_commit();
         };
@@ -781,8 +844,6 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
         wcopy(gi_begin + 1);
 
         float accl = 0.f, msg = 0.f, dprev = 0.f;
-        const int rows_left = N - R0;
-        const bool full_rows = rows_left >= 32;
         // Band-wrap input (global memory): the slots of the next group are
         // loaded one group ahead.
         uint64_t wpf = 0;
@@ -876,12 +937,26 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
                     e = (lane == rows_left - 1 && col == M - 1) ? gb : e;
                     e = live ? e : 0.f;
                 }
-                El[static_cast<size_t>(t) * 32] = e;  // one coalesced row store per step
                 const float dn = e * w.x;            // to the diagonal predecessor (two steps on)
                 msg = fmaf(e, w.y, dprev);           // to the row above: upper share + previous diagonal
                 accl = fmaf(-e, w.y, e - dn);        // left share: e * (1 - wd - wu)
                 dprev = dn;
                 if (lane == 0) pub_s[u] = msg;
+                if constexpr (GD == 0) {
+                    El[static_cast<size_t>(t) * 32] = e;  // one coalesced row store per step
+                } else {
+                    // Row: E y_j with y_j = window row t - lane.
+                    const float4* yr = reinterpret_cast<const float4*>(ywin + ((t - lane) & (kYRows - 1)) * YP);
+                    rsum += e;
+#pragma unroll
+                    for (int q = 0; q < GD / 4; ++q) {
+                        const float4 yv = yr[q];
+                        racc[4 * q + 0] = fmaf(e, yv.x, racc[4 * q + 0]);
+                        racc[4 * q + 1] = fmaf(e, yv.y, racc[4 * q + 1]);
+                        racc[4 * q + 2] = fmaf(e, yv.z, racc[4 * q + 2]);
+                        racc[4 * q + 3] = fmaf(e, yv.w, racc[4 * q + 3]);
+                    }
+                }
             }
             __syncwarp();
             // ---- messages of row 0 to the stripe above: lane u stores column t0 - u.
@@ -909,7 +984,9 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
         };
         for (int gi = gi_begin; gi < gi_end; gi += NPH) {
             run(P0{}, gi);
-            if (gi + 1 < gi_end) run(P1{}, gi + 1);
+            if constexpr (NPH == 2) {
+                if (gi + 1 < gi_end) run(P1{}, gi + 1);
+            }
             if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
@@ -918,9 +995,19 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
         // The band's copies are complete before the next band's first group.
         cp_async_wait<0>();
         __syncwarp();
-        // Rows outside the groups that ran (padding, or out of the band): zero.
-        for (int t = 0; t <= t_last - gi_end * PF; ++t) El[static_cast<size_t>(t) * 32] = 0.f;
-        for (int t = t_top + 1; t < P.n_diag; ++t) El[static_cast<size_t>(t) * 32] = 0.f;
+        if constexpr (GD == 0) {
+            // Rows outside the groups that ran (padding, or out of the band): zero.
+            for (int t = 0; t <= t_last - gi_end * PF; ++t) El[static_cast<size_t>(t) * 32] = 0.f;
+            for (int t = t_top + 1; t < P.n_diag; ++t) El[static_cast<size_t>(t) * 32] = 0.f;
+        } else {
+            if (lane < rows_left) {
+                const float* xr = a.x + static_cast<size_t>(b) * a.x_bstride + static_cast<size_t>(R0 + lane) * D;
+                float* go = a.gx + (static_cast<size_t>(b) * N + R0 + lane) * D;
+#pragma unroll
+                for (int f = 0; f < GD; ++f)
+                    if (f < D) go[f] = 2.f * (__ldg(xr + f) * rsum - racc[f]);
+            }
+        }
         if (__any_sync(SDTW_FULL_MASK, !ok)) quit = true;
     }
     cluster_sync_all();
@@ -929,7 +1016,7 @@ __global__ void __launch_bounds__(512) bwdw_kernel(const BwdArgs a) {
 // ------------------------------------------------------------------ launchers
 size_t fwdx_smem(const WavePlan& P, int dp) { return fx_smem_bytes(P.wpc, dp); }
 int fwdx_threads(const WavePlan& P) { return 2 * P.wpc * 32; }  // a chain warp and its helper per stripe
-size_t bwdw_smem(const WavePlan& P) { return bw_smem_bytes(P.wpc); }
+size_t bwdw_smem(const WavePlan& P, int gd) { return bw_smem_bytes(P.wpc, gd); }
 
 // dp: 0 = costs from a table; 4, 8, 16, 32, 64 = fused x/y costs with the
 // features padded to dp (the x/y entry points, which store the shares).
@@ -960,9 +1047,20 @@ int fused_dp(int dim, const float* x, const float* y) {
     while (dp < dim) dp *= 2;
     return dp;
 }
-const void* bwdw_fn(bool banded) {
-    return banded ? (const void*)bwdw_kernel<true> : (const void*)bwdw_kernel<false>;
+const void* bwdw_fn(bool banded, int gd) {
+    if (gd == 0) return banded ? (const void*)bwdw_kernel<true, 0> : (const void*)bwdw_kernel<false, 0>;
+    if (banded) return nullptr;
+    switch (gd) {
+        case 4: return (const void*)bwdw_kernel<false, 4>;
+        case 8: return (const void*)bwdw_kernel<false, 8>;
+        case 16: return (const void*)bwdw_kernel<false, 16>;
+        default: return nullptr;
+    }
 }
+// Feature padding of the reverse pass with gradients: as the fused forward's
+// (up to 16 features; more, or a count above 3 that is not a multiple of 4,
+// or y not 16-byte aligned: 0, E is stored and a gradient kernel follows).
+int grad_fused_gd(int dim, const float* y) { return fused_dp(dim, y, y); }
 
 cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
@@ -979,9 +1077,10 @@ cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
     if (P.K != 1 || !args.weights) return cudaErrorInvalidValue;
     const bool banded = args.ibw < P.N + P.M;
+    const void* fn = bwdw_fn(banded, args.gd);
+    if (!fn || (args.gd && (!args.x || !args.y || !args.gx || args.dim > args.gd))) return cudaErrorInvalidValue;
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
-    return launch_cluster(bwdw_fn(banded), dim3(P.B * P.csize), dim3(P.wpc * 32), bwdw_smem(P), P.csize, stream,
-                          kargs);
+    return launch_cluster(fn, dim3(P.B * P.csize), dim3(P.wpc * 32), bwdw_smem(P, args.gd), P.csize, stream, kargs);
 }
 
 }  // namespace sdtw
