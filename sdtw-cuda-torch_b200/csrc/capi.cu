@@ -312,17 +312,17 @@ WavePlan plan(int B, int N, int M, int pass) {
 // The band-wrap ring (needed when a pass's plan has more than one band; its
 // size does not depend on the plan) of the D-input passes, and of the x/y
 // passes (whose forward may compute its costs from x and y: plan 2 + dp).
+// The ring is sized whenever the problem has more than one stripe: every pass
+// and launch picks its own plan (forward, reverse pass, their variants), and
+// any of them may split the stripes into bands.
 size_t wave_ws(int B, int N, int M) {
-    return align_up(std::max(wrap_bytes(plan(B, N, M, 0)), wrap_bytes(plan(B, N, M, 1))), 256);
+    const int K = rows_per_lane(N, g_k_override.load());
+    const int stripes = (N + 32 * K - 1) / (32 * K);
+    return stripes > 1 ? align_up(static_cast<size_t>(B) * M * 16u, 256) : 0;
 }
 size_t wave_ws_xy(int B, int N, int M, int dim) {
-    size_t w = std::max(wrap_bytes(plan(B, N, M, 0)), wrap_bytes(plan(B, N, M, 1)));
-    if (rows_per_lane(N, g_k_override.load()) == 1 && (dim < 4 || (dim <= 16 && dim % 4 == 0))) {
-        int dp = 4;  // as fused_dp (alignment aside)
-        while (dp < dim) dp *= 2;
-        w = std::max(w, wrap_bytes(plan(B, N, M, 2 + dp)));
-    }
-    return align_up(w, 256);
+    (void)dim;
+    return wave_ws(B, N, M);
 }
 size_t wl_bytes(int B, int N, int M) { return align_up(wl_cells(B, N, M, g_k_override.load()) * sizeof(float), 256); }
 size_t pad32(int n) { return (static_cast<size_t>(n) + 31) & ~static_cast<size_t>(31); }
@@ -380,7 +380,17 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
                 const float* x = nullptr, const float* y = nullptr, int dim = 0, int dp = 0,
                 bool x_shared = false) {
     FwdArgs a{};
-    a.P = plan(B, N, M, dp ? 2 + dp : 0);
+    const int pass = dp ? 2 + dp : 0;
+    a.P = plan(B, N, M, pass);
+    // The 128-register forward when all of the launch's clusters fit at once
+    // at its occupancy (K = 1 only).
+    if (a.P.K == 1 && dp < 8) {
+        const WavePlan pw = plan(B, N, M, 32 + pass);
+        if (cached_cluster_fit(pw, 32 + pass) >= B) {
+            a.P = pw;
+            a.wide = 1;
+        }
+    }
     a.x = x;
     a.x_bstride = x_shared ? 0 : static_cast<size_t>(N) * dim;
     a.y = y;

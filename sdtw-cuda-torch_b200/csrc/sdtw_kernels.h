@@ -33,6 +33,7 @@ struct FwdArgs {
     int dim;
     int dp;           // 0: costs from Dw; else the feature padding (fused_dp)
     size_t x_bstride;  // floats between problems' x (N * dim; 0 = one x for every problem)
+    int wide;          // nonzero: the 128-register forward (fwdx_kernel WIDE), pass 32 + (its pass)
     WaitCtx wait;
 };
 
@@ -69,12 +70,13 @@ size_t fwdx_smem(const WavePlan& P, int dp);
 int fwdx_threads(const WavePlan& P);
 int fused_dp(int dim, const float* x, const float* y);
 size_t bwdw_smem(const WavePlan& P, int gd = 0);
-const void* fwdx_fn(bool banded, bool weights, int dp);
+const void* fwdx_fn(bool banded, bool weights, int dp, bool wide = false);
 const void* bwdw_fn(bool banded, int gd = 0);
 // Feature padding of the reverse pass with grad_x (4, 8, 16), or 0.
 int grad_fused_gd(int dim, const float* y);
 // pass: 0 forward with costs from a table, 1 reverse pass, 2 + dp the fused
-// forward, 64 + gd the reverse pass with grad_x.
+// forward, 32 + those forward passes their 128-register variants, 64 + gd the
+// reverse pass with grad_x.
 int max_active_clusters(const WavePlan& P, int pass);
 cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream);
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream);

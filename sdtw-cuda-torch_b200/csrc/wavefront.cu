@@ -939,20 +939,22 @@ int max_active_clusters(const WavePlan& P, int pass) {
     size_t smem[4] = {0, 0, 0, 0};
     int threads[4] = {P.wpc * 32, P.wpc * 32, P.wpc * 32, P.wpc * 32};
     switch (P.K) {
-        case 1:
-            if (pass == 0) {
-                fns[0] = fwdx_fn(false, false, 0);
+        case 1: {
+            const bool wide = pass >= 32 && pass < 64;
+            const int fp = wide ? pass - 32 : pass;
+            if (fp == 0) {
+                fns[0] = fwdx_fn(false, false, 0, wide);
                 smem[0] = fwdx_smem(P, 0);
                 threads[0] = fwdx_threads(P);
-                fns[2] = fwdx_fn(false, true, 0);
+                fns[2] = fwdx_fn(false, true, 0, wide);
                 smem[2] = fwdx_smem(P, 0);
                 threads[2] = fwdx_threads(P);
             } else if (pass >= 64) {
                 fns[0] = bwdw_fn(false, pass - 64);
                 smem[0] = bwdw_smem(P, pass - 64);
-            } else if (pass >= 2) {
-                fns[0] = fwdx_fn(false, true, pass - 2);
-                smem[0] = fwdx_smem(P, pass - 2);
+            } else if (fp >= 2) {
+                fns[0] = fwdx_fn(false, true, fp - 2, wide);
+                smem[0] = fwdx_smem(P, fp - 2);
                 threads[0] = fwdx_threads(P);
             } else {
                 fns[1] = (const void*)bwd_kernel<1, false, false>;
@@ -961,6 +963,7 @@ int max_active_clusters(const WavePlan& P, int pass) {
                 smem[3] = bwdw_smem(P);
             }
             break;
+        }
         case 2:
             fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<2, false, false> : (const void*)bwd_kernel<2, false, false>;
             smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);

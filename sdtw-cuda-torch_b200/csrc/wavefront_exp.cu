@@ -68,7 +68,6 @@ constexpr int kShiftMin = -96;           // terms below 2^-96 of the largest are
 constexpr int kErange = 1 << 29;         // valid exponents lie in (-2^29, 2^29)
 constexpr float kPmax = 4194304.f;       // |D| * log2(e) / gamma per cell must stay below 2^22
 constexpr float kMagic = 12582912.f;     // 1.5 * 2^23: adding it rounds to an integer in the low bits
-constexpr int kBwdPhases = 2;            // reverse pass: step bodies per loop iteration
 constexpr int kFusedMaxDim = 16;         // the forward computes its costs for up to this many features
 }  // namespace
 
@@ -175,8 +174,13 @@ __device__ __forceinline__ bool mbar_wait_fx(uint32_t mbar, uint32_t parity, con
 
 // 512 threads (8 pairs) per CTA; two CTAs per SM except in the fused mode with
 // 8 or 16 features, whose row of x takes registers.
-template <bool BANDED, bool W, int DP>
-__global__ void __launch_bounds__(512, DP >= 8 ? 1 : 2) fwdx_kernel(const FwdArgs a) {
+// WIDE: up to 128 registers a thread (one CTA of 512 threads per SM) instead
+// of 64 (two), for launches whose clusters all fit at once at that occupancy:
+// the compiler interleaves more of the steps' independent work (C2 forward
+// 0.118 -> 0.104 ms); launches with more problems than fit keep the
+// occupancy.  The fused forward with 8 or more features always takes 128.
+template <bool BANDED, bool W, int DP, bool WIDE>
+__global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(const FwdArgs a) {
     constexpr int PF = kPF;
     constexpr int YP = DP > 0 ? y_pitch(DP) : 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -701,7 +705,6 @@ __host__ __device__ constexpr size_t bw_smem_bytes(int wpc, int gd = 0) {
 template <bool BANDED, int GD>
 __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kernel(const BwdArgs a) {
     constexpr int PF = kPF;
-    constexpr int NPH = GD > 0 ? 1 : kBwdPhases;
     constexpr int YP = y_pitch(GD > 0 ? GD : 4);
     static_assert(GD == 0 || !BANDED, "the gradient mode runs without a band");
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -781,7 +784,7 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
         if constexpr (BANDED) {
             const int t_lo = max(0, R0 - ibw);
             const int t_hi = min(n_steps - 1, 31 + min(M - 1, R0 + 31 + ibw));
-            gi_begin = ((t_last - t_hi) / PF) / NPH * NPH;
+            gi_begin = (t_last - t_hi) / PF;
             gi_end = max(gi_begin, min(n_groups, (t_last - t_lo) / PF + 1));
         }
         const int t_top = t_last - gi_begin * PF;  // first (highest) step that runs
@@ -852,8 +855,7 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
             if (has_below && below_wrap && col >= c_min && col < M) wpf = ld_one(in_g + static_cast<uint32_t>(col) * 16u);
         }
 
-        auto group = [&](auto phase_c, auto masked_c, int t0) {
-            (void)phase_c;  // two step bodies per loop iteration (compile-time unrolled)
+        auto group = [&](auto masked_c, int t0) {
             constexpr bool MASKED = decltype(masked_c)::value;
             // ---- messages for lane 31 (columns colb0 .. colb0-PF+1); lane u
             // (mod PF) holds column colb0 - u, handed to lane 31 at step u.
@@ -970,24 +972,21 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
             }
 
         };
-        using P0 = std::integral_constant<int, 0>;
-        using P1 = std::integral_constant<int, 1>;
-        auto run = [&](auto phase_c, int gi) {
+        // One step body per loop iteration (two, unrolled, measured slower on
+        // B200: C2 reverse pass 0.115 -> 0.103 ms, C3 1.42 -> 1.19 ms with one).
+        auto run = [&](int gi) {
             const int t0 = t_last - gi * PF;
             if constexpr (!BANDED) {
                 const bool interior = full_rows && t0 - (PF - 1) >= 32 && t0 <= M - 1;
-                if (interior) group(phase_c, std::false_type{}, t0);
-                else group(phase_c, std::true_type{}, t0);
+                if (interior) group(std::false_type{}, t0);
+                else group(std::true_type{}, t0);
             } else {
-                group(phase_c, std::true_type{}, t0);
+                group(std::true_type{}, t0);
             }
         };
-        for (int gi = gi_begin; gi < gi_end; gi += NPH) {
-            run(P0{}, gi);
-            if constexpr (NPH == 2) {
-                if (gi + 1 < gi_end) run(P1{}, gi + 1);
-            }
-            if ((gi & 15) == 16 - NPH && __any_sync(SDTW_FULL_MASK, !ok)) {
+        for (int gi = gi_begin; gi < gi_end; ++gi) {
+            run(gi);
+            if ((gi & 15) == 15 && __any_sync(SDTW_FULL_MASK, !ok)) {
                 quit = true;
                 break;
             }
@@ -1020,16 +1019,21 @@ size_t bwdw_smem(const WavePlan& P, int gd) { return bw_smem_bytes(P.wpc, gd); }
 
 // dp: 0 = costs from a table; 4, 8, 16, 32, 64 = fused x/y costs with the
 // features padded to dp (the x/y entry points, which store the shares).
-const void* fwdx_fn(bool banded, bool weights, int dp) {
+const void* fwdx_fn(bool banded, bool weights, int dp, bool wide) {
+#define SDTW_FWDX(BW, WW, DD) \
+    (wide ? (const void*)fwdx_kernel<BW, WW, DD, true> : (const void*)fwdx_kernel<BW, WW, DD, false>)
     switch (dp) {
         case 0:
-            if (weights) return banded ? (const void*)fwdx_kernel<true, true, 0> : (const void*)fwdx_kernel<false, true, 0>;
-            return banded ? (const void*)fwdx_kernel<true, false, 0> : (const void*)fwdx_kernel<false, false, 0>;
-        case 4: return banded ? (const void*)fwdx_kernel<true, true, 4> : (const void*)fwdx_kernel<false, true, 4>;
-        case 8: return banded ? (const void*)fwdx_kernel<true, true, 8> : (const void*)fwdx_kernel<false, true, 8>;
-        case 16: return banded ? (const void*)fwdx_kernel<true, true, 16> : (const void*)fwdx_kernel<false, true, 16>;
+            if (weights) return banded ? SDTW_FWDX(true, true, 0) : SDTW_FWDX(false, true, 0);
+            return banded ? SDTW_FWDX(true, false, 0) : SDTW_FWDX(false, false, 0);
+        case 4: return banded ? SDTW_FWDX(true, true, 4) : SDTW_FWDX(false, true, 4);
+        // 8 and 16 features: 128 registers either way.
+        case 8: return banded ? (const void*)fwdx_kernel<true, true, 8, true> : (const void*)fwdx_kernel<false, true, 8, true>;
+        case 16:
+            return banded ? (const void*)fwdx_kernel<true, true, 16, true> : (const void*)fwdx_kernel<false, true, 16, true>;
         default: return nullptr;
     }
+#undef SDTW_FWDX
 }
 // Feature padding of the fused forward for dim features, or 0 when the fused
 // costs come from a cost table in the workspace: more than kFusedMaxDim
@@ -1066,7 +1070,7 @@ cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
     if (P.K != 1 || P.wpc > 8 || (args.dp && !args.weights)) return cudaErrorInvalidValue;
     const bool banded = args.ibw < P.N + P.M;
-    const void* fn = fwdx_fn(banded, args.weights != 0, args.dp);
+    const void* fn = fwdx_fn(banded, args.weights != 0, args.dp, args.wide != 0);
     if (!fn) return cudaErrorInvalidValue;
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
     return launch_cluster(fn, dim3(P.B * P.csize), dim3(fwdx_threads(P)), fwdx_smem(P, args.dp), P.csize, stream,

@@ -37,8 +37,12 @@ def test_sizes_without_gpu():
     assert L.sdtw_score_elems(0, 4, 4) == 0
     cells = 4 * 2 * n_diag * 32
     assert L.sdtw_cost_elems(4, 64, 64) == cells
-    # One band: no wrap ring; the wavefront-layout table of the cost / E.
-    assert L.sdtw_workspace_bytes(4, 64, 64) == -(-cells * 4 // 256) * 256
+    # More than one stripe: the band-wrap ring (B x M slots of 16 bytes, sized
+    # for any plan a pass may pick), then the wavefront-layout table of the
+    # cost / E.
+    assert L.sdtw_workspace_bytes(4, 64, 64) == -(-4 * 64 * 16 // 256) * 256 + -(-cells * 4 // 256) * 256
+    # One stripe: no ring.
+    assert L.sdtw_workspace_bytes(4, 32, 64) == -(-(4 * 1 * n_diag * 32) * 4 // 256) * 256
     # x/y backward adds the gradient operands.
     up = lambda v: -(-v // 256) * 256
     # Up to 16 features: column sums per split of 8 stripes (B x splits x M x
