@@ -60,7 +60,8 @@ PUBLISHED = {  # the reference's published numbers: B=32 N=M=512 D=64 fwd+bwd (u
 }
 MUFU_PER_CELL = 7          # algorithmic ex2/lg2 per DP cell, forward + backward (reference algorithm)
 MUFU_PER_SM_CLK = 16       # ex2/lg2 results per SM per clock
-DEP_CYCLES = 105           # dependency chain of one cell (SHFL, max, adds, EX2, LG2, TwoSum, select)
+DEP_CYCLES = 49            # dependent chain of one exponential-domain step (SHFL, integer max/add-max/add,
+                           # 2 FADD, FMUL), clock64 microbenchmark, one warp per SM sub-partition
 # Algorithmic HBM bytes per DP cell of each library kernel: every table entry
 # read or written once (cost 4 B, score 8 B as a (hi, lo) pair, E 4 B).
 ALG_BYTES = {"cost_wl": 4, "cost_tc": 4, "wavefront_fwd": 12, "wavefront_bwd": 12, "wl_to_rm": 8, "grad_xy": 8,
@@ -70,7 +71,7 @@ ALG_BYTES = {"cost_wl": 4, "cost_tc": 4, "wavefront_fwd": 12, "wavefront_bwd": 1
 ALG_MUFU = {"wavefront_fwd": 3, "wavefront_bwd": 4}
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum,
 # one launch each, cold L2) for the C2 workload, fused mode (profiles/c2_kernels_full.md).
-TRAFFIC_C2 = {"wavefront_fwd": 57.34e6, "wavefront_bwd": 81.58e6, "cost_wl": 8.47e6, "grad_xy": 54.46e6}
+TRAFFIC_C2 = {"wavefront_fwd": 58.83e6, "wavefront_bwd": 84.35e6, "cost_wl": 8.48e6, "grad_xy": 54.63e6}
 
 
 def parse():
