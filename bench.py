@@ -86,6 +86,8 @@ def parse():
     ap.add_argument("--fused-only", action="store_true")
     # Profiling runs of one mode (it becomes the headline; implies --fused-only).
     ap.add_argument("--only-mode", default=None)
+    # Profiling runs under a forced launch geometry: stripes per CTA x cluster size ("8x8").
+    ap.add_argument("--plan", default=None)
     args = ap.parse_args()
     if args.only_mode:
         args.fused_only = True
@@ -542,6 +544,9 @@ def main():
                 "roofline_latency": roofline_latency, "clocks": clocks}
 
     sampler = ClockSampler(local)
+    if args.plan:
+        w, c = (int(v) for v in args.plan.split("x"))
+        _native.set_plan_override(w, c, 1)
     res = run_one(args.workload, args.steps, args.warmup, args.fused_only, args.only_mode, sampler)
     name, B, N, Dm, desc = res["name"], res["B"], res["N"], res["Dm"], res["desc"]
     head_mode, is_bary, modes, breakdown = res["head_mode"], res["is_bary"], res["modes"], res["breakdown"]
@@ -589,7 +594,8 @@ def main():
                                    else f"dp{world} (batch-sharded, no collective)"),
                    "l2": ("per-iteration working set (about 1 GB of tables) larger than the 126 MB L2" if is_bary else
                           "flushed before every timed step (256 MiB write, outside the events)"),
-                   "vs_baseline_basis": "per-GPU value / the reference's published number (unstated GPU)"},
+                   "vs_baseline_basis": "per-GPU value / the reference's published number (unstated GPU)",
+                   **({"forced_plan": args.plan} if args.plan else {})},
         "modes": modes,
         "kernel_ms_per_step": breakdown,
         "roofline": roofline,
