@@ -66,7 +66,7 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream);
 // K = 1 to them.
 cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream);
-size_t fwdx_smem(const WavePlan& P, int dp);
+size_t fwdx_smem(const WavePlan& P, int dp, bool wide = false);
 int fwdx_threads(const WavePlan& P);
 int fused_dp(int dim, const float* x, const float* y);
 size_t bwdw_smem(const WavePlan& P, int gd = 0);

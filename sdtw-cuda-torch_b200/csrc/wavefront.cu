@@ -944,17 +944,17 @@ int max_active_clusters(const WavePlan& P, int pass) {
             const int fp = wide ? pass - 32 : pass;
             if (fp == 0) {
                 fns[0] = fwdx_fn(false, false, 0, wide);
-                smem[0] = fwdx_smem(P, 0);
+                smem[0] = fwdx_smem(P, 0, wide);
                 threads[0] = fwdx_threads(P);
                 fns[2] = fwdx_fn(false, true, 0, wide);
-                smem[2] = fwdx_smem(P, 0);
+                smem[2] = fwdx_smem(P, 0, wide);
                 threads[2] = fwdx_threads(P);
             } else if (pass >= 64) {
                 fns[0] = bwdw_fn(false, pass - 64);
                 smem[0] = bwdw_smem(P, pass - 64);
             } else if (fp >= 2) {
                 fns[0] = fwdx_fn(false, true, fp - 2, wide);
-                smem[0] = fwdx_smem(P, fp - 2);
+                smem[0] = fwdx_smem(P, fp - 2, wide);
                 threads[0] = fwdx_threads(P);
             } else {
                 fns[1] = (const void*)bwd_kernel<1, false, false>;

@@ -24,7 +24,7 @@
 // operations (ex2, lg2) there.  K's split into mantissa and exponent
 // (one ex2) depends only on the cost and runs off the chain.  Mantissas grow
 // by at most 6x a step and every held value is renormalised once per group of
-// 8 steps.  The scaled terms are exact, so the weights of the reverse pass (a
+// 16 steps (so mantissas stay below 2^46).  The scaled terms are exact, so the weights of the reverse pass (a
 // predecessor's term over their sum) have float32 relative accuracy at any
 // magnitude of R.
 // Valid exponents stay within +-2^29 (|R| / gamma < 3.7e8) and |D| * log2(e)
@@ -45,9 +45,9 @@
 // from the neighbour lane by shuffle, and for lane 0 from the previous
 // stripe's warp through a ring of tagged u64 slots in the consumer's shared
 // memory (DSMEM stores inside a thread-block cluster; a global ring between
-// bands).  Steps run in groups of 8: per group the consumer checks the 8 ring
-// slots it needs with one warp-wide load and a vote, the producer checks flow
-// control once and publishes the stripe's bottom row for the group's 8
+// bands).  Steps run in groups of 16: per group the consumer checks the 16
+// ring slots it needs with one warp-wide load and a vote, the producer checks
+// flow control once and publishes the stripe's bottom row for the group's 16
 // columns with one warp-wide store, the inputs of the group after next are
 // copied into shared memory (cp.async), and every step's table row leaves as
 // one coalesced 128- or 256-byte store.  Groups whose cells all lie inside the
@@ -62,7 +62,12 @@
 namespace sdtw {
 
 namespace {
-constexpr int kPF = 8;                   // steps per group
+// Steps per group: the unit of hand-over between the warps of a pair, of the
+// ring publish and of the prefetch.  Measured on B200, 16 against 8: C2
+// forward 0.104 -> 0.089 ms, reverse pass 0.101 -> 0.082 ms, C3 4.43 -> 3.69
+// ms per step (half the per-group synchronisation per step).  The forward's
+// 64-register variant keeps 8 (fx_pf).
+constexpr int kPF = 16;
 constexpr int kEneg = -(1 << 30);        // exponent of P = 0 (outside the table or the band)
 constexpr int kShiftMin = -96;           // terms below 2^-96 of the largest are dropped
 constexpr int kErange = 1 << 29;         // valid exponents lie in (-2^29, 2^29)
@@ -72,7 +77,7 @@ constexpr int kFusedMaxDim = 16;         // the forward computes its costs for u
 }  // namespace
 
 // m * 2^s for s <= 0 by an add to the exponent field.  m is a normal float
-// >= 1 below 2^26 and s >= kShiftMin, so the result is a normal float.
+// >= 1 below 2^48 and s >= kShiftMin, so the result is a normal float.
 __device__ __forceinline__ float scale_pow2(float m, int s) {
     return __int_as_float(__float_as_int(m) + s * (1 << 23));
 }
@@ -125,31 +130,41 @@ __device__ __forceinline__ float2 to_score(float m, int e) {
 // input [kNB][PF] (m, e), the chain's bottom-row output [PF] (m, e), and the
 // mbarriers [2][kNB].
 constexpr int kNB = 3;
-constexpr int kYRows = 64;             // y window rows per pair (ring of segments of PF rows)
-constexpr int kYSeg = kYRows / kPF;    // window segments
+constexpr int kYRows = 128;            // y window rows per pair (ring of segments of PF rows)
+// Steps per group of the forward: kPF for the 128-register variants; 8 for the
+// 64-register variant, which serves launches with more problems than fit at
+// once (short problems): its smaller buffers keep more CTAs resident and its
+// stripes enter the pipeline 8 steps sooner (C5 forward 0.324 ms at 16, 0.267
+// ms at 8).
+__host__ __device__ constexpr int fx_pf(int dp, bool wide) { return (wide || dp >= 8) ? kPF : 8; }
+// Segments before a group's own that its cells read (the 32 lanes reach 31
+// rows back), and the window's segments.
+__host__ __device__ constexpr int seg_back(int pf) { return (31 + pf - 1) / pf; }
+static_assert(seg_back(8) + 3 <= kYRows / 8 && seg_back(kPF) + 3 <= kYRows / kPF,
+              "the y window holds the segments read and the two in flight");
 // Row pitch of the y window: for DP a multiple of 4, the number of 16-byte
 // units per row is odd, so the 8 lanes of one 128-bit load phase, which read 8
 // consecutive rows, hit distinct banks; DP = 4 also serves D < 4 with dense
 // rows of D floats (odd D or 2: conflict-free for 32- and 64-bit loads).
 __host__ __device__ constexpr int y_pitch(int dp) { return (dp / 4) % 2 ? dp : dp + 4; }
-__host__ __device__ constexpr size_t fx_in_bytes(int dp) {
-    return dp == 0 ? static_cast<size_t>(3) * kPF * 32 * 4 : static_cast<size_t>(kYRows) * y_pitch(dp) * 4;
+__host__ __device__ constexpr size_t fx_in_bytes(int dp, int pf) {
+    return dp == 0 ? static_cast<size_t>(3) * pf * 32 * 4 : static_cast<size_t>(kYRows) * y_pitch(dp) * 4;
 }
 __host__ __device__ constexpr size_t fx_in_off(int wpc) { return fwd_stage_offset(wpc); }
-__host__ __device__ constexpr size_t fx_k_off(int wpc, int dp) {
-    return fx_in_off(wpc) + static_cast<size_t>(wpc) * fx_in_bytes(dp);
+__host__ __device__ constexpr size_t fx_k_off(int wpc, int dp, int pf) {
+    return fx_in_off(wpc) + static_cast<size_t>(wpc) * fx_in_bytes(dp, pf);
 }
-__host__ __device__ constexpr size_t fx_rin_off(int wpc, int dp) {
-    return fx_k_off(wpc, dp) + static_cast<size_t>(wpc) * kNB * kPF * 32 * 8;
+__host__ __device__ constexpr size_t fx_rin_off(int wpc, int dp, int pf) {
+    return fx_k_off(wpc, dp, pf) + static_cast<size_t>(wpc) * kNB * pf * 32 * 8;
 }
-__host__ __device__ constexpr size_t fx_pub_off(int wpc, int dp) {
-    return fx_rin_off(wpc, dp) + static_cast<size_t>(wpc) * kNB * kPF * 8;
+__host__ __device__ constexpr size_t fx_pub_off(int wpc, int dp, int pf) {
+    return fx_rin_off(wpc, dp, pf) + static_cast<size_t>(wpc) * kNB * pf * 8;
 }
-__host__ __device__ constexpr size_t fx_mbar_off(int wpc, int dp) {
-    return fx_pub_off(wpc, dp) + static_cast<size_t>(wpc) * kPF * 8;
+__host__ __device__ constexpr size_t fx_mbar_off(int wpc, int dp, int pf) {
+    return fx_pub_off(wpc, dp, pf) + static_cast<size_t>(wpc) * pf * 8;
 }
-__host__ __device__ constexpr size_t fx_smem_bytes(int wpc, int dp) {
-    return fx_mbar_off(wpc, dp) + static_cast<size_t>(wpc) * 2 * kNB * 8;
+__host__ __device__ constexpr size_t fx_smem_bytes(int wpc, int dp, int pf) {
+    return fx_mbar_off(wpc, dp, pf) + static_cast<size_t>(wpc) * 2 * kNB * 8;
 }
 
 __device__ __forceinline__ uint64_t pack_tagged_bits(uint32_t v, uint32_t tag) {
@@ -181,7 +196,9 @@ __device__ __forceinline__ bool mbar_wait_fx(uint32_t mbar, uint32_t parity, con
 // occupancy.  The fused forward with 8 or more features always takes 128.
 template <bool BANDED, bool W, int DP, bool WIDE>
 __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(const FwdArgs a) {
-    constexpr int PF = kPF;
+    constexpr int PF = fx_pf(DP, WIDE);
+    constexpr int YSEG = kYRows / PF;      // window segments
+    constexpr int SEGBACK = seg_back(PF);
     constexpr int YP = DP > 0 ? y_pitch(DP) : 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const WavePlan P = a.P;
@@ -197,25 +214,25 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][kRing][2]
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
-    unsigned char* in_raw = smem_raw + fx_in_off(wpc) + static_cast<size_t>(warp) * fx_in_bytes(DP);
+    unsigned char* in_raw = smem_raw + fx_in_off(wpc) + static_cast<size_t>(warp) * fx_in_bytes(DP, PF);
     const float* cost = reinterpret_cast<const float*>(in_raw);  // table mode
     const uint32_t cost_s = smem_addr(cost);
     float* ywin = reinterpret_cast<float*>(in_raw);  // fused mode: [kYRows][YP]
-    uint2* kbuf = reinterpret_cast<uint2*>(smem_raw + fx_k_off(wpc, DP)) + warp * kNB * PF * 32;
-    uint2* rin = reinterpret_cast<uint2*>(smem_raw + fx_rin_off(wpc, DP)) + warp * kNB * PF;
-    uint2* pub_s = reinterpret_cast<uint2*>(smem_raw + fx_pub_off(wpc, DP)) + warp * PF;
-    const uint32_t mb_full = smem_addr(reinterpret_cast<uint64_t*>(smem_raw + fx_mbar_off(wpc, DP)) + warp * 2 * kNB);
+    uint2* kbuf = reinterpret_cast<uint2*>(smem_raw + fx_k_off(wpc, DP, PF)) + warp * kNB * PF * 32;
+    uint2* rin = reinterpret_cast<uint2*>(smem_raw + fx_rin_off(wpc, DP, PF)) + warp * kNB * PF;
+    uint2* pub_s = reinterpret_cast<uint2*>(smem_raw + fx_pub_off(wpc, DP, PF)) + warp * PF;
+    const uint32_t mb_full = smem_addr(reinterpret_cast<uint64_t*>(smem_raw + fx_mbar_off(wpc, DP, PF)) + warp * 2 * kNB);
     const uint32_t mb_empty = mb_full + kNB * 8u;
     for (int i = threadIdx.x; i < wpc * 2 * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     if (threadIdx.x < wpc * 2 * kNB)
-        mbar_init(smem_addr(reinterpret_cast<uint64_t*>(smem_raw + fx_mbar_off(wpc, DP)) + threadIdx.x), 32);
+        mbar_init(smem_addr(reinterpret_cast<uint64_t*>(smem_raw + fx_mbar_off(wpc, DP, PF)) + threadIdx.x), 32);
     if constexpr (DP > 0) {
         // y windows start as zeros (the rows left of column 0 are read only by
         // cells outside the table, whose values must stay finite).
         for (int i = threadIdx.x; i < wpc * kYRows * YP; i += blockDim.x) {
             const int w = i / (kYRows * YP);
-            reinterpret_cast<float*>(smem_raw + fx_in_off(wpc) + static_cast<size_t>(w) * fx_in_bytes(DP))
+            reinterpret_cast<float*>(smem_raw + fx_in_off(wpc) + static_cast<size_t>(w) * fx_in_bytes(DP, PF))
                 [i - w * kYRows * YP] = 0.f;
         }
     }
@@ -308,13 +325,13 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
             }
             const float* yb = a.y + static_cast<size_t>(b) * M * D;
             // Rows seg*PF .. seg*PF+PF-1 of y (those below M) into window slot
-            // seg mod kYSeg by cp.async, one commit group per segment: 16-byte
+            // seg mod YSEG by cp.async, one commit group per segment: 16-byte
             // copies into the padded rows, or 4-byte copies of dense rows (D < 4).
             // (Bulk copies of single rows measured several microseconds from
             // issue to landing on B200, more than the two groups of prefetch.)
             auto y_issue = [&](int seg) {
                 if constexpr (DP > 0) {
-                    const int sl = seg & (kYSeg - 1);
+                    const int sl = seg & (YSEG - 1);
                     const int r0 = seg * PF;
                     const int nr = (seg < g_end) ? max(0, min(PF, M - r0)) : 0;
                     if (dense) {
@@ -344,9 +361,9 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                 cost_copy(g_begin);
                 cost_copy(g_begin + 1);
             } else {
-                // The window rows of the first group (segments g_begin-4 .. g_begin)
-                // and the next one in flight.
-                const int s_lo = max(0, g_begin - 4);
+                // The window rows of the first group (segments g_begin -
+                // SEGBACK .. g_begin) and the next one in flight.
+                const int s_lo = max(0, g_begin - SEGBACK);
                 for (int sg = s_lo; sg < g_begin + 2; ++sg) y_issue(sg);
             }
             if (t_begin > 0)
@@ -415,7 +432,7 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
 #pragma unroll
                         for (int u = 0; u < PF; ++u) cv[u] = lo_f32x2(acc[u]) + hi_f32x2(acc[u]);
                     }
-                    y_issue(gi + 2);  // into the slot of segment gi - 6, no longer read
+                    y_issue(gi + 2);  // into the slot of segment gi + 2 - YSEG, no longer read
                 }
 #pragma unroll
                 for (int u = 0; u < PF; ++u) {
@@ -705,6 +722,8 @@ __host__ __device__ constexpr size_t bw_smem_bytes(int wpc, int gd = 0) {
 template <bool BANDED, int GD>
 __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kernel(const BwdArgs a) {
     constexpr int PF = kPF;
+    constexpr int YSEG = kYRows / PF;      // window segments
+    constexpr int SEGBACK = seg_back(PF);
     constexpr int YP = y_pitch(GD > 0 ? GD : 4);
     static_assert(GD == 0 || !BANDED, "the gradient mode runs without a band");
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -802,12 +821,12 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
         for (int f = 0; f < (GD > 0 ? GD : 1); ++f) racc[f] = 0.f;
         const float* yb = GD > 0 ? a.y + static_cast<size_t>(b) * M * D : nullptr;
         // y rows 8 seg .. 8 seg + 7 (those inside y) into window slot seg mod
-        // kYSeg: 16-byte copies, or 4-byte copies into padded rows for D < 4.
+        // YSEG: 16-byte copies, or 4-byte copies into padded rows for D < 4.
         auto y_issue = [&](int seg) {
             if constexpr (GD > 0) {
                 const int r0 = seg * PF;
                 const int nr = (seg >= 0) ? max(0, min(PF, M - r0)) : 0;
-                float* dst = ywin + (seg & (kYSeg - 1)) * PF * YP;
+                float* dst = ywin + (seg & (YSEG - 1)) * PF * YP;
                 if (D < 4) {
                     for (int e = lane; e < nr * D; e += 32) {
                         const int r = e / D, f = e - r * D;
@@ -825,8 +844,8 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
         // Group gi's shares: rows t0 - PF + 1 .. t0 (t0 = t_last - gi * PF),
         // or an empty commit past the last group.  In the gradient mode the
         // same commit carries the lowest y segment group gi reads (its cells
-        // read segments k - 4 .. k, k = n_groups - 1 - gi; the first commit
-        // carries all five).
+        // read segments k - SEGBACK .. k, k = n_groups - 1 - gi; the first
+        // commit carries all of them).
         auto wcopy = [&](int gi) {
             if (gi < gi_end) {
                 const float2* src = Ts + static_cast<size_t>(t_last - gi * PF - PF + 1) * 32;
@@ -836,9 +855,9 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
                 if constexpr (GD > 0) {
                     const int k = n_groups - 1 - gi;
                     if (gi == gi_begin)
-                        for (int sg = k; sg >= k - 4; --sg) y_issue(sg);
+                        for (int sg = k; sg >= k - SEGBACK; --sg) y_issue(sg);
                     else
-                        y_issue(k - 4);
+                        y_issue(k - SEGBACK);
                 }
             }
             cp_async_commit();
@@ -1013,7 +1032,7 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
 }
 
 // ------------------------------------------------------------------ launchers
-size_t fwdx_smem(const WavePlan& P, int dp) { return fx_smem_bytes(P.wpc, dp); }
+size_t fwdx_smem(const WavePlan& P, int dp, bool wide) { return fx_smem_bytes(P.wpc, dp, fx_pf(dp, wide)); }
 int fwdx_threads(const WavePlan& P) { return 2 * P.wpc * 32; }  // a chain warp and its helper per stripe
 size_t bwdw_smem(const WavePlan& P, int gd) { return bw_smem_bytes(P.wpc, gd); }
 
@@ -1073,7 +1092,7 @@ cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream) {
     const void* fn = fwdx_fn(banded, args.weights != 0, args.dp, args.wide != 0);
     if (!fn) return cudaErrorInvalidValue;
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
-    return launch_cluster(fn, dim3(P.B * P.csize), dim3(fwdx_threads(P)), fwdx_smem(P, args.dp), P.csize, stream,
+    return launch_cluster(fn, dim3(P.B * P.csize), dim3(fwdx_threads(P)), fwdx_smem(P, args.dp, args.wide != 0), P.csize, stream,
                           kargs);
 }
 
