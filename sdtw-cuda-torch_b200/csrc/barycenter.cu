@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(kReduceThreads) bary_reduce_part_kernel(const 
                                                                          const float* __restrict__ w,
                                                                          const float* __restrict__ out,
                                                                          float* __restrict__ part, int B, size_t n) {
+    pdl_trigger();
+    pdl_wait();
     const size_t v = static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
     if (v > n) return;
     const int S = gridDim.y, s = blockIdx.y;
@@ -71,6 +73,8 @@ __global__ void __launch_bounds__(kReduceThreads) bary_reduce_part_kernel(const 
 __global__ void __launch_bounds__(kReduceThreads) bary_reduce_final_kernel(const float* __restrict__ part,
                                                                           float* __restrict__ grad_loss, int S,
                                                                           size_t n) {
+    pdl_trigger();
+    pdl_wait();
     const size_t v = static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
     if (v > n) return;
     float acc = 0.f;
@@ -99,6 +103,8 @@ __global__ void __launch_bounds__(kAdamThreads) bary_adam_kernel(float* __restri
                                                                 float* __restrict__ bary_hist, float beta1, float beta2,
                                                                 float eps, float max_norm) {
     __shared__ float red[kAdamThreads];
+    pdl_trigger();
+    pdl_wait();
     const int it = *step;
     if (it < 0 || it >= max_iter) return;  // more replays than iterations: nothing to do
     float sq = 0.f;
@@ -143,19 +149,16 @@ cudaError_t launch_bary_reduce(const float* gx, const float* w, const float* out
                                size_t n, cudaStream_t st) {
     const int S = reduce_slices(B);
     const unsigned bx = static_cast<unsigned>((n + 1 + kReduceThreads - 1) / kReduceThreads);
-    bary_reduce_part_kernel<<<dim3(bx, S), kReduceThreads, 0, st>>>(gx, w, out, part, B, n);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(true, bary_reduce_part_kernel, dim3(bx, S), dim3(kReduceThreads), 0, st, gx, w, out, part, B, n);
     if (e != cudaSuccess) return e;
-    bary_reduce_final_kernel<<<bx, kReduceThreads, 0, st>>>(part, grad_loss, S, n);
-    return cudaGetLastError();
+    return launch_pdl(true, bary_reduce_final_kernel, dim3(bx), dim3(kReduceThreads), 0, st, part, grad_loss, S, n);
 }
 
 cudaError_t launch_bary_adam(float* bary, float* exp_avg, float* exp_avg_sq, const float* grad_loss, size_t n,
                              const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
                              float beta1, float beta2, float eps, float max_norm, cudaStream_t st) {
-    bary_adam_kernel<<<1, kAdamThreads, 0, st>>>(bary, exp_avg, exp_avg_sq, grad_loss, n, lr_table, max_iter, step,
-                                                 loss_hist, bary_hist, beta1, beta2, eps, max_norm);
-    return cudaGetLastError();
+    return launch_pdl(true, bary_adam_kernel, dim3(1), dim3(kAdamThreads), 0, st, bary, exp_avg, exp_avg_sq, grad_loss, n,
+                      lr_table, max_iter, step, loss_hist, bary_hist, beta1, beta2, eps, max_norm);
 }
 
 }  // namespace sdtw

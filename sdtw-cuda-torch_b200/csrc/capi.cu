@@ -446,7 +446,8 @@ int run_backward(const float* score, const float* grad_out, float* Ew, int B, in
 // The reverse pass that applies the squared-Euclidean chain rule for grad_x
 // itself (no E table), see bwdw_kernel.
 int run_backward_grad(const float* score, const float* grad_out, int B, int N, int M, uint64_t* wrap,
-                      cudaStream_t stream, const float* x, size_t x_bstride, const float* y, int dim, int gd, float* gx) {
+                      cudaStream_t stream, const float* x, size_t x_bstride, const float* y, int dim, int gd, float* gx,
+                      bool pdl = false) {
     BwdArgs a{};
     a.P = plan(B, N, M, 64 + gd);
     a.weights = 1;
@@ -464,6 +465,7 @@ int run_backward_grad(const float* score, const float* grad_out, int B, int N, i
     a.gd = gd;
     a.x_bstride = x_bstride;
     a.gx = gx;
+    a.pdl = (pdl && a.P.n_bands <= 1) ? 1 : 0;  // a multi-band launch follows its ring reset
     cudaError_t e = reset_wrap(a.P, wrap, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(band-wrap ring)");
     {
@@ -967,7 +969,7 @@ int sdtw_barycenter_grad_f32(const float* bary, const float* X, const float* w, 
                               true)))
             return rc;
         // grad_x of every problem straight from the reverse pass.
-        if ((rc = run_backward_grad(score, w, B, N, M, wrap, st, bary, 0, X, dim, dp, gx))) return rc;
+        if ((rc = run_backward_grad(score, w, B, N, M, wrap, st, bary, 0, X, dim, dp, gx, true))) return rc;
     } else {
         // General path: the barycenter broadcast to every problem, then the
         // x/y pair.

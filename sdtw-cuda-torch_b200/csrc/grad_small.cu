@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
                                                                       float* __restrict__ part, WavePlan P, int dim,
                                                                       int n_split, size_t xbs) {
     extern __shared__ __align__(16) float sm[];
+    pdl_trigger();
+    pdl_wait();
     const int warps = blockDim.x >> 5;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* Et = sm + warp * SmallSmem<DP>::E;
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(256) grad_small_finalize_kernel(const float* _
                                                                   const float* __restrict__ y,
                                                                   float* __restrict__ gy, int B, int M, int dim,
                                                                   int n_split) {
+    pdl_trigger();
+    pdl_wait();
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(B) * M * dim) return;
     const int d = static_cast<int>(i % dim);
@@ -197,15 +201,15 @@ static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, co
     const dim3 grid(n_split, P.B);
     float* pp = gy ? part : nullptr;
     if (Mw)
-        grad_small_kernel<DP, true><<<grid, 32 * warps, smem, st>>>(Ew, Mw, x, y, gx, pp, P, dim, n_split, xbs);
+        e = launch_pdl(false, grad_small_kernel<DP, true>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, P, dim,
+                       n_split, xbs);
     else
-        grad_small_kernel<DP, false><<<grid, 32 * warps, smem, st>>>(Ew, Mw, x, y, gx, pp, P, dim, n_split, xbs);
-    e = cudaGetLastError();
+        e = launch_pdl(false, grad_small_kernel<DP, false>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, P, dim,
+                       n_split, xbs);
     if (e != cudaSuccess || !gy) return e;
     const size_t n = static_cast<size_t>(P.B) * P.M * dim;
-    grad_small_finalize_kernel<DP><<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(part, y, gy, P.B, P.M, dim,
-                                                                                          n_split);
-    return cudaGetLastError();
+    return launch_pdl(false, grad_small_finalize_kernel<DP>, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st,
+                      part, y, gy, P.B, P.M, dim, n_split);
 }
 
 cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,

@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
     constexpr int PITCH = CostPitch<FC>::v;
     constexpr int NOFF = (SR + CJ + 3) / 4 * 4;  // norms region, rounded to 16 bytes
     extern __shared__ __align__(16) float cs[];
+    pdl_trigger();
+    pdl_wait();
     float* xn = cs;                      // [SR]
     float* yn = xn + SR;                 // [CJ]
     float* xs0 = cs + NOFF;                  // [SR + CJ][PITCH]: x rows then y rows
@@ -357,6 +359,8 @@ __global__ void __launch_bounds__(256) transpose_chunked_kernel(const float* __r
                                                                 int R0, const float* __restrict__ in1,
                                                                 float* __restrict__ out1, int R1, int B, int C) {
     __shared__ float tile[32][33];
+    pdl_trigger();
+    pdl_wait();
     const bool second = static_cast<int>(blockIdx.z) >= B;
     const float* __restrict__ in = second ? in1 : in0;
     float* __restrict__ out = second ? out1 : out0;
@@ -407,8 +411,7 @@ static cudaError_t cost_wl_launch(const float* x, const float* y, float* Dw, con
                      : (vec ? cost_wl_kernel<K, false, FC, true> : cost_wl_kernel<K, false, FC, false>);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    fn<<<g, 256, smem, stream>>>(x, y, Dw, P, dim);
-    return cudaGetLastError();
+    return launch_pdl(false, fn, g, dim3(256), smem, stream, x, y, Dw, P, dim);  // first of its call
 }
 
 template <int K>
@@ -472,8 +475,7 @@ cudaError_t launch_transpose_chunked(const float* in0, float* out0, int R0, cons
     if (B <= 0 || C <= 0 || (!in0 && !in1)) return cudaSuccess;
     const int rows = std::max(in0 ? R0 : 0, in1 ? R1 : 0);
     const dim3 g((rows + 31) / 32, (C + 31) / 32, 2 * B);
-    transpose_chunked_kernel<<<g, 256, 0, stream>>>(in0, out0, R0, in1, out1, R1, B, C);
-    return cudaGetLastError();
+    return launch_pdl(false, transpose_chunked_kernel, g, dim3(256), 0, stream, in0, out0, R0, in1, out1, R1, B, C);
 }
 
 cudaError_t launch_transpose_brc(const float* in, float* out, int B, int R, int C, int ldo, cudaStream_t stream) {

@@ -161,6 +161,38 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 // 4-byte global -> shared asynchronous copy (any 4-byte alignment).
+// Programmatic dependent launch.  A kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may be scheduled while the
+// kernel before it in the stream is finishing; pdl_wait() blocks until that
+// kernel has completed and its memory is visible, so it must come before the
+// first access to global memory the previous kernel writes or reads.
+// pdl_trigger() lets the next such kernel be launched once every CTA of this
+// one has executed it (or exited).  Both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch of a kernel that calls pdl_wait() before touching global memory,
+// with programmatic stream serialization when `pdl`.  Used inside the
+// barycenter iteration, a chain of short library kernels replayed from a CUDA
+// graph (512 sequences: 0.122 -> 0.103 ms per iteration).  In the loss path
+// measured on B200 it gained nothing on the device and made a step followed by
+// a device-to-host copy ~20 us slower, so those launches keep the plain form.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }

@@ -57,6 +57,7 @@ struct BwdArgs {
     int gd;             // features padded to 4, 8 or 16; 0 = store E
     size_t x_bstride;   // floats between problems' x (N * dim; 0 = one x for all)
     float* gx;          // (B,N,dim) grad_x
+    int pdl;            // nonzero: launched with programmatic stream serialization (after the forward)
     WaitCtx wait;
 };
 

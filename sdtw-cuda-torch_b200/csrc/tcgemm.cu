@@ -871,6 +871,8 @@ constexpr int kWlThreads = 32 * (kWlSplitWarps + 2);  // split warps, the copy w
 
 __global__ void __launch_bounds__(kWlThreads, 1) grad_wl_kernel(const __grid_constant__ GradTcArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    pdl_trigger();
+    pdl_wait();  // E and the transposed operands of the previous kernels
     if (static_cast<int>(blockIdx.x) < a.tiles_x * a.n_fblk) grad_wl_tile<true>(a, smem_raw);
     else grad_wl_tile<false>(a, smem_raw);
 }
@@ -959,8 +961,7 @@ cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
     dim3 grid((args.tiles_x + args.tiles_y) * args.n_fblk, P.B);
     e = cudaFuncSetAttribute(grad_wl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    grad_wl_kernel<<<grid, kWlThreads, smem, stream>>>(args);
-    return cudaGetLastError();
+    return launch_pdl(false, grad_wl_kernel, grid, dim3(kWlThreads), smem, stream, args);
 }
 
 // ============================================================== unfused cost

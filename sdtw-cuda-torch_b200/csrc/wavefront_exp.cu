@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
     const int b = blockIdx.x / P.csize;
     const int g = crank * wpc + warp;
     const int N = P.N, M = P.M;
+    pdl_trigger();
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);                    // [wpc][kRing][2]
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * 2 * kRing);  // [wpc]
@@ -238,6 +239,10 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     cluster_sync_all();
+    // Set-up above touched shared memory only.  (The forward is launched
+    // plainly; the wait is a no-op then.  Its trigger above lets a reverse pass
+    // launched with programmatic serialization be scheduled early.)
+    pdl_wait();
 
     const uint32_t my_consumed = smem_addr(consumed + warp);
     const uint32_t my_ring_s = smem_addr(ring + warp * 2 * kRing);
@@ -735,6 +740,7 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
     const int b = blockIdx.x / P.csize;
     const int g = crank * wpc + warp;
     const int N = P.N, M = P.M;
+    pdl_trigger();
 
     uint64_t* ring = reinterpret_cast<uint64_t*>(smem_raw);
     uint32_t* consumed = reinterpret_cast<uint32_t*>(ring + wpc * kRing);
@@ -751,6 +757,7 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
         for (int i = threadIdx.x; i < wpc * kYRows * YP; i += blockDim.x) yw_all[i] = 0.f;
     }
     cluster_sync_all();
+    pdl_wait();  // the shares and y of the previous kernels are read from here on
 
     // Messages flow upward: this warp's input comes from warp g+1 (the stripe
     // below), its output goes to warp g-1.
@@ -1103,7 +1110,8 @@ cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream) {
     const void* fn = bwdw_fn(banded, args.gd);
     if (!fn || (args.gd && (!args.x || !args.y || !args.gx || args.dim > args.gd))) return cudaErrorInvalidValue;
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
-    return launch_cluster(fn, dim3(P.B * P.csize), dim3(P.wpc * 32), bwdw_smem(P, args.gd), P.csize, stream, kargs);
+    return launch_cluster(fn, dim3(P.B * P.csize), dim3(P.wpc * 32), bwdw_smem(P, args.gd), P.csize, stream, kargs,
+                          args.pdl != 0);
 }
 
 }  // namespace sdtw

@@ -38,20 +38,24 @@ __host__ __device__ __forceinline__ size_t stripe_base(const WavePlan& P, int b,
 }
 
 // One launch of `fn` in thread-block clusters of `csize` CTAs along x.
+// pdl: the kernel calls pdl_wait() before touching global memory, so it may
+// be launched with programmatic stream serialization.
 inline cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t smem, int csize,
-                                  cudaStream_t stream, void** args) {
+                                  cudaStream_t stream, void** args, bool pdl = false) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = csize;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
