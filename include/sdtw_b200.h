@@ -191,6 +191,23 @@ int sdtw_grad_sqeuclid_f32(const float *G, const float *D_mask, const float *x, 
  * -- replaces softdtw_cuda/barycenters.py:134-137 (clip_grad_norm_, Adam
  *    step, cosine-annealing scheduler step) */
 size_t sdtw_barycenter_workspace_bytes(int B, int N, int M, int dim);
+/* Multi-GPU form of the Adam step: sums [gradient | loss] over `world` ranks
+ * through exchange buffers in peer memory, then steps as
+ * sdtw_barycenter_adam_f32 (one kernel per rank; replaces an all-reduce and the
+ * Adam launch).  peers: device array of the `world` ranks' exchange buffers
+ * (sdtw_barycenter_sync_bytes each, zeroed before first use, every one mapped
+ * into this process, e.g. CUDA IPC or symmetric memory); epoch: a device u64,
+ * zero before first use, advanced by one per call and equal on all ranks.
+ * grad_loss (n + 1 floats, this rank's) is replaced by the sum.  Every rank
+ * must make the same sequence of calls; a rank that does not arrive makes the
+ * others' wait run out (status SDTW_ERR_TIMEOUT at the next call).
+ * -- replaces the all-reduce of softdtw_cuda/distributed.py's sharded
+ *    barycenter (no reference counterpart) and barycenters.py:134-137 */
+size_t sdtw_barycenter_sync_bytes(size_t n, int world);
+int sdtw_barycenter_sync_adam_f32(float *grad_loss, size_t n, const unsigned long long *peers, int world, int rank,
+                                  unsigned long long *epoch, float *bary, float *exp_avg, float *exp_avg_sq,
+                                  const float *lr_table, int max_iter, int *step, float *loss_hist, float *bary_hist,
+                                  float beta1, float beta2, float eps, float max_norm, void *stream);
 int sdtw_barycenter_grad_f32(const float *bary, const float *X, const float *w, float *grad_loss, int B, int N,
                              int M, int dim, float gamma, void *workspace, size_t workspace_bytes, void *stream);
 int sdtw_barycenter_adam_f32(float *bary, float *exp_avg, float *exp_avg_sq, const float *grad_loss, size_t n,

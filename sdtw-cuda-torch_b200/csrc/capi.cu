@@ -147,13 +147,16 @@ std::string diag_text_of(const volatile int* d) {
                   "%s pass, %s wait, problem %d, warp %d, band %d: expected %d, last seen %d",
                   d[0] == 1 ? "forward"
                             : (d[0] == 2 ? "backward"
-                                         : (d[0] == 5 ? "tensor-core gradient" : (d[0] == 6 ? "tensor-core cost" : "?"))),
+                                         : (d[0] == 5 ? "tensor-core gradient"
+                                                      : (d[0] == 6 ? "tensor-core cost"
+                                                                   : (d[0] == 7 ? "barycenter exchange" : "?")))),
                   d[1] == 1 ? "shared-memory ring"
                             : (d[1] == 2 ? "global ring"
                                          : (d[1] == 3 ? "flow-control"
                                                       : (d[1] == 4 ? "MMA completion"
                                                                    : (d[1] == 5 ? "aborted (another wait failed)"
-                                                                                : (d[1] == 6 ? "value range" : "?"))))),
+                                                                                : (d[1] == 6 ? "value range"
+                                                                                             : (d[1] == 7 ? "peer flag" : "?")))))),
                   d[2], d[3], d[4], d[5], d[6]);
     return buf;
 }
@@ -1009,6 +1012,35 @@ int sdtw_barycenter_adam_f32(float* bary, float* exp_avg, float* exp_avg_sq, con
                              beta1, beta2, eps, max_norm, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "adam launch");
+    return SDTW_OK;
+}
+
+size_t sdtw_barycenter_sync_bytes(size_t n, int world) {
+    if (n == 0 || world <= 0) return 0;
+    return bary_sync_bytes(n, world);
+}
+
+int sdtw_barycenter_sync_adam_f32(float* grad_loss, size_t n, const unsigned long long* peers, int world, int rank,
+                                  unsigned long long* epoch, float* bary, float* exp_avg, float* exp_avg_sq,
+                                  const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
+                                  float beta1, float beta2, float eps, float max_norm, void* stream) {
+    int rc;
+    if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+    if (!grad_loss || !peers || !epoch || !bary || !exp_avg || !exp_avg_sq || !lr_table || !step || !loss_hist ||
+        !bary_hist)
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (n == 0 || max_iter <= 0 || world <= 0 || rank < 0 || rank >= world || world > 512)
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "need n, max_iter > 0 and 0 <= rank < world <= 512");
+    if (!(beta1 >= 0.f && beta1 < 1.f) || !(beta2 >= 0.f && beta2 < 1.f) || !(eps >= 0.f) || !(max_norm > 0.f))
+        return fail(SDTW_ERR_INVALID_ARGUMENT, "need 0 <= beta1, beta2 < 1, eps >= 0 and max_norm > 0");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    {
+        KernelTimer kt("bary_sync_adam", st);
+        e = launch_bary_sync_adam(grad_loss, n, peers, world, rank, epoch, bary, exp_avg, exp_avg_sq, lr_table, max_iter,
+                                  step, loss_hist, bary_hist, beta1, beta2, eps, max_norm, wait_ctx(), st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "sync-adam launch");
     return SDTW_OK;
 }
 

@@ -172,6 +172,15 @@ cudaError_t launch_bary_reduce(const float* gx, const float* w, const float* out
 cudaError_t launch_bary_adam(float* bary, float* exp_avg, float* exp_avg_sq, const float* grad_loss, size_t n,
                              const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
                              float beta1, float beta2, float eps, float max_norm, cudaStream_t st);
+//   bary_sync_adam: the sum over `world` ranks of [grad | loss] through the
+//     exchange buffers `peers` (every rank's, bary_sync_bytes each) and the
+//     Adam step in one kernel; grad_loss is replaced by the sum.
+size_t bary_sync_bytes(size_t n, int world);
+cudaError_t launch_bary_sync_adam(float* grad_loss, size_t n, const unsigned long long* peers, int world, int rank,
+                                  unsigned long long* epoch, float* bary, float* exp_avg, float* exp_avg_sq,
+                                  const float* lr_table, int max_iter, int* step, float* loss_hist, float* bary_hist,
+                                  float beta1, float beta2, float eps, float max_norm, const WaitCtx& wc,
+                                  cudaStream_t st);
 // tcgemm.cu: the unfused (expanded, clamped) cost on the tensor cores, written
 // in the wavefront layout.  Requires dim >= 16, dim % 4 == 0 and 16-byte
 // aligned x, y (cost_tc_supported).

@@ -58,6 +58,9 @@ _SIGS = {
     "sdtw_barycenter_workspace_bytes": ([_I, _I, _I, _I], _SZ),
     "sdtw_barycenter_grad_f32": ([_P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _SZ, _P], _I),
     "sdtw_barycenter_adam_f32": ([_P, _P, _P, _P, _SZ, _P, _I, _P, _P, _P, _F, _F, _F, _F, _P], _I),
+    "sdtw_barycenter_sync_bytes": ([_SZ, _I], _SZ),
+    "sdtw_barycenter_sync_adam_f32": ([_P, _SZ, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _F, _F, _F, _F, _P],
+                                      _I),
     "sdtw_cpu_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
     "sdtw_cpu_backward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl], _I),
 }
@@ -247,6 +250,27 @@ def barycenter_adam(bary, exp_avg, exp_avg_sq, grad_loss, lr_table, step, loss_h
                                             _ptr(bary_hist), float(beta1), float(beta2), float(eps), float(max_norm),
                                             _stream(bary.device))
     _check(rc, "barycenter Adam step")
+
+
+def barycenter_sync_bytes(n: int, world: int) -> int:
+    return int(lib().sdtw_barycenter_sync_bytes(n, world))
+
+
+def barycenter_sync_adam(grad_loss, peers, world, rank, epoch, bary, exp_avg, exp_avg_sq, lr_table, step, loss_hist,
+                         bary_hist, beta1=0.9, beta2=0.999, eps=1e-8, max_norm=1.0) -> None:
+    """Sum grad_loss (n + 1,) over the ranks through the exchange buffers whose
+    addresses `peers` (int64 device tensor, one per rank) holds, then the Adam
+    step of barycenter_adam.  `epoch`: int64 device counter (zero at first)."""
+    n = bary.numel()
+    if step.dtype != torch.int32 or epoch.dtype != torch.int64 or peers.dtype != torch.int64:
+        raise ValueError("barycenter_sync_adam: step int32, epoch and peers int64 tensors")
+    with torch.cuda.device(bary.device):
+        rc = lib().sdtw_barycenter_sync_adam_f32(_ptr(grad_loss), n, _ptr(peers), int(world), int(rank), _ptr(epoch),
+                                                 _ptr(bary), _ptr(exp_avg), _ptr(exp_avg_sq), _ptr(lr_table),
+                                                 lr_table.numel(), _ptr(step), _ptr(loss_hist), _ptr(bary_hist),
+                                                 float(beta1), float(beta2), float(eps), float(max_norm),
+                                                 _stream(bary.device))
+    _check(rc, "barycenter exchange and Adam step")
 
 
 def cost_sqeuclid(x: torch.Tensor, y: torch.Tensor, direct: bool = False) -> torch.Tensor:

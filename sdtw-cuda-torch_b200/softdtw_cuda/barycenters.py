@@ -95,9 +95,16 @@ class _BaryGraph:
     (``_native.barycenter_grad``), then clipping, Adam and the histories in
     one kernel (``_native.barycenter_adam``) -- a handful of launches per
     iteration.  Other configurations capture the torch loop body
-    (SoftDTW module, autograd, clip_grad_norm_, capturable Adam)."""
+    (SoftDTW module, autograd, clip_grad_norm_, capturable Adam).
 
-    def __init__(self, X, N, gamma, fused, max_iter, lr, reduce):
+    ``exchange``, if given with the library's path, is called once with the
+    gradient length n and returns the peer-memory exchange of the sharded
+    barycenter (``peers``, ``world``, ``rank``, ``epoch``), or None; the sum
+    over ranks and the Adam step are then one kernel
+    (``_native.barycenter_sync_adam``) in place of ``reduce`` and the Adam
+    launch."""
+
+    def __init__(self, X, N, gamma, fused, max_iter, lr, reduce, exchange=None):
         B, M, Dm = X.shape
         dev = X.device
         self.B, self.N, self.D, self.max_iter = B, N, Dm, max_iter
@@ -113,7 +120,7 @@ class _BaryGraph:
         self.buf = torch.zeros(N * Dm + 1, dtype=X.dtype, device=dev)
         self.native = fused is not False and X.dtype == torch.float32 and X.is_contiguous()
         if self.native:
-            body = self._native_body(X, gamma, reduce)
+            body = self._native_body(X, gamma, reduce, exchange)
         else:
             body = self._torch_body(X, gamma, fused, reduce)
 
@@ -130,8 +137,10 @@ class _BaryGraph:
         with torch.cuda.graph(self.graph):
             body()
 
-    def _native_body(self, X, gamma, reduce):
+    def _native_body(self, X, gamma, reduce, exchange):
         B, N, Dm, dev = self.B, self.N, self.D, X.device
+        self.exchange = exchange(N * Dm) if exchange is not None else None
+        ex = self.exchange
         self.bary = torch.zeros((N, Dm), dtype=torch.float32, device=dev)
         self.exp_avg = torch.zeros_like(self.bary)
         self.exp_avg_sq = torch.zeros_like(self.bary)
@@ -144,6 +153,11 @@ class _BaryGraph:
                 _native.barycenter_grad(bary, X, w, buf, gamma, ws)
             else:
                 buf.zero_()
+            if ex is not None:
+                _native.barycenter_sync_adam(buf, ex.peers, ex.world, ex.rank, ex.epoch, bary, self.exp_avg,
+                                             self.exp_avg_sq, self.lr_table, self.step, self.loss_hist,
+                                             self.bary_hist)
+                return
             if reduce is not None:
                 reduce(buf)
             _native.barycenter_adam(bary, self.exp_avg, self.exp_avg_sq, buf, self.lr_table, self.step,
@@ -242,17 +256,22 @@ class _BaryGraph:
 
 
 def _graph_barycenter(X, w, bary0, gamma, fused, max_iter, lr, early_stopping, patience, tol, verbose,
-                      reduce=None, reduce_key=None, stats=None):
+                      reduce=None, reduce_key=None, stats=None, exchange=None, agree=None):
     """The loop as a replayed CUDA graph (see the module docstring), captured
     once per configuration.  ``stats``, if a dict, receives the number of
-    iterations run and whether this call captured the graph."""
+    iterations run and whether this call captured the graph.  ``agree``, for
+    the sharded barycenter, turns this rank's "the graph is cached" into the
+    answer of all ranks (true only if true everywhere), so that every rank
+    captures -- and runs the collectives of the capture's warm-up -- together."""
     N = bary0.shape[0]
     key = (X.device.index, X.data_ptr(), tuple(X.shape), X.dtype, N, float(gamma), fused, int(max_iter), float(lr),
            reduce_key)
     g = _graphs.pop(key, None)
+    if agree is not None and not agree(g is not None):
+        g = None
     captured = g is None
     if captured:
-        g = _BaryGraph(X, N, gamma, fused, max_iter, lr, reduce)
+        g = _BaryGraph(X, N, gamma, fused, max_iter, lr, reduce, exchange)
         while len(_graphs) >= _GRAPH_CACHE_SIZE:
             _graphs.pop(next(iter(_graphs)))
     _graphs[key] = g  # newest last

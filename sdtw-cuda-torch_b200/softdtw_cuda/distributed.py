@@ -21,8 +21,15 @@ is single-device; these functions are new and keep its single-device results:
   max_iter // 2 on the global loss).  On CUDA one iteration, all-reduce
   included, is captured in a CUDA graph and replayed (barycenters.py's graph
   engine), so a step costs no host launch overhead; every rank captures and
-  replays the same collective sequence.  The cached graphs hold captured NCCL
-  calls: call ``release_graphs()`` (after a device synchronize) before
+  replays the same collective sequence.  With the library's path the sum
+  over ranks does not go through NCCL: each rank writes its [gradient | loss]
+  into every rank's exchange buffer in symmetric (peer-mapped) memory over
+  NVLink and sets a flag there, waits for everybody's flags, sums the slots in
+  rank order and takes the Adam step -- one kernel per rank
+  (``sdtw_barycenter_sync_adam_f32``); NCCL remains for the torch loop body
+  and when symmetric memory is unavailable (``USE_PEER_EXCHANGE``).  The
+  cached graphs hold captured NCCL calls and peer mappings: call
+  ``release_graphs()`` (after a device synchronize) before
   ``torch.distributed.destroy_process_group()``, whose teardown otherwise waits
   on them.
 """
@@ -33,6 +40,7 @@ import time
 import torch
 import torch.distributed as dist
 
+from . import _native
 from .module import SoftDTW
 
 
@@ -108,6 +116,31 @@ class ShardedSoftDTW(torch.nn.Module):
         return sharded_mean(self.loss(x, y), n)
 
 
+# Sum the sharded barycenter's [gradient | loss] over ranks through peer
+# memory (symmetric memory, one kernel with the Adam step) rather than NCCL.
+USE_PEER_EXCHANGE = True
+
+
+class _PeerExchange:
+    """This rank's exchange buffer of the barycenter's sum over ranks, in
+    symmetric memory mapped into every rank, and the addresses of all ranks'
+    buffers (index = rank in `group`).  Creating it is collective."""
+
+    def __init__(self, n: int, group, device):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.rank, self.world = _world(group)
+        nbytes = _native.barycenter_sync_bytes(n, self.world)
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
+        self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=device)
+        # Every buffer is zero before any rank writes into another's.
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+
 def release_graphs() -> None:
     """Release the cached barycenter graphs (and the NCCL calls captured in
     them); to be called before destroying the process group."""
@@ -159,15 +192,25 @@ def sharded_barycenter(
 
     from . import barycenters as _bc
     if _bc.USE_CUDA_GRAPH and X.is_cuda and max_iter >= _bc.GRAPH_MIN_ITERS:
-        reduce = None
+        reduce = exchange = agree = None
         if world > 1:
             def reduce(t):
                 dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+
+            def agree(flag: bool) -> bool:
+                t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=X.device)
+                dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+                return bool(t.item())
+
+            if USE_PEER_EXCHANGE:
+                def exchange(n):
+                    return _PeerExchange(n, group, X.device)
         t0 = time.time()
         info = {}
         res = _bc._graph_barycenter(X, w, bary.detach(), gamma, fused, max_iter, lr, early_stopping, patience, tol,
-                                    verbose and rank == 0, reduce=reduce, reduce_key=("sum", id(group), world),
-                                    stats=info)
+                                    verbose and rank == 0, reduce=reduce,
+                                    reduce_key=("sum", id(group), world, exchange is not None),
+                                    stats=info, exchange=exchange, agree=agree)
         if stats is not None:
             # The all-reduce runs inside the graph, where it cannot be timed
             # apart from the iteration: allreduce_s is None.
