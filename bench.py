@@ -18,11 +18,13 @@ value distributions):
   c5   barycenter of 4096 sequences (length 100, D=3, random-phase sines with
        random shifts + noise), gamma=1, Adam lr 0.1; one step = one Adam
        iteration over the whole set, cells = 4096*100*100.  The set is sharded
-       over the ranks (strong scaling, one NCCL all-reduce per step); the other
+       over the ranks (strong scaling; per step the sum over ranks of [gradient |
+       loss] through peer memory, fused with the Adam step); the other
        workloads run B problems per rank (weak scaling, no collective).
 The default run (c2) also times c3 and c5 and reports them under "workloads"
-(their own ms per step, kernel breakdown, MUFU fraction and latency floor; the
-all-reduce time per step for c5).
+(their own ms per step, kernel breakdown, MUFU fraction and latency floor; for
+c5 on several GPUs the NCCL all-reduce of the gradient buffer and the
+peer-memory exchange + Adam kernel, each timed on its own).
 Metric: DP cells per second summed over all GPUs.  `--impl reference` times the
 reference's CPU algorithm (the oracle restatement in oracle/, all host
 threads) on a bounded sample of the same workload.
@@ -278,6 +280,7 @@ def main():
     from softdtw_cuda import SoftDTW, _native
     from softdtw_cuda.distributed import shard_bounds, sharded_barycenter
     import softdtw_cuda.barycenters as _bc
+    import softdtw_cuda.distributed as _dist
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -371,6 +374,7 @@ def main():
                     # The all-reduce of [gradient | loss] on its own, as the
                     # iteration issues it.
                     allreduce_ms = 0.0
+                    exchange_ms = None
                     if world > 1:
                         buf = torch.zeros(N * Dm + 1, device=dev)
                         for _ in range(5):
@@ -378,6 +382,30 @@ def main():
                         torch.cuda.synchronize(dev)
                         barrier()
                         allreduce_ms = statistics.median(timed(lambda: dist.all_reduce(buf), 20))
+                        if _dist.USE_PEER_EXCHANGE:
+                            # What the iteration runs instead: the peer-memory
+                            # sum over ranks fused with the Adam step (one
+                            # kernel), timed on scratch state.
+                            ex = _dist._PeerExchange(N * Dm, None, dev)
+                            kx = 30
+                            st = dict(bary=torch.zeros(N, Dm, device=dev), m=torch.zeros(N, Dm, device=dev),
+                                      v=torch.zeros(N, Dm, device=dev), lr=torch.full((kx,), 0.1, device=dev),
+                                      step=torch.zeros(1, dtype=torch.int32, device=dev),
+                                      lh=torch.zeros(kx, device=dev), bh=torch.zeros(kx, N, Dm, device=dev))
+
+                            def sync_step():
+                                _native.barycenter_sync_adam(buf, ex.peers, ex.world, ex.rank, ex.epoch, st["bary"],
+                                                             st["m"], st["v"], st["lr"], st["step"], st["lh"],
+                                                             st["bh"])
+
+                            for _ in range(5):
+                                sync_step()
+                            torch.cuda.synchronize(dev)
+                            barrier()
+                            exchange_ms = statistics.median(timed(sync_step, 20))
+                            torch.cuda.synchronize(dev)
+                            barrier()
+                            del ex
                     # The timed call: K iterations of the replayed CUDA graph
                     # (the untimed call of the same length captures it); the
                     # per-step figure is the average.
@@ -419,7 +447,12 @@ def main():
                 modes[mode] = {"value": cells / (mean_ms / 1e3), "ms_per_step": mean_ms,
                                "median_ms": statistics.median(ms), "kernel_ms_per_step": bd, "gpu_launches": n_launch}
                 if allreduce_ms is not None:
+                    # NCCL all-reduce of [grad | loss] on its own; the replayed
+                    # iteration uses the peer-memory exchange when it is on.
                     modes[mode]["allreduce_ms_per_step"] = max_over_ranks(allreduce_ms)
+                    if is_bary and world > 1:
+                        modes[mode]["exchange_adam_ms_per_step"] = (max_over_ranks(exchange_ms)
+                                                                    if exchange_ms is not None else None)
                 pub = PUBLISHED.get(name, {}).get(mode)
                 modes[mode]["vs_published"] = (modes[mode]["value"] / world / pub) if pub else None
 
@@ -622,6 +655,8 @@ def main():
                          "roofline_latency": r["roofline_latency"], "clocks": r["clocks"]}
             if "allreduce_ms_per_step" in hm:
                 subs[sub]["allreduce_ms_per_step"] = hm["allreduce_ms_per_step"]
+            if "exchange_adam_ms_per_step" in hm:
+                subs[sub]["exchange_adam_ms_per_step"] = hm["exchange_adam_ms_per_step"]
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = time_oracle(name, 10.0)
@@ -644,7 +679,7 @@ def main():
         "dtype": "f32", "data": "synthetic, seeded (BASELINE config shapes and distributions)",
         "config": {"workload": f"{name}: {desc}; headline mode = {head_mode}",
                    "global_batch": B if is_bary else B * world, "seq_len": N, "dim": Dm,
-                   "parallelism": (f"dp{world} (sequence-sharded barycenter, NCCL all-reduce per step)" if is_bary
+                   "parallelism": (f"dp{world} (sequence-sharded barycenter, peer-memory sum over ranks per step)" if is_bary
                                    else f"dp{world} (batch-sharded, no collective)"),
                    "l2": ("per-iteration working set (about 1 GB of tables) larger than the 126 MB L2" if is_bary else
                           "flushed before every timed step (256 MiB write, outside the events)"),
