@@ -24,11 +24,9 @@
 //   * the backward weight exp((R[c] - D[c] - R[p]) / gamma) equals the softmax
 //     weight of predecessor p among c's three predecessors, so the reverse pass
 //     recomputes it from the stored scores of c's predecessors, normalised to
-//     sum to one.  It needs no cost values and no log-space E table.  With the
-//     weight store (W, one row per lane: the x/y entry points) the forward
-//     writes those weights itself -- it has the three exponentials at hand --
-//     as (diagonal, upper), the left one being 1 minus both, and the reverse
-//     step is three multiply-adds and a shuffle.
+//     sum to one.  It needs no cost values and no log-space E table.  (The x/y
+//     entry points store the weights themselves instead of scores: the
+//     kernels of wavefront_exp.cu.)
 //   * one warp per stripe of 32*K rows, three live anti-diagonals in registers,
 //     neighbour rows exchanged with one warp shuffle per step, stripe-to-stripe
 //     rows handed over through tagged u64 ring slots in the consumer's shared
@@ -53,23 +51,18 @@ __host__ __device__ constexpr int fwd_pf(int K) { return K >= 4 ? 4 : 8; }
 __host__ __device__ constexpr size_t fwd_cost_offset(int wpc, int K) {
     return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * kFwdPhases * fwd_pf(K) * 32 * K * 8;
 }
-// The reverse pass's weight staging follows its E staging ([wpc][nph][PF][32K] floats).
-__host__ __device__ constexpr size_t bwd_weight_offset(int wpc, int K, int nph) {
+// End of the reverse pass's E staging ([wpc][nph][PF][32K] floats).
+__host__ __device__ constexpr size_t bwd_stage_end(int wpc, int K, int nph) {
     return fwd_stage_offset(wpc) + static_cast<size_t>(wpc) * nph * fwd_pf(K) * 32 * K * 4;
 }
-// Step bodies of the reverse pass with the weight store (one E staging buffer
-// each).  Two measured faster than one and than four on B200 (C2 / C3 / C5
-// shapes), both while its weights sat in a register queue (two groups of
-// prefetch: 9-18 % faster than one) and with the shared-memory staging.
-constexpr int kBwdWeightPhases = 2;
 
 // ============================================================== step groups
 // Steps run in groups of PF.  Per group (warp-uniform code): the consumer lane
 // reads and checks the PF ring slots it will need, the producer lane checks
 // flow control once, and every 32 columns a relaxed store reports progress.
 // Per step: shuffles, the cell math, one shared-memory read of the step's cost
-// (forward) or weights (reverse pass, weight store) and one staged table
-// store, one predicated ring store -- no branches.  A group's input rows are
+// (forward) and one staged table store, one predicated ring store -- no
+// branches.  A group's input rows are
 // copied into shared memory two groups ahead, its output rows leave as one
 // bulk copy (the score-store reverse pass loads its score rows one group ahead
 // into registers).
@@ -91,9 +84,8 @@ struct StepCfg {
 // rows past N) or the band are stored as -inf.  The rows of a group go out as
 // one bulk copy from shared memory; the last cell's score is kept in registers
 // by its lane as it passes.
-template <int K, bool BANDED, bool W>
+template <int K, bool BANDED>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a) {
-    static_assert(!W || K == 1, "the weight store is built for one row per lane");
     constexpr int PF = StepCfg<K>::PF;
     constexpr int NPH = kFwdPhases;  // step bodies (phases): store staging buffer per phase
     constexpr int SR = 32 * K;
@@ -130,12 +122,8 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
     if (g > 0) prev_consumed = mapa_shared(smem_addr(consumed + (g - 1) % wpc), (g - 1) / wpc);
 
     const float kk = a.kk;
-    // Cells outside the table or the band.  The weight store uses a large
-    // finite value instead of -inf: ex2 of (it - m) is still 0 next to any
-    // live score, and a cell whose predecessors are all outside gets finite
-    // weights (1/3 each, with lo = 0) instead of NaN, so its weights need no
-    // mask (the reverse pass multiplies them by E = 0).
-    const float NEG = W ? -1.0e30f : neg_inf();
+    // Cells outside the table or the band.
+    const float NEG = neg_inf();
     const int ibw = a.ibw;
     WaitCtx wc = a.wait;
     wc.kernel = 1;
@@ -363,16 +351,7 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
                         live = live && static_cast<unsigned>(R0 + q0 + k - col + ibw) <= static_cast<unsigned>(2 * ibw);
                     nh[k] = live ? hi : NEG;
                     nl[k] = live ? lo : 0.f;
-                    if constexpr (W) {
-                        // The softmax weights of the diagonal and upper
-                        // predecessors (the left one is 1 minus both): all the
-                        // reverse pass needs of this cell.  Finite for every
-                        // cell (see NEG); outside the table E is 0.
-                        const float inv = rcpf(sm);
-                        Tg[u * SR] = make_float2(ed * inv, eu * inv);
-                    } else {
-                        Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
-                    }
+                    Tg[u * SR + k * 32] = make_float2(nh[k], nl[k]);
                     if (K == 1 || k == k_last) {
                         last_h = (t == t_last) ? nh[k] : last_h;
                         last_l = (t == t_last) ? nl[k] : last_l;
@@ -426,8 +405,8 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) fwd_kernel(const FwdArgs a
         cp_async_wait<0>();
         __syncwarp();
         // Rows outside the groups that ran (padding, or out of the band): -inf,
-        // like every cell outside the table (weights: zero).
-        const float2 fill = W ? make_float2(0.f, 0.f) : make_float2(NEG, 0.f);
+        // like every cell outside the table.
+        const float2 fill = make_float2(NEG, 0.f);
         for (int t = 0; t < t_begin; ++t)
 #pragma unroll
             for (int k = 0; k < K; ++k) Tl[static_cast<size_t>(t) * SR + k * 32] = fill;
@@ -461,14 +440,12 @@ __device__ __forceinline__ float2 load_score(const float2* __restrict__ S, const
 // loads, PF steps ahead), the row above from the neighbour lane by shuffle,
 // and for lane 0 the last row of the previous stripe (one prefetched load).
 // E is written in the wavefront layout.
-template <int K, bool BANDED, bool W>
+template <int K, bool BANDED>
 __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a) {
-    static_assert(!W || K == 1, "the weight store is built for one row per lane");
     constexpr int PF = StepCfg<K>::PF;
     // Prefetch distance: one group (K = 1, whose 512-thread launches leave 128
-    // registers per thread), two groups (K > 1), or with the weight store,
-    // whose steps are short and load one float2 each, kBwdWeightPhases groups.
-    constexpr int NPH = W ? kBwdWeightPhases : (K == 1 ? 1 : 2);
+    // registers per thread), two groups (K > 1).
+    constexpr int NPH = K == 1 ? 1 : 2;
     constexpr int PD = NPH * PF;
     constexpr int SR = 32 * K;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -488,10 +465,6 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
     // by one bulk copy (the rows of a group are contiguous).
     float* bstage = reinterpret_cast<float*>(smem_raw + fwd_stage_offset(wpc)) + warp * NPH * PF * SR;
     const uint32_t bstage_s = smem_addr(bstage);
-    // Weight store: the weights of group g's rows are copied (16-byte cp.async)
-    // two groups ahead into buffer (g - gi_begin) % 3 of [3][PF][SR] float2.
-    const float2* wbuf = reinterpret_cast<const float2*>(smem_raw + bwd_weight_offset(wpc, K, NPH)) + warp * 3 * PF * SR;
-    const uint32_t wbuf_s = smem_addr(wbuf);
     for (int i = threadIdx.x; i < wpc * kRing; i += blockDim.x) ring[i] = ~0ull;
     if (threadIdx.x < wpc) consumed[threadIdx.x] = 0u;
     cluster_sync_all();
@@ -584,41 +557,23 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
             return __ldg(Tp + static_cast<size_t>(cc) * SR);
         };
 
-        // Weight store (W): each step reads its own cell's weights, row t,
-        // staged in shared memory (wcopy); nothing else is loaded.
-        float2 aq[PD][K];  // A(t-2) for the step due in slot j (score store)
+        float2 aq[PD][K];  // A(t-2) for the step due in slot j
         float2 pq[PD];     // PS(t-1) for the step due in slot j
         float2 A1[K];      // A(t-1)
         float2 S1;         // row above at anti-diagonal t-1
-        // Group gi's weights: rows t0 - PF + 1 .. t0 (t0 = t_last - gi * PF), or
-        // an empty commit past the last group.
-        auto wcopy = [&](int gi) {
-            if (gi < gi_end) {
-                const float2* src = Ts + static_cast<size_t>(t_last - gi * PF - PF + 1) * SR;
-                const uint32_t dst = wbuf_s + static_cast<uint32_t>((gi - gi_begin) % 3) * PF * SR * 8u;
 #pragma unroll
-                for (int i = 0; i < PF * SR / 64; ++i) cp_async16(dst + (lane + 32 * i) * 16u, src + (lane + 32 * i) * 2);
-            }
-            cp_async_commit();
-        };
-        if constexpr (W) {
-            wcopy(gi_begin);
-            wcopy(gi_begin + 1);
-        } else {
+        for (int j = 0; j < PD; ++j) {
+            const int t = t_top - j;
 #pragma unroll
-            for (int j = 0; j < PD; ++j) {
-                const int t = t_top - j;
-#pragma unroll
-                for (int k = 0; k < K; ++k) aq[j][k] = loadA(t - 2, k);
-                pq[j] = loadPS(t - 1);
-            }
-#pragma unroll
-            for (int k = 0; k < K; ++k) A1[k] = loadA(t_top - 1, k);
-            const float2 ps = loadPS(t_top);
-            S1.x = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].x, 1);
-            S1.y = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].y, 1);
-            if (lane == 0) S1 = ps_live ? ps : make_float2(NEG, 0.f);
+            for (int k = 0; k < K; ++k) aq[j][k] = loadA(t - 2, k);
+            pq[j] = loadPS(t - 1);
         }
+#pragma unroll
+        for (int k = 0; k < K; ++k) A1[k] = loadA(t_top - 1, k);
+        const float2 ps = loadPS(t_top);
+        S1.x = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].x, 1);
+        S1.y = __shfl_up_sync(SDTW_FULL_MASK, A1[K - 1].y, 1);
+        if (lane == 0) S1 = ps_live ? ps : make_float2(NEG, 0.f);
 
         float accl[K], msg[K], dprev[K];
 #pragma unroll
@@ -705,15 +660,6 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
             }
             // ---- PF reverse steps (step u fills staged row PF - 1 - u, i.e. t0 - u).
             if (lane == 0) bulk_wait_read<NPH - 1>();
-            const float2* wb = wbuf;  // this group's weights (weight store)
-            (void)wb;
-            if constexpr (W) {
-                cp_async_wait<1>();  // committed two groups back
-                __syncwarp();
-                const int gi = (t_last - t0) / PF;
-                wb = wbuf + ((gi - gi_begin) % 3) * PF * SR + (PF - 1) * SR + lane;
-                wcopy(gi + 2);  // into the buffer the previous group read
-            }
             __syncwarp();
             float* Eg = bstage + PH * PF * SR + (PF - 1) * SR + lane;
 #pragma unroll
@@ -721,93 +667,69 @@ __global__ void __launch_bounds__(K == 1 ? 512 : 256) bwd_kernel(const BwdArgs a
                 const int t = t0 - u;
                 constexpr int J0 = PH * PF;
                 (void)J0;
-                if constexpr (W) {
-                    const float2 w = wb[-u * SR];  // (diagonal, upper) weights of cell (q0, t - q0)
-                    float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
-                    const float rv = __shfl_sync(SDTW_FULL_MASK, v, u);
-                    below = (lane == 31) ? rv : below;
-                    const int col = t - q0;
-                    bool live = q0 < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
-                    if constexpr (BANDED)
-                        live = live && static_cast<unsigned>(R0 + q0 - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                    float e = accl[0] + below;
-                    e = (q0 == rows_left - 1 && col == M - 1) ? gb : e;
-                    e = live ? e : 0.f;
-                    Eg[-static_cast<ptrdiff_t>(u) * SR] = e;
-                    const float wl = (1.f - w.x) - w.y;
-                    accl[0] = e * wl;
-                    const float nm = fmaf(e, w.y, dprev[0]);
-                    dprev[0] = e * w.x;
-                    const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
-                    const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
-                    const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
-                    st_one_if(pub, out_g + slot * 8u, pack_tagged(nm, tgo));
-                    msg[0] = nm;
-                } else {
-                    float2 A2[K];
+                float2 A2[K];
 #pragma unroll
-                    for (int k = 0; k < K; ++k) {
-                        A2[k] = aq[J0 + u][k];
-                        aq[J0 + u][k] = loadA(t - 2 - PD, k);
-                    }
-                    float2 S2;
-                    {
-                        const float2 ps = pq[J0 + u];
-                        pq[J0 + u] = loadPS(t - 1 - PD);
-                        S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
-                        S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
-                        S2.x = (lane == 0) ? (ps_live ? ps.x : NEG) : S2.x;
-                        S2.y = (lane == 0) ? (ps_live ? ps.y : 0.f) : S2.y;
-                    }
-                    float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
-                    const float rv = __shfl_sync(SDTW_FULL_MASK, v, u);
-                    below = (lane == 31) ? rv : below;
-                    float nmsg[K];
-#pragma unroll
-                    for (int k = K - 1; k >= 0; --k) {
-                        const int q = q0 + k;
-                        const int col = t - q;
-                        const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
-                        float e = accl[k] + in_below;
-                        float2 tl = A1[k];
-                        float2 tu = (k == 0) ? S1 : A1[k > 0 ? k - 1 : 0];
-                        float2 td = (k == 0) ? S2 : A2[k > 0 ? k - 1 : 0];
-                        bool live = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
-                        if constexpr (BANDED)
-                            live = live && static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
-                        e = (q == rows_left - 1 && col == M - 1) ? gb : e;
-                        e = live ? e : 0.f;
-                        // Predecessor scores; column -1 is the border (+inf R),
-                        // except the corner (-1, -1) of row 0 (R = 0).
-                        const bool c0 = (col == 0);
-                        tl.x = c0 ? NEG : tl.x;
-                        tl.y = c0 ? 0.f : tl.y;
-                        td.x = c0 ? ((R0 + q == 0) ? 0.f : NEG) : td.x;
-                        td.y = c0 ? 0.f : td.y;
-                        Eg[-static_cast<ptrdiff_t>(u) * SR + k * 32] = e;
-                        // Softmax of the predecessors' scores; the lo of the max cancels.
-                        const float m = max3f(td.x, tu.x, tl.x);
-                        const float ed = ex2f((td.x - m) + td.y);
-                        const float eu = ex2f((tu.x - m) + tu.y);
-                        const float el = ex2f((tl.x - m) + tl.y);
-                        const float inv = live ? rcpf(ed + eu + el) : 0.f;
-                        const float ei = e * inv;
-                        accl[k] = ei * el;
-                        nmsg[k] = fmaf(ei, eu, dprev[k]);
-                        dprev[k] = ei * ed;
-                    }
-                    // Message of row 0 to the stripe above, column t.
-                    const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
-                    const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
-                    const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
-                    st_one_if(pub, out_g + slot * 8u, pack_tagged(nmsg[0], tgo));
-#pragma unroll
-                    for (int k = 0; k < K; ++k) {
-                        msg[k] = nmsg[k];
-                        A1[k] = A2[k];
-                    }
-                    S1 = S2;
+                for (int k = 0; k < K; ++k) {
+                    A2[k] = aq[J0 + u][k];
+                    aq[J0 + u][k] = loadA(t - 2 - PD, k);
                 }
+                float2 S2;
+                {
+                    const float2 ps = pq[J0 + u];
+                    pq[J0 + u] = loadPS(t - 1 - PD);
+                    S2.x = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].x, 1);
+                    S2.y = __shfl_up_sync(SDTW_FULL_MASK, A2[K - 1].y, 1);
+                    S2.x = (lane == 0) ? (ps_live ? ps.x : NEG) : S2.x;
+                    S2.y = (lane == 0) ? (ps_live ? ps.y : 0.f) : S2.y;
+                }
+                float below = __shfl_down_sync(SDTW_FULL_MASK, msg[0], 1);
+                const float rv = __shfl_sync(SDTW_FULL_MASK, v, u);
+                below = (lane == 31) ? rv : below;
+                float nmsg[K];
+#pragma unroll
+                for (int k = K - 1; k >= 0; --k) {
+                    const int q = q0 + k;
+                    const int col = t - q;
+                    const float in_below = (k == K - 1) ? below : msg[k < K - 1 ? k + 1 : 0];
+                    float e = accl[k] + in_below;
+                    float2 tl = A1[k];
+                    float2 tu = (k == 0) ? S1 : A1[k > 0 ? k - 1 : 0];
+                    float2 td = (k == 0) ? S2 : A2[k > 0 ? k - 1 : 0];
+                    bool live = q < rows_left && static_cast<unsigned>(col) < static_cast<unsigned>(M);
+                    if constexpr (BANDED)
+                        live = live && static_cast<unsigned>(R0 + q - col + ibw) <= static_cast<unsigned>(2 * ibw);
+                    e = (q == rows_left - 1 && col == M - 1) ? gb : e;
+                    e = live ? e : 0.f;
+                    // Predecessor scores; column -1 is the border (+inf R),
+                    // except the corner (-1, -1) of row 0 (R = 0).
+                    const bool c0 = (col == 0);
+                    tl.x = c0 ? NEG : tl.x;
+                    tl.y = c0 ? 0.f : tl.y;
+                    td.x = c0 ? ((R0 + q == 0) ? 0.f : NEG) : td.x;
+                    td.y = c0 ? 0.f : td.y;
+                    Eg[-static_cast<ptrdiff_t>(u) * SR + k * 32] = e;
+                    // Softmax of the predecessors' scores; the lo of the max cancels.
+                    const float m = max3f(td.x, tu.x, tl.x);
+                    const float ed = ex2f((td.x - m) + td.y);
+                    const float eu = ex2f((tu.x - m) + tu.y);
+                    const float el = ex2f((tl.x - m) + tl.y);
+                    const float inv = live ? rcpf(ed + eu + el) : 0.f;
+                    const float ei = e * inv;
+                    accl[k] = ei * el;
+                    nmsg[k] = fmaf(ei, eu, dprev[k]);
+                    dprev[k] = ei * ed;
+                }
+                // Message of row 0 to the stripe above, column t.
+                const bool pub = has_up && lane == 0 && static_cast<unsigned>(t) < static_cast<unsigned>(M);
+                const uint32_t tgo = up_wrap ? out_tag_wrap : band_base + static_cast<uint32_t>(M - 1 - t);
+                const uint32_t slot = up_wrap ? static_cast<uint32_t>(t) * 2u : (tgo % kRing);
+                st_one_if(pub, out_g + slot * 8u, pack_tagged(nmsg[0], tgo));
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    msg[k] = nmsg[k];
+                    A1[k] = A2[k];
+                }
+                S1 = S2;
             }
             // Rows t0 - PF + 1 .. t0 of E: one bulk copy.
             fence_proxy_async_smem();
@@ -905,12 +827,8 @@ static size_t ring_smem_bytes(const WavePlan& P) {
     return static_cast<size_t>(P.wpc) * 2 * kRing * 8u + static_cast<size_t>(P.wpc) * 4u;
 }
 // The reverse pass stages E rows ([wpc][phases][PF][32K] floats) at the same
-// offset, then (weight store) its weights ([wpc][3][PF][32K] float2).
-static size_t bwd_smem_bytes(const WavePlan& P, bool weights) {
-    const int nph = weights ? kBwdWeightPhases : (P.K == 1 ? 1 : 2);
-    const size_t w = weights ? static_cast<size_t>(P.wpc) * 3 * fwd_pf(P.K) * 32 * P.K * 8u : 0;
-    return bwd_weight_offset(P.wpc, P.K, nph) + w;
-}
+// offset.
+static size_t bwd_smem_bytes(const WavePlan& P) { return bwd_stage_end(P.wpc, P.K, P.K == 1 ? 1 : 2); }
 // The forward adds its store staging ([wpc][phases][PF][32K] float2) and cost
 // staging ([wpc][3][PF][32K] floats) after the ring.
 static size_t fwd_smem_bytes(const WavePlan& P) {
@@ -957,20 +875,20 @@ int max_active_clusters(const WavePlan& P, int pass) {
                 smem[0] = fwdx_smem(P, fp - 2, wide);
                 threads[0] = fwdx_threads(P);
             } else {
-                fns[1] = (const void*)bwd_kernel<1, false, false>;
-                smem[1] = bwd_smem_bytes(P, false);
+                fns[1] = (const void*)bwd_kernel<1, false>;
+                smem[1] = bwd_smem_bytes(P);
                 fns[3] = bwdw_fn(false);
                 smem[3] = bwdw_smem(P);
             }
             break;
         }
         case 2:
-            fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<2, false, false> : (const void*)bwd_kernel<2, false, false>;
-            smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
+            fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<2, false> : (const void*)bwd_kernel<2, false>;
+            smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P);
             break;
         case 4:
-            fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<4, false, false> : (const void*)bwd_kernel<4, false, false>;
-            smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P, false);
+            fns[pass == 1] = pass != 1 ? (const void*)fwd_kernel<4, false> : (const void*)bwd_kernel<4, false>;
+            smem[pass == 1] = pass != 1 ? fwd_smem_bytes(P) : bwd_smem_bytes(P);
             break;
         default: return -1;
     }
@@ -1006,8 +924,8 @@ cudaError_t launch_forward(const FwdArgs& args, cudaStream_t stream) {
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
     const void* fn = nullptr;
     switch (P.K) {
-        case 2: fn = banded ? (const void*)fwd_kernel<2, true, false> : (const void*)fwd_kernel<2, false, false>; break;
-        case 4: fn = banded ? (const void*)fwd_kernel<4, true, false> : (const void*)fwd_kernel<4, false, false>; break;
+        case 2: fn = banded ? (const void*)fwd_kernel<2, true> : (const void*)fwd_kernel<2, false>; break;
+        case 4: fn = banded ? (const void*)fwd_kernel<4, true> : (const void*)fwd_kernel<4, false>; break;
         default: return cudaErrorInvalidValue;
     }
     return launch_cluster(fn, grid, block, fwd_smem_bytes(P), P.csize, stream, kargs);
@@ -1021,12 +939,12 @@ cudaError_t launch_backward(const BwdArgs& args, cudaStream_t stream) {
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
     const void* fn = nullptr;
     switch (P.K) {
-        case 1: fn = banded ? (const void*)bwd_kernel<1, true, false> : (const void*)bwd_kernel<1, false, false>; break;
-        case 2: fn = banded ? (const void*)bwd_kernel<2, true, false> : (const void*)bwd_kernel<2, false, false>; break;
-        case 4: fn = banded ? (const void*)bwd_kernel<4, true, false> : (const void*)bwd_kernel<4, false, false>; break;
+        case 1: fn = banded ? (const void*)bwd_kernel<1, true> : (const void*)bwd_kernel<1, false>; break;
+        case 2: fn = banded ? (const void*)bwd_kernel<2, true> : (const void*)bwd_kernel<2, false>; break;
+        case 4: fn = banded ? (const void*)bwd_kernel<4, true> : (const void*)bwd_kernel<4, false>; break;
         default: return cudaErrorInvalidValue;
     }
-    return launch_cluster(fn, grid, block, bwd_smem_bytes(P, false), P.csize, stream, kargs);
+    return launch_cluster(fn, grid, block, bwd_smem_bytes(P), P.csize, stream, kargs);
 }
 
 cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, float inv_k, cudaStream_t stream) {
