@@ -28,7 +28,8 @@ whose wavefront needs more than one band resets its band-wrap ring inside the
 graph, so every shape can be replayed.  Runs shorter than GRAPH_MIN_ITERS
 iterations, and any capture failure, use the step-by-step loop.  The same
 engine serves ``softdtw_cuda.distributed.sharded_barycenter``, whose captured
-iteration includes the NCCL all-reduce of [gradient | loss].
+iteration includes the sum of [gradient | loss] over the ranks (the library's
+peer-memory exchange fused with the Adam step, or an NCCL all-reduce).
 """
 from __future__ import annotations
 
@@ -53,7 +54,7 @@ def _cosine_lrs(lr: float, max_iter: int) -> list[float]:
     computed by running the scheduler on a throw-away optimizer, so the values
     are the eager loop's exactly."""
     p = torch.zeros(1, requires_grad=True)
-    opt = torch.optim.SGD([p], lr=lr)
+    opt = torch.optim.Adam([p], lr=lr)  # as the loop's optimizer
     sched = torch.optim.lr_scheduler.CosineAnnealingLR(opt, T_max=max_iter, eta_min=lr * 0.1)
     out = []
     for _ in range(max_iter):
