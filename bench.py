@@ -382,11 +382,16 @@ def main():
                         torch.cuda.synchronize(dev)
                         barrier()
                         allreduce_ms = statistics.median(timed(lambda: dist.all_reduce(buf), 20))
+                        ex = None
                         if _dist.USE_PEER_EXCHANGE:
+                            try:
+                                ex = _dist._PeerExchange(N * Dm, None, dev)
+                            except (RuntimeError, ImportError, AttributeError) as err:
+                                print(f"bench: no peer-memory exchange ({err})", file=sys.stderr)
+                        if ex is not None:
                             # What the iteration runs instead: the peer-memory
                             # sum over ranks fused with the Adam step (one
                             # kernel), timed on scratch state.
-                            ex = _dist._PeerExchange(N * Dm, None, dev)
                             kx = 30
                             st = dict(bary=torch.zeros(N, Dm, device=dev), m=torch.zeros(N, Dm, device=dev),
                                       v=torch.zeros(N, Dm, device=dev), lr=torch.full((kx,), 0.1, device=dev),

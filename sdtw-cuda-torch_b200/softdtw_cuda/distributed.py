@@ -36,6 +36,7 @@ is single-device; these functions are new and keep its single-device results:
 from __future__ import annotations
 
 import time
+import warnings
 
 import torch
 import torch.distributed as dist
@@ -204,7 +205,13 @@ def sharded_barycenter(
 
             if USE_PEER_EXCHANGE:
                 def exchange(n):
-                    return _PeerExchange(n, group, X.device)
+                    # Symmetric memory unavailable (it fails on every rank
+                    # before any peer access): the NCCL all-reduce instead.
+                    try:
+                        return _PeerExchange(n, group, X.device)
+                    except (RuntimeError, ImportError, AttributeError) as err:
+                        warnings.warn(f"softdtw_cuda: peer-memory exchange unavailable ({err}); using NCCL")
+                        return None
         t0 = time.time()
         info = {}
         res = _bc._graph_barycenter(X, w, bary.detach(), gamma, fused, max_iter, lr, early_stopping, patience, tol,
