@@ -73,7 +73,7 @@ ALG_BYTES = {"cost_wl": 4, "cost_tc": 4, "wavefront_fwd": 12, "wavefront_bwd": 1
 ALG_MUFU = {"wavefront_fwd": 3, "wavefront_bwd": 4}
 # DRAM bytes per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum,
 # one launch each, cold L2) for the C2 workload, fused mode (profiles/c2_kernels_full.md).
-TRAFFIC_C2 = {"wavefront_fwd": 58.83e6, "wavefront_bwd": 84.35e6, "cost_wl": 8.48e6, "grad_xy": 54.63e6}
+TRAFFIC_C2 = {"wavefront_fwd": 55.90e6, "wavefront_bwd": 82.36e6, "cost_wl": 8.48e6, "grad_xy": 54.63e6}
 
 
 def parse():
