@@ -78,7 +78,8 @@ __global__ void __launch_bounds__(kReduceThreads) bary_reduce_final_kernel(const
     const size_t v = static_cast<size_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
     if (v > n) return;
     float acc = 0.f;
-    for (int s = 0; s < S; ++s) acc += __ldg(part + static_cast<size_t>(s) * (n + 1) + v);
+#pragma unroll 8
+    for (int s = 0; s < S; ++s) acc += __ldg(part + static_cast<size_t>(s) * (n + 1) + v);  // loads in flight together
     grad_loss[v] = acc;
 }
 
