@@ -11,16 +11,20 @@
 // bound by the one read of E; the tensor-core kernels (tcgemm.cu) need tiles of
 // 16+ features to pay their operand preparation.
 //
-// One warp per stripe, up to 8 stripes (a split) per CTA.  For every block of
-// 32 columns the warp stages the 32 x 32 cells of its stripe -- anti-diagonal
-// rows t in [j0, j0 + 63), cell (l, j) at row j - j0 + l, lane l -- in shared
-// memory (pitch 33 floats) and makes two passes over them:
+// One warp per stripe, up to 8 stripes (a split) per CTA, and the columns cut
+// into ranges (column splits) so that the launch has CTAs for every SM.  For
+// every block of 32 columns the warp loads the 32 x 32 cells of its stripe --
+// anti-diagonal rows t in [j0, j0 + 63), cell (l, j) at row j - j0 + l, lane l
+// -- stores them in shared memory by (column, row) with an XOR swizzle, and
+// makes two passes over them:
 //   row pass     lane l: row l over the 32 columns, y rows broadcast; the row
-//                sums stay in registers across all blocks (grad_x at the end)
+//                sums stay in registers across the range's blocks (grad_x at
+//                the end, or a partial per column split)
 //   column pass  lane c: column c over the 32 rows, x rows broadcast; the
 //                split's warps' column sums are added in warp order and stored
 //                to the split's slice of the partial buffer (no atomics)
-// grad_small_finalize_kernel sums the splits' column partials into grad_y.
+// grad_small_finalize_kernel sums the splits' column partials into grad_y,
+// grad_small_finalize_x_kernel the column splits' row partials into grad_x.
 #include <algorithm>
 #include <cstdint>
 
@@ -29,17 +33,27 @@
 namespace sdtw {
 
 constexpr int kSmallTile = 63;   // anti-diagonal rows of a (stripe, 32-column block)
-constexpr int kSmallPitch = 33;  // floats per staged row: the column pass hits 32 banks
 constexpr int kSmallWarps = 8;   // stripes per CTA
+constexpr int kSmallCtas = 148 * 4;  // CTAs that fill a B200 at this kernel's occupancy
+constexpr int kSmallMinBlocks = 8;   // 32-column blocks per column split, at least
 
 template <int DP>
 struct SmallSmem {
-    static constexpr int E = (kSmallTile * kSmallPitch + 3) / 4 * 4;  // per warp (16-byte multiple)
-    static constexpr int X = 32 * DP;                   // per warp: its stripe's x rows
-    static constexpr int RED = 32 * (DP + 1);           // per warp: column sums of a block
-    static constexpr int Y = 32 * DP;                   // the block's y rows
+    static constexpr int E = (32 * 33 + 3) / 4 * 4;  // per warp: the block's cells
+    static constexpr int X = 32 * DP;          // per warp: its stripe's x rows
+    static constexpr int RED = 32 * (DP + 1);  // per warp: column sums of a block
+    static constexpr int Y = 32 * DP;          // the block's y rows
     static constexpr int floats(int warps) { return warps * (E + X + RED) + Y; }
 };
+// Cell (row l, column c) of a warp's block sits at c * 33 + row_slot(l), where
+// row_slot (0, 2, .., 30, 1, 3, .., 31) permutes the rows: the row pass (lanes
+// = rows, one column: banks c + row_slot(l)) and the column pass (lanes =
+// columns, one row: banks c + row_slot(l)) read 32 distinct banks, and the
+// anti-diagonal stores (lane l, column r - l: banks r + row_slot(l) - l) as
+// well but for one pair of lanes in one store of the 63.  Every address is a
+// per-lane base plus a constant offset (33 r), so the stores need no address
+// arithmetic.
+__device__ __forceinline__ int row_slot(int l) { return ((l & 15) << 1) | (l >> 4); }
 
 template <int DP, bool MASKED>
 __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const float* __restrict__ Ew,
@@ -47,7 +61,8 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
                                                                       const float* __restrict__ x,
                                                                       const float* __restrict__ y,
                                                                       float* __restrict__ gx,
-                                                                      float* __restrict__ part, WavePlan P, int dim,
+                                                                      float* __restrict__ part,
+                                                                      float* __restrict__ part_x, WavePlan P, int dim,
                                                                       int n_split, size_t xbs) {
     extern __shared__ __align__(16) float sm[];
     pdl_trigger();
@@ -60,6 +75,10 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
     float* Yt = red + warps * SmallSmem<DP>::RED;
     const int N = P.N, M = P.M;
     const int b = blockIdx.y, split = blockIdx.x;  // problem, split of 8 stripes
+    const int cs = blockIdx.z, n_cs = gridDim.z;   // column split: blocks [blk0, blk1)
+    const int nblk = (M + 31) / 32;
+    const int blk0 = static_cast<int>(static_cast<long long>(nblk) * cs / n_cs);
+    const int blk1 = static_cast<int>(static_cast<long long>(nblk) * (cs + 1) / n_cs);
     const int s = split * warps + warp;
     const bool live = s < P.n_stripes;  // warp-uniform
     const int R0 = s * 32;
@@ -71,11 +90,12 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
     for (int d = 0; d < DP; ++d)
         Xt[lane * DP + d] =
             (live && R0 + lane < N && d < dim) ? __ldg(x + b * xbs + static_cast<size_t>(R0 + lane) * dim + d) : 0.f;
+    const int rs = row_slot(lane);
     float racc[DP + 1];  // row R0 + lane: sum_j G y_j (DP), sum_j G
 #pragma unroll
     for (int d = 0; d <= DP; ++d) racc[d] = 0.f;
 
-    for (int j0 = 0; j0 < M; j0 += 32) {
+    for (int j0 = blk0 * 32; j0 < blk1 * 32; j0 += 32) {
         __syncthreads();  // Yt and red of the previous block are consumed
         for (int i = threadIdx.x; i < 32 * DP; i += blockDim.x) {
             const int jj = i / DP, d = i % DP;
@@ -94,8 +114,10 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
                     if (MASKED && !(__ldg(Mw + base + static_cast<size_t>(j0 + r) * 32) > 0.f)) v[r] = 0.f;
                 }
             }
+            const int sbase = row_slot(lane) - 33 * lane;  // cell (row lane, column r - lane) at sbase + 33 r
 #pragma unroll
-            for (int r = 0; r < kSmallTile; ++r) Et[r * kSmallPitch + lane] = v[r];
+            for (int r = 0; r < kSmallTile; ++r)
+                if (static_cast<unsigned>(r - lane) < 32u) Et[sbase + 33 * r] = v[r];
         }
         __syncthreads();
         float cacc[DP + 1];
@@ -105,7 +127,7 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
             if (need_x) {
 #pragma unroll 4
                 for (int jj = 0; jj < 32; ++jj) {
-                    const float g = Et[(jj + lane) * kSmallPitch + lane];
+                    const float g = Et[jj * 33 + rs];  // cell (row lane, column jj)
                     const float4* y4 = reinterpret_cast<const float4*>(Yt + jj * DP);
                     racc[DP] += g;
 #pragma unroll
@@ -121,7 +143,7 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
             if (need_y) {
 #pragma unroll 4
                 for (int l = 0; l < 32; ++l) {
-                    const float g = Et[(lane + l) * kSmallPitch + l];
+                    const float g = Et[lane * 33 + row_slot(l)];  // cell (row l, column lane)
                     const float4* x4 = reinterpret_cast<const float4*>(Xt + l * DP);
                     cacc[DP] += g;
 #pragma unroll
@@ -149,11 +171,38 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
         }
     }
     if (need_x && live && R0 + lane < N) {
-        const size_t o = (static_cast<size_t>(b) * N + R0 + lane) * dim;
+        if (n_cs == 1) {
+            const size_t o = (static_cast<size_t>(b) * N + R0 + lane) * dim;
 #pragma unroll
-        for (int d = 0; d < DP; ++d)
-            if (d < dim) gx[o + d] = 2.f * (Xt[lane * DP + d] * racc[DP] - racc[d]);
+            for (int d = 0; d < DP; ++d)
+                if (d < dim) gx[o + d] = 2.f * (Xt[lane * DP + d] * racc[DP] - racc[d]);
+        } else {
+            // This column split's row sums; grad_small_finalize_x_kernel adds them up.
+            float* px = part_x + ((static_cast<size_t>(b) * n_cs + cs) * N + R0 + lane) * (DP + 1);
+#pragma unroll
+            for (int d = 0; d <= DP; ++d) px[d] = racc[d];
+        }
     }
+}
+
+// grad_x from the column splits' row partials, summed in split order.
+template <int DP>
+__global__ void __launch_bounds__(256) grad_small_finalize_x_kernel(const float* __restrict__ part_x,
+                                                                    const float* __restrict__ x,
+                                                                    float* __restrict__ gx, int B, int N, int dim,
+                                                                    int n_cs, size_t xbs) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(B) * N * dim) return;
+    const int d = static_cast<int>(i % dim);
+    const size_t bi = i / dim;
+    const int r = static_cast<int>(bi % N), b = static_cast<int>(bi / N);
+    float s = 0.f, t = 0.f;
+    for (int k = 0; k < n_cs; ++k) {
+        const float* px = part_x + ((static_cast<size_t>(b) * n_cs + k) * N + r) * (DP + 1);
+        s += __ldg(px + DP);
+        t += __ldg(px + d);
+    }
+    gx[i] = 2.f * (__ldg(x + b * xbs + static_cast<size_t>(r) * dim + d) * s - t);
 }
 
 // grad_y from the splits' column partials, summed in split order.
@@ -185,8 +234,25 @@ int grad_small_splits(const WavePlan& P) { return (P.n_stripes + kSmallWarps - 1
 
 bool grad_small_supported(const WavePlan& P, int dim) { return P.K == 1 && dim >= 1 && dim <= 16; }
 
+// Column splits: enough CTAs to fill the GPU, with at least kSmallMinBlocks
+// blocks of 32 columns each (C3, 16 x 4096^2 x 8: 3 splits, 768 CTAs).
+static int small_colsplits(const WavePlan& P) {
+    const int nblk = (P.M + 31) / 32;
+    const int ctas = grad_small_splits(P) * P.B;
+    const int want = (kSmallCtas + ctas - 1) / ctas;
+    return std::max(1, std::min(want, nblk / kSmallMinBlocks));
+}
+
+static size_t part_y_floats(const WavePlan& P, int dim) {
+    return static_cast<size_t>(P.B) * grad_small_splits(P) * P.M * (small_dp(dim) + 1);
+}
+
+// The splits' column partials of grad_y, then (more than one column split)
+// the column splits' row partials of grad_x.
 size_t grad_small_part_bytes(const WavePlan& P, int dim) {
-    return static_cast<size_t>(P.B) * grad_small_splits(P) * P.M * (small_dp(dim) + 1) * sizeof(float);
+    const int n_cs = small_colsplits(P);
+    const size_t px = n_cs > 1 ? static_cast<size_t>(P.B) * n_cs * P.N * (small_dp(dim) + 1) : 0;
+    return (part_y_floats(P, dim) + px) * sizeof(float);
 }
 
 template <int DP>
@@ -198,15 +264,25 @@ static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, co
     const void* fn = Mw ? (const void*)grad_small_kernel<DP, true> : (const void*)grad_small_kernel<DP, false>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const dim3 grid(n_split, P.B);
+    const int n_cs = small_colsplits(P);
+    const dim3 grid(n_split, P.B, n_cs);
     float* pp = gy ? part : nullptr;
+    float* px = part + part_y_floats(P, dim);
     if (Mw)
-        e = launch_pdl(false, grad_small_kernel<DP, true>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, P, dim,
-                       n_split, xbs);
+        e = launch_pdl(false, grad_small_kernel<DP, true>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, px, P,
+                       dim, n_split, xbs);
     else
-        e = launch_pdl(false, grad_small_kernel<DP, false>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, P, dim,
-                       n_split, xbs);
-    if (e != cudaSuccess || !gy) return e;
+        e = launch_pdl(false, grad_small_kernel<DP, false>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, px, P,
+                       dim, n_split, xbs);
+    if (e != cudaSuccess) return e;
+    if (gx && n_cs > 1) {
+        const size_t nx = static_cast<size_t>(P.B) * P.N * dim;
+        grad_small_finalize_x_kernel<DP><<<static_cast<unsigned>((nx + 255) / 256), 256, 0, st>>>(px, x, gx, P.B, P.N,
+                                                                                                 dim, n_cs, xbs);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (!gy) return cudaSuccess;
     const size_t n = static_cast<size_t>(P.B) * P.M * dim;
     return launch_pdl(false, grad_small_finalize_kernel<DP>, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st,
                       part, y, gy, P.B, P.M, dim, n_split);
