@@ -34,7 +34,10 @@ namespace sdtw {
 
 constexpr int kSmallTile = 63;   // anti-diagonal rows of a (stripe, 32-column block)
 constexpr int kSmallWarps = 8;   // stripes per CTA
-constexpr int kSmallCtas = 148 * 4;  // CTAs that fill a B200 at this kernel's occupancy
+// CTAs a launch aims at (column splits multiply the stripe splits up to it):
+// measured at C3 (256 stripe-split CTAs), 2 / 3 / 4 / 6 column splits took
+// 0.663 / 0.717 / 0.607 / 0.626 ms.
+constexpr int kSmallCtas = 1024;
 constexpr int kSmallMinBlocks = 8;   // 32-column blocks per column split, at least
 
 template <int DP>
@@ -234,8 +237,8 @@ int grad_small_splits(const WavePlan& P) { return (P.n_stripes + kSmallWarps - 1
 
 bool grad_small_supported(const WavePlan& P, int dim) { return P.K == 1 && dim >= 1 && dim <= 16; }
 
-// Column splits: enough CTAs to fill the GPU, with at least kSmallMinBlocks
-// blocks of 32 columns each (C3, 16 x 4096^2 x 8: 3 splits, 768 CTAs).
+// Column splits: about kSmallCtas CTAs, with at least kSmallMinBlocks blocks
+// of 32 columns each (C3, 16 x 4096^2 x 8: 4 splits, 1024 CTAs).
 static int small_colsplits(const WavePlan& P) {
     const int nblk = (P.M + 31) / 32;
     const int ctas = grad_small_splits(P) * P.B;
