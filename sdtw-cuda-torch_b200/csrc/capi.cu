@@ -381,7 +381,7 @@ cudaError_t reset_wrap(const WavePlan& P, uint64_t* wrap, cudaStream_t stream) {
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr,
                 const float* x = nullptr, const float* y = nullptr, int dim = 0, int dp = 0,
-                bool x_shared = false) {
+                bool x_shared = false, bool clamp_mask = false) {
     FwdArgs a{};
     const int pass = dp ? 2 + dp : 0;
     a.P = plan(B, N, M, pass);
@@ -396,6 +396,7 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
     }
     a.x = x;
     a.x_bstride = x_shared ? 0 : static_cast<size_t>(N) * dim;
+    a.clamp_mask = (clamp_mask && weights) ? 1 : 0;
     a.y = y;
     a.dim = dim;
     a.dp = dp;
@@ -1063,8 +1064,10 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
         e = launch_cost_wl(x, y, cost, plan(B, N, M, 0), dim, false, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "cost launch");
+    // With the share store the clamp mask of the gradient is marked in the
+    // shares, so the reverse pass stores E already masked.
     return run_forward(cost, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st,
-                       weight_store(B, N, M));
+                       weight_store(B, N, M), nullptr, nullptr, nullptr, 0, 0, false, true);
 }
 
 int sdtw_backward_sqeuclid_f32(const float* x, const float* y, const float* score, const float* cost,
@@ -1075,8 +1078,10 @@ int sdtw_backward_sqeuclid_f32(const float* x, const float* y, const float* scor
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !cost) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     if ((rc = check_ws(workspace, workspace_bytes, sdtw_workspace_bytes_xy(B, N, M, dim)))) return rc;
-    return backward_xy_common(x, y, score, cost, grad_out, grad_x, grad_y, B, N, M, dim, bandwidth, workspace,
-                              static_cast<cudaStream_t>(stream));
+    // Share store: E comes out of the reverse pass masked (the forward marked
+    // the clamped costs); score store: the gradient kernels apply the mask.
+    return backward_xy_common(x, y, score, weight_store(B, N, M) ? nullptr : cost, grad_out, grad_x, grad_y, B, N, M,
+                              dim, bandwidth, workspace, static_cast<cudaStream_t>(stream));
 }
 
 int sdtw_grad_sqeuclid_f32(const float* G, const float* D_mask, const float* x, const float* y, float* grad_x,

@@ -34,6 +34,8 @@ struct FwdArgs {
     int dp;           // 0: costs from Dw; else the feature padding (fused_dp)
     size_t x_bstride;  // floats between problems' x (N * dim; 0 = one x for every problem)
     int wide;          // nonzero: the 128-register forward (fwdx_kernel WIDE), pass 32 + (its pass)
+    int clamp_mask;    // nonzero (share store): the sign bit of a cell's diagonal share marks a cost that
+                       // is not > 0 (the unfused cost's clamp), and the reverse pass stores E = 0 there
     WaitCtx wait;
 };
 

@@ -465,7 +465,9 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                     if constexpr (BANDED)
                         live = live && static_cast<unsigned>(R0 + lane - col + ibw) <= static_cast<unsigned>(2 * ibw);
                     pmax = max_nan(pmax, (live || !masked) ? pa : 0.f);
-                    kb[u * 32] = make_uint2(__float_as_uint(km), static_cast<uint32_t>(kx));
+                    // The clamp mark travels in K's mantissa sign bit (K > 0).
+                    const uint32_t mark = (W && a.clamp_mask && !(c > 0.f)) ? 0x80000000u : 0u;
+                    kb[u * 32] = make_uint2(__float_as_uint(km) | mark, static_cast<uint32_t>(kx));
                 }
                 if constexpr (DP == 0) cost_copy(gi + 2);  // into the buffer just read
                 // ---- ring input: the row above for columns t0 .. t0+PF-1, slot u
@@ -579,7 +581,8 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                     }
                 }
                 const int t = t0 + u;
-                const float km = __uint_as_float(kq[u % PH].x);
+                const uint32_t kbits = kq[u % PH].x;
+                const float km = __uint_as_float(kbits & 0x7fffffffu);
                 const int ke = static_cast<int>(kq[u % PH].y);
                 const uint2 ri = rq[u % PH];
                 float mu = __shfl_up_sync(SDTW_FULL_MASK, m_l, 1);
@@ -603,8 +606,9 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                 if constexpr (W) {
                     // The shares of the diagonal and upper predecessors: all the
                     // reverse pass needs of this cell.
+                    // (With the clamp mark in the diagonal share's sign bit.)
                     const float inv = rcpf(sum);
-                    rec = make_float2(vd * inv, vu * inv);
+                    rec = make_float2(__uint_as_float(__float_as_uint(vd * inv) | (kbits & 0x80000000u)), vu * inv);
                 } else {
                     rec = (en == kEneg) ? make_float2(neg_inf(), 0.f) : to_score(mn, en);
                 }
@@ -965,24 +969,27 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
                     e = (lane == rows_left - 1 && col == M - 1) ? gb : e;
                     e = live ? e : 0.f;
                 }
-                const float dn = e * w.x;            // to the diagonal predecessor (two steps on)
+                const float dn = e * fabsf(w.x);     // to the diagonal predecessor (two steps on)
                 msg = fmaf(e, w.y, dprev);           // to the row above: upper share + previous diagonal
                 accl = fmaf(-e, w.y, e - dn);        // left share: e * (1 - wd - wu)
                 dprev = dn;
                 if (lane == 0) pub_s[u] = msg;
+                // The stored (and chain-ruled) E is zero where the forward marked
+                // a clamped cost; the recurrence itself carries e unmasked.
+                const float eo = (__float_as_uint(w.x) >> 31) ? 0.f : e;
                 if constexpr (GD == 0) {
-                    El[static_cast<size_t>(t) * 32] = e;  // one coalesced row store per step
+                    El[static_cast<size_t>(t) * 32] = eo;  // one coalesced row store per step
                 } else {
                     // Row: E y_j with y_j = window row t - lane.
                     const float4* yr = reinterpret_cast<const float4*>(ywin + ((t - lane) & (kYRows - 1)) * YP);
-                    rsum += e;
+                    rsum += eo;
 #pragma unroll
                     for (int q = 0; q < GD / 4; ++q) {
                         const float4 yv = yr[q];
-                        racc[4 * q + 0] = fmaf(e, yv.x, racc[4 * q + 0]);
-                        racc[4 * q + 1] = fmaf(e, yv.y, racc[4 * q + 1]);
-                        racc[4 * q + 2] = fmaf(e, yv.z, racc[4 * q + 2]);
-                        racc[4 * q + 3] = fmaf(e, yv.w, racc[4 * q + 3]);
+                        racc[4 * q + 0] = fmaf(eo, yv.x, racc[4 * q + 0]);
+                        racc[4 * q + 1] = fmaf(eo, yv.y, racc[4 * q + 1]);
+                        racc[4 * q + 2] = fmaf(eo, yv.z, racc[4 * q + 2]);
+                        racc[4 * q + 3] = fmaf(eo, yv.w, racc[4 * q + 3]);
                     }
                 }
             }
