@@ -148,6 +148,8 @@ int sdtw_backward_xy_f32(const float *x, const float *y, const float *score, con
 /* Unfused x/y path: the cost ||x||^2 + ||y||^2 - 2 x.y clamped at 0 (as
  * softdtw_cuda/distances.py:6-28) is computed into `cost` (sdtw_cost_elems
  * floats, kept by the caller for the backward), then the forward DP runs on it.
+ * With one row per lane the `score` buffer also marks the clamped cells (for
+ * the backward's chain rule), so it differs from sdtw_forward_xy_f32's.
  * -- replaces softdtw_cuda/module.py:116-118 (pairwise_distance followed by
  *    SoftDTWAutograd.apply) for CUDA tensors */
 int sdtw_forward_sqeuclid_f32(const float *x, const float *y, float *score, float *cost, float *out, int B,
