@@ -165,6 +165,33 @@ int sdtw_backward_sqeuclid_f32(const float *x, const float *y, const float *scor
                                float gamma, float bandwidth, void *workspace, size_t workspace_bytes,
                                void *stream);
 
+/* normalize=True: the 3B problems (x_b, y_b), (x_b, x_b), (y_b, y_b), b < B,
+ * read x (B,N,dim) and y (B,N,dim) in place, without concatenated copies.
+ * `out` gets 3B losses in that order; score and cost are sized for 3B
+ * problems of N x N (sdtw_score_elems(3B, N, N), sdtw_cost_elems(3B, N, N)).
+ * The backward takes the 3B upstream gradients (NULL = ones) and writes
+ * grad_x and grad_y (both required) of sum_p grad_out[p] * out[p], the self
+ * pairs' two sides included.  Workspace bytes: the fused forward
+ * sdtw_workspace_bytes_xy(3B, N, N, dim), the unfused forward
+ * sdtw_workspace_bytes(3B, N, N), the backwards sdtw_workspace_bytes_norm(B, N, dim).
+ * -- replaces softdtw_cuda/module.py:99-111 (torch.cat([x, x, y]),
+ *    torch.cat([y, x, y]) and one call on the 3B pairs), with
+ *    sdtw_forward_xy_f32 / sdtw_backward_xy_f32 (fused) or
+ *    sdtw_forward_sqeuclid_f32 / sdtw_backward_sqeuclid_f32 (unfused) on them */
+size_t sdtw_workspace_bytes_norm(int B, int N, int dim);
+int sdtw_forward_xy_norm_f32(const float *x, const float *y, float *score, float *out, int B, int N, int dim,
+                             float gamma, float bandwidth, void *workspace, size_t workspace_bytes, void *stream);
+int sdtw_backward_xy_norm_f32(const float *x, const float *y, const float *score, const float *grad_out,
+                              float *grad_x, float *grad_y, int B, int N, int dim, float gamma, float bandwidth,
+                              void *workspace, size_t workspace_bytes, void *stream);
+int sdtw_forward_sqeuclid_norm_f32(const float *x, const float *y, float *score, float *cost, float *out, int B,
+                                   int N, int dim, float gamma, float bandwidth, void *workspace,
+                                   size_t workspace_bytes, void *stream);
+int sdtw_backward_sqeuclid_norm_f32(const float *x, const float *y, const float *score, const float *cost,
+                                    const float *grad_out, float *grad_x, float *grad_y, int B, int N, int dim,
+                                    float gamma, float bandwidth, void *workspace, size_t workspace_bytes,
+                                    void *stream);
+
 /* Chain rule of the unfused cost: given G = dL/dD (B,N,M) and the clamped cost
  * D used as the clamp mask (NULL = no mask), writes grad_x, grad_y.
  * -- replaces torch autograd of softdtw_cuda/distances.py:20-28 */

@@ -380,8 +380,8 @@ cudaError_t reset_wrap(const WavePlan& P, uint64_t* wrap, cudaStream_t stream) {
 // Dw: the cost table, or null with x, y, dim, dp (> 0) for the fused costs.
 int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, float gamma, float bw,
                 uint64_t* wrap, cudaStream_t stream, bool weights = false, const WaitCtx* wait = nullptr,
-                const float* x = nullptr, const float* y = nullptr, int dim = 0, int dp = 0,
-                bool x_shared = false, bool clamp_mask = false) {
+                SeqIn x = one_seq<const float>(nullptr), SeqIn y = one_seq<const float>(nullptr), int dim = 0,
+                int dp = 0, bool x_shared = false, bool clamp_mask = false) {
     FwdArgs a{};
     const int pass = dp ? 2 + dp : 0;
     a.P = plan(B, N, M, pass);
@@ -424,10 +424,11 @@ int run_forward(const float* Dw, float* score, float* out, int B, int N, int M, 
 }
 
 int run_backward(const float* score, const float* grad_out, float* Ew, int B, int N, int M, float bw,
-                 uint64_t* wrap, cudaStream_t stream, bool weights = false) {
+                 uint64_t* wrap, cudaStream_t stream, bool weights = false, bool clamp_mask = false) {
     BwdArgs a{};
     a.P = plan(B, N, M, 1);
     a.weights = weights ? 1 : 0;
+    a.clamp_mask = (weights && clamp_mask) ? 1 : 0;
     a.score = reinterpret_cast<const float2*>(score);
     a.grad_out = grad_out;
     a.Ew = Ew;
@@ -786,15 +787,11 @@ int sdtw_backward_f32(const float* score, const float* grad_out, float* E, int B
     return SDTW_OK;
 }
 
-int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out, int B, int N, int M, int dim,
-                        float gamma, float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
-    int rc;
-    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
-    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
-    if (!x || !y || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+// The fused forward over B problems whose sequences x, y name (one batch, or
+// the normalized triple); the caller has checked the arguments.
+static int forward_xy_common(const SeqIn& x, const SeqIn& y, float* score, float* out, int B, int N, int M, int dim,
+                      float gamma, float bandwidth, void* workspace, cudaStream_t st) {
     const size_t w0 = wave_ws_xy(B, N, M, dim);
-    if ((rc = check_ws(workspace, workspace_bytes, w0 + wl_bytes(B, N, M)))) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     // Up to 16 features: the costs are computed inside the forward from x and
     // y (no cost table); more features: a cost table first (see fused_dp).
     const int dp = weight_store(B, N, M) ? fused_dp(dim, x, y) : 0;
@@ -812,23 +809,37 @@ int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out
                        weight_store(B, N, M));
 }
 
+int sdtw_forward_xy_f32(const float* x, const float* y, float* score, float* out, int B, int N, int M, int dim,
+                        float gamma, float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_common(B, N, M, gamma)) || (rc = check_score(score))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if ((rc = check_ws(workspace, workspace_bytes, wave_ws_xy(B, N, M, dim) + wl_bytes(B, N, M)))) return rc;
+    return forward_xy_common(one_seq(x), one_seq(y), score, out, B, N, M, dim, gamma, bandwidth, workspace,
+                             static_cast<cudaStream_t>(stream));
+}
+
 // Backward through the x/y chain rule; mask_w (WL cost) applies the clamp mask
 // of the unfused cost, or is null for the fused cost.
-int backward_xy_common(const float* x, const float* y, const float* score, const float* mask_w, const float* grad_out,
-                       float* grad_x, float* grad_y, int B, int N, int M, int dim, float bandwidth, void* workspace,
-                       cudaStream_t st) {
+// marked: the shares carry the unfused forward's clamp marks (share store).
+static int backward_xy_common(const SeqIn& x, const SeqIn& y, const float* score, const float* mask_w, bool marked,
+                              const float* grad_out, const SeqOut& gxs, const SeqOut& gys, int B, int N, int M, int dim,
+                              float bandwidth, void* workspace, cudaStream_t st) {
     const size_t w0 = wave_ws_xy(B, N, M, dim);
     float* Ew = reinterpret_cast<float*>(static_cast<char*>(workspace) + w0);
-    // Only grad_x, fused cost, up to 16 features, no band: the reverse pass
-    // applies the chain rule as it goes and E never reaches memory.
-    const int gd = (!mask_w && grad_x && !grad_y && weight_store(B, N, M) && int_band(bandwidth) >= N + M)
-                       ? grad_fused_gd(dim, y)
+    const bool grad_x = !gxs.null(), grad_y = !gys.null();
+    // Only grad_x of one batch, fused cost, up to 16 features, no band: the
+    // reverse pass applies the chain rule as it goes and E never reaches memory.
+    const int gd = (!mask_w && grad_x && !grad_y && x.per >= B && weight_store(B, N, M) &&
+                    int_band(bandwidth) >= N + M)
+                       ? grad_fused_gd(dim, y.p[0])
                        : 0;
     if (gd)
-        return run_backward_grad(score, grad_out, B, N, M, static_cast<uint64_t*>(workspace), st, x,
-                                 static_cast<size_t>(N) * dim, y, dim, gd, grad_x);
+        return run_backward_grad(score, grad_out, B, N, M, static_cast<uint64_t*>(workspace), st, x.p[0],
+                                 static_cast<size_t>(N) * dim, y.p[0], dim, gd, gxs.p[0]);
     int rc = run_backward(score, grad_out, Ew, B, N, M, bandwidth, static_cast<uint64_t*>(workspace), st,
-                          weight_store(B, N, M));
+                          weight_store(B, N, M), marked);
     if (rc) return rc;
     if (!grad_x && !grad_y) return SDTW_OK;
     GradTcArgs g{};
@@ -837,8 +848,8 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     g.Mw = mask_w;
     g.x = x;
     g.y = y;
-    g.gx = grad_x;
-    g.gy = grad_y;
+    g.gx = gxs;
+    g.gy = gys;
     g.dim = dim;
     g.tiles_x = grad_x ? (N + 127) / 128 : 0;
     g.tiles_y = grad_y ? (M + 127) / 128 : 0;
@@ -849,7 +860,7 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
     if (grad_small_supported(g.P, dim)) {
         // Few features: the contraction on the FP32 pipes, one read of E.
         KernelTimer kt("grad_xy", st, grad_y ? 2 : 1);
-        e = launch_grad_small(Ew, mask_w, x, y, grad_x, grad_y, reinterpret_cast<float*>(region), g.P, dim, st,
+        e = launch_grad_small(Ew, mask_w, x, y, gxs, gys, reinterpret_cast<float*>(region), g.P, dim, st,
                               static_cast<size_t>(N) * dim);
         if (e != cudaSuccess) return cuda_fail(e, "grad launch");
         return SDTW_OK;
@@ -862,7 +873,8 @@ int backward_xy_common(const float* x, const float* y, const float* score, const
         float* yTc = reinterpret_cast<float*>(region + o.yt);
         {
             KernelTimer kt("grad_operands", st);
-            e = launch_transpose_chunked(grad_y ? x : nullptr, xTc, N, grad_x ? y : nullptr, yTc, M, B, dim, st);
+            const SeqIn none = one_seq<const float>(nullptr);
+            e = launch_transpose_chunked(grad_y ? x : none, xTc, N, grad_x ? y : none, yTc, M, B, dim, st);
         }
         if (e != cudaSuccess) return cuda_fail(e, "layout launch");
         g.xTc = xTc;
@@ -910,8 +922,8 @@ int sdtw_backward_xy_f32(const float* x, const float* y, const float* score, con
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     if ((rc = check_ws(workspace, workspace_bytes, sdtw_workspace_bytes_xy(B, N, M, dim)))) return rc;
-    return backward_xy_common(x, y, score, nullptr, grad_out, grad_x, grad_y, B, N, M, dim, bandwidth, workspace,
-                              static_cast<cudaStream_t>(stream));
+    return backward_xy_common(one_seq(x), one_seq(y), score, nullptr, false, grad_out, one_seq(grad_x), one_seq(grad_y),
+                              B, N, M, dim, bandwidth, workspace, static_cast<cudaStream_t>(stream));
 }
 
 // ----------------------------------------------------------------------------
@@ -963,14 +975,14 @@ int sdtw_barycenter_grad_f32(const float* bary, const float* X, const float* w, 
     float* part = reinterpret_cast<float*>(ws + L.part);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t nd = static_cast<size_t>(N) * dim;
-    const int dp = weight_store(B, N, M) ? fused_dp(dim, bary, X) : 0;
+    const int dp = weight_store(B, N, M) ? fused_dp(dim, one_seq(bary), one_seq(X)) : 0;
     cudaError_t e;
     if (dp && grad_fused_gd(dim, X) == dp) {
         // The forward and the gradient read the one barycenter for every
         // problem (x batch stride 0); the costs are computed in the forward.
         uint64_t* wrap = static_cast<uint64_t*>(workspace);
-        if ((rc = run_forward(nullptr, score, out, B, N, M, gamma, 0.f, wrap, st, true, nullptr, bary, X, dim, dp,
-                              true)))
+        if ((rc = run_forward(nullptr, score, out, B, N, M, gamma, 0.f, wrap, st, true, nullptr, one_seq(bary),
+                              one_seq(X), dim, dp, true)))
             return rc;
         // grad_x of every problem straight from the reverse pass.
         if ((rc = run_backward_grad(score, w, B, N, M, wrap, st, bary, 0, X, dim, dp, gx, true))) return rc;
@@ -985,7 +997,9 @@ int sdtw_barycenter_grad_f32(const float* bary, const float* X, const float* w, 
         if (e != cudaSuccess) return cuda_fail(e, "broadcast launch");
         if ((rc = sdtw_forward_xy_f32(xb, X, score, out, B, N, M, dim, gamma, 0.f, workspace, workspace_bytes, stream)))
             return rc;
-        if ((rc = backward_xy_common(xb, X, score, nullptr, w, gx, nullptr, B, N, M, dim, 0.f, workspace, st))) return rc;
+        if ((rc = backward_xy_common(one_seq<const float>(xb), one_seq(X), score, nullptr, false, w, one_seq(gx),
+                                     one_seq<float>(nullptr), B, N, M, dim, 0.f, workspace, st)))
+            return rc;
     }
     {
         KernelTimer kt("bary_reduce", st, 2);
@@ -1045,6 +1059,9 @@ int sdtw_barycenter_sync_adam_f32(float* grad_loss, size_t n, const unsigned lon
     return SDTW_OK;
 }
 
+static int forward_sqeuclid_common(const SeqIn& x, const SeqIn& y, float* score, float* cost, float* out, int B, int N, int M,
+                            int dim, float gamma, float bandwidth, void* workspace, cudaStream_t st);
+
 int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, float* cost, float* out, int B, int N,
                               int M, int dim, float gamma, float bandwidth, void* workspace, size_t workspace_bytes,
                               void* stream) {
@@ -1054,7 +1071,14 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
     if (!x || !y || !cost || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     if (reinterpret_cast<uintptr_t>(cost) % 16u) return fail(SDTW_ERR_INVALID_ARGUMENT, "cost table must be 16-byte aligned");
     if ((rc = check_ws(workspace, workspace_bytes, wave_ws(B, N, M)))) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return forward_sqeuclid_common(one_seq(x), one_seq(y), score, cost, out, B, N, M, dim, gamma, bandwidth, workspace,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+// The unfused forward over B problems whose sequences x, y name (one batch,
+// or the normalized triple); the caller has checked the arguments.
+static int forward_sqeuclid_common(const SeqIn& x, const SeqIn& y, float* score, float* cost, float* out, int B, int N, int M,
+                            int dim, float gamma, float bandwidth, void* workspace, cudaStream_t st) {
     cudaError_t e;
     if (cost_tc_supported(x, y, dim)) {
         KernelTimer kt("cost_tc", st);
@@ -1067,7 +1091,8 @@ int sdtw_forward_sqeuclid_f32(const float* x, const float* y, float* score, floa
     // With the share store the clamp mask of the gradient is marked in the
     // shares, so the reverse pass stores E already masked.
     return run_forward(cost, score, out, B, N, M, gamma, bandwidth, static_cast<uint64_t*>(workspace), st,
-                       weight_store(B, N, M), nullptr, nullptr, nullptr, 0, 0, false, true);
+                       weight_store(B, N, M), nullptr, one_seq<const float>(nullptr), one_seq<const float>(nullptr), 0,
+                       0, false, true);
 }
 
 int sdtw_backward_sqeuclid_f32(const float* x, const float* y, const float* score, const float* cost,
@@ -1080,8 +1105,108 @@ int sdtw_backward_sqeuclid_f32(const float* x, const float* y, const float* scor
     if ((rc = check_ws(workspace, workspace_bytes, sdtw_workspace_bytes_xy(B, N, M, dim)))) return rc;
     // Share store: E comes out of the reverse pass masked (the forward marked
     // the clamped costs); score store: the gradient kernels apply the mask.
-    return backward_xy_common(x, y, score, weight_store(B, N, M) ? nullptr : cost, grad_out, grad_x, grad_y, B, N, M,
-                              dim, bandwidth, workspace, static_cast<cudaStream_t>(stream));
+    const bool ws = weight_store(B, N, M);
+    return backward_xy_common(one_seq(x), one_seq(y), score, ws ? nullptr : cost, ws, grad_out, one_seq(grad_x),
+                              one_seq(grad_y), B, N, M, dim, bandwidth, workspace, static_cast<cudaStream_t>(stream));
+}
+
+// ----------------------------------------------------------------------------
+// normalize=True (module.py:99-106 of the reference, which concatenates
+// [x, x, y] and [y, x, y]): the 3B problems (x_b, y_b), (x_b, x_b), (y_b, y_b)
+// read x and y in place.  The backward's gradients of the first B problems go
+// straight to grad_x / grad_y; those of the self pairs go to four scratch
+// blocks after the 3B-problem workspace and one kernel adds them in.
+static size_t norm_block_bytes(int B, int N, int dim) {
+    return align_up(static_cast<size_t>(B) * N * dim * sizeof(float), 256);
+}
+static size_t norm_scratch_off(int B, int N, int dim) {
+    return align_up(sdtw_workspace_bytes_xy(3 * B, N, N, dim), 256);
+}
+
+size_t sdtw_workspace_bytes_norm(int B, int N, int dim) {
+    if (B <= 0 || N <= 0 || dim <= 0 || B > (1 << 30) / 3) return 0;
+    return norm_scratch_off(B, N, dim) + 4 * norm_block_bytes(B, N, dim);
+}
+
+// need: 0 = the fused forward's workspace, 1 = the unfused forward's, 2 = the backward's.
+static int check_norm(const float* x, const float* y, const float* score, int B, int N, int dim, float gamma,
+                      void* workspace, size_t workspace_bytes, int need) {
+    int rc;
+    if (B <= 0 || B > (1 << 30) / 3) return fail(SDTW_ERR_INVALID_ARGUMENT, "B must be > 0");
+    if ((rc = check_common(3 * B, N, N, gamma)) || (rc = check_score(score))) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t bytes = need == 0   ? wave_ws_xy(3 * B, N, N, dim) + wl_bytes(3 * B, N, N)
+                         : need == 1 ? wave_ws(3 * B, N, N)
+                                     : sdtw_workspace_bytes_norm(B, N, dim);
+    return check_ws(workspace, workspace_bytes, bytes);
+}
+
+int sdtw_forward_xy_norm_f32(const float* x, const float* y, float* score, float* out, int B, int N, int dim,
+                             float gamma, float bandwidth, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_norm(x, y, score, B, N, dim, gamma, workspace, workspace_bytes, 0))) return rc;
+    if (!out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    return forward_xy_common(norm_x(x, y, B), norm_y(x, y, B), score, out, 3 * B, N, N, dim, gamma, bandwidth,
+                             workspace, static_cast<cudaStream_t>(stream));
+}
+
+int sdtw_forward_sqeuclid_norm_f32(const float* x, const float* y, float* score, float* cost, float* out, int B, int N,
+                                   int dim, float gamma, float bandwidth, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    int rc;
+    if ((rc = check_norm(x, y, score, B, N, dim, gamma, workspace, workspace_bytes, 1))) return rc;
+    if (!cost || !out) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    if (reinterpret_cast<uintptr_t>(cost) % 16u) return fail(SDTW_ERR_INVALID_ARGUMENT, "cost table must be 16-byte aligned");
+    return forward_sqeuclid_common(norm_x(x, y, B), norm_y(x, y, B), score, cost, out, 3 * B, N, N, dim, gamma,
+                                   bandwidth, workspace, static_cast<cudaStream_t>(stream));
+}
+
+static int backward_norm(const float* x, const float* y, const float* score, const float* mask_w, bool marked,
+                         const float* grad_out, float* grad_x, float* grad_y, int B, int N, int dim, float bandwidth,
+                         void* workspace, cudaStream_t st) {
+    if (!grad_x || !grad_y) return fail(SDTW_ERR_INVALID_ARGUMENT, "the normalized backward writes both gradients");
+    char* scratch = static_cast<char*>(workspace) + norm_scratch_off(B, N, dim);
+    const size_t blk = norm_block_bytes(B, N, dim);
+    float* s0 = reinterpret_cast<float*>(scratch);            // (x, x): gradient of the first x
+    float* s1 = reinterpret_cast<float*>(scratch + blk);      // (x, x): of the second
+    float* s2 = reinterpret_cast<float*>(scratch + 2 * blk);  // (y, y): of the first y
+    float* s3 = reinterpret_cast<float*>(scratch + 3 * blk);  // (y, y): of the second
+    const SeqOut gx{{grad_x, s0, s2}, B};
+    const SeqOut gy{{grad_y, s1, s3}, B};
+    int rc = backward_xy_common(norm_x(x, y, B), norm_y(x, y, B), score, mask_w, marked, grad_out, gx, gy, 3 * B, N, N,
+                                dim, bandwidth, workspace, st);
+    if (rc) return rc;
+    const size_t n = static_cast<size_t>(B) * N * dim;
+    cudaError_t e;
+    {
+        KernelTimer kt("norm_fold", st, 2);
+        e = launch_add2(grad_x, s0, s1, n, st);
+        if (e == cudaSuccess) e = launch_add2(grad_y, s2, s3, n, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "fold launch");
+    return SDTW_OK;
+}
+
+int sdtw_backward_xy_norm_f32(const float* x, const float* y, const float* score, const float* grad_out,
+                              float* grad_x, float* grad_y, int B, int N, int dim, float gamma, float bandwidth,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    int rc;
+    if ((rc = check_norm(x, y, score, B, N, dim, gamma, workspace, workspace_bytes, 2))) return rc;
+    return backward_norm(x, y, score, nullptr, false, grad_out, grad_x, grad_y, B, N, dim, bandwidth, workspace,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int sdtw_backward_sqeuclid_norm_f32(const float* x, const float* y, const float* score, const float* cost,
+                                    const float* grad_out, float* grad_x, float* grad_y, int B, int N, int dim,
+                                    float gamma, float bandwidth, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+    int rc;
+    if ((rc = check_norm(x, y, score, B, N, dim, gamma, workspace, workspace_bytes, 2))) return rc;
+    if (!cost) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    const bool ws = weight_store(3 * B, N, N);
+    return backward_norm(x, y, score, ws ? nullptr : cost, ws, grad_out, grad_x, grad_y, B, N, dim, bandwidth,
+                         workspace, static_cast<cudaStream_t>(stream));
 }
 
 int sdtw_grad_sqeuclid_f32(const float* G, const float* D_mask, const float* x, const float* y, float* grad_x,

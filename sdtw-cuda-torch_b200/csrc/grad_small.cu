@@ -61,9 +61,8 @@ __device__ __forceinline__ int row_slot(int l) { return ((l & 15) << 1) | (l >> 
 template <int DP, bool MASKED>
 __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const float* __restrict__ Ew,
                                                                       const float* __restrict__ Mw,
-                                                                      const float* __restrict__ x,
-                                                                      const float* __restrict__ y,
-                                                                      float* __restrict__ gx,
+                                                                      const SeqIn x_s, const SeqIn y_s,
+                                                                      const SeqOut gx_s,
                                                                       float* __restrict__ part,
                                                                       float* __restrict__ part_x, WavePlan P, int dim,
                                                                       int n_split, size_t xbs) {
@@ -85,14 +84,15 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
     const int s = split * warps + warp;
     const bool live = s < P.n_stripes;  // warp-uniform
     const int R0 = s * 32;
-    const bool need_x = gx != nullptr, need_y = part != nullptr;
+    const bool need_x = !gx_s.null(), need_y = part != nullptr;
+    const float* __restrict__ x = x_s.at(b, xbs);
     const size_t base = (static_cast<size_t>(b) * P.n_stripes + (live ? s : 0)) * P.n_diag * 32 + lane;
 
     // The stripe's x rows (zeros past N and past dim).
 #pragma unroll
     for (int d = 0; d < DP; ++d)
         Xt[lane * DP + d] =
-            (live && R0 + lane < N && d < dim) ? __ldg(x + b * xbs + static_cast<size_t>(R0 + lane) * dim + d) : 0.f;
+            (live && R0 + lane < N && d < dim) ? __ldg(x + static_cast<size_t>(R0 + lane) * dim + d) : 0.f;
     const int rs = row_slot(lane);
     float racc[DP + 1];  // row R0 + lane: sum_j G y_j (DP), sum_j G
 #pragma unroll
@@ -100,9 +100,10 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
 
     for (int j0 = blk0 * 32; j0 < blk1 * 32; j0 += 32) {
         __syncthreads();  // Yt and red of the previous block are consumed
+        const float* __restrict__ y = y_s.at(b, static_cast<size_t>(M) * dim);
         for (int i = threadIdx.x; i < 32 * DP; i += blockDim.x) {
             const int jj = i / DP, d = i % DP;
-            Yt[i] = (j0 + jj < M && d < dim) ? __ldg(y + (static_cast<size_t>(b) * M + j0 + jj) * dim + d) : 0.f;
+            Yt[i] = (j0 + jj < M && d < dim) ? __ldg(y + static_cast<size_t>(j0 + jj) * dim + d) : 0.f;
         }
         if (live) {
             // All 63 loads in flight at once, then the stores (one round trip
@@ -175,10 +176,10 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
     }
     if (need_x && live && R0 + lane < N) {
         if (n_cs == 1) {
-            const size_t o = (static_cast<size_t>(b) * N + R0 + lane) * dim;
+            float* gx = gx_s.at(b, static_cast<size_t>(N) * dim) + static_cast<size_t>(R0 + lane) * dim;
 #pragma unroll
             for (int d = 0; d < DP; ++d)
-                if (d < dim) gx[o + d] = 2.f * (Xt[lane * DP + d] * racc[DP] - racc[d]);
+                if (d < dim) gx[d] = 2.f * (Xt[lane * DP + d] * racc[DP] - racc[d]);
         } else {
             // This column split's row sums; grad_small_finalize_x_kernel adds them up.
             float* px = part_x + ((static_cast<size_t>(b) * n_cs + cs) * N + R0 + lane) * (DP + 1);
@@ -191,9 +192,8 @@ __global__ void __launch_bounds__(32 * kSmallWarps) grad_small_kernel(const floa
 // grad_x from the column splits' row partials, summed in split order.
 template <int DP>
 __global__ void __launch_bounds__(256) grad_small_finalize_x_kernel(const float* __restrict__ part_x,
-                                                                    const float* __restrict__ x,
-                                                                    float* __restrict__ gx, int B, int N, int dim,
-                                                                    int n_cs, size_t xbs) {
+                                                                    const SeqIn x, const SeqOut gx, int B, int N,
+                                                                    int dim, int n_cs, size_t xbs) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(B) * N * dim) return;
     const int d = static_cast<int>(i % dim);
@@ -205,15 +205,15 @@ __global__ void __launch_bounds__(256) grad_small_finalize_x_kernel(const float*
         s += __ldg(px + DP);
         t += __ldg(px + d);
     }
-    gx[i] = 2.f * (__ldg(x + b * xbs + static_cast<size_t>(r) * dim + d) * s - t);
+    const size_t o = static_cast<size_t>(r) * dim + d;
+    gx.at(b, static_cast<size_t>(N) * dim)[o] = 2.f * (__ldg(x.at(b, xbs) + o) * s - t);
 }
 
 // grad_y from the splits' column partials, summed in split order.
 template <int DP>
 __global__ void __launch_bounds__(256) grad_small_finalize_kernel(const float* __restrict__ part,
-                                                                  const float* __restrict__ y,
-                                                                  float* __restrict__ gy, int B, int M, int dim,
-                                                                  int n_split) {
+                                                                  const SeqIn y, const SeqOut gy, int B, int M,
+                                                                  int dim, int n_split) {
     pdl_trigger();
     pdl_wait();
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -227,7 +227,8 @@ __global__ void __launch_bounds__(256) grad_small_finalize_kernel(const float* _
         s += __ldg(pp + DP);
         t += __ldg(pp + d);
     }
-    gy[i] = 2.f * (__ldg(y + i) * s - t);
+    const size_t o = static_cast<size_t>(j) * dim + d, stride = static_cast<size_t>(M) * dim;
+    gy.at(b, stride)[o] = 2.f * (__ldg(y.at(b, stride) + o) * s - t);
 }
 
 static int small_dp(int dim) { return dim <= 4 ? 4 : dim <= 8 ? 8 : 16; }
@@ -259,8 +260,8 @@ size_t grad_small_part_bytes(const WavePlan& P, int dim) {
 }
 
 template <int DP>
-static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
-                            float* part, const WavePlan& P, int dim, cudaStream_t st, size_t xbs) {
+static cudaError_t go_small(const float* Ew, const float* Mw, const SeqIn& x, const SeqIn& y, const SeqOut& gx,
+                            const SeqOut& gy, float* part, const WavePlan& P, int dim, cudaStream_t st, size_t xbs) {
     const int n_split = grad_small_splits(P);
     const int warps = small_warps(P);
     const size_t smem = static_cast<size_t>(SmallSmem<DP>::floats(warps)) * sizeof(float);
@@ -269,7 +270,7 @@ static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, co
     if (e != cudaSuccess) return e;
     const int n_cs = small_colsplits(P);
     const dim3 grid(n_split, P.B, n_cs);
-    float* pp = gy ? part : nullptr;
+    float* pp = gy.null() ? nullptr : part;
     float* px = part + part_y_floats(P, dim);
     if (Mw)
         e = launch_pdl(false, grad_small_kernel<DP, true>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, px, P,
@@ -278,23 +279,23 @@ static cudaError_t go_small(const float* Ew, const float* Mw, const float* x, co
         e = launch_pdl(false, grad_small_kernel<DP, false>, grid, dim3(32 * warps), smem, st, Ew, Mw, x, y, gx, pp, px, P,
                        dim, n_split, xbs);
     if (e != cudaSuccess) return e;
-    if (gx && n_cs > 1) {
+    if (!gx.null() && n_cs > 1) {
         const size_t nx = static_cast<size_t>(P.B) * P.N * dim;
         grad_small_finalize_x_kernel<DP><<<static_cast<unsigned>((nx + 255) / 256), 256, 0, st>>>(px, x, gx, P.B, P.N,
                                                                                                  dim, n_cs, xbs);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    if (!gy) return cudaSuccess;
+    if (gy.null()) return cudaSuccess;
     const size_t n = static_cast<size_t>(P.B) * P.M * dim;
     return launch_pdl(false, grad_small_finalize_kernel<DP>, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st,
                       part, y, gy, P.B, P.M, dim, n_split);
 }
 
-cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
-                              float* part, const WavePlan& P, int dim, cudaStream_t st, size_t xbs) {
+cudaError_t launch_grad_small(const float* Ew, const float* Mw, const SeqIn& x, const SeqIn& y, const SeqOut& gx,
+                              const SeqOut& gy, float* part, const WavePlan& P, int dim, cudaStream_t st, size_t xbs) {
     if (!grad_small_supported(P, dim)) return cudaErrorInvalidValue;
-    if (!gx && !gy) return cudaSuccess;
+    if (gx.null() && gy.null()) return cudaSuccess;
     switch (small_dp(dim)) {
         case 4: return go_small<4>(Ew, Mw, x, y, gx, gy, part, P, dim, st, xbs);
         case 8: return go_small<8>(Ew, Mw, x, y, gx, gy, part, P, dim, st, xbs);

@@ -50,7 +50,7 @@ struct CostPitch {
 };
 
 template <int K, bool DIRECT, int FC, bool VEC>
-__global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict__ x, const float* __restrict__ y,
+__global__ void __launch_bounds__(256, 3) cost_wl_kernel(const SeqIn x, const SeqIn y,
                                                          float* __restrict__ Dw, WavePlan P, int dim) {
     constexpr int SR = 32 * K;
     constexpr int CJ = 4096 / SR;        // columns per tile
@@ -68,8 +68,6 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
     const int s = blockIdx.y;
     const int b = blockIdx.z;
     const int R0 = s * SR;
-    const float* xb = x + static_cast<size_t>(b) * P.N * dim;
-    const float* yb = y + static_cast<size_t>(b) * P.M * dim;
     const int jb = threadIdx.x % CG;  // columns j0 + jb + CG c
     const int ag = threadIdx.x / CG;  // rows 4ag .. 4ag+3
 
@@ -89,6 +87,8 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
     // 16-byte cp.async into two buffers, the next chunk's copies in flight
     // while this one is computed.
     auto stage_async = [&](float* dstb, int f0) {
+        const float* __restrict__ xb = x.at(b, static_cast<size_t>(P.N) * dim);
+        const float* __restrict__ yb = y.at(b, static_cast<size_t>(P.M) * dim);
         for (int e = threadIdx.x; e < (SR + CJ) * (FC / 4); e += 256) {
             const int r = e / (FC / 4), f = (e % (FC / 4)) * 4;
             const bool isx = r < SR;
@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(256, 3) cost_wl_kernel(const float* __restrict
             __syncthreads();
         } else {
             __syncthreads();
+            const float* __restrict__ xb = x.at(b, static_cast<size_t>(P.N) * dim);
+            const float* __restrict__ yb = y.at(b, static_cast<size_t>(P.M) * dim);
             for (int e = threadIdx.x; e < (SR + CJ) * FC; e += 256) {
                 const int r = e / FC, f = e % FC;
                 const bool isx = r < SR;
@@ -333,16 +335,16 @@ __global__ void __launch_bounds__(256) wl_to_rm_cm_kernel(const float* __restric
 
 // 32 x 32 tiles through shared memory; grid (ceil(C/32), ceil(ldo/32), B).
 // Output columns R .. ldo are written as zeros.
-__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int R,
-                                                        int C, int ldo) {
+__global__ void __launch_bounds__(256) transpose_kernel(const SeqIn in_s, float* __restrict__ out, int R, int C,
+                                                        int ldo) {
     __shared__ float tile[32][33];
     const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-    const size_t in_off = static_cast<size_t>(blockIdx.z) * R * C;
+    const float* __restrict__ in = in_s.at(blockIdx.z, static_cast<size_t>(R) * C);
     const size_t out_off = static_cast<size_t>(blockIdx.z) * C * ldo;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = warp; i < 32; i += 8) {
         const int r = r0 + i, c = c0 + lane;
-        if (r < R && c < C) tile[i][lane] = __ldg(in + in_off + static_cast<size_t>(r) * C + c);
+        if (r < R && c < C) tile[i][lane] = __ldg(in + static_cast<size_t>(r) * C + c);
     }
     __syncthreads();
     for (int i = warp; i < 32; i += 8) {
@@ -355,26 +357,26 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
 // grid (ceil(max(R0, R1)/32), ceil(C/32), 2B): z < B transposes in0 (rows R0),
 // the rest in1 (rows R1); either may be null.  Output rows are 36 floats: 32
 // positions and 4 zeros.
-__global__ void __launch_bounds__(256) transpose_chunked_kernel(const float* __restrict__ in0, float* __restrict__ out0,
-                                                                int R0, const float* __restrict__ in1,
-                                                                float* __restrict__ out1, int R1, int B, int C) {
+__global__ void __launch_bounds__(256) transpose_chunked_kernel(const SeqIn in0, float* __restrict__ out0, int R0,
+                                                                const SeqIn in1, float* __restrict__ out1, int R1,
+                                                                int B, int C) {
     __shared__ float tile[32][33];
     pdl_trigger();
     pdl_wait();
     const bool second = static_cast<int>(blockIdx.z) >= B;
-    const float* __restrict__ in = second ? in1 : in0;
     float* __restrict__ out = second ? out1 : out0;
     const int R = second ? R1 : R0;
     const int b = second ? blockIdx.z - B : blockIdx.z;
     const int c = blockIdx.x, f0 = blockIdx.y * 32;
     const int n_chunks = (R + 31) / 32;
-    if (!in || c >= n_chunks) return;  // block-uniform
-    const size_t in_off = static_cast<size_t>(b) * R * C;
+    if ((second ? in1.null() : in0.null()) || c >= n_chunks) return;  // block-uniform
+    const size_t rc = static_cast<size_t>(R) * C;
+    const float* __restrict__ in = second ? in1.at(b, rc) : in0.at(b, rc);
     const size_t out_off = (static_cast<size_t>(b) * n_chunks + c) * C * 36;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = warp; i < 32; i += 8) {
         const int r = 32 * c + i, f = f0 + lane;
-        tile[i][lane] = (r < R && f < C) ? __ldg(in + in_off + static_cast<size_t>(r) * C + f) : 0.f;
+        tile[i][lane] = (r < R && f < C) ? __ldg(in + static_cast<size_t>(r) * C + f) : 0.f;
     }
     __syncthreads();
     for (int i = warp; i < 32; i += 8) {
@@ -385,6 +387,30 @@ __global__ void __launch_bounds__(256) transpose_chunked_kernel(const float* __r
             if (lane < 4) row[32 + lane] = 0.f;
         }
     }
+}
+
+// g += a + b, four floats per thread (n4 = n / 4 units of 16 bytes) and the
+// tail one by one: normalize folds its triple's other gradients into x's / y's.
+__global__ void __launch_bounds__(256) add2_kernel(float* __restrict__ g, const float* __restrict__ a,
+                                                   const float* __restrict__ b, size_t n, int vec) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    size_t done = 0;
+    if (vec) {
+        const size_t n4 = n / 4;
+        for (size_t u = i; u < n4; u += stride) {
+            float4 v = reinterpret_cast<float4*>(g)[u];
+            const float4 p = __ldg(reinterpret_cast<const float4*>(a) + u);
+            const float4 q = __ldg(reinterpret_cast<const float4*>(b) + u);
+            v.x += p.x + q.x;
+            v.y += p.y + q.y;
+            v.z += p.z + q.z;
+            v.w += p.w + q.w;
+            reinterpret_cast<float4*>(g)[u] = v;
+        }
+        done = n4 * 4;
+    }
+    for (size_t k = done + i; k < n; k += stride) g[k] += __ldg(a + k) + __ldg(b + k);
 }
 
 static dim3 wl_grid(const WavePlan& P) {
@@ -401,12 +427,12 @@ static size_t cost_wl_smem() {
 }
 
 template <int K, int FC>
-static cudaError_t cost_wl_launch(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+static cudaError_t cost_wl_launch(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, bool direct,
                                   cudaStream_t stream) {
     constexpr int CJ = 4096 / (32 * K);
     const dim3 g((P.M + CJ - 1) / CJ, P.n_stripes, P.B);
     const size_t smem = cost_wl_smem<K, FC>();
-    const bool vec = (dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+    const bool vec = (dim % 4 == 0) && x.aligned16() && y.aligned16();
     auto fn = direct ? (vec ? cost_wl_kernel<K, true, FC, true> : cost_wl_kernel<K, true, FC, false>)
                      : (vec ? cost_wl_kernel<K, false, FC, true> : cost_wl_kernel<K, false, FC, false>);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -415,7 +441,7 @@ static cudaError_t cost_wl_launch(const float* x, const float* y, float* Dw, con
 }
 
 template <int K>
-static cudaError_t cost_wl_by_dim(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+static cudaError_t cost_wl_by_dim(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, bool direct,
                                   cudaStream_t stream) {
     // Feature chunk sized to the feature count: no padded work for small dims.
     if (dim <= 4) return cost_wl_launch<K, 4>(x, y, Dw, P, dim, direct, stream);
@@ -424,7 +450,7 @@ static cudaError_t cost_wl_by_dim(const float* x, const float* y, float* Dw, con
     return cost_wl_launch<K, 32>(x, y, Dw, P, dim, direct, stream);
 }
 
-cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+cudaError_t launch_cost_wl(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, bool direct,
                            cudaStream_t stream) {
     switch (P.K) {
         case 1: return cost_wl_by_dim<1>(x, y, Dw, P, dim, direct, stream);
@@ -470,15 +496,25 @@ cudaError_t launch_wl_to_rm_cm(const float* Aw, const float* maskw, float* A, in
     return cudaGetLastError();
 }
 
-cudaError_t launch_transpose_chunked(const float* in0, float* out0, int R0, const float* in1, float* out1, int R1,
+cudaError_t launch_transpose_chunked(const SeqIn& in0, float* out0, int R0, const SeqIn& in1, float* out1, int R1,
                                      int B, int C, cudaStream_t stream) {
-    if (B <= 0 || C <= 0 || (!in0 && !in1)) return cudaSuccess;
-    const int rows = std::max(in0 ? R0 : 0, in1 ? R1 : 0);
+    if (B <= 0 || C <= 0 || (in0.null() && in1.null())) return cudaSuccess;
+    const int rows = std::max(in0.null() ? 0 : R0, in1.null() ? 0 : R1);
     const dim3 g((rows + 31) / 32, (C + 31) / 32, 2 * B);
     return launch_pdl(false, transpose_chunked_kernel, g, dim3(256), 0, stream, in0, out0, R0, in1, out1, R1, B, C);
 }
 
-cudaError_t launch_transpose_brc(const float* in, float* out, int B, int R, int C, int ldo, cudaStream_t stream) {
+cudaError_t launch_add2(float* g, const float* a, const float* b, size_t n, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    const int vec = ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) &
+                     15u) == 0;
+    const size_t units = vec ? n / 4 + 1 : n;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>((units + 255) / 256, 148 * 16));
+    add2_kernel<<<blocks, 256, 0, stream>>>(g, a, b, n, vec);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_brc(const SeqIn& in, float* out, int B, int R, int C, int ldo, cudaStream_t stream) {
     if (B <= 0 || R <= 0 || C <= 0) return cudaSuccess;
     const dim3 g((C + 31) / 32, (ldo + 31) / 32, B);
     transpose_kernel<<<g, 256, 0, stream>>>(in, out, R, C, ldo);

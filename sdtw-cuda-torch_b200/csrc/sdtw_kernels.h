@@ -12,6 +12,35 @@
 
 namespace sdtw {
 
+// Where the problems of a launch find their sequences.  Problem b lies in
+// segment s (0 for b < per, 1 for b < 2 per, else 2) and uses row block
+// b - s * per of p[s].  A plain batch is one segment (one_seq); the three
+// segments (x, y), (x, x), (y, y) of B problems each are the normalized loss's
+// triple, read from the caller's x and y in place (norm_x / norm_y).
+template <typename T>
+struct Seqs {
+    T* p[3];
+    int per;
+    __host__ __device__ __forceinline__ T* at(int b, size_t stride) const {
+        const int s = b < per ? 0 : (b - per < per ? 1 : 2);
+        return (s == 0 ? p[0] : (s == 1 ? p[1] : p[2])) + static_cast<size_t>(b - s * per) * stride;
+    }
+    __host__ __device__ __forceinline__ bool null() const { return p[0] == nullptr; }
+    bool aligned16() const {
+        return ((reinterpret_cast<uintptr_t>(p[0]) | reinterpret_cast<uintptr_t>(p[1]) |
+                 reinterpret_cast<uintptr_t>(p[2])) & 15u) == 0;
+    }
+};
+using SeqIn = Seqs<const float>;
+using SeqOut = Seqs<float>;
+template <typename T>
+inline Seqs<T> one_seq(T* p) {
+    return Seqs<T>{{p, p, p}, 1 << 30};
+}
+// The normalized triple's first and second operands over B problems each.
+inline SeqIn norm_x(const float* x, const float* y, int B) { return SeqIn{{x, x, y}, B}; }
+inline SeqIn norm_y(const float* x, const float* y, int B) { return SeqIn{{y, x, y}, B}; }
+
 struct FwdArgs {
     WavePlan P;
     const float* Dw;  // (B,N,M) cost in the wavefront layout (layout.cu)
@@ -28,8 +57,8 @@ struct FwdArgs {
     int weights;      // nonzero: store each cell's predecessor weights instead of its score (one row per lane)
     // Fused costs (wavefront_exp.cu, dp > 0): sum_k (x_ik - y_jk)^2 computed in
     // the kernel from x (B,N,dim) and y (B,M,dim); Dw is then unused.
-    const float* x;
-    const float* y;
+    SeqIn x;
+    SeqIn y;
     int dim;
     int dp;           // 0: costs from Dw; else the feature padding (fused_dp)
     size_t x_bstride;  // floats between problems' x (N * dim; 0 = one x for every problem)
@@ -50,6 +79,7 @@ struct BwdArgs {
     uint32_t seq;
     int debug_stall;
     int weights;  // nonzero: `score` holds the forward's predecessor weights (one row per lane)
+    int clamp_mask;  // nonzero: those weights carry the forward's clamp marks (FwdArgs::clamp_mask)
     // grad_x in the reverse pass (gd > 0; the fused cost, weight store, no
     // band): E is not stored; each lane accumulates its row's sum_j E y_j and
     // sum_j E and writes grad_x.
@@ -71,10 +101,12 @@ cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream);
 cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream);
 size_t fwdx_smem(const WavePlan& P, int dp, bool wide = false);
 int fwdx_threads(const WavePlan& P);
-int fused_dp(int dim, const float* x, const float* y);
+int fused_dp(int dim, const SeqIn& x, const SeqIn& y);
 size_t bwdw_smem(const WavePlan& P, int gd = 0);
-const void* fwdx_fn(bool banded, bool weights, int dp, bool wide = false);
-const void* bwdw_fn(bool banded, int gd = 0);
+// cm: the variants that mark clamped costs (shares of an unfused cost table);
+// seg: the fused variants for problems in several segments (SeqIn).
+const void* fwdx_fn(bool banded, bool weights, int dp, bool wide = false, bool cm = false, bool seg = false);
+const void* bwdw_fn(bool banded, int gd = 0, bool cm = false);
 // Feature padding of the reverse pass with grad_x (4, 8, 16), or 0.
 int grad_fused_gd(int dim, const float* y);
 // pass: 0 forward with costs from a table, 1 reverse pass, 2 + dp the fused
@@ -86,7 +118,7 @@ cudaError_t launch_score_to_R(const float2* S, float* R, const WavePlan& P, floa
 cudaError_t launch_R_to_score(const float* R, float2* S, const WavePlan& P, float kk, cudaStream_t stream);
 
 // layout.cu
-cudaError_t launch_cost_wl(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, bool direct,
+cudaError_t launch_cost_wl(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, bool direct,
                            cudaStream_t stream);
 cudaError_t launch_rm_to_wl(const float* A, float* Aw, const WavePlan& P, cudaStream_t stream);
 cudaError_t launch_wl_to_rm(const float* Aw, const float* maskw, float* A, const WavePlan& P, cudaStream_t stream);
@@ -98,9 +130,9 @@ cudaError_t launch_wl_to_rm_cm(const float* Aw, const float* maskw, float* A, in
 // (B,R,C) -> chunked (B, ceil(R/32), C, 36): out[b][c][f][kk] = in[b][32c+kk][f]
 // for kk < 32, zero for 32c+kk >= R and for kk >= 32; two arrays (rows R0 and
 // R1, either input may be null) in one launch.
-cudaError_t launch_transpose_chunked(const float* in0, float* out0, int R0, const float* in1, float* out1, int R1,
+cudaError_t launch_transpose_chunked(const SeqIn& in0, float* out0, int R0, const SeqIn& in1, float* out1, int R1,
                                      int B, int C, cudaStream_t stream);
-cudaError_t launch_transpose_brc(const float* in, float* out, int B, int R, int C, int ldo, cudaStream_t stream);
+cudaError_t launch_transpose_brc(const SeqIn& in, float* out, int B, int R, int C, int ldo, cudaStream_t stream);
 
 // dense.cu
 cudaError_t launch_cost(const float* x, const float* y, float* D, int B, int N, int M, int dim, bool direct,
@@ -126,10 +158,10 @@ struct GradTcArgs {
     const float* xT;  // x transposed (B,dim,Np)
     const float* yT;  // y transposed (B,dim,Mp)
     const float* Mw;  // unfused cost in the wavefront layout (clamp mask: G = E * (D > 0)), or null
-    const float* x;   // (B,N,dim)
-    const float* y;   // (B,M,dim)
-    float* gx;        // (B,N,dim) or null
-    float* gy;        // (B,M,dim) or null
+    SeqIn x;          // (B,N,dim)
+    SeqIn y;          // (B,M,dim)
+    SeqOut gx;        // (B,N,dim) or null
+    SeqOut gy;        // (B,M,dim) or null
     int dim;
     int fb;           // features per block
     int nt;           // fb rounded up to 16
@@ -157,8 +189,9 @@ cudaError_t launch_grad_rm(const GradTcArgs& args, cudaStream_t stream);
 bool grad_small_supported(const WavePlan& P, int dim);
 size_t grad_small_part_bytes(const WavePlan& P, int dim);
 // x_bstride: floats between problems' x (N * dim; 0 = one x shared by all).
-cudaError_t launch_grad_small(const float* Ew, const float* Mw, const float* x, const float* y, float* gx, float* gy,
-                              float* part, const WavePlan& P, int dim, cudaStream_t st, size_t x_bstride);
+cudaError_t launch_grad_small(const float* Ew, const float* Mw, const SeqIn& x, const SeqIn& y, const SeqOut& gx,
+                              const SeqOut& gy, float* part, const WavePlan& P, int dim, cudaStream_t st,
+                              size_t x_bstride);
 
 // barycenter.cu: the reductions and the optimiser step of the barycenter loop.
 //   bary_broadcast: xb[b] = bary for every problem b (materialised x).
@@ -186,9 +219,11 @@ cudaError_t launch_bary_sync_adam(float* grad_loss, size_t n, const unsigned lon
 // tcgemm.cu: the unfused (expanded, clamped) cost on the tensor cores, written
 // in the wavefront layout.  Requires dim >= 16, dim % 4 == 0 and 16-byte
 // aligned x, y (cost_tc_supported).
-bool cost_tc_supported(const float* x, const float* y, int dim);
-cudaError_t launch_cost_tc(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
+bool cost_tc_supported(const SeqIn& x, const SeqIn& y, int dim);
+cudaError_t launch_cost_tc(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
                            cudaStream_t stream);
+// normalize: gx += a + b over n floats (the triple's gradients folded into x's / y's)
+cudaError_t launch_add2(float* g, const float* a, const float* b, size_t n, cudaStream_t stream);
 
 // f64.cu: the float64 pipeline (reference layout R, one CTA per problem).
 cudaError_t launch_forward_f64(const double* D, double* R, double* out, int B, int N, int M, double gamma, double bw,

@@ -333,13 +333,14 @@ __device__ __forceinline__ void grad_rm_tile(const GradTcArgs& a, unsigned char*
         const int quarter = warp & 3;
         const int half = warp >> 2;
         const int r = r0 + quarter * 32 + lane;
-        const float* own = GX ? a.x : a.y;
-        float* g = GX ? a.gx : a.gy;
+        const size_t rstride = static_cast<size_t>(rows_out) * dim;
+        const float* own = GX ? a.x.at(b, rstride) : a.y.at(b, rstride);
+        float* g = GX ? a.gx.at(b, rstride) : a.gy.at(b, rstride);
         const uint32_t tw = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         float v[16], w[16];
         tmem_ld16(tw + static_cast<uint32_t>(2 * nt), v);
         const float sum = v[0];
-        const size_t row_off = (static_cast<size_t>(b) * rows_out + r) * dim + f0;
+        const size_t row_off = static_cast<size_t>(r) * dim + f0;
         const bool vec = ((dim & 3) == 0) && ((f0 & 3) == 0) &&
                          ((reinterpret_cast<uintptr_t>(own) | reinterpret_cast<uintptr_t>(g)) & 15u) == 0;
         for (int c16 = half; c16 * 16 < fb; c16 += 2) {  // warp-uniform
@@ -826,13 +827,14 @@ __device__ __forceinline__ void grad_wl_tile(const GradTcArgs& a, unsigned char*
         const int quarter = warp & 3;
         const int half = warp >> 2;  // column group (0 .. 3)
         const int r = r0 + quarter * 32 + lane;
-        const float* own = GX ? a.x : a.y;
-        float* g = GX ? a.gx : a.gy;
+        const size_t rstride = static_cast<size_t>(rows_out) * dim;
+        const float* own = GX ? a.x.at(b, rstride) : a.y.at(b, rstride);
+        float* g = GX ? a.gx.at(b, rstride) : a.gy.at(b, rstride);
         const uint32_t tw = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         float v[16], w[16];
         tmem_ld16(tw + static_cast<uint32_t>(2 * nt), v);
         const float sum = v[0];
-        const size_t row_off = (static_cast<size_t>(b) * rows_out + r) * dim + f0;
+        const size_t row_off = static_cast<size_t>(r) * dim + f0;
         const bool vec = ((dim & 3) == 0) && ((f0 & 3) == 0) &&
                          ((reinterpret_cast<uintptr_t>(own) | reinterpret_cast<uintptr_t>(g)) & 15u) == 0;
         for (int c16 = half; c16 * 16 < fb; c16 += kWlSplitWarps / 4) {  // warp-uniform
@@ -982,8 +984,8 @@ cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
 // chunk but halves the shared memory, so that two CTAs share an SM and one's
 // epilogue stores overlap the other's chunks.
 template <int K, int ST>
-__global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __restrict__ x, const float* __restrict__ y,
-                                                              float* __restrict__ Dw, const WavePlan P, int dim,
+__global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const SeqIn x, const SeqIn y, float* __restrict__ Dw,
+                                                              const WavePlan P, int dim,
                                                               const WaitCtx wait) {
     constexpr int kCostStages = ST;
     constexpr int SR = 32 * K;
@@ -1011,8 +1013,8 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const float* __res
     float* xn = reinterpret_cast<float*>(ctrl + 128);  // [2][128] partial, then [128]
     float* yn = xn + 2 * kTileM;                      // [2][128] partial, then [128]
     const uint32_t smem_base = smem_addr(smem_raw);
-    const float* xb = x + static_cast<size_t>(b) * N * dim;
-    const float* yb = y + static_cast<size_t>(b) * M * dim;
+    const float* xb = x.at(b, static_cast<size_t>(N) * dim);
+    const float* yb = y.at(b, static_cast<size_t>(M) * dim);
     const int n_chunks = (dim + kKT - 1) / kKT;
 
     WaitCtx wc = wait;
@@ -1314,12 +1316,12 @@ static size_t cost_tc_smem_bytes(int K, int stages) {
     return (ops > stage ? ops : stage) + 128 + 4 * kTileM * sizeof(float) + 2 * kTileM * 8 * sizeof(float);
 }
 
-bool cost_tc_supported(const float* x, const float* y, int dim) {
-    return dim >= 16 && dim % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+bool cost_tc_supported(const SeqIn& x, const SeqIn& y, int dim) {
+    return dim >= 16 && dim % 4 == 0 && x.aligned16() && y.aligned16();
 }
 
 template <int K, int ST>
-static cudaError_t cost_tc_go(const float* x, const float* y, float* Dw, const WavePlan& P, int dim,
+static cudaError_t cost_tc_go(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim,
                               const WaitCtx& wait, cudaStream_t stream) {
     const dim3 grid((P.M + kTileM - 1) / kTileM, (P.N + kTileM - 1) / kTileM, P.B);
     const size_t smem = cost_tc_smem_bytes(K, ST);
@@ -1330,7 +1332,7 @@ static cudaError_t cost_tc_go(const float* x, const float* y, float* Dw, const W
     return cudaGetLastError();
 }
 
-cudaError_t launch_cost_tc(const float* x, const float* y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
+cudaError_t launch_cost_tc(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
                            cudaStream_t stream) {
     // One stage where that lets two CTAs share an SM (K <= 2: the shared memory
     // is then the epilogue's staging area, under 100 KB).  Measured on B200

@@ -194,8 +194,10 @@ __device__ __forceinline__ bool mbar_wait_fx(uint32_t mbar, uint32_t parity, con
 // the compiler interleaves more of the steps' independent work (C2 forward
 // 0.118 -> 0.104 ms); launches with more problems than fit keep the
 // occupancy.  The fused forward with 8 or more features always takes 128.
-template <bool BANDED, bool W, int DP, bool WIDE>
+template <bool BANDED, bool W, int DP, bool WIDE, bool CM = false, bool SEG = false>
 __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(const FwdArgs a) {
+    static_assert(!CM || (W && DP == 0), "clamp marks: shares of a cost table only");
+    static_assert(!SEG || DP > 0, "sequence maps: fused costs only");
     constexpr int PF = fx_pf(DP, WIDE);
     constexpr int YSEG = kYRows / PF;      // window segments
     constexpr int SEGBACK = seg_back(PF);
@@ -320,7 +322,8 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
             unsigned long long xq[DP > 0 ? DP / 2 : 1];
             if constexpr (DP > 0) {
                 float xv[DP];
-                const float* xr = a.x + static_cast<size_t>(b) * a.x_bstride + static_cast<size_t>(R0 + lane) * D;
+                const float* xr = (SEG ? a.x.at(b, a.x_bstride) : a.x.p[0] + static_cast<size_t>(b) * a.x_bstride) +
+                                  static_cast<size_t>(R0 + lane) * D;
 #pragma unroll
                 for (int f = 0; f < DP; ++f) xv[f] = (lane < rows_left && f < D) ? __ldg(xr + f) : 0.f;
 #pragma unroll
@@ -328,7 +331,10 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                     xq[f] = (static_cast<unsigned long long>(__float_as_uint(xv[2 * f + 1])) << 32) |
                             __float_as_uint(xv[2 * f]);
             }
-            const float* yb = a.y + static_cast<size_t>(b) * M * D;
+            // (Resolved here in the single-batch variant in the same form as
+            // before the sequence maps existed: a select-based form measured
+            // 2 % slower on the C3 forward, the address being re-derived per copy.)
+            const float* yb = SEG ? a.y.at(b, static_cast<size_t>(M) * D) : a.y.p[0] + static_cast<size_t>(b) * M * D;
             // Rows seg*PF .. seg*PF+PF-1 of y (those below M) into window slot
             // seg mod YSEG by cp.async, one commit group per segment: 16-byte
             // copies into the padded rows, or 4-byte copies of dense rows (D < 4).
@@ -466,7 +472,7 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                         live = live && static_cast<unsigned>(R0 + lane - col + ibw) <= static_cast<unsigned>(2 * ibw);
                     pmax = max_nan(pmax, (live || !masked) ? pa : 0.f);
                     // The clamp mark travels in K's mantissa sign bit (K > 0).
-                    const uint32_t mark = (W && a.clamp_mask && !(c > 0.f)) ? 0x80000000u : 0u;
+                    const uint32_t mark = (CM && !(c > 0.f)) ? 0x80000000u : 0u;
                     kb[u * 32] = make_uint2(__float_as_uint(km) | mark, static_cast<uint32_t>(kx));
                 }
                 if constexpr (DP == 0) cost_copy(gi + 2);  // into the buffer just read
@@ -582,7 +588,7 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                 }
                 const int t = t0 + u;
                 const uint32_t kbits = kq[u % PH].x;
-                const float km = __uint_as_float(kbits & 0x7fffffffu);
+                const float km = __uint_as_float(CM ? kbits & 0x7fffffffu : kbits);
                 const int ke = static_cast<int>(kq[u % PH].y);
                 const uint2 ri = rq[u % PH];
                 float mu = __shfl_up_sync(SDTW_FULL_MASK, m_l, 1);
@@ -608,7 +614,8 @@ __global__ void __launch_bounds__(512, (DP >= 8 || WIDE) ? 1 : 2) fwdx_kernel(co
                     // reverse pass needs of this cell.
                     // (With the clamp mark in the diagonal share's sign bit.)
                     const float inv = rcpf(sum);
-                    rec = make_float2(__uint_as_float(__float_as_uint(vd * inv) | (kbits & 0x80000000u)), vu * inv);
+                    rec = make_float2(CM ? __uint_as_float(__float_as_uint(vd * inv) | (kbits & 0x80000000u)) : vd * inv,
+                                      vu * inv);
                 } else {
                     rec = (en == kEneg) ? make_float2(neg_inf(), 0.f) : to_score(mn, en);
                 }
@@ -728,8 +735,9 @@ __host__ __device__ constexpr size_t bw_smem_bytes(int wpc, int gd = 0) {
 // shuffles, one per feature per step -- measured slower on B200 than the E
 // table and grad_small: C3 reverse pass 1.42 -> 2.96 ms against a 0.79 ms
 // gradient kernel; the extra shuffles delay the chain's own.)
-template <bool BANDED, int GD>
+template <bool BANDED, int GD, bool CM = false>
 __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kernel(const BwdArgs a) {
+    static_assert(!CM || GD == 0, "clamp marks: unfused costs only");
     constexpr int PF = kPF;
     constexpr int YSEG = kYRows / PF;      // window segments
     constexpr int SEGBACK = seg_back(PF);
@@ -969,14 +977,14 @@ __global__ void __launch_bounds__(GD > 0 ? 256 : 512, GD > 0 ? 2 : 1) bwdw_kerne
                     e = (lane == rows_left - 1 && col == M - 1) ? gb : e;
                     e = live ? e : 0.f;
                 }
-                const float dn = e * fabsf(w.x);     // to the diagonal predecessor (two steps on)
+                const float dn = e * (CM ? fabsf(w.x) : w.x);  // to the diagonal predecessor (two steps on)
                 msg = fmaf(e, w.y, dprev);           // to the row above: upper share + previous diagonal
                 accl = fmaf(-e, w.y, e - dn);        // left share: e * (1 - wd - wu)
                 dprev = dn;
                 if (lane == 0) pub_s[u] = msg;
                 // The stored (and chain-ruled) E is zero where the forward marked
                 // a clamped cost; the recurrence itself carries e unmasked.
-                const float eo = (__float_as_uint(w.x) >> 31) ? 0.f : e;
+                const float eo = (CM && (__float_as_uint(w.x) >> 31)) ? 0.f : e;
                 if constexpr (GD == 0) {
                     El[static_cast<size_t>(t) * 32] = eo;  // one coalesced row store per step
                 } else {
@@ -1052,11 +1060,30 @@ size_t bwdw_smem(const WavePlan& P, int gd) { return bw_smem_bytes(P.wpc, gd); }
 
 // dp: 0 = costs from a table; 4, 8, 16, 32, 64 = fused x/y costs with the
 // features padded to dp (the x/y entry points, which store the shares).
-const void* fwdx_fn(bool banded, bool weights, int dp, bool wide) {
+const void* fwdx_fn(bool banded, bool weights, int dp, bool wide, bool cm, bool seg) {
+    if (seg && dp > 0) {  // problems in several segments (the normalized triple)
+        switch (dp) {
+            case 4:
+                if (wide) return banded ? (const void*)fwdx_kernel<true, true, 4, true, false, true>
+                                        : (const void*)fwdx_kernel<false, true, 4, true, false, true>;
+                return banded ? (const void*)fwdx_kernel<true, true, 4, false, false, true>
+                              : (const void*)fwdx_kernel<false, true, 4, false, false, true>;
+            case 8:
+                return banded ? (const void*)fwdx_kernel<true, true, 8, true, false, true>
+                              : (const void*)fwdx_kernel<false, true, 8, true, false, true>;
+            case 16:
+                return banded ? (const void*)fwdx_kernel<true, true, 16, true, false, true>
+                              : (const void*)fwdx_kernel<false, true, 16, true, false, true>;
+            default: return nullptr;
+        }
+    }
 #define SDTW_FWDX(BW, WW, DD) \
     (wide ? (const void*)fwdx_kernel<BW, WW, DD, true> : (const void*)fwdx_kernel<BW, WW, DD, false>)
+#define SDTW_FWDX_CM(BW) \
+    (wide ? (const void*)fwdx_kernel<BW, true, 0, true, true> : (const void*)fwdx_kernel<BW, true, 0, false, true>)
     switch (dp) {
         case 0:
+            if (weights && cm) return banded ? SDTW_FWDX_CM(true) : SDTW_FWDX_CM(false);
             if (weights) return banded ? SDTW_FWDX(true, true, 0) : SDTW_FWDX(false, true, 0);
             return banded ? SDTW_FWDX(true, false, 0) : SDTW_FWDX(false, false, 0);
         case 4: return banded ? SDTW_FWDX(true, true, 4) : SDTW_FWDX(false, true, 4);
@@ -1067,6 +1094,7 @@ const void* fwdx_fn(bool banded, bool weights, int dp, bool wide) {
         default: return nullptr;
     }
 #undef SDTW_FWDX
+#undef SDTW_FWDX_CM
 }
 // Feature padding of the fused forward for dim features, or 0 when the fused
 // costs come from a cost table in the workspace: more than kFusedMaxDim
@@ -1076,16 +1104,18 @@ const void* fwdx_fn(bool banded, bool weights, int dp, bool wide) {
 // fused against 0.155 ms with the table, 64 features 0.239 against 0.175.
 // Inside the wavefront every cell reads all of its y row from shared memory;
 // the separate cost kernel reuses each load across four cells.
-int fused_dp(int dim, const float* x, const float* y) {
+int fused_dp(int dim, const SeqIn& x, const SeqIn& y) {
     if (dim < 4) return 4;
-    if (dim > kFusedMaxDim || dim % 4 || (reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(y) & 15u))
-        return 0;
+    if (dim > kFusedMaxDim || dim % 4 || !x.aligned16() || !y.aligned16()) return 0;
     int dp = 4;
     while (dp < dim) dp *= 2;
     return dp;
 }
-const void* bwdw_fn(bool banded, int gd) {
-    if (gd == 0) return banded ? (const void*)bwdw_kernel<true, 0> : (const void*)bwdw_kernel<false, 0>;
+const void* bwdw_fn(bool banded, int gd, bool cm) {
+    if (gd == 0) {
+        if (cm) return banded ? (const void*)bwdw_kernel<true, 0, true> : (const void*)bwdw_kernel<false, 0, true>;
+        return banded ? (const void*)bwdw_kernel<true, 0> : (const void*)bwdw_kernel<false, 0>;
+    }
     if (banded) return nullptr;
     switch (gd) {
         case 4: return (const void*)bwdw_kernel<false, 4>;
@@ -1097,13 +1127,14 @@ const void* bwdw_fn(bool banded, int gd) {
 // Feature padding of the reverse pass with gradients: as the fused forward's
 // (up to 16 features; more, or a count above 3 that is not a multiple of 4,
 // or y not 16-byte aligned: 0, E is stored and a gradient kernel follows).
-int grad_fused_gd(int dim, const float* y) { return fused_dp(dim, y, y); }
+int grad_fused_gd(int dim, const float* y) { return fused_dp(dim, one_seq(y), one_seq(y)); }
 
 cudaError_t launch_forward_x(const FwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
     if (P.K != 1 || P.wpc > 8 || (args.dp && !args.weights)) return cudaErrorInvalidValue;
     const bool banded = args.ibw < P.N + P.M;
-    const void* fn = fwdx_fn(banded, args.weights != 0, args.dp, args.wide != 0);
+    const bool seg = args.x.per < P.B || args.y.per < P.B;
+    const void* fn = fwdx_fn(banded, args.weights != 0, args.dp, args.wide != 0, args.clamp_mask != 0, seg);
     if (!fn) return cudaErrorInvalidValue;
     void* kargs[] = {const_cast<FwdArgs*>(&args)};
     return launch_cluster(fn, dim3(P.B * P.csize), dim3(fwdx_threads(P)), fwdx_smem(P, args.dp, args.wide != 0), P.csize, stream,
@@ -1114,7 +1145,7 @@ cudaError_t launch_backward_w(const BwdArgs& args, cudaStream_t stream) {
     const WavePlan& P = args.P;
     if (P.K != 1 || !args.weights) return cudaErrorInvalidValue;
     const bool banded = args.ibw < P.N + P.M;
-    const void* fn = bwdw_fn(banded, args.gd);
+    const void* fn = bwdw_fn(banded, args.gd, args.clamp_mask != 0);
     if (!fn || (args.gd && (!args.x || !args.y || !args.gx || args.dim > args.gd))) return cudaErrorInvalidValue;
     void* kargs[] = {const_cast<BwdArgs*>(&args)};
     return launch_cluster(fn, dim3(P.B * P.csize), dim3(P.wpc * 32), bwdw_smem(P, args.gd), P.csize, stream, kargs,

@@ -50,6 +50,11 @@ _SIGS = {
     "sdtw_forward_sqeuclid_f32": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_backward_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_grad_sqeuclid_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "sdtw_workspace_bytes_norm": ([_I, _I, _I], _SZ),
+    "sdtw_forward_xy_norm_f32": ([_P, _P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_backward_xy_norm_f32": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_forward_sqeuclid_norm_f32": ([_P, _P, _P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
+    "sdtw_backward_sqeuclid_norm_f32": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _F, _P, _SZ, _P], _I),
     "sdtw_score_to_R_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
     "sdtw_R_to_score_f32": ([_P, _P, _I, _I, _I, _F, _P], _I),
     "sdtw_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
@@ -392,6 +397,88 @@ def backward_sqeuclid(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, cos
                                               _stream(x.device))
     _check(rc, "unfused backward")
     _op_end("backward_sqeuclid", x.device, ev, 2 + int(need_x) + int(need_y))
+    return gx, gy
+
+
+# ----------------------------------------------------------------------------- normalize=True
+# The 3B problems (x_b, y_b), (x_b, x_b), (y_b, y_b) read x and y in place
+# (softdtw_cuda/module.py:99-111 of the reference concatenates copies).
+def _norm_ws(B: int, N: int, dim: int, device) -> torch.Tensor:
+    n = lib().sdtw_workspace_bytes_norm(B, N, dim)
+    return torch.empty(max(int(n), 256), dtype=torch.uint8, device=device)
+
+
+def forward_xy_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float):
+    """Fused forward of the normalized triple: (out (3B,) [xy | xx | yy], score)."""
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    score = torch.empty(score_elems(3 * B, N, N), dtype=torch.float32, device=x.device)
+    out = torch.empty(3 * B, dtype=torch.float32, device=x.device)
+    ws = workspace(3 * B, N, N, x.device, dim)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_forward_xy_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(out), B, N, dim, float(gamma),
+                                            float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
+    _check(rc, "fused normalized forward")
+    _op_end("forward_xy", x.device, ev)
+    return out, score
+
+
+def backward_xy_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad_out: torch.Tensor | None,
+                     gamma: float, bandwidth: float):
+    """grad_x, grad_y of sum_p grad_out[p] * out[p] over the normalized triple."""
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    gx = torch.empty_like(x)
+    gy = torch.empty_like(y)
+    g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    ws = _norm_ws(B, N, dim, x.device)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_backward_xy_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(g), _ptr(gx), _ptr(gy), B, N, dim,
+                                             float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
+    _check(rc, "fused normalized backward")
+    _op_end("backward_xy", x.device, ev)
+    return gx, gy
+
+
+def forward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float):
+    """Unfused forward of the normalized triple: (out (3B,), score, cost)."""
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    score = torch.empty(score_elems(3 * B, N, N), dtype=torch.float32, device=x.device)
+    cost = torch.empty(cost_elems(3 * B, N, N), dtype=torch.float32, device=x.device)
+    out = torch.empty(3 * B, dtype=torch.float32, device=x.device)
+    ws = workspace(3 * B, N, N, x.device)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_forward_sqeuclid_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(out), B, N, dim,
+                                                  float(gamma), float(bandwidth), _ptr(ws), ws.numel(),
+                                                  _stream(x.device))
+    _check(rc, "unfused normalized forward")
+    _op_end("forward_sqeuclid", x.device, ev)
+    return out, score, cost
+
+
+def backward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, cost: torch.Tensor,
+                           grad_out: torch.Tensor | None, gamma: float, bandwidth: float):
+    x = _f32(x)
+    y = _f32(y)
+    B, N, dim = x.shape
+    gx = torch.empty_like(x)
+    gy = torch.empty_like(y)
+    g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    ws = _norm_ws(B, N, dim, x.device)
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_backward_sqeuclid_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(g), _ptr(gx),
+                                                   _ptr(gy), B, N, dim, float(gamma), float(bandwidth), _ptr(ws),
+                                                   ws.numel(), _stream(x.device))
+    _check(rc, "unfused normalized backward")
+    _op_end("backward_sqeuclid", x.device, ev)
     return gx, gy
 
 

@@ -93,3 +93,29 @@ class SoftDTWSqEuclidAutograd(Function):
         gx, gy = _native.backward_sqeuclid(X, Y, score, cost, grad_output, ctx.gamma, ctx.bandwidth,
                                            need_x=ctx.needs_input_grad[0], need_y=ctx.needs_input_grad[1])
         return (None if gx is None else gx.to(X.dtype)), (None if gy is None else gy.to(Y.dtype)), None, None
+
+
+class SoftDTWSqEuclidNormAutograd(Function):
+    """The unfused normalized triple: the 3B losses [xy | xx | yy] of
+    softdtw_cuda/module.py:99-111 on the clamped expanded cost, x and y read
+    in place instead of concatenated; the backward folds the self pairs'
+    gradients into dL/dX and dL/dY."""
+
+    @staticmethod
+    def forward(ctx, X: torch.Tensor, Y: torch.Tensor, gamma: float, bandwidth: float | None):
+        gamma_f = float(gamma)
+        if gamma_f <= 0:
+            raise ValueError(f"gamma must be > 0, got {gamma_f}")
+        bw = _normalize_bandwidth(bandwidth)
+        out, score, cost = _native.forward_sqeuclid_norm(X, Y, gamma_f, bw)
+        ctx.save_for_backward(X, Y, score, cost)
+        ctx.gamma = gamma_f
+        ctx.bandwidth = bw
+        return out.to(X.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        X, Y, score, cost = ctx.saved_tensors
+        gx, gy = _native.backward_sqeuclid_norm(X, Y, score, cost, grad_output, ctx.gamma, ctx.bandwidth)
+        return (gx.to(X.dtype) if ctx.needs_input_grad[0] else None,
+                gy.to(Y.dtype) if ctx.needs_input_grad[1] else None, None, None)

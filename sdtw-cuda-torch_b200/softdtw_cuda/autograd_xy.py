@@ -58,3 +58,28 @@ class SoftDTWXYAutograd(Function):
         gx, gy = _native.backward_xy(X, Y, score, grad_output, ctx.gamma, ctx.bandwidth,
                                      need_x=ctx.needs_input_grad[0], need_y=ctx.needs_input_grad[1])
         return (None if gx is None else gx.to(X.dtype)), (None if gy is None else gy.to(Y.dtype)), None, None
+
+
+class SoftDTWXYNormAutograd(Function):
+    """The fused normalized triple: ``apply(X, Y, gamma, bandwidth)`` returns
+    the 3B losses [SoftDTW(x_b, y_b) | SoftDTW(x_b, x_b) | SoftDTW(y_b, y_b)]
+    of softdtw_cuda/module.py:99-111, with x and y read in place instead of
+    concatenated; the backward folds the self pairs' gradients into dL/dX and
+    dL/dY.  float32 CUDA tensors (bf16/fp16 are computed in float32)."""
+
+    @staticmethod
+    def forward(ctx, X: torch.Tensor, Y: torch.Tensor, gamma: float, bandwidth: float | None):
+        gamma_f = float(gamma)
+        bw = _normalize_bandwidth(bandwidth)
+        out, score = _native.forward_xy_norm(X, Y, gamma_f, bw)
+        ctx.save_for_backward(X, Y, score)
+        ctx.gamma = gamma_f
+        ctx.bandwidth = bw
+        return out.to(X.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        X, Y, score = ctx.saved_tensors
+        gx, gy = _native.backward_xy_norm(X, Y, score, grad_output, ctx.gamma, ctx.bandwidth)
+        return (gx.to(X.dtype) if ctx.needs_input_grad[0] else None,
+                gy.to(Y.dtype) if ctx.needs_input_grad[1] else None, None, None)

@@ -7,7 +7,10 @@ reference:
   CUDA device and ``dist`` is squared Euclidean; ``fused=True`` requires that;
   ``fused=False`` always builds the cost matrix.
 * ``normalize=True`` returns SoftDTW(x,y) - (SoftDTW(x,x) + SoftDTW(y,y)) / 2,
-  evaluated as one batch of 3B problems.
+  evaluated as one batch of 3B problems.  On CUDA float tensors the library
+  reads x and y in place for the three pairs (no concatenated copies); other
+  inputs (float64, CPU, other costs, torch.compile tracing) take the
+  reference's concatenation.
 """
 from __future__ import annotations
 
@@ -17,8 +20,8 @@ import torch
 from torch import nn
 
 from . import ops  # noqa: F401  (registers torch.ops.softdtw_cuda.*)
-from .autograd import SoftDTWAutograd, SoftDTWSqEuclidAutograd, _normalize_bandwidth
-from .autograd_xy import SoftDTWXYAutograd
+from .autograd import SoftDTWAutograd, SoftDTWSqEuclidAutograd, SoftDTWSqEuclidNormAutograd, _normalize_bandwidth
+from .autograd_xy import SoftDTWXYAutograd, SoftDTWXYNormAutograd
 from .distances import _KERNEL_DTYPES, _SQEUCLID_NAMES, pairwise_distance
 
 
@@ -89,12 +92,22 @@ class SoftDTW(nn.Module):
 
         use_fused = self._use_fused(x, y)
         if self.normalize:
-            xs = torch.cat([x, x, y], dim=0)
-            ys = torch.cat([y, x, y], dim=0)
-            out = self._pairs(xs, ys, use_fused)
+            if self._kernel_pair(x, y) and not torch.compiler.is_compiling():
+                fn = SoftDTWXYNormAutograd if use_fused else SoftDTWSqEuclidNormAutograd
+                out = fn.apply(x, y, self.gamma, self.bandwidth)
+            else:
+                xs = torch.cat([x, x, y], dim=0)
+                ys = torch.cat([y, x, y], dim=0)
+                out = self._pairs(xs, ys, use_fused)
             o_xy, o_xx, o_yy = out.split(bx, dim=0)
             return o_xy - 0.5 * (o_xx + o_yy)
         return self._pairs(x, y, use_fused)
+
+    def _kernel_pair(self, x: torch.Tensor, y: torch.Tensor) -> bool:
+        # Squared Euclidean on CUDA tensors of one device and a float32 (or
+        # bf16/fp16, computed in float32) dtype: the library's x/y kernels.
+        return (self.dist.lower() in _SQEUCLID_NAMES and x.is_cuda and y.is_cuda and x.device == y.device
+                and x.dtype in _KERNEL_DTYPES and y.dtype == x.dtype)
 
     def _pairs(self, x: torch.Tensor, y: torch.Tensor, use_fused: bool) -> torch.Tensor:
         if (torch.compiler.is_compiling() and self.dist.lower() in _SQEUCLID_NAMES and x.is_cuda and y.is_cuda
@@ -108,8 +121,7 @@ class SoftDTW(nn.Module):
             return op(x, y, float(self.gamma), bw)[0]
         if use_fused:
             return SoftDTWXYAutograd.apply(x, y, self.gamma, self.bandwidth)
-        if (self.dist.lower() in _SQEUCLID_NAMES and x.is_cuda and y.is_cuda and x.device == y.device
-                and x.dtype in _KERNEL_DTYPES and y.dtype == x.dtype):
+        if self._kernel_pair(x, y):
             # Unfused: explicit cost matrix (kept by the library for the backward).
             return SoftDTWSqEuclidAutograd.apply(x, y, self.gamma, self.bandwidth)
         D = pairwise_distance(x, y, dist=self.dist)

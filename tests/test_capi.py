@@ -53,6 +53,11 @@ def test_sizes_without_gpu():
     assert L.sdtw_workspace_bytes_xy(4, 64, 64, 20) == L.sdtw_workspace_bytes(4, 64, 64) + 2 * up(4 * 64 * 64 * 4) + 2 * up(4 * 20 * 64 * 4)
     # Longer: x, y chunked and transposed, rows of 36 floats per 32 positions.
     assert L.sdtw_workspace_bytes_xy(4, 200, 64, 20) == L.sdtw_workspace_bytes(4, 200, 64) + up(4 * 7 * 20 * 36 * 4) + up(4 * 2 * 20 * 36 * 4)
+    # normalize: the x/y workspace of the 3B problems, then four (B,N,dim)
+    # gradient blocks of the self pairs.
+    for B, N, dim in ((4, 64, 3), (2, 200, 20)):
+        assert L.sdtw_workspace_bytes_norm(B, N, dim) == up(L.sdtw_workspace_bytes_xy(3 * B, N, N, dim)) + 4 * up(B * N * dim * 4)
+    assert L.sdtw_workspace_bytes_norm(0, 64, 3) == 0
 
 
 def test_invalid_arguments_rejected():
@@ -65,6 +70,10 @@ def test_invalid_arguments_rejected():
     rc = L.sdtw_cost_sqeuclid_f32(None, None, None, 1, 4, 4, 0, 0, None)
     assert rc == 1
     assert L.sdtw_error_string(3) == b"device-side wait timed out"
+    rc = L.sdtw_forward_xy_norm_f32(None, None, None, None, 0, 4, 3, 1.0, -1.0, None, 0, None)
+    assert rc == 1 and b"must be > 0" in L.sdtw_last_error_message()
+    rc = L.sdtw_backward_sqeuclid_norm_f32(None, None, None, None, None, None, None, 1, 4, 3, 0.0, -1.0, None, 0, None)
+    assert rc == 1 and b"gamma" in L.sdtw_last_error_message()
 
 
 def test_timing_registry_without_gpu():
