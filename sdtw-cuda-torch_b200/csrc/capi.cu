@@ -740,7 +740,12 @@ int sdtw_cost_sqeuclid_f32(const float* x, const float* y, float* D, int B, int 
     if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
     if (!x || !y || !D) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
     cudaError_t e;
-    {
+    if (!direct && cost_tc_supported(one_seq(x), one_seq(y), dim)) {
+        // The expanded cost with its dot products on the tensor cores.
+        if ((rc = ensure_status()) || (rc = pending_status())) return rc;
+        KernelTimer kt("cost_rowmajor", static_cast<cudaStream_t>(stream));
+        e = launch_cost_tc_rm(x, y, D, B, N, M, dim, wait_ctx(), static_cast<cudaStream_t>(stream));
+    } else {
         KernelTimer kt("cost_rowmajor", static_cast<cudaStream_t>(stream));
         e = launch_cost(x, y, D, B, N, M, dim, direct != 0, static_cast<cudaStream_t>(stream));
     }

@@ -222,6 +222,9 @@ cudaError_t launch_bary_sync_adam(float* grad_loss, size_t n, const unsigned lon
 bool cost_tc_supported(const SeqIn& x, const SeqIn& y, int dim);
 cudaError_t launch_cost_tc(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,
                            cudaStream_t stream);
+// The same cost row-major (B, N, M) for distances.sqeuclidean (same requirements).
+cudaError_t launch_cost_tc_rm(const float* x, const float* y, float* D, int B, int N, int M, int dim,
+                              const WaitCtx& wait, cudaStream_t stream);
 // normalize: gx += a + b over n floats (the triple's gradients folded into x's / y's)
 cudaError_t launch_add2(float* g, const float* a, const float* b, size_t n, cudaStream_t stream);
 

@@ -983,10 +983,13 @@ cudaError_t launch_grad_wl(const GradTcArgs& args_in, cudaStream_t stream) {
 // ST = 1 or 2 operand stages.  One stage serialises copy, split and MMAs of a
 // chunk but halves the shared memory, so that two CTAs share an SM and one's
 // epilogue stores overlap the other's chunks.
-template <int K, int ST>
+// RM: the cost row-major (B, N, M) instead (distances.sqeuclidean): the tile is
+// staged in shared memory rows of 129 floats and stored by coalesced rows.
+template <int K, int ST, bool RM = false>
 __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const SeqIn x, const SeqIn y, float* __restrict__ Dw,
                                                               const WavePlan P, int dim,
                                                               const WaitCtx wait) {
+    static_assert(!RM || K == 1, "row-major output: one tile layout");
     constexpr int kCostStages = ST;
     constexpr int SR = 32 * K;
     constexpr int NSL = kTileM / SR;       // stripes in the 128-row tile
@@ -1257,6 +1260,44 @@ __global__ void __launch_bounds__(kThreads, 1) cost_tc_kernel(const SeqIn x, con
     }
     __syncthreads();
 
+    if constexpr (RM) {
+        // ---- row-major epilogue: thread (row r, column half) stages its 64
+        // cells at stg[r][c] (pitch 129: the lanes' rows fall in distinct
+        // banks), then warp w stores tile rows w, w + 8, ... as 128-float rows.
+        constexpr int kPitch = kTileM + 1;
+        float* stg = reinterpret_cast<float*>(smem_raw);
+        if (all_ok) {
+            const int quarter = warp & 3, half = warp >> 2;
+            const int r = quarter * 32 + lane;
+            const float xr = xn[r];
+            const uint32_t tw = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+            float v[16];
+            for (int c16 = half * 4; c16 < half * 4 + 4; ++c16) {
+                tmem_ld16(tw + static_cast<uint32_t>(c16 * 16), v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = c16 * 16 + i;
+                    stg[r * kPitch + c] = fmaxf((xr + yn[c]) - 2.f * v[i], 0.f);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) tmem_dealloc(tmem, 128u);
+        if (all_ok) {
+            for (int rr = warp; rr < kTileM; rr += kThreads / 32) {
+                const int q = q0 + rr;
+                if (q >= N) break;
+                float* drow = Dw + (static_cast<size_t>(b) * N + q) * M + j0;
+#pragma unroll
+                for (int k = 0; k < kTileM / 32; ++k) {
+                    const int c = k * 32 + lane;
+                    if (j0 + c < M) drow[c] = stg[rr * kPitch + c];
+                }
+            }
+        }
+        return;
+    }
     if (all_ok) {
         // ---- epilogue: warp w holds tile rows 32 (w % 4) + lane, columns of
         // half w / 4; cells go to shared memory by (stripe slice, anti-diagonal).
@@ -1320,16 +1361,28 @@ bool cost_tc_supported(const SeqIn& x, const SeqIn& y, int dim) {
     return dim >= 16 && dim % 4 == 0 && x.aligned16() && y.aligned16();
 }
 
-template <int K, int ST>
+template <int K, int ST, bool RM = false>
 static cudaError_t cost_tc_go(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim,
                               const WaitCtx& wait, cudaStream_t stream) {
     const dim3 grid((P.M + kTileM - 1) / kTileM, (P.N + kTileM - 1) / kTileM, P.B);
-    const size_t smem = cost_tc_smem_bytes(K, ST);
-    cudaError_t e = cudaFuncSetAttribute(cost_tc_kernel<K, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    size_t smem = cost_tc_smem_bytes(K, ST);
+    if (RM) smem = std::max(smem, static_cast<size_t>(kTileM) * (kTileM + 1) * sizeof(float) + 128 +
+                                      4 * kTileM * sizeof(float) + 2 * kTileM * 8 * sizeof(float));
+    cudaError_t e = cudaFuncSetAttribute(cost_tc_kernel<K, ST, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    cost_tc_kernel<K, ST><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
+    cost_tc_kernel<K, ST, RM><<<grid, kThreads, smem, stream>>>(x, y, Dw, P, dim, wait);
     return cudaGetLastError();
+}
+
+cudaError_t launch_cost_tc_rm(const float* x, const float* y, float* D, int B, int N, int M, int dim,
+                              const WaitCtx& wait, cudaStream_t stream) {
+    WavePlan P{};
+    P.B = B;
+    P.N = N;
+    P.M = M;
+    P.K = 1;
+    return cost_tc_go<1, 1, true>(one_seq(x), one_seq(y), D, P, dim, wait, stream);
 }
 
 cudaError_t launch_cost_tc(const SeqIn& x, const SeqIn& y, float* Dw, const WavePlan& P, int dim, const WaitCtx& wait,

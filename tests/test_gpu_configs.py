@@ -93,11 +93,12 @@ def test_c4b_normalize(fused):
 
 # ------------------------------------------------------------------ distances
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=str)
-@pytest.mark.parametrize("dim", [1, 8, 33, 65])
+@pytest.mark.parametrize("dim", [1, 8, 16, 33, 64, 65, 128])
 def test_sqeuclidean_cuda_matches_reference_expression(dim, dtype):
     """distances.sqeuclidean on CUDA against the reference's expression
     (distances.py:6-28) evaluated in float64 on the same (rounded) inputs, N != M;
-    gradients of sum(W * D) against torch autograd of that expression."""
+    gradients of sum(W * D) against torch autograd of that expression.  Feature
+    counts of 16 and more that are multiples of 4 take the tensor-core cost."""
     g = torch.Generator().manual_seed(dim)
     x = torch.randn(3, 37, dim, generator=g).to(dtype)
     y = torch.randn(3, 29, dim, generator=g).to(dtype)
@@ -121,6 +122,19 @@ def test_sqeuclidean_cuda_matches_reference_expression(dim, dtype):
                                atol=out_tol * gscale + 1e-5)
     np.testing.assert_allclose(yd.grad.float().cpu().numpy(), y64.grad.numpy(), rtol=out_tol,
                                atol=out_tol * gscale + 1e-5)
+
+
+@pytest.mark.parametrize("N,M,dim", [(300, 200, 64), (129, 257, 16), (128, 128, 128)])
+def test_sqeuclidean_tensor_core_tiles(N, M, dim):
+    """The tensor-core cost across several 128 x 128 tiles and ragged edges,
+    against the reference's expression in float64."""
+    g = torch.Generator().manual_seed(N + M + dim)
+    x = torch.randn(2, N, dim, generator=g)
+    y = torch.randn(2, M, dim, generator=g)
+    D = sqeuclidean(x.cuda(), y.cuda())
+    D64 = _sqeuclidean_torch(x.double(), y.double())
+    scale = float(D64.abs().max())
+    np.testing.assert_allclose(D.cpu().numpy(), D64.numpy(), rtol=2e-6, atol=2e-6 * scale)
 
 
 def test_sqeuclidean_clamp_mask_and_pairwise_name():
