@@ -353,38 +353,50 @@ __global__ void __launch_bounds__(256) transpose_kernel(const SeqIn in_s, float*
     }
 }
 
-// 32 x 32 blocks (32 sequence positions x 32 features) through shared memory;
-// grid (ceil(max(R0, R1)/32), ceil(C/32), 2B): z < B transposes in0 (rows R0),
-// the rest in1 (rows R1); either may be null.  Output rows are 36 floats: 32
-// positions and 4 zeros.
+// 32 sequence positions x up to kTransTiles * 32 features per block through
+// shared memory, every tile's loads issued before the first store; grid
+// (ceil(max(R0, R1)/32), ceil(C/(32 kTransTiles)), 2B): z < B transposes in0
+// (rows R0), the rest in1 (rows R1); either may be null.  Output rows are 36
+// floats: 32 positions and 4 zeros.  (One 32 x 32 tile per block measured
+// 12.8 us for C2's x and y, 1.4 TB/s.)
+constexpr int kTransTiles = 4;
 __global__ void __launch_bounds__(256) transpose_chunked_kernel(const SeqIn in0, float* __restrict__ out0, int R0,
                                                                 const SeqIn in1, float* __restrict__ out1, int R1,
                                                                 int B, int C) {
-    __shared__ float tile[32][33];
+    __shared__ float tile[kTransTiles][32][33];
     pdl_trigger();
     pdl_wait();
     const bool second = static_cast<int>(blockIdx.z) >= B;
     float* __restrict__ out = second ? out1 : out0;
     const int R = second ? R1 : R0;
     const int b = second ? blockIdx.z - B : blockIdx.z;
-    const int c = blockIdx.x, f0 = blockIdx.y * 32;
+    const int c = blockIdx.x, f0 = blockIdx.y * 32 * kTransTiles;
     const int n_chunks = (R + 31) / 32;
     if ((second ? in1.null() : in0.null()) || c >= n_chunks) return;  // block-uniform
     const size_t rc = static_cast<size_t>(R) * C;
     const float* __restrict__ in = second ? in1.at(b, rc) : in0.at(b, rc);
     const size_t out_off = (static_cast<size_t>(b) * n_chunks + c) * C * 36;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = warp; i < 32; i += 8) {
-        const int r = 32 * c + i, f = f0 + lane;
-        tile[i][lane] = (r < R && f < C) ? __ldg(in + static_cast<size_t>(r) * C + f) : 0.f;
+    const int tiles = min(kTransTiles, (C - f0 + 31) / 32);  // block-uniform
+#pragma unroll
+    for (int t = 0; t < kTransTiles; ++t) {
+        if (t < tiles) {
+#pragma unroll
+            for (int i = warp; i < 32; i += 8) {
+                const int r = 32 * c + i, f = f0 + 32 * t + lane;
+                tile[t][i][lane] = (r < R && f < C) ? __ldg(in + static_cast<size_t>(r) * C + f) : 0.f;
+            }
+        }
     }
     __syncthreads();
-    for (int i = warp; i < 32; i += 8) {
-        const int f = f0 + i;
-        if (f < C) {
-            float* row = out + out_off + static_cast<size_t>(f) * 36;
-            row[lane] = tile[lane][i];
-            if (lane < 4) row[32 + lane] = 0.f;
+    for (int t = 0; t < tiles; ++t) {
+        for (int i = warp; i < 32; i += 8) {
+            const int f = f0 + 32 * t + i;
+            if (f < C) {
+                float* row = out + out_off + static_cast<size_t>(f) * 36;
+                row[lane] = tile[t][lane][i];
+                if (lane < 4) row[32 + lane] = 0.f;
+            }
         }
     }
 }
@@ -500,7 +512,7 @@ cudaError_t launch_transpose_chunked(const SeqIn& in0, float* out0, int R0, cons
                                      int B, int C, cudaStream_t stream) {
     if (B <= 0 || C <= 0 || (in0.null() && in1.null())) return cudaSuccess;
     const int rows = std::max(in0.null() ? 0 : R0, in1.null() ? 0 : R1);
-    const dim3 g((rows + 31) / 32, (C + 31) / 32, 2 * B);
+    const dim3 g((rows + 31) / 32, (C + 32 * kTransTiles - 1) / (32 * kTransTiles), 2 * B);
     return launch_pdl(false, transpose_chunked_kernel, g, dim3(256), 0, stream, in0, out0, R0, in1, out1, R1, B, C);
 }
 

@@ -129,3 +129,42 @@ def test_in_place_needs_no_concatenated_copies(fused):
         peaks.append(torch.cuda.max_memory_allocated() - base)
         del out, xt, yt
     assert peaks[0] <= peaks[1] - 0.9 * copies, f"peaks {peaks}, copies {copies}"
+
+
+def test_in_place_half_inputs():
+    """bfloat16 x, y: the losses equal the concatenated batch's; the gradients,
+    computed in float32 and rounded once, are within bfloat16 rounding of the
+    float32 run on the same (rounded) inputs."""
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(2, 80, 24, generator=g).to(torch.bfloat16).cuda()
+    y = torch.randn(2, 80, 24, generator=g).to(torch.bfloat16).cuda()
+    w = torch.ones(2, device="cuda")
+    for fused in (False, True):
+        a = _pair(x, y, fused=fused, gamma=1.0, bw=None, w=w, in_place=True)
+        b = _pair(x, y, fused=fused, gamma=1.0, bw=None, w=w, in_place=False)
+        ref = _pair(x.float(), y.float(), fused=fused, gamma=1.0, bw=None, w=w, in_place=True)
+        assert a[0].dtype == torch.bfloat16 and torch.equal(a[0], b[0])
+        for ours, r in ((a[1], ref[1]), (a[2], ref[2])):
+            assert ours.dtype == torch.bfloat16
+            torch.testing.assert_close(ours.float(), r, rtol=8e-3, atol=8e-3 * float(r.abs().max()))
+
+
+def test_norm_entry_points_reject_missing_gradient():
+    """The normalized backward writes both gradients: a null one is refused
+    before any launch."""
+    B, N, dim = 2, 40, 4
+    x = torch.randn(B, N, dim, device="cuda")
+    y = torch.randn(B, N, dim, device="cuda")
+    out, score = _native.forward_xy_norm(x, y, 1.0, -1.0)
+    L = _native.lib()
+    ws = torch.empty(L.sdtw_workspace_bytes_norm(B, N, dim), dtype=torch.uint8, device="cuda")
+    gx = torch.empty_like(x)
+    stream = _native._stream(x.device)
+    rc = L.sdtw_backward_xy_norm_f32(_native._ptr(x), _native._ptr(y), _native._ptr(score), None, _native._ptr(gx),
+                                     None, B, N, dim, 1.0, -1.0, _native._ptr(ws), ws.numel(), stream)
+    assert rc == 1 and b"both gradients" in L.sdtw_last_error_message()
+    rc = L.sdtw_backward_xy_norm_f32(_native._ptr(x), _native._ptr(y), _native._ptr(score), None, _native._ptr(gx),
+                                     _native._ptr(gx), B, N, dim, 1.0, -1.0, _native._ptr(ws), 16, stream)
+    assert rc == 1 and b"workspace" in L.sdtw_last_error_message()
+    torch.cuda.synchronize()
+    _native.check_status()
