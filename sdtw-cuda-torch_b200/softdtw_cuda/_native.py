@@ -403,6 +403,12 @@ def backward_sqeuclid(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, cos
 # ----------------------------------------------------------------------------- normalize=True
 # The 3B problems (x_b, y_b), (x_b, x_b), (y_b, y_b) read x and y in place
 # (softdtw_cuda/module.py:99-111 of the reference concatenates copies).
+def _norm_pair(x: torch.Tensor, y: torch.Tensor):
+    if x.dim() != 3 or x.shape != y.shape or not (x.is_cuda and y.is_cuda) or x.device != y.device:
+        raise ValueError(f"normalize: expected CUDA x, y of one shape (B,N,D); got {tuple(x.shape)}, {tuple(y.shape)}")
+    return _f32(x), _f32(y)
+
+
 def _norm_ws(B: int, N: int, dim: int, device) -> torch.Tensor:
     n = lib().sdtw_workspace_bytes_norm(B, N, dim)
     return torch.empty(max(int(n), 256), dtype=torch.uint8, device=device)
@@ -410,8 +416,7 @@ def _norm_ws(B: int, N: int, dim: int, device) -> torch.Tensor:
 
 def forward_xy_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float):
     """Fused forward of the normalized triple: (out (3B,) [xy | xx | yy], score)."""
-    x = _f32(x)
-    y = _f32(y)
+    x, y = _norm_pair(x, y)
     B, N, dim = x.shape
     score = torch.empty(score_elems(3 * B, N, N), dtype=torch.float32, device=x.device)
     out = torch.empty(3 * B, dtype=torch.float32, device=x.device)
@@ -428,12 +433,13 @@ def forward_xy_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: f
 def backward_xy_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad_out: torch.Tensor | None,
                      gamma: float, bandwidth: float):
     """grad_x, grad_y of sum_p grad_out[p] * out[p] over the normalized triple."""
-    x = _f32(x)
-    y = _f32(y)
+    x, y = _norm_pair(x, y)
     B, N, dim = x.shape
     gx = torch.empty_like(x)
     gy = torch.empty_like(y)
     g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    if g is not None and g.numel() != 3 * B:
+        raise ValueError(f"normalize: expected {3 * B} upstream gradients, got {g.numel()}")
     ws = _norm_ws(B, N, dim, x.device)
     ev = _op_begin(x.device)
     with torch.cuda.device(x.device):
@@ -446,8 +452,7 @@ def backward_xy_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad
 
 def forward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float):
     """Unfused forward of the normalized triple: (out (3B,), score, cost)."""
-    x = _f32(x)
-    y = _f32(y)
+    x, y = _norm_pair(x, y)
     B, N, dim = x.shape
     score = torch.empty(score_elems(3 * B, N, N), dtype=torch.float32, device=x.device)
     cost = torch.empty(cost_elems(3 * B, N, N), dtype=torch.float32, device=x.device)
@@ -465,12 +470,13 @@ def forward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwi
 
 def backward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, cost: torch.Tensor,
                            grad_out: torch.Tensor | None, gamma: float, bandwidth: float):
-    x = _f32(x)
-    y = _f32(y)
+    x, y = _norm_pair(x, y)
     B, N, dim = x.shape
     gx = torch.empty_like(x)
     gy = torch.empty_like(y)
     g = None if grad_out is None else _f32(grad_out.reshape(-1))
+    if g is not None and g.numel() != 3 * B:
+        raise ValueError(f"normalize: expected {3 * B} upstream gradients, got {g.numel()}")
     ws = _norm_ws(B, N, dim, x.device)
     ev = _op_begin(x.device)
     with torch.cuda.device(x.device):
