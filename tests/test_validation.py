@@ -97,3 +97,14 @@ def test_unbatched_inputs():
     torch.manual_seed(0)
     out = softdtw(torch.randn(7, 3), torch.randn(5, 3))
     assert out.shape == (1,)
+
+
+def test_normalize_bindings_check_their_pair():
+    """The in-place normalize bindings refuse mismatched or host tensors
+    before calling the library."""
+    from softdtw_cuda import _native
+    x = torch.zeros(2, 5, 3)
+    with pytest.raises(ValueError, match="normalize"):
+        _native.forward_xy_norm(x, x, 1.0, -1.0)
+    with pytest.raises(ValueError, match="normalize"):
+        _native.forward_sqeuclid_norm(x, torch.zeros(2, 4, 3), 1.0, -1.0)
