@@ -281,6 +281,13 @@ int sdtw_backward_f64(const double *D, const double *R, const double *grad_out, 
 int sdtw_cost_sqeuclid_f64(const double *x, const double *y, double *D, int B, int N, int M, int dim,
                            void *stream);
 
+/* Chain rule of the fused cost in double: given G = dL/dD (B,N,M), writes
+ * grad_x = 2 (x rowsum(G) - G y) and grad_y = 2 (y colsum(G) - G^T x)
+ * (either pointer may be NULL), B <= 65535.
+ * -- replaces the two bmm of softdtw_cuda/autograd_xy.py:41-49 for float64 x, y */
+int sdtw_grad_sqeuclid_f64(const double *G, const double *x, const double *y, double *grad_x, double *grad_y,
+                           int B, int N, int M, int dim, void *stream);
+
 /* Allocation-free variant of sdtw_forward_f32 (no counterpart in the
  * reference).  For callers that cannot allocate device memory at call time --
  * a host runtime whose allocator owns all of device memory, a plugin boundary

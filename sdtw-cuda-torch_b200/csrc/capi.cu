@@ -718,6 +718,21 @@ int sdtw_backward_f64(const double* D, const double* R, const double* grad_out, 
     return SDTW_OK;
 }
 
+int sdtw_grad_sqeuclid_f64(const double* G, const double* x, const double* y, double* grad_x, double* grad_y, int B,
+                           int N, int M, int dim, void* stream) {
+    int rc = check_dims(B, N, M);
+    if (rc) return rc;
+    if (dim <= 0) return fail(SDTW_ERR_INVALID_ARGUMENT, "dim must be > 0");
+    if (!G || !x || !y) return fail(SDTW_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e;
+    {
+        KernelTimer kt("grad_f64", static_cast<cudaStream_t>(stream), (grad_x ? 1 : 0) + (grad_y ? 1 : 0));
+        e = launch_grad_f64(G, x, y, grad_x, grad_y, B, N, M, dim, static_cast<cudaStream_t>(stream));
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "grad launch");
+    return SDTW_OK;
+}
+
 int sdtw_cost_sqeuclid_f64(const double* x, const double* y, double* D, int B, int N, int M, int dim, void* stream) {
     int rc = check_dims(B, N, M);
     if (rc) return rc;

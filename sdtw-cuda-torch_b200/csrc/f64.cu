@@ -13,6 +13,8 @@
 //   bwd_f64_kernel   launcher.py:327-353  E[i,j] = sum over successors of E[s] * exp((R[s] - R[i,j] - D[s]) / gamma),
 //                                          then grad_D = grad_out[b] * E (autograd.py:46-47)
 //   cost_f64_kernel  kernels.py:27-31     D[i,j] = sum_k (x_ik - y_jk)^2 (the fused cost, direct form)
+//   grad_f64_kernel  autograd_xy.py:41-49 grad_x = 2 (x rowsum(G) - G y), grad_y = 2 (y colsum(G) - G^T x),
+//                                          the sums over the other sequence in double, in index order
 #include <cmath>
 #include <cstdint>
 
@@ -144,6 +146,43 @@ cudaError_t launch_cost_f64(const double* x, const double* y, double* D, int B, 
                             cudaStream_t stream) {
     const dim3 grid((M + 255) / 256, N, B);
     cost_f64_kernel<<<grid, 256, 0, stream>>>(x, y, D, N, M, dim);
+    return cudaGetLastError();
+}
+
+// One thread per (row r of the own sequence, feature f): lanes take 32
+// consecutive features of one row (the G element is a broadcast, the other
+// sequence's row a coalesced load); 8 rows per block.  COL = false: grad_x,
+// own = x (rows N), G row r; COL = true: grad_y, own = y (rows M), G column r.
+template <bool COL>
+__global__ void __launch_bounds__(256) grad_f64_kernel(const double* __restrict__ G, const double* __restrict__ own,
+                                                       const double* __restrict__ other, double* __restrict__ g,
+                                                       int N, int M, int dim) {
+    const int b = blockIdx.z;
+    const int r = blockIdx.x * 8 + threadIdx.y;
+    const int f = blockIdx.y * 32 + threadIdx.x;
+    const int rows = COL ? M : N, cols = COL ? N : M;
+    if (r >= rows || f >= dim) return;
+    const double* Gb = G + static_cast<size_t>(b) * N * M;
+    const double* ob = other + static_cast<size_t>(b) * cols * dim;
+    double s = 0.0, t = 0.0;
+    for (int c = 0; c < cols; ++c) {
+        const double w = COL ? Gb[static_cast<size_t>(c) * M + r] : Gb[static_cast<size_t>(r) * M + c];
+        s += w;
+        t = fma(w, ob[static_cast<size_t>(c) * dim + f], t);
+    }
+    const size_t o = (static_cast<size_t>(b) * rows + r) * dim + f;
+    g[o] = 2.0 * (own[o] * s - t);
+}
+
+cudaError_t launch_grad_f64(const double* G, const double* x, const double* y, double* gx, double* gy, int B, int N,
+                            int M, int dim, cudaStream_t stream) {
+    const dim3 block(32, 8);
+    if (gx) {
+        grad_f64_kernel<false><<<dim3((N + 7) / 8, (dim + 31) / 32, B), block, 0, stream>>>(G, x, y, gx, N, M, dim);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (gy) grad_f64_kernel<true><<<dim3((M + 7) / 8, (dim + 31) / 32, B), block, 0, stream>>>(G, y, x, gy, N, M, dim);
     return cudaGetLastError();
 }
 

@@ -235,5 +235,8 @@ cudaError_t launch_backward_f64(const double* D, const double* R, const double* 
                                 int M, double gamma, double bw, cudaStream_t stream);
 cudaError_t launch_cost_f64(const double* x, const double* y, double* D, int B, int N, int M, int dim,
                             cudaStream_t stream);
+// grad_x, grad_y (either may be null) of the direct cost from G = dL/dD (B,N,M), in double.
+cudaError_t launch_grad_f64(const double* G, const double* x, const double* y, double* gx, double* gy, int B, int N,
+                            int M, int dim, cudaStream_t stream);
 
 }  // namespace sdtw

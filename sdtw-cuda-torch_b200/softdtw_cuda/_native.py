@@ -60,6 +60,7 @@ _SIGS = {
     "sdtw_forward_f64": ([_P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
     "sdtw_backward_f64": ([_P, _P, _P, _P, _I, _I, _I, _Dbl, _Dbl, _P], _I),
     "sdtw_cost_sqeuclid_f64": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "sdtw_grad_sqeuclid_f64": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
     "sdtw_barycenter_workspace_bytes": ([_I, _I, _I, _I], _SZ),
     "sdtw_barycenter_grad_f32": ([_P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _SZ, _P], _I),
     "sdtw_barycenter_adam_f32": ([_P, _P, _P, _P, _SZ, _P, _I, _P, _P, _P, _F, _F, _F, _F, _P], _I),
@@ -577,6 +578,25 @@ def cost_sqeuclid_f64(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     _check(rc, "float64 cost")
     _op_end("cost_f64", x.device, ev)
     return D
+
+
+def grad_sqeuclid_f64(G: torch.Tensor, x: torch.Tensor, y: torch.Tensor, need_x: bool = True,
+                      need_y: bool = True):
+    """grad_x = 2 (x rowsum(G) - G y), grad_y = 2 (y colsum(G) - G^T x) in float64 on the GPU."""
+    G = _f64(G)
+    x = _f64(x)
+    y = _f64(y)
+    B, N, dim = x.shape
+    M = y.shape[1]
+    gx = torch.empty_like(x) if need_x else None
+    gy = torch.empty_like(y) if need_y else None
+    ev = _op_begin(x.device)
+    with torch.cuda.device(x.device):
+        rc = lib().sdtw_grad_sqeuclid_f64(_ptr(G), _ptr(x), _ptr(y), _ptr(gx), _ptr(gy), B, N, M, dim,
+                                          _stream(x.device))
+    _check(rc, "float64 chain rule")
+    _op_end("grad_f64", x.device, ev)
+    return gx, gy
 
 
 # ----------------------------------------------------------------------------- CPU ops

@@ -5,8 +5,8 @@ sum_k (x_ik - y_jk)^2 inside the library (no cost tensor is returned to the
 caller) and its backward returns dL/dX and dL/dY directly:
     grad_X = 2 (X * rowsum(G) - G Y),  grad_Y = 2 (Y * colsum(G) - G^T X),
 G = grad_out[b] * E[b].  CUDA only, as in the reference.  float64 inputs take
-the library's float64 device path (cost, forward and backward in double);
-their two contractions with G are float64 torch bmm.
+the library's float64 device path (cost, forward, backward and this chain rule
+in double).
 """
 from __future__ import annotations
 
@@ -47,13 +47,8 @@ class SoftDTWXYAutograd(Function):
         if ctx.f64:
             X, Y, D, R = ctx.saved_tensors
             G = _native.backward_f64(D, R, grad_output, ctx.gamma, ctx.bandwidth)
-            Xd, Yd = X.detach().double(), Y.detach().double()
-            gx = gy = None
-            if ctx.needs_input_grad[0]:
-                gx = (2.0 * (Xd * G.sum(dim=2, keepdim=True) - torch.bmm(G, Yd))).to(X.dtype)
-            if ctx.needs_input_grad[1]:
-                gy = (2.0 * (Yd * G.sum(dim=1).unsqueeze(2) - torch.bmm(G.transpose(1, 2), Xd))).to(Y.dtype)
-            return gx, gy, None, None
+            gx, gy = _native.grad_sqeuclid_f64(G, X, Y, ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+            return (None if gx is None else gx.to(X.dtype)), (None if gy is None else gy.to(Y.dtype)), None, None
         X, Y, score = ctx.saved_tensors
         gx, gy = _native.backward_xy(X, Y, score, grad_output, ctx.gamma, ctx.bandwidth,
                                      need_x=ctx.needs_input_grad[0], need_y=ctx.needs_input_grad[1])

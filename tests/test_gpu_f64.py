@@ -81,3 +81,21 @@ def test_f64_fused_equals_unfused():
     torch.testing.assert_close(a, b, rtol=1e-10, atol=1e-10)
     for u, v in zip(ga, gb):
         torch.testing.assert_close(u, v, rtol=1e-8, atol=1e-10)
+
+
+@pytest.mark.parametrize("N,M,dim", [(37, 29, 3), (20, 45, 70)])
+def test_f64_chain_rule_kernel(N, M, dim):
+    """sdtw_grad_sqeuclid_f64 against numpy in double: N != M, feature counts
+    below and above one 32-feature block, either gradient alone."""
+    rng = np.random.default_rng(N * M + dim)
+    G = rng.random((3, N, M))
+    x = rng.standard_normal((3, N, dim))
+    y = rng.standard_normal((3, M, dim))
+    gx_ref = 2.0 * (x * G.sum(2)[:, :, None] - G @ y)
+    gy_ref = 2.0 * (y * G.sum(1)[:, :, None] - np.swapaxes(G, 1, 2) @ x)
+    t = lambda a: torch.tensor(a, device="cuda")
+    gx, gy = _native.grad_sqeuclid_f64(t(G), t(x), t(y))
+    np.testing.assert_allclose(gx.cpu().numpy(), gx_ref, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(gy.cpu().numpy(), gy_ref, rtol=1e-12, atol=1e-12)
+    gx_only, none = _native.grad_sqeuclid_f64(t(G), t(x), t(y), True, False)
+    assert none is None and torch.equal(gx_only, gx)
