@@ -7,6 +7,7 @@ current CUDA stream; the kernels are the library's.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -136,6 +137,16 @@ def _ptr(t: torch.Tensor | None):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+_SAME_DEVICE = contextlib.nullcontext()
+
+
+def _on(device: torch.device):
+    """The device's context for a library call: a no-op when it is already current."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _SAME_DEVICE
+    return torch.cuda.device(device)
+
+
 def _stream(device: torch.device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
@@ -216,6 +227,8 @@ def workspace(B: int, N: int, M: int, device, dim: int | None = None) -> torch.T
 
 
 def _f32(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype is torch.float32 and t.is_contiguous():
+        return t.detach()
     return t.detach().to(dtype=torch.float32).contiguous()
 
 
@@ -237,7 +250,7 @@ def barycenter_grad(bary: torch.Tensor, X: torch.Tensor, w: torch.Tensor, grad_l
             raise ValueError("barycenter_grad: operands must be contiguous float32 tensors on one device")
     if bary.shape != (N, dim) or w.shape != (B,) or grad_loss.numel() != N * dim + 1:
         raise ValueError("barycenter_grad: shape mismatch")
-    with torch.cuda.device(X.device):
+    with _on(X.device):
         rc = lib().sdtw_barycenter_grad_f32(_ptr(bary), _ptr(X), _ptr(w), _ptr(grad_loss), B, N, M, dim,
                                             float(gamma), _ptr(ws), ws.numel(), _stream(X.device))
     _check(rc, "barycenter gradient")
@@ -250,7 +263,7 @@ def barycenter_adam(bary, exp_avg, exp_avg_sq, grad_loss, lr_table, step, loss_h
     n = bary.numel()
     if step.dtype != torch.int32:
         raise ValueError("barycenter_adam: step must be an int32 tensor")
-    with torch.cuda.device(bary.device):
+    with _on(bary.device):
         rc = lib().sdtw_barycenter_adam_f32(_ptr(bary), _ptr(exp_avg), _ptr(exp_avg_sq), _ptr(grad_loss), n,
                                             _ptr(lr_table), lr_table.numel(), _ptr(step), _ptr(loss_hist),
                                             _ptr(bary_hist), float(beta1), float(beta2), float(eps), float(max_norm),
@@ -270,7 +283,7 @@ def barycenter_sync_adam(grad_loss, peers, world, rank, epoch, bary, exp_avg, ex
     n = bary.numel()
     if step.dtype != torch.int32 or epoch.dtype != torch.int64 or peers.dtype != torch.int64:
         raise ValueError("barycenter_sync_adam: step int32, epoch and peers int64 tensors")
-    with torch.cuda.device(bary.device):
+    with _on(bary.device):
         rc = lib().sdtw_barycenter_sync_adam_f32(_ptr(grad_loss), n, _ptr(peers), int(world), int(rank), _ptr(epoch),
                                                  _ptr(bary), _ptr(exp_avg), _ptr(exp_avg_sq), _ptr(lr_table),
                                                  lr_table.numel(), _ptr(step), _ptr(loss_hist), _ptr(bary_hist),
@@ -286,7 +299,7 @@ def cost_sqeuclid(x: torch.Tensor, y: torch.Tensor, direct: bool = False) -> tor
     M = y.shape[1]
     D = torch.empty((B, N, M), dtype=torch.float32, device=x.device)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_cost_sqeuclid_f32(_ptr(x), _ptr(y), _ptr(D), B, N, M, dim, int(direct), _stream(x.device))
     _check(rc, "cost")
     _op_end("cost", x.device, ev)
@@ -301,7 +314,7 @@ def forward(D: torch.Tensor, gamma: float, bandwidth: float):
     out = torch.empty(B, dtype=torch.float32, device=D.device)
     ws = workspace(B, N, M, D.device)
     ev = _op_begin(D.device)
-    with torch.cuda.device(D.device):
+    with _on(D.device):
         rc = lib().sdtw_forward_f32(_ptr(D), _ptr(score), _ptr(out), B, N, M, float(gamma), float(bandwidth),
                                     _ptr(ws), ws.numel(), _stream(D.device))
     _check(rc, "forward")
@@ -317,7 +330,7 @@ def backward(score: torch.Tensor, grad_out: torch.Tensor | None, B: int, N: int,
     g = None if grad_out is None else _f32(grad_out.reshape(-1))
     ws = workspace(B, N, M, dev)
     ev = _op_begin(dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         rc = lib().sdtw_backward_f32(_ptr(score), _ptr(g), _ptr(E), B, N, M, float(gamma), float(bandwidth),
                                      _ptr(ws), ws.numel(), _stream(dev))
     _check(rc, "backward")
@@ -334,7 +347,7 @@ def forward_xy(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: float)
     out = torch.empty(B, dtype=torch.float32, device=x.device)
     ws = workspace(B, N, M, x.device, dim)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_forward_xy_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(out), B, N, M, dim, float(gamma),
                                        float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
     _check(rc, "fused forward")
@@ -353,7 +366,7 @@ def backward_xy(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad_out:
     g = None if grad_out is None else _f32(grad_out.reshape(-1))
     ws = workspace(B, N, M, x.device, dim)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_backward_xy_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(g), _ptr(gx), _ptr(gy), B, N, M, dim,
                                         float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
     _check(rc, "fused backward")
@@ -372,7 +385,7 @@ def forward_sqeuclid(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: 
     out = torch.empty(B, dtype=torch.float32, device=x.device)
     ws = workspace(B, N, M, x.device)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_forward_sqeuclid_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(out), B, N, M, dim,
                                              float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
     _check(rc, "unfused forward")
@@ -392,7 +405,7 @@ def backward_sqeuclid(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, cos
     g = None if grad_out is None else _f32(grad_out.reshape(-1))
     ws = workspace(B, N, M, x.device, dim)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_backward_sqeuclid_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(g), _ptr(gx), _ptr(gy),
                                               B, N, M, dim, float(gamma), float(bandwidth), _ptr(ws), ws.numel(),
                                               _stream(x.device))
@@ -423,7 +436,7 @@ def forward_xy_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwidth: f
     out = torch.empty(3 * B, dtype=torch.float32, device=x.device)
     ws = workspace(3 * B, N, N, x.device, dim)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_forward_xy_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(out), B, N, dim, float(gamma),
                                             float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
     _check(rc, "fused normalized forward")
@@ -443,7 +456,7 @@ def backward_xy_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor, grad
         raise ValueError(f"normalize: expected {3 * B} upstream gradients, got {g.numel()}")
     ws = _norm_ws(B, N, dim, x.device)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_backward_xy_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(g), _ptr(gx), _ptr(gy), B, N, dim,
                                              float(gamma), float(bandwidth), _ptr(ws), ws.numel(), _stream(x.device))
     _check(rc, "fused normalized backward")
@@ -460,7 +473,7 @@ def forward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, gamma: float, bandwi
     out = torch.empty(3 * B, dtype=torch.float32, device=x.device)
     ws = workspace(3 * B, N, N, x.device)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_forward_sqeuclid_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(out), B, N, dim,
                                                   float(gamma), float(bandwidth), _ptr(ws), ws.numel(),
                                                   _stream(x.device))
@@ -480,7 +493,7 @@ def backward_sqeuclid_norm(x: torch.Tensor, y: torch.Tensor, score: torch.Tensor
         raise ValueError(f"normalize: expected {3 * B} upstream gradients, got {g.numel()}")
     ws = _norm_ws(B, N, dim, x.device)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_backward_sqeuclid_norm_f32(_ptr(x), _ptr(y), _ptr(score), _ptr(cost), _ptr(g), _ptr(gx),
                                                    _ptr(gy), B, N, dim, float(gamma), float(bandwidth), _ptr(ws),
                                                    ws.numel(), _stream(x.device))
@@ -500,7 +513,7 @@ def grad_sqeuclid(G: torch.Tensor, D_mask: torch.Tensor | None, x: torch.Tensor,
     gx = torch.empty_like(x) if need_x else None
     gy = torch.empty_like(y) if need_y else None
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_grad_sqeuclid_f32(_ptr(G), _ptr(Dm), _ptr(x), _ptr(y), _ptr(gx), _ptr(gy), B, N, M, dim,
                                           _stream(x.device))
     _check(rc, "cost gradient")
@@ -510,7 +523,7 @@ def grad_sqeuclid(G: torch.Tensor, D_mask: torch.Tensor | None, x: torch.Tensor,
 
 def score_to_R(score: torch.Tensor, B: int, N: int, M: int, gamma: float) -> torch.Tensor:
     R = torch.empty((B, N + 2, M + 2), dtype=torch.float32, device=score.device)
-    with torch.cuda.device(score.device):
+    with _on(score.device):
         rc = lib().sdtw_score_to_R_f32(_ptr(score), _ptr(R), B, N, M, float(gamma), _stream(score.device))
     _check(rc, "score_to_R")
     _op_end("score_to_R", score.device, None)
@@ -522,7 +535,7 @@ def R_to_score(R: torch.Tensor, gamma: float) -> torch.Tensor:
     B, N2, M2 = R.shape
     N, M = N2 - 2, M2 - 2
     score = torch.empty(score_elems(B, N, M), dtype=torch.float32, device=R.device)
-    with torch.cuda.device(R.device):
+    with _on(R.device):
         rc = lib().sdtw_R_to_score_f32(_ptr(R), _ptr(score), B, N, M, float(gamma), _stream(R.device))
     _check(rc, "R_to_score")
     _op_end("R_to_score", R.device, None)
@@ -541,7 +554,7 @@ def forward_f64(D: torch.Tensor, gamma: float, bandwidth: float):
     R = torch.empty((B, N + 2, M + 2), dtype=torch.float64, device=D.device)
     out = torch.empty(B, dtype=torch.float64, device=D.device)
     ev = _op_begin(D.device)
-    with torch.cuda.device(D.device):
+    with _on(D.device):
         rc = lib().sdtw_forward_f64(_ptr(D), _ptr(R), _ptr(out), B, N, M, float(gamma), float(bandwidth),
                                     _stream(D.device))
     _check(rc, "float64 forward")
@@ -557,7 +570,7 @@ def backward_f64(D: torch.Tensor, R: torch.Tensor, grad_out: torch.Tensor | None
     E = torch.empty((B, N, M), dtype=torch.float64, device=D.device)
     g = None if grad_out is None else grad_out.detach().reshape(-1).to(device=D.device, dtype=torch.float64).contiguous()
     ev = _op_begin(D.device)
-    with torch.cuda.device(D.device):
+    with _on(D.device):
         rc = lib().sdtw_backward_f64(_ptr(D), _ptr(R), _ptr(g), _ptr(E), B, N, M, float(gamma), float(bandwidth),
                                      _stream(D.device))
     _check(rc, "float64 backward")
@@ -573,7 +586,7 @@ def cost_sqeuclid_f64(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     M = y.shape[1]
     D = torch.empty((B, N, M), dtype=torch.float64, device=x.device)
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_cost_sqeuclid_f64(_ptr(x), _ptr(y), _ptr(D), B, N, M, dim, _stream(x.device))
     _check(rc, "float64 cost")
     _op_end("cost_f64", x.device, ev)
@@ -591,7 +604,7 @@ def grad_sqeuclid_f64(G: torch.Tensor, x: torch.Tensor, y: torch.Tensor, need_x:
     gx = torch.empty_like(x) if need_x else None
     gy = torch.empty_like(y) if need_y else None
     ev = _op_begin(x.device)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         rc = lib().sdtw_grad_sqeuclid_f64(_ptr(G), _ptr(x), _ptr(y), _ptr(gx), _ptr(gy), B, N, M, dim,
                                           _stream(x.device))
     _check(rc, "float64 chain rule")
