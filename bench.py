@@ -339,11 +339,11 @@ def main():
 
         def timed(fn, k):
             times = []
-            # About 0.2 ms of device work ahead of the first step (outside the
+            # About 0.7 ms of device work ahead of the first step (outside the
             # events): the first step then finds its kernels queued, as every
             # later step does, instead of the device waiting on the host's
             # first launches.
-            for _ in range(4):
+            for _ in range(16):
                 flush.zero_()
             for _ in range(k):
                 flush.zero_()
@@ -703,7 +703,7 @@ def main():
                                    else f"dp{world} (batch-sharded, no collective)"),
                    "l2": ("per-iteration working set (about 1 GB of tables) larger than the 126 MB L2" if is_bary else
                           "flushed before every timed step (256 MiB write, outside the events)"),
-                   "queue_warmup": "4 L2-flush writes (about 0.2 ms) queued ahead of the first timed step, outside the events",
+                   "queue_warmup": "16 L2-flush writes (about 0.7 ms) queued ahead of the first timed step, outside the events",
                    "kernel_timing": ("kernel_ms_per_step and the roofline's launch durations: per-kernel CUDA events "
                                      "in a second pass of the same K steps; ms_per_step comes from the pass "
                                      "without them"),
