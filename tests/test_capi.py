@@ -74,6 +74,10 @@ def test_invalid_arguments_rejected():
     assert rc == 1 and b"must be > 0" in L.sdtw_last_error_message()
     rc = L.sdtw_backward_sqeuclid_norm_f32(None, None, None, None, None, None, None, 1, 4, 3, 0.0, -1.0, None, 0, None)
     assert rc == 1 and b"gamma" in L.sdtw_last_error_message()
+    rc = L.sdtw_grad_sqeuclid_f64(None, None, None, None, None, 2, 4, 4, 3, None)
+    assert rc == 1 and b"null pointer" in L.sdtw_last_error_message()
+    rc = L.sdtw_grad_sqeuclid_f64(None, None, None, None, None, 0, 4, 4, 3, None)
+    assert rc == 1 and b"must be > 0" in L.sdtw_last_error_message()
 
 
 def test_timing_registry_without_gpu():
